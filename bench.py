@@ -1,0 +1,489 @@
+#!/usr/bin/env python3
+"""Benchmark of the mHC layer hot path (dynamic-H forward + backward).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
+                    [--config cfg3|cfg5|cfg4|cfg4_bf16]
+
+Metric: mHC layer fwd+bwd tokens/s at n=4, C=4096; weak
+scaling (8192 tokens per GPU, the cfg3 workload) on 1/2/4/8 GPUs of one node.
+A step = one fused forward + one fused backward of the layer over one batch,
+with a fixed synthetic upstream gradient; at N>1 it also all-reduces the
+parameter gradients over NCCL (one flat bucket).  Inputs (512 MiB of x,
+512 MiB of grad_out) are larger than the 126 MB L2, so no flush is needed
+between steps.  The timed region is K steps bracketed by barrier +
+synchronize, timed with CUDA events on the launching stream, max over ranks.
+
+``--impl reference`` times the reference's algorithm on the host CPU (the
+oracle restatement of its fp32 PyTorch formulation, which is the reference's
+own CPU code path) on a bounded token sample per step, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (tokens per GPU, n, C, mode)
+    "cfg3": (8192, 4, 4096, "dynamic"),
+    "cfg5": (32768, 4, 7168, "dynamic"),
+    "cfg4": (65536, 4, 4096, "static_fwd"),
+    "cfg4_bf16": (65536, 4, 4096, "static_fwd_bf16"),
+}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def algorithmic_bytes(mode, B, n, C):
+    """SURVEY 8(d) accounting: fwd reads x, writes out; bwd reads x and g,
+    writes gx; phi read twice + dphi written (fp32); w read + gw written."""
+    s = 4
+    nC = n * C
+    P = nC * (n * n + 2 * n)
+    if mode == "dynamic":
+        return B * 5 * nC * s + 12 * P + 8 * C
+    if mode == "static_fwd":
+        return B * 2 * nC * 4
+    if mode == "static_fwd_bf16":
+        return B * 2 * nC * 2
+    raise ValueError(mode)
+
+
+def kernel_bytes(name, B, n, C):
+    """Algorithmic bytes per launch of the layer kernels (unique data a launch
+    must move: its inputs once and its outputs once)."""
+    nC = n * C
+    NH = n * n + 2 * n
+    x = B * nC * 4
+    return {
+        "proj_stats": x + NH * nC * 4,
+        "stream_fwd": 2 * x + C * 4,
+        "bwd_stats": 2 * x + C * 4,
+        "grad_x": 3 * x + 2 * NH * nC * 4 + C * 4,
+        "static_fwd": 2 * x,
+    }.get(name)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        backend = "nccl" if args.impl == "mine" else "gloo"
+        if args.impl == "mine":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend=backend)
+    return world, rank, local
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def time_cpu_oracle(n, C, mode, sample_tokens, seconds, min_reps=2):
+    """Reference's fp32 formulation on the host cores: tokens/s over a bounded
+    sample (repeated steps of `sample_tokens` tokens for about `seconds`)."""
+    from oracle import mhc_oracle as O
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(sample_tokens, n, C, generator=gen)
+    params = O.make_dynamic_params(n, C, gen)
+    grad = torch.randn(sample_tokens, n, C, generator=gen)
+
+    def step():
+        if mode == "dynamic":
+            O.dynamic_fwd_bwd(x, params, grad)
+        else:
+            with torch.no_grad():
+                O.mhc_layer_static(x, torch.ones(C), torch.randn(n, generator=gen),
+                                   torch.randn(n, generator=gen), torch.randn(n, n, generator=gen))
+
+    step()  # warm-up
+    times = []
+    t_end = time.perf_counter() + seconds
+    while len(times) < min_reps or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": sample_tokens / med, "unit": "tokens/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{len(times)} steps of {sample_tokens} tokens (n={n}, C={C}, {mode}, fp32), "
+                      f"median {med * 1e3:.1f} ms/step, CPU: {cpu_model()}"}
+
+
+def run_reference(args, world, rank):
+    tokens, n, C, mode = CONFIGS[args.config]
+    if rank != 0:
+        return
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    from oracle import mhc_oracle as O
+    gen = torch.Generator().manual_seed(0)
+    w = torch.ones(C)
+    Hs = (torch.randn(n, generator=gen), torch.randn(n, generator=gen),
+          torch.randn(n, n, generator=gen))
+    params = O.make_dynamic_params(n, C, gen)
+
+    def make(sample):
+        return (torch.randn(sample, n, C, generator=gen), torch.randn(sample, n, C, generator=gen))
+
+    # bounded sample: size the per-step token count so warm-up + steps take
+    # about two minutes of host time in total
+    sample = 256
+    x, grad = make(sample)
+    t0 = time.perf_counter()
+    if mode == "dynamic":
+        O.dynamic_fwd_bwd(x, params, grad)
+    else:
+        with torch.no_grad():
+            O.mhc_layer_static(x, w, *Hs)
+    per_token = (time.perf_counter() - t0) / sample
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    sample = int(max(8, min(2048, budget / max(per_token, 1e-9))))
+    x, grad = make(sample)
+
+    def step():
+        if mode == "dynamic":
+            O.dynamic_fwd_bwd(x, params, grad)
+        else:
+            with torch.no_grad():
+                O.mhc_layer_static(x, w, *Hs)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = sample / dt
+    line = {
+        "metric": "mHC layer fwd+bwd tokens/s (n=4, C=4096)" if mode == "dynamic"
+        else "mHC static-H layer forward tokens/s",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": f"{args.config}: {mode}, n={n}, C={C}, {tokens} tokens per step "
+                               f"on the GPU arm; CPU sample {sample} tokens per step",
+                   "global_batch": sample, "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} tokens per step x {args.steps} steps, "
+                                   f"oracle restatement of the reference's fp32 PyTorch path, "
+                                   f"CPU: {cpu_model()}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_mine(args, world, rank, local):
+    import torch.distributed as dist
+    import mhc_ascend_b200 as mhc
+    from mhc_ascend_b200 import _C, ops
+    from mhc_ascend_b200.dp import GradBucket
+
+    tokens, n, C, mode = CONFIGS[args.config]
+    if args.tokens:
+        tokens = args.tokens
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(tokens, n, C, device=dev, generator=gen)
+    g = torch.randn(tokens, n, C, device=dev, generator=gen)
+    dynamic = mode == "dynamic"
+    layer = mhc.MHCLayer(hidden_dim=C, expansion_rate=n, use_dynamic_h=dynamic,
+                         bf16_io=(mode == "static_fwd_bf16")).to(dev)
+    bucket = GradBucket(layer.parameters())
+    if mode == "static_fwd_bf16":
+        x = x.bfloat16()
+        layer.eval()
+    elif mode == "static_fwd":
+        layer.eval()
+
+    def step():
+        if dynamic:
+            out = layer(x)
+            out.backward(g)
+            if world > 1:
+                bucket.allreduce()
+            for p in layer.parameters():
+                p.grad = None
+        else:
+            with torch.no_grad():
+                layer(x)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = start.elapsed_time(stop) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    value = tokens * world / (ms * 1e-3)
+
+    # Per-kernel timing (CUDA events around each launch on the launch stream)
+    prof_steps = max(3, min(args.steps, 50))
+    torch.cuda.synchronize()
+    _C.profile_enable(True)
+    for _ in range(prof_steps):
+        step()
+    torch.cuda.synchronize()
+    _C.profile_enable(False)
+    rep = _C.profile_report()
+    launches_per_step = sum(c for c, _ in rep.values()) / prof_steps
+    kernels = {}
+    for name, (cnt, tot) in rep.items():
+        avg = tot / cnt
+        kb = kernel_bytes(name, tokens, n, C)
+        kernels[name] = {"launches_per_step": cnt / prof_steps, "avg_ms": avg,
+                         "share": tot / sum(t for _, t in rep.values()),
+                         "gbs": (kb / (avg * 1e-3) / 1e9) if kb else None}
+    dom = max(rep, key=lambda k: rep[k][1])
+    peak, peak_kind = peaks()
+    dom_avg = rep[dom][1] / rep[dom][0]
+    dom_bytes = kernel_bytes(dom, tokens, n, C)
+    achieved = dom_bytes / (dom_avg * 1e-3) / 1e9 if dom_bytes else None
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    if os.path.exists(tf):
+        for line in open(tf):
+            parts = line.split()
+            if len(parts) >= 3 and parts[0] == dom and parts[1] == args.config:
+                traffic = float(parts[2])
+    step_bytes = algorithmic_bytes(mode, tokens, n, C)
+    step_gbs = step_bytes / (ms * 1e-3) / 1e9
+
+    # End to end through the public API with host buffers: pinned x -> device,
+    # fwd + loss + bwd, loss -> host, every step.
+    e2e = None
+    if dynamic and not args.no_e2e:
+        xh = x.cpu().pin_memory()
+        e2e_steps = max(3, min(args.steps // 20, 30))
+
+        def e2e_step():
+            xd = xh.to(dev, non_blocking=True)
+            out = layer(xd)
+            loss = (out * out).sum()
+            loss.backward()
+            if world > 1:
+                bucket.allreduce()
+            for p in layer.parameters():
+                p.grad = None
+            return loss.item()
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1) / e2e_steps
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = t.item()
+        e2e = {"value": tokens * world / (ems * 1e-3), "unit": "tokens/s",
+               "h2d_bytes_per_step": xh.numel() * xh.element_size(), "d2h_bytes_per_step": 4,
+               "ms_per_step": ems,
+               "note": "MHCLayer(x) with x copied from pinned host memory each step, "
+                       "loss=sum(out^2), backward, loss.item()"}
+    elif not dynamic and not args.no_e2e:
+        xh = x.cpu().pin_memory()
+        oh = torch.empty(tokens, n, C, dtype=x.dtype).pin_memory()
+        e2e_steps = max(3, min(args.steps // 20, 30))
+
+        def e2e_step():
+            with torch.no_grad():
+                out = layer(xh.to(dev, non_blocking=True))
+            oh.copy_(out, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1) / e2e_steps
+        e2e = {"value": tokens * world / (ems * 1e-3), "unit": "tokens/s",
+               "h2d_bytes_per_step": xh.numel() * xh.element_size(),
+               "d2h_bytes_per_step": oh.numel() * oh.element_size(), "ms_per_step": ems}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = time_cpu_oracle(n, C, mode, 512 if C <= 4096 else 256, args.cpu_seconds)
+
+    if rank == 0:
+        metric = ("mHC layer fwd+bwd tokens/s (n=4, C=4096)" if dynamic
+                  else "mHC static-H layer forward tokens/s")
+        line = {
+            "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if mode == "static_fwd_bf16" else "f32", "data": "synthetic",
+            "impl": "mine",
+            "config": {"workload": f"{args.config}: {mode}, n={n}, C={C}, {tokens} tokens per GPU "
+                                   f"per step" + (", NCCL grad all-reduce" if world > 1 else ""),
+                       "tokens_per_gpu": tokens, "global_batch": tokens * world,
+                       "parallelism": f"dp{world}",
+                       "l2": "no flush: each step streams >= 1 GiB (x, grad_out), > 126 MB L2"},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
+                         "traffic": traffic, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": dom_bytes},
+            "step_roofline": {"algorithmic_bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
+                              "frac": step_gbs / peak, "peak_kind": peak_kind},
+            "kernels": kernels,
+            "gpu_launches": int(round(launches_per_step * args.steps)),
+            "clocks": clk,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg3")
+    ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_mine(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,216 @@
+/*
+ * mhc_b200.h -- C-ABI of the B200 (sm_100a) mHC kernels.
+ *
+ * This is the drop-in boundary that replaces the reference's pybind11 module
+ * `mhc_ascend` (ParadoxZW/mHC_Ascend, src/python/bindings.cpp:1020-1117).  Each
+ * entry point below names the reference function it replaces.
+ *
+ * Conventions (all entry points):
+ *   - Every pointer is a DEVICE pointer to contiguous row-major fp32 data
+ *     (bf16 only where the name says so), on the device that is current for
+ *     the calling thread.  `stream` is a cudaStream_t passed as void*.
+ *   - Outputs are written, never accumulated into; the caller allocates them
+ *     (the reference allocates fresh outputs with at::empty; here the Python
+ *     layer allocates them with torch and passes them in).
+ *   - Scalars that are parameters of the model (alpha, biases) are passed as
+ *     device pointers, so a call never synchronises the host (the reference
+ *     calls .item() on them: src/python/mhc/ops.py:420-422, 533-535).
+ *   - Entry points that need scratch memory take (workspace, workspace_bytes)
+ *     and have a *_workspace_bytes() query; they never allocate.
+ *   - Return 0 (MHC_OK) on success, a negative MHC_ERR_* code otherwise;
+ *     mhc_get_last_error_string() then describes the failure (per thread).
+ *   - No entry point synchronises the stream or the device.
+ */
+#ifndef MHC_B200_H_
+#define MHC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MHC_API __attribute__((visibility("default")))
+#else
+#define MHC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MHC_OK 0
+#define MHC_ERR_INVALID_ARG (-1)  /* bad shape / NULL pointer / bad hyper-parameter */
+#define MHC_ERR_UNSUPPORTED (-2)  /* valid request this build does not implement */
+#define MHC_ERR_ALIGNMENT (-3)    /* pointer not 16-byte aligned where required */
+#define MHC_ERR_WORKSPACE (-4)    /* workspace NULL or smaller than *_workspace_bytes() */
+#define MHC_ERR_CUDA (-5)         /* a CUDA launch reported an error */
+
+/* Library identification and the per-thread description of the last error. */
+MHC_API const char* mhc_version(void);
+MHC_API const char* mhc_get_last_error_string(void);
+
+/* ---------------------------------------------------------------------------
+ * Sinkhorn-Knopp on a batch of square matrices [batch, n, n], 1 <= n <= 32.
+ * Each iteration divides rows by (row sum + eps), then columns by
+ * (column sum + eps) -- reference formulation ops_pytorch_backward.py:9-33.
+ * ------------------------------------------------------------------------- */
+/* replaces sinkhorn_knopp_fwd (bindings.cpp:155-187) */
+MHC_API int mhc_sinkhorn_knopp_fwd(const float* inp, float* out, int64_t batch, int32_t n,
+                           int32_t num_iters, float eps, void* stream);
+/* replaces sinkhorn_knopp_bwd (bindings.cpp:189-231); exact reverse mode of
+ * the forward above.  `out` (the forward result) is accepted for interface
+ * parity and is not read: the forward is replayed from `inp`. */
+MHC_API int mhc_sinkhorn_knopp_bwd(const float* grad_out, const float* inp, const float* out,
+                           float* grad_inp, int64_t batch, int32_t n, int32_t num_iters,
+                           float eps, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * RMSNorm over rows of [batch, hidden]: out = inp / sqrt(mean(inp^2)+eps) * w
+ * ------------------------------------------------------------------------- */
+/* replaces rmsnorm_fwd (bindings.cpp:237-265); rms[batch] receives the row rms */
+MHC_API int mhc_rmsnorm_fwd(const float* inp, const float* weight, float* out, float* rms,
+                    int64_t batch, int64_t hidden, float eps, void* stream);
+/* replaces rmsnorm_bwd (bindings.cpp:267-301).  grad_weight is a fixed-order
+ * (atomic-free, deterministic) reduction over rows through the workspace. */
+MHC_API size_t mhc_rmsnorm_bwd_workspace_bytes(int64_t batch, int64_t hidden);
+MHC_API int mhc_rmsnorm_bwd(const float* grad_out, const float* inp, const float* weight,
+                    const float* rms, float* grad_inp, float* grad_weight, int64_t batch,
+                    int64_t hidden, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Stream aggregate: out[b,c] = sum_i sigmoid(H_pre_raw[b,i]) * inp[b,i,c]
+ * ------------------------------------------------------------------------- */
+/* replaces stream_aggregate_fwd (bindings.cpp:307-340); also writes
+ * H_pre_act = sigmoid(H_pre_raw).  Output is fp32 (the reference writes bf16). */
+MHC_API int mhc_stream_aggregate_fwd(const float* inp, const float* H_pre_raw, float* out,
+                             float* H_pre_act, int64_t batch, int32_t n, int64_t hidden,
+                             void* stream);
+/* replaces stream_aggregate_bwd (bindings.cpp:342-374): grad_inp[b,i,c] =
+ * H_pre_act[b,i]*grad_out[b,c]; grad_H_pre_act[b,i] = sum_c grad_out*inp. */
+MHC_API int mhc_stream_aggregate_bwd(const float* grad_out, const float* inp, const float* H_pre_act,
+                             float* grad_inp, float* grad_H_pre_act, int64_t batch, int32_t n,
+                             int64_t hidden, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Stream distribute-mix-add:
+ *   out[b,i,c] = 2*sigmoid(H_post_raw[b,i]) * y_norm[b,c] + sum_j M[b,i,j] x[b,j,c]
+ * ------------------------------------------------------------------------- */
+/* replaces stream_distribute_mix_add_fwd (bindings.cpp:380-412); also writes
+ * H_post_act = 2*sigmoid(H_post_raw). */
+MHC_API int mhc_stream_distribute_mix_add_fwd(const float* y_norm, const float* H_post_raw,
+                                      const float* M, const float* x_inp, float* out,
+                                      float* H_post_act, int64_t batch, int32_t n,
+                                      int64_t hidden, void* stream);
+/* replaces stream_distribute_mix_add_bwd (bindings.cpp:414-460): gradients
+ * w.r.t. x, y_norm, M and H_post_act (the caller applies the activation
+ * derivative, as ops.py:240-242 does). */
+MHC_API int mhc_stream_distribute_mix_add_bwd(const float* grad_out, const float* x_inp,
+                                      const float* y_norm, const float* M,
+                                      const float* H_post_act, float* grad_x,
+                                      float* grad_y_norm, float* grad_M,
+                                      float* grad_H_post_act, int64_t batch, int32_t n,
+                                      int64_t hidden, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Row RMS and the dynamic-H projection
+ * ------------------------------------------------------------------------- */
+/* replaces compute_rms_fwd (bindings.cpp:543-566): rms[b] = sqrt(mean(inp[b]^2)+eps) */
+MHC_API int mhc_compute_rms_fwd(const float* inp, float* rms, int64_t batch, int64_t k, float eps,
+                        void* stream);
+/* replaces fused_rmsnorm_matmul_fwd (bindings.cpp:480-528): out[b,o] =
+ * sum_k inp[b,k]*weight[o,k], computed in fp32 (the reference casts to bf16). */
+MHC_API int mhc_fused_rmsnorm_matmul_fwd(const float* inp, const float* weight, float* out,
+                                 int64_t batch, int64_t k, int32_t out_dim, void* stream);
+/* replaces fused_rmsnorm_matmul_bwd (bindings.cpp:530-541): grad_inp =
+ * grad_out @ weight, grad_weight = grad_out^T @ inp (fixed-order reduction). */
+MHC_API size_t mhc_fused_rmsnorm_matmul_bwd_workspace_bytes(int64_t batch, int64_t k, int32_t out_dim);
+MHC_API int mhc_fused_rmsnorm_matmul_bwd(const float* grad_out, const float* inp, const float* weight,
+                                 float* grad_inp, float* grad_weight, int64_t batch, int64_t k,
+                                 int32_t out_dim, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused mHC layer, dynamic H.
+ *
+ * Per-token record saved by the forward for the backward ("token_state",
+ * [batch, mhc_token_state_stride(n)] fp32):
+ *   [0] rms_h  (rms of the flattened n*C token vector)
+ *   [1] rms    (rms of the aggregated stream, RMSNorm denominator)
+ *   [2, 2+n)          H_pre_act  = sigmoid(H_pre_tilde)
+ *   [2+n, 2+2n)       H_post_act = 2*sigmoid(H_post_tilde)
+ *   [2+2n, 2+2n+n*n)  M          = Sinkhorn(exp(H_res_tilde))
+ *   [2+2n+n*n, ...+n*n+2n)  raw projections p = x_flat @ phi^T (pre|post|res)
+ * ------------------------------------------------------------------------- */
+MHC_API int32_t mhc_token_state_stride(int32_t n);
+
+/* replaces mhc_layer_fwd_dynamic (bindings.cpp:880-952).  alpha_* point to
+ * one device float each; b_res is [n,n].  token_state may be NULL for
+ * inference (nothing saved). */
+MHC_API size_t mhc_layer_fwd_dynamic_workspace_bytes(int64_t batch, int32_t n, int64_t hidden);
+MHC_API int mhc_layer_fwd_dynamic(const float* x, const float* rmsnorm_weight, const float* phi_pre,
+                          const float* phi_post, const float* phi_res, const float* alpha_pre,
+                          const float* alpha_post, const float* alpha_res, const float* b_pre,
+                          const float* b_post, const float* b_res, float* out,
+                          float* token_state, int64_t batch, int32_t n, int64_t hidden,
+                          int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* replaces mhc_layer_bwd_dynamic (bindings.cpp:600-874).  All parameter
+ * gradients are written (not accumulated); they are fixed-order reductions
+ * over the batch, so results are bitwise reproducible run to run. */
+MHC_API size_t mhc_layer_bwd_dynamic_workspace_bytes(int64_t batch, int32_t n, int64_t hidden);
+MHC_API int mhc_layer_bwd_dynamic(const float* grad_out, const float* x, const float* rmsnorm_weight,
+                          const float* phi_pre, const float* phi_post, const float* phi_res,
+                          const float* alpha_pre, const float* alpha_post,
+                          const float* alpha_res, const float* b_pre, const float* b_post,
+                          const float* b_res, const float* token_state, float* grad_x,
+                          float* grad_rmsnorm_weight, float* grad_phi_pre,
+                          float* grad_phi_post, float* grad_phi_res, float* grad_alpha_pre,
+                          float* grad_alpha_post, float* grad_alpha_res, float* grad_b_pre,
+                          float* grad_b_post, float* grad_b_res, int64_t batch, int32_t n,
+                          int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
+                          float rmsnorm_eps, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused mHC layer, static H (shared logits H_pre[n], H_post[n], H_res[n,n]).
+ * The reference composes this from four operators (layer.py:142-170); these
+ * entry points run the same math as one forward kernel and a fused backward.
+ * The forward saves rms[batch] (RMSNorm denominators) when rms != NULL.
+ * x/out are fp32 (..._f32) or bf16 with fp32 arithmetic (..._bf16).
+ * ------------------------------------------------------------------------- */
+MHC_API size_t mhc_layer_static_workspace_bytes(int64_t batch, int32_t n, int64_t hidden);
+MHC_API int mhc_layer_fwd_static_f32(const float* x, const float* rmsnorm_weight, const float* H_pre,
+                             const float* H_post, const float* H_res, float* out, float* rms,
+                             int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters,
+                             float sinkhorn_eps, float rmsnorm_eps, void* workspace,
+                             size_t workspace_bytes, void* stream);
+MHC_API int mhc_layer_fwd_static_bf16(const void* x, const float* rmsnorm_weight, const float* H_pre,
+                              const float* H_post, const float* H_res, void* out, float* rms,
+                              int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters,
+                              float sinkhorn_eps, float rmsnorm_eps, void* workspace,
+                              size_t workspace_bytes, void* stream);
+MHC_API int mhc_layer_bwd_static(const float* grad_out, const float* x, const float* rmsnorm_weight,
+                         const float* H_pre, const float* H_post, const float* H_res,
+                         const float* rms, float* grad_x, float* grad_rmsnorm_weight,
+                         float* grad_H_pre, float* grad_H_post, float* grad_H_res,
+                         int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters,
+                         float sinkhorn_eps, float rmsnorm_eps, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Kernel timing (tracing).  No counterpart in the reference, which times
+ * whole calls from Python (benchmark.py:156-269).  While enabled, every kernel
+ * this library launches is bracketed by two CUDA events on its own stream;
+ * mhc_profile_report() waits for them and writes one line per kernel name:
+ * "<name> <launches> <total_ms>\n" (NUL-terminated, truncated to cap), then
+ * clears the record.  Returns the number of bytes written, or < 0 on error.
+ * Process-wide; meant for benchmarking, not for concurrent production use.
+ * ------------------------------------------------------------------------- */
+MHC_API int mhc_profile_enable(int enable);
+MHC_API int mhc_profile_report(char* buf, size_t cap);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MHC_B200_H_ */

@@ -1,0 +1,1379 @@
+// Fused mHC layer: dynamic-H and static-H forward and backward for sm_100a.
+//
+// Replaces the reference's host orchestration mhc_layer_fwd_dynamic
+// (bindings.cpp:880-952) and mhc_layer_bwd_dynamic (bindings.cpp:600-874),
+// which run ~10 kernels + ~35 ATen ops with a host sync before every launch,
+// and the static-H composition of layer.py:142-170.
+//
+// Math (per token, x[i,c] for n streams i and C channels; xf = flattened x):
+//   rms_h = sqrt(mean(xf^2) + eps_r)          p = xf @ phi^T  (phi: [n^2+2n, nC])
+//   t = alpha * p / rms_h + b ;  h = sigmoid(t_pre), hp = 2 sigmoid(t_post),
+//   M = Sinkhorn(exp(t_res)) ;  x_agg[c] = sum_i h_i x[i,c]
+//   r = sqrt(mean_c(x_agg^2) + eps_r) ;  y[c] = x_agg[c] / r * w[c]
+//   out[i,c] = hp_i y[c] + sum_j M[i,j] x[j,c]
+//
+// Every token-wide reduction is expressed through per-token "moments" that a
+// single pass over the token's data produces:
+//   forward : p (n^2+2n dots with phi) and the n x n Gram matrix G = x x^T
+//             (sum(xf^2) = trace G, sum_c x_agg^2 = h^T G h);
+//   backward: gM = g x^T, W = g diag(w) x^T and G again; from these every
+//             per-token scalar of the backward follows in closed form (see
+//             dyn_token_bwd_kernel).
+// So the forward reads x twice and writes out once; the backward reads g and
+// x twice and writes grad_x once; parameter gradients are fixed-order
+// reductions (no atomics: bitwise reproducible).
+//
+// Kernels (launch order):
+//   fwd : proj_stats   -> token_fwd (gates, Sinkhorn, r) -> stream_fwd
+//   bwd : bwd_stats    -> token_bwd (Sinkhorn reverse, d_p) -> grad_x (gx, dphi/gw
+//         partials) -> reduce_* (fixed-order sums over splits / tokens)
+#include "common.cuh"
+#include "sinkhorn.cuh"
+#include <cuda_bf16.h>
+
+namespace mhc {
+namespace {
+
+// ---------------------------------------------------------------------------
+// Layout constants
+// ---------------------------------------------------------------------------
+template <int N>
+struct L {
+  static constexpr int NH = N * N + 2 * N;              // projections (pre|post|res)
+  static constexpr int NHP = (NH + 3) / 4 * 4;           // padded to float4
+  static constexpr int NG = N * (N + 1) / 2;             // Gram upper triangle
+  static constexpr int REC_RAW = 2 + 2 * N + N * N + NH;  // token_state record
+  static constexpr int REC = (REC_RAW + 3) / 4 * 4;
+  static constexpr int OFF_H = 2, OFF_HP = 2 + N, OFF_M = 2 + 2 * N, OFF_P = 2 + 2 * N + N * N;
+  static constexpr int NS1 = 2 * N * N + NG;             // bwd moments: gM, W, G
+  static constexpr int TB = 4 + NHP;                      // bwd per-token: beta, inv_r, coef, -, d_p
+  static constexpr int NR = NH + 3;                       // bwd per-token reduce: dt, dalpha
+  static constexpr int NRS = 2 * N + N * N;               // static per-token reduce: dt_pre, dt_post, gM
+};
+
+__host__ __device__ inline int rec_stride(int n) {
+  const int raw = 2 + 2 * n + n * n + (n * n + 2 * n);
+  return (raw + 3) / 4 * 4;
+}
+
+__device__ __forceinline__ int gram_index(int i, int j, int N) {
+  // upper triangle, row-major: (0,0),(0,1)..(0,N-1),(1,1)...
+  if (i > j) { int t = i; i = j; j = t; }
+  return i * N - i * (i - 1) / 2 + (j - i);
+}
+
+__device__ __forceinline__ const float* phi_row(const float* pre, const float* post,
+                                                const float* res, int k, int N, int64_t nC) {
+  if (k < N) return pre + (int64_t)k * nC;
+  if (k < 2 * N) return post + (int64_t)(k - N) * nC;
+  return res + (int64_t)(k - 2 * N) * nC;
+}
+
+// ---------------------------------------------------------------------------
+// Forward 1: projections and Gram moments, split over channel ranges.
+//   CTA = 8 warps; warp w owns TPW tokens, lane owns one channel of each
+//   32-channel chunk.  phi for the chunk is staged in shared memory
+//   [32 ch][N][NHP] (row stride = SROW floats, == 4 mod 32 for conflict-free
+//   float4 reads) and reused by the CTA's 8*TPW tokens.
+// ---------------------------------------------------------------------------
+template <int N>
+struct ProjCfg {
+  static constexpr int TPW = N <= 4 ? 4 : 1;
+  static constexpr int TT = 8 * TPW;  // tokens per CTA
+  static constexpr int ROW = N * L<N>::NHP;
+  static constexpr int SROW = (ROW + 27) / 32 * 32 + 4;  // >= ROW, == 4 (mod 32)
+  static constexpr int SMEM_FLOATS = 2 * 32 * SROW;
+};
+
+template <int N>
+__global__ void __launch_bounds__(256, 1)
+    proj_stats_kernel(const float* __restrict__ x, const float* __restrict__ phi_pre,
+                      const float* __restrict__ phi_post, const float* __restrict__ phi_res,
+                      float* __restrict__ ppart, float* __restrict__ gpart, int64_t B, int64_t C,
+                      int cps) {
+  using Lc = L<N>;
+  using P = ProjCfg<N>;
+  constexpr int NHP = Lc::NHP, NH = Lc::NH, NG = Lc::NG, TPW = P::TPW, SROW = P::SROW;
+  extern __shared__ float smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t nC = (int64_t)N * C;
+  const int64_t t0 = (int64_t)blockIdx.x * P::TT + warp * TPW;
+  const int split = blockIdx.y;
+  const int64_t c_begin = (int64_t)split * cps;
+  int64_t c_end = c_begin + cps;
+  if (c_end > C) c_end = C;
+
+  float acc[TPW][NHP];
+  float gacc[TPW][NG];
+#pragma unroll
+  for (int t = 0; t < TPW; ++t) {
+#pragma unroll
+    for (int k = 0; k < NHP; ++k) acc[t][k] = 0.f;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) gacc[t][g] = 0.f;
+  }
+
+  // cooperative phi staging: element e of the chunk -> (k, i, ch)
+  auto stage = [&](int buf, int64_t cc) {
+    float* dst = smem + buf * 32 * SROW;
+    for (int e = threadIdx.x; e < NHP * N * 32; e += blockDim.x) {
+      const int ch = e & 31;
+      const int ki = e >> 5;  // k * N + i
+      const int k = ki / N, i = ki % N;
+      const int64_t c = cc + ch;
+      float v = 0.f;
+      if (k < NH && c < c_end) v = __ldg(phi_row(phi_pre, phi_post, phi_res, k, N, nC) + i * C + c);
+      dst[ch * SROW + i * NHP + k] = v;
+    }
+  };
+
+  float xv[TPW][N], xn[TPW][N];
+  auto load_x = [&](float (&dst)[TPW][N], int64_t cc) {
+    const int64_t c = cc + lane;
+#pragma unroll
+    for (int t = 0; t < TPW; ++t) {
+      const int64_t tok = t0 + t;
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        dst[t][i] = (tok < B && c < c_end) ? __ldcs(x + tok * nC + (int64_t)i * C + c) : 0.f;
+    }
+  };
+
+  if (c_begin < c_end) {
+    stage(0, c_begin);
+    load_x(xv, c_begin);
+  }
+  __syncthreads();
+  int buf = 0;
+  for (int64_t cc = c_begin; cc < c_end; cc += 32) {
+    const bool more = cc + 32 < c_end;
+    if (more) {
+      stage(buf ^ 1, cc + 32);
+      load_x(xn, cc + 32);
+    }
+    const float* row = smem + buf * 32 * SROW + lane * SROW;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+#pragma unroll
+      for (int k4 = 0; k4 < NHP / 4; ++k4) {
+        const float4 f = *reinterpret_cast<const float4*>(row + i * NHP + 4 * k4);
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          acc[t][4 * k4 + 0] = fmaf(xv[t][i], f.x, acc[t][4 * k4 + 0]);
+          acc[t][4 * k4 + 1] = fmaf(xv[t][i], f.y, acc[t][4 * k4 + 1]);
+          acc[t][4 * k4 + 2] = fmaf(xv[t][i], f.z, acc[t][4 * k4 + 2]);
+          acc[t][4 * k4 + 3] = fmaf(xv[t][i], f.w, acc[t][4 * k4 + 3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TPW; ++t) {
+      int g = 0;
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int j = i; j < N; ++j) {
+          gacc[t][g] = fmaf(xv[t][i], xv[t][j], gacc[t][g]);
+          ++g;
+        }
+    }
+    if (more) {
+#pragma unroll
+      for (int t = 0; t < TPW; ++t)
+#pragma unroll
+        for (int i = 0; i < N; ++i) xv[t][i] = xn[t][i];
+    }
+    __syncthreads();
+    buf ^= 1;
+  }
+
+  // reduce over the 32 lanes (channels) and write this split's partials
+#pragma unroll
+  for (int t = 0; t < TPW; ++t) {
+    const int64_t tok = t0 + t;
+#pragma unroll
+    for (int k = 0; k < NHP; ++k) {
+      const float v = warp_sum(acc[t][k]);
+      if (lane == (k & 31) && tok < B) ppart[((int64_t)split * B + tok) * NHP + k] = v;
+    }
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const float v = warp_sum(gacc[t][g]);
+      if (lane == (g & 31) && tok < B) gpart[((int64_t)split * B + tok) * NG + g] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward 2: per-token gates, Sinkhorn and RMS (one thread per token).
+// ---------------------------------------------------------------------------
+template <int N>
+__global__ void __launch_bounds__(128)
+    token_fwd_kernel(const float* __restrict__ ppart, const float* __restrict__ gpart, int ks,
+                     const float* __restrict__ a_pre, const float* __restrict__ a_post,
+                     const float* __restrict__ a_res, const float* __restrict__ b_pre,
+                     const float* __restrict__ b_post, const float* __restrict__ b_res,
+                     float* __restrict__ rec, int64_t B, int64_t C, int iters, float s_eps,
+                     float r_eps) {
+  using Lc = L<N>;
+  constexpr int NH = Lc::NH, NHP = Lc::NHP, NG = Lc::NG;
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  float p[NH], G[NG];
+#pragma unroll
+  for (int k = 0; k < NH; ++k) p[k] = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) G[g] = 0.f;
+  for (int s = 0; s < ks; ++s) {
+    const float* pp = ppart + ((int64_t)s * B + b) * NHP;
+    const float* gp = gpart + ((int64_t)s * B + b) * NG;
+#pragma unroll
+    for (int k = 0; k < NH; ++k) p[k] += pp[k];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) G[g] += gp[g];
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) ss += G[gram_index(i, i, N)];
+  const float rms_h = sqrtf(ss / (float)(N * C) + r_eps);
+  const float inv_h = 1.f / rms_h;
+  const float ap = *a_pre, aq = *a_post, ar = *a_res;
+  float h[N], hp[N], m[N * N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    h[i] = sigmoidf_((ap * p[i]) * inv_h + b_pre[i]);
+    hp[i] = 2.f * sigmoidf_((aq * p[N + i]) * inv_h + b_post[i]);
+  }
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) m[e] = expf((ar * p[2 * N + e]) * inv_h + b_res[e]);
+  sk_forward<N>(m, iters, s_eps);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) q += h[i] * h[j] * G[gram_index(i, j, N)];
+  const float r = sqrtf(fmaxf(q, 0.f) / (float)C + r_eps);
+  float* o = rec + b * Lc::REC;
+  o[0] = rms_h;
+  o[1] = r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    o[Lc::OFF_H + i] = h[i];
+    o[Lc::OFF_HP + i] = hp[i];
+  }
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) o[Lc::OFF_M + e] = m[e];
+#pragma unroll
+  for (int k = 0; k < NH; ++k) o[Lc::OFF_P + k] = p[k];
+}
+
+// ---------------------------------------------------------------------------
+// Forward 3: out[i,c] = sum_j M_ij x[j,c] + hp_i * (w_c / r) * sum_j h_j x[j,c]
+//   One CTA per token (grid-stride over tokens); per-token record in smem;
+//   rec_stride 0 = one shared record (static H) with per-token r from rms[].
+// ---------------------------------------------------------------------------
+template <int N, bool VEC>
+__global__ void __launch_bounds__(256)
+    stream_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                      const float* __restrict__ rec, int rec_stride,
+                      const float* __restrict__ rms, float* __restrict__ out, int64_t B,
+                      int64_t C) {
+  using Lc = L<N>;
+  __shared__ float s_rec[Lc::REC];
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < Lc::REC; e += blockDim.x) s_rec[e] = rec[b * rec_stride + e];
+    __syncthreads();
+    const float r = rms ? rms[b] : s_rec[1];
+    const float inv_r = 1.f / r;
+    const float* h = s_rec + Lc::OFF_H;
+    const float* hp = s_rec + Lc::OFF_HP;
+    const float* m = s_rec + Lc::OFF_M;
+    const float* xb = x + b * N * C;
+    float* ob = out + b * N * C;
+    if (VEC) {
+      for (int64_t q = threadIdx.x; q < C / 4; q += blockDim.x) {
+        float4 xv[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) xv[j] = __ldcs(reinterpret_cast<const float4*>(xb + j * C) + q);
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + q);
+        float4 xa = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          xa.x = fmaf(h[j], xv[j].x, xa.x); xa.y = fmaf(h[j], xv[j].y, xa.y);
+          xa.z = fmaf(h[j], xv[j].z, xa.z); xa.w = fmaf(h[j], xv[j].w, xa.w);
+        }
+        float4 y;
+        y.x = (xa.x * inv_r) * wv.x; y.y = (xa.y * inv_r) * wv.y;
+        y.z = (xa.z * inv_r) * wv.z; y.w = (xa.w * inv_r) * wv.w;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          float4 o;
+          o.x = hp[i] * y.x; o.y = hp[i] * y.y; o.z = hp[i] * y.z; o.w = hp[i] * y.w;
+#pragma unroll
+          for (int j = 0; j < N; ++j) {
+            const float mij = m[i * N + j];
+            o.x = fmaf(mij, xv[j].x, o.x); o.y = fmaf(mij, xv[j].y, o.y);
+            o.z = fmaf(mij, xv[j].z, o.z); o.w = fmaf(mij, xv[j].w, o.w);
+          }
+          __stcs(reinterpret_cast<float4*>(ob + i * C) + q, o);
+        }
+      }
+    } else {
+      for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+        float xv[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) xv[j] = xb[j * C + c];
+        float xa = 0.f;
+#pragma unroll
+        for (int j = 0; j < N; ++j) xa = fmaf(h[j], xv[j], xa);
+        const float y = (xa * inv_r) * w[c];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          float o = hp[i] * y;
+#pragma unroll
+          for (int j = 0; j < N; ++j) o = fmaf(m[i * N + j], xv[j], o);
+          ob[i * C + c] = o;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Static-H forward, single pass: one CTA per token holds the token in
+// registers (QPT float4 channel quads per thread), block-reduces sum(x_agg^2)
+// and writes out.  T = float or __nv_bfloat16 (fp32 arithmetic either way).
+// ---------------------------------------------------------------------------
+struct bf16x4 { __nv_bfloat162 a, b; };
+
+template <typename T> struct IO;
+template <> struct IO<float> {
+  static __device__ __forceinline__ float4 load4(const float* p, int64_t q) {
+    return __ldcs(reinterpret_cast<const float4*>(p) + q);
+  }
+  static __device__ __forceinline__ void store4(float* p, int64_t q, float4 v) {
+    __stcs(reinterpret_cast<float4*>(p) + q, v);
+  }
+};
+template <> struct IO<__nv_bfloat16> {
+  static __device__ __forceinline__ float4 load4(const __nv_bfloat16* p, int64_t q) {
+    const uint2 u = __ldcs(reinterpret_cast<const uint2*>(p) + q);
+    __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+    __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+    float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  static __device__ __forceinline__ void store4(__nv_bfloat16* p, int64_t q, float4 v) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    __stcs(reinterpret_cast<uint2*>(p) + q, u);
+  }
+};
+
+template <int N, int QPT, typename T>
+__global__ void __launch_bounds__(256)
+    static_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                      const float* __restrict__ rec, float* __restrict__ rms,
+                      T* __restrict__ out, int64_t B, int64_t C, float r_eps) {
+  using Lc = L<N>;
+  __shared__ float s_rec[Lc::REC];
+  __shared__ float red[8];
+  for (int e = threadIdx.x; e < Lc::REC; e += blockDim.x) s_rec[e] = rec[e];
+  __syncthreads();
+  const float* h = s_rec + Lc::OFF_H;
+  const float* hp = s_rec + Lc::OFF_HP;
+  const float* m = s_rec + Lc::OFF_M;
+  const int64_t C4 = C / 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const T* xb = x + b * N * C;
+    T* ob = out + b * N * C;
+    float4 xv[QPT][N];
+    float4 xa[QPT];
+    float sq = 0.f;
+#pragma unroll
+    for (int u = 0; u < QPT; ++u) {
+      const int64_t q = threadIdx.x + (int64_t)u * blockDim.x;
+      xa[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (q < C4) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) xv[u][j] = IO<T>::load4(xb + j * C, q);
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          xa[u].x = fmaf(h[j], xv[u][j].x, xa[u].x); xa[u].y = fmaf(h[j], xv[u][j].y, xa[u].y);
+          xa[u].z = fmaf(h[j], xv[u][j].z, xa[u].z); xa[u].w = fmaf(h[j], xv[u][j].w, xa[u].w);
+        }
+        sq += xa[u].x * xa[u].x + xa[u].y * xa[u].y + xa[u].z * xa[u].z + xa[u].w * xa[u].w;
+      }
+    }
+    sq = warp_sum(sq);
+    if (lane == 0) red[warp] = sq;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot += red[k];
+    __syncthreads();
+    const float r = sqrtf(tot / (float)C + r_eps);
+    const float inv_r = 1.f / r;
+    if (threadIdx.x == 0 && rms) rms[b] = r;
+#pragma unroll
+    for (int u = 0; u < QPT; ++u) {
+      const int64_t q = threadIdx.x + (int64_t)u * blockDim.x;
+      if (q < C4) {
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + q);
+        float4 y;
+        y.x = (xa[u].x * inv_r) * wv.x; y.y = (xa[u].y * inv_r) * wv.y;
+        y.z = (xa[u].z * inv_r) * wv.z; y.w = (xa[u].w * inv_r) * wv.w;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          float4 o;
+          o.x = hp[i] * y.x; o.y = hp[i] * y.y; o.z = hp[i] * y.z; o.w = hp[i] * y.w;
+#pragma unroll
+          for (int j = 0; j < N; ++j) {
+            const float mij = m[i * N + j];
+            o.x = fmaf(mij, xv[u][j].x, o.x); o.y = fmaf(mij, xv[u][j].y, o.y);
+            o.z = fmaf(mij, xv[u][j].z, o.z); o.w = fmaf(mij, xv[u][j].w, o.w);
+          }
+          IO<T>::store4(ob + i * C, q, o);
+        }
+      }
+    }
+  }
+}
+
+// Scalar fallback for the static forward (C not a multiple of 4 or too large
+// for the register-resident kernel): two passes over the token, the second
+// one served by L1/L2.
+template <int N, typename T>
+__global__ void __launch_bounds__(256)
+    static_fwd_generic_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                              const float* __restrict__ rec, float* __restrict__ rms,
+                              T* __restrict__ out, int64_t B, int64_t C, float r_eps) {
+  using Lc = L<N>;
+  __shared__ float s_rec[Lc::REC];
+  __shared__ float red[8];
+  for (int e = threadIdx.x; e < Lc::REC; e += blockDim.x) s_rec[e] = rec[e];
+  __syncthreads();
+  const float* h = s_rec + Lc::OFF_H;
+  const float* hp = s_rec + Lc::OFF_HP;
+  const float* m = s_rec + Lc::OFF_M;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const T* xb = x + b * N * C;
+    T* ob = out + b * N * C;
+    float sq = 0.f;
+    for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+      float xa = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) xa = fmaf(h[j], (float)xb[j * C + c], xa);
+      sq += xa * xa;
+    }
+    sq = warp_sum(sq);
+    if (lane == 0) red[warp] = sq;
+    __syncthreads();
+    float tot = 0.f;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) tot += red[k];
+    __syncthreads();
+    const float r = sqrtf(tot / (float)C + r_eps);
+    const float inv_r = 1.f / r;
+    if (threadIdx.x == 0 && rms) rms[b] = r;
+    for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+      float xv[N];
+      float xa = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        xv[j] = (float)xb[j * C + c];
+        xa = fmaf(h[j], xv[j], xa);
+      }
+      const float y = (xa * inv_r) * w[c];
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float o = hp[i] * y;
+#pragma unroll
+        for (int j = 0; j < N; ++j) o = fmaf(m[i * N + j], xv[j], o);
+        ob[i * C + c] = (T)o;
+      }
+    }
+  }
+}
+
+// Shared record for static H: h = sigmoid(H_pre), hp = 2 sigmoid(H_post),
+// M = Sinkhorn(exp(H_res)).  Written into rec (REC floats).
+template <int N>
+__global__ void static_prep_kernel(const float* __restrict__ H_pre,
+                                   const float* __restrict__ H_post,
+                                   const float* __restrict__ H_res, float* __restrict__ rec,
+                                   int iters, float s_eps) {
+  using Lc = L<N>;
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float m[N * N];
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) m[e] = expf(H_res[e]);
+  sk_forward<N>(m, iters, s_eps);
+  for (int e = 0; e < Lc::REC; ++e) rec[e] = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    rec[Lc::OFF_H + i] = sigmoidf_(H_pre[i]);
+    rec[Lc::OFF_HP + i] = 2.f * sigmoidf_(H_post[i]);
+  }
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) rec[Lc::OFF_M + e] = m[e];
+}
+
+// ---------------------------------------------------------------------------
+// Backward 1: per-token moments gM = g x^T, W = g diag(w) x^T, G = x x^T.
+//   One CTA (128 threads) per token, float4 over channel quads when VEC.
+// ---------------------------------------------------------------------------
+template <int V>
+__device__ __forceinline__ void block_reduce_to_global(float (&acc)[V], float* smem,
+                                                       float* __restrict__ dst) {
+  // smem: [nwarps][V]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const float s = warp_sum(acc[v]);
+    if (lane == 0) smem[warp * V + v] = s;
+  }
+  __syncthreads();
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += smem[w * V + v];
+    dst[v] = s;
+  }
+  __syncthreads();
+}
+
+template <int N, bool VEC>
+__global__ void __launch_bounds__(128)
+    bwd_stats_kernel(const float* __restrict__ g, const float* __restrict__ x,
+                     const float* __restrict__ w, float* __restrict__ stats, int64_t B,
+                     int64_t C) {
+  using Lc = L<N>;
+  constexpr int NS1 = Lc::NS1, NG = Lc::NG;
+  __shared__ float red[4 * NS1];
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    float acc[NS1];
+#pragma unroll
+    for (int v = 0; v < NS1; ++v) acc[v] = 0.f;
+    const float* gb = g + b * N * C;
+    const float* xb = x + b * N * C;
+    auto accum = [&](const float (&gv)[N], const float (&xv)[N], float wv) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const float gw = gv[i] * wv;
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          acc[i * N + j] = fmaf(gv[i], xv[j], acc[i * N + j]);
+          acc[N * N + i * N + j] = fmaf(gw, xv[j], acc[N * N + i * N + j]);
+        }
+      }
+      int e = 2 * N * N;
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int j = i; j < N; ++j) { acc[e] = fmaf(xv[i], xv[j], acc[e]); ++e; }
+    };
+    if (VEC) {
+      for (int64_t q = threadIdx.x; q < C / 4; q += blockDim.x) {
+        float4 g4[N], x4[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          g4[i] = __ldg(reinterpret_cast<const float4*>(gb + i * C) + q);
+          x4[i] = __ldg(reinterpret_cast<const float4*>(xb + i * C) + q);
+        }
+        const float4 w4 = __ldg(reinterpret_cast<const float4*>(w) + q);
+        float gv[N], xv[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) { gv[i] = g4[i].x; xv[i] = x4[i].x; }
+        accum(gv, xv, w4.x);
+#pragma unroll
+        for (int i = 0; i < N; ++i) { gv[i] = g4[i].y; xv[i] = x4[i].y; }
+        accum(gv, xv, w4.y);
+#pragma unroll
+        for (int i = 0; i < N; ++i) { gv[i] = g4[i].z; xv[i] = x4[i].z; }
+        accum(gv, xv, w4.z);
+#pragma unroll
+        for (int i = 0; i < N; ++i) { gv[i] = g4[i].w; xv[i] = x4[i].w; }
+        accum(gv, xv, w4.w);
+      }
+    } else {
+      for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+        float gv[N], xv[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) { gv[i] = gb[i * C + c]; xv[i] = xb[i * C + c]; }
+        accum(gv, xv, w[c]);
+      }
+    }
+    block_reduce_to_global<NS1>(acc, red, stats + b * NS1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward 2 (dynamic): per-token closed-form scalars, one thread per token.
+//   With W = g diag(w) x^T, G = x x^T, gM = g x^T (sums over c):
+//     ghp_i = (W h)_i / r                     (= sum_c g_i y)
+//     dot   = hp^T W h                        (= sum_c gy w x_agg)
+//     A_i   = (W^T hp)_i                      (= sum_c gy w x_i)
+//     Q_i   = (G h)_i                         (= sum_c x_agg x_i)
+//     beta  = dot / (C r^3);  gh_i = A_i / r - beta Q_i   (= sum_c gx_agg x_i)
+//   then the gate derivatives, Sinkhorn reverse on gM, and the projection
+//   backward: d_p = dt alpha / rms_h, coef = -(sum dt alpha p) / (rms_h^3 nC).
+// ---------------------------------------------------------------------------
+template <int N>
+__global__ void __launch_bounds__(128)
+    token_bwd_kernel(const float* __restrict__ stats, const float* __restrict__ rec,
+                     const float* __restrict__ a_pre, const float* __restrict__ a_post,
+                     const float* __restrict__ a_res, const float* __restrict__ b_res,
+                     float* __restrict__ tokb, float* __restrict__ tokr, int64_t B, int64_t C,
+                     int iters, float s_eps) {
+  using Lc = L<N>;
+  constexpr int NH = Lc::NH, NS1 = Lc::NS1;
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const float* st = stats + b * NS1;
+  const float* rc = rec + b * Lc::REC;
+  const float rms_h = rc[0], r = rc[1];
+  const float inv_h = 1.f / rms_h, inv_r = 1.f / r;
+  float h[N], hp[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) { h[i] = rc[Lc::OFF_H + i]; hp[i] = rc[Lc::OFF_HP + i]; }
+  float dt[NH];
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float wh = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) wh = fmaf(st[N * N + i * N + j], h[j], wh);
+    dot = fmaf(hp[i], wh, dot);
+    const float ghp = wh * inv_r;
+    dt[N + i] = ghp * hp[i] * (1.f - 0.5f * hp[i]);
+  }
+  const float beta = dot / ((float)C * r * r * r);
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float A = 0.f, Q = 0.f;
+#pragma unroll
+    for (int k = 0; k < N; ++k) A = fmaf(hp[k], st[N * N + k * N + i], A);
+#pragma unroll
+    for (int j = 0; j < N; ++j) Q = fmaf(st[2 * N * N + gram_index(i, j, N)], h[j], Q);
+    const float gh = A * inv_r - beta * Q;
+    dt[i] = gh * h[i] * (1.f - h[i]);
+  }
+  const float ap = *a_pre, aq = *a_post, ar = *a_res;
+  float e0[N * N], gm[N * N];
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) {
+    e0[e] = expf((ar * rc[Lc::OFF_P + 2 * N + e]) * inv_h + b_res[e]);
+    gm[e] = st[e];
+  }
+  sk_backward<N>(e0, gm, iters, s_eps);
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) dt[2 * N + e] = gm[e] * e0[e];
+  float* tb = tokb + b * Lc::TB;
+  float* tr = tokr + b * Lc::NR;
+  float s = 0.f, da0 = 0.f, da1 = 0.f, da2 = 0.f;
+#pragma unroll
+  for (int k = 0; k < NH; ++k) {
+    const float a = k < N ? ap : (k < 2 * N ? aq : ar);
+    const float pk = rc[Lc::OFF_P + k];
+    tb[4 + k] = dt[k] * a * inv_h;
+    s = fmaf(dt[k] * a, pk, s);
+    const float dak = dt[k] * pk * inv_h;
+    if (k < N) da0 += dak; else if (k < 2 * N) da1 += dak; else da2 += dak;
+    tr[k] = dt[k];
+  }
+#pragma unroll
+  for (int k = NH; k < Lc::NHP; ++k) tb[4 + k] = 0.f;
+  tb[0] = beta;
+  tb[1] = inv_r;
+  tb[2] = -s * inv_h * inv_h * inv_h / (float)(N * C);
+  tb[3] = 0.f;
+  tr[NH + 0] = da0;
+  tr[NH + 1] = da1;
+  tr[NH + 2] = da2;
+}
+
+// Static-H per-token scalars: beta, inv_r for grad_x, and per-token gate
+// gradients (dt_pre, dt_post) and gM for the reductions over the batch.
+template <int N>
+__global__ void __launch_bounds__(128)
+    token_bwd_static_kernel(const float* __restrict__ stats, const float* __restrict__ rec,
+                            const float* __restrict__ rms, float* __restrict__ tokb,
+                            float* __restrict__ tokr, int64_t B, int64_t C) {
+  using Lc = L<N>;
+  constexpr int NS1 = Lc::NS1;
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const float* st = stats + b * NS1;
+  const float r = rms[b], inv_r = 1.f / r;
+  float h[N], hp[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) { h[i] = rec[Lc::OFF_H + i]; hp[i] = rec[Lc::OFF_HP + i]; }
+  float* tr = tokr + b * Lc::NRS;
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float wh = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) wh = fmaf(st[N * N + i * N + j], h[j], wh);
+    dot = fmaf(hp[i], wh, dot);
+    tr[N + i] = wh * inv_r * hp[i] * (1.f - 0.5f * hp[i]);
+  }
+  const float beta = dot / ((float)C * r * r * r);
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float A = 0.f, Q = 0.f;
+#pragma unroll
+    for (int k = 0; k < N; ++k) A = fmaf(hp[k], st[N * N + k * N + i], A);
+#pragma unroll
+    for (int j = 0; j < N; ++j) Q = fmaf(st[2 * N * N + gram_index(i, j, N)], h[j], Q);
+    tr[i] = (A * inv_r - beta * Q) * h[i] * (1.f - h[i]);
+  }
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) tr[2 * N + e] = st[e];
+  float* tb = tokb + b * 4;
+  tb[0] = beta;
+  tb[1] = inv_r;
+  tb[2] = 0.f;
+  tb[3] = 0.f;
+}
+
+// ---------------------------------------------------------------------------
+// Backward 3: grad_x, and per-split partials of dphi and grad_w.
+//   Thread = one column (stream i, channel c) of a CW-channel tile; the CTA
+//   walks a contiguous token range.  phi for the thread's column and its
+//   dphi accumulator stay in registers for the whole range.
+//   grad_x[i,c] = sum_j M[j,i] g[j,c] + h_i (gy[c] w[c] / r - x_agg[c] beta)
+//                 + sum_k d_p[k] phi[k, iC+c] + coef x[i,c]
+//   dphi[k, iC+c] += d_p[k] x[i,c] ;  grad_w[c] += gy[c] x_agg[c] / r
+// ---------------------------------------------------------------------------
+constexpr int GX_CW = 64;   // channels per CTA tile
+constexpr int GX_TB = 8;    // tokens staged per smem batch
+
+template <int N, bool DYN>
+__global__ void __launch_bounds__(GX_CW* N)
+    grad_x_kernel(const float* __restrict__ g, const float* __restrict__ x,
+                  const float* __restrict__ w, const float* __restrict__ phi_pre,
+                  const float* __restrict__ phi_post, const float* __restrict__ phi_res,
+                  const float* __restrict__ rec, int rec_stride, const float* __restrict__ tokb,
+                  float* __restrict__ gx, float* __restrict__ dphi_part,
+                  float* __restrict__ gw_part, int64_t B, int64_t C, int ntiles, int nsplit) {
+  using Lc = L<N>;
+  constexpr int NH = Lc::NH, NHP = Lc::NHP;
+  constexpr int TBS = DYN ? Lc::TB : 4;      // per-token tokb stride
+  constexpr int SREC = 2 * N + N * N;        // h, hp, M
+  constexpr int STOK = TBS + SREC;           // smem floats per staged token
+  __shared__ __align__(16) float s_tok[GX_TB][STOK + (4 - (STOK & 3)) % 4];
+  constexpr int SSTR = STOK + (4 - (STOK & 3)) % 4;
+  const int tile = blockIdx.x % ntiles;
+  const int split = blockIdx.x / ntiles;
+  const int i = threadIdx.x / GX_CW;
+  const int cl = threadIdx.x % GX_CW;
+  const int64_t c = (int64_t)tile * GX_CW + cl;
+  const bool cval = c < C;
+  const int64_t nC = (int64_t)N * C;
+  const int64_t col = (int64_t)i * C + c;
+  // token range of this split
+  const int64_t tb0 = B * split / nsplit, tb1 = B * (split + 1) / nsplit;
+
+  float phi[DYN ? NHP : 1];
+  float dph[DYN ? NHP : 1];
+  if (DYN) {
+#pragma unroll
+    for (int k = 0; k < NHP; ++k) {
+      phi[k] = (k < NH && cval) ? __ldg(phi_row(phi_pre, phi_post, phi_res, k, N, nC) + col) : 0.f;
+      dph[k] = 0.f;
+    }
+  }
+  const float wc = cval ? w[c] : 0.f;
+  float gwacc = 0.f;
+
+  for (int64_t t0 = tb0; t0 < tb1; t0 += GX_TB) {
+    const int nt = (int)((tb1 - t0) < GX_TB ? (tb1 - t0) : GX_TB);
+    __syncthreads();
+    for (int e = threadIdx.x; e < nt * STOK; e += blockDim.x) {
+      const int tt = e / STOK, f = e % STOK;
+      const int64_t tok = t0 + tt;
+      float v;
+      if (f < TBS) v = tokb[tok * TBS + f];
+      else v = rec[tok * rec_stride + Lc::OFF_H + (f - TBS)];
+      s_tok[tt][f] = v;
+    }
+    __syncthreads();
+    if (!cval) continue;
+    for (int tt = 0; tt < nt; ++tt) {
+      const int64_t tok = t0 + tt;
+      const float* st = s_tok[tt];
+      const float beta = st[0], inv_r = st[1];
+      const float* h = st + TBS;
+      const float* hp = h + N;
+      const float* m = hp + N;
+      const float* gb = g + tok * nC + c;
+      const float* xb = x + tok * nC + c;
+      float gv[N], xv[N];
+#pragma unroll
+      for (int j = 0; j < N; ++j) { gv[j] = __ldg(gb + j * C); xv[j] = __ldg(xb + j * C); }
+      float gy = 0.f, xa = 0.f, mix = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        gy = fmaf(hp[j], gv[j], gy);
+        xa = fmaf(h[j], xv[j], xa);
+        mix = fmaf(m[j * N + i], gv[j], mix);
+      }
+      const float xi = xv[i];
+      float acc = mix + h[i] * (gy * wc * inv_r - xa * beta);
+      if (DYN) {
+        const float coef = st[2];
+        const float* dp = st + 4;
+        float2 a2 = make_float2(0.f, 0.f);
+        const float2 x2 = make_float2(xi, xi);
+#pragma unroll
+        for (int k = 0; k < NHP; k += 2) {
+          const float2 d2 = *reinterpret_cast<const float2*>(dp + k);
+          const float2 p2 = make_float2(phi[k], phi[k + 1]);
+          a2 = __ffma2_rn(d2, p2, a2);
+          float2 q2 = make_float2(dph[k], dph[k + 1]);
+          q2 = __ffma2_rn(d2, x2, q2);
+          dph[k] = q2.x;
+          dph[k + 1] = q2.y;
+        }
+        acc += (a2.x + a2.y) + coef * xi;
+      }
+      __stcs(gx + tok * nC + col, acc);
+      if (i == 0) gwacc = fmaf(gy * xa, inv_r, gwacc);
+    }
+  }
+  if (cval) {
+    if (DYN) {
+#pragma unroll
+      for (int k = 0; k < NH; ++k) dphi_part[((int64_t)split * NH + k) * nC + col] = dph[k];
+    }
+    if (i == 0) gw_part[(int64_t)split * C + c] = gwacc;
+  }
+}
+
+// out[l] = sum_s part[s * L + l]   (fixed order over splits)
+__global__ void __launch_bounds__(256)
+    reduce_splits_kernel(const float* __restrict__ part, int nsplit, int64_t L,
+                         float* __restrict__ out) {
+  for (int64_t l = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; l < L;
+       l += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < nsplit; ++k) s += part[(int64_t)k * L + l];
+    out[l] = s;
+  }
+}
+
+// dphi[k, :] = sum_s part[s, k, :] written straight into the three grad tensors
+__global__ void __launch_bounds__(256)
+    reduce_dphi_kernel(const float* __restrict__ part, int nsplit, int NHn, int N, int64_t nC,
+                       float* __restrict__ d_pre, float* __restrict__ d_post,
+                       float* __restrict__ d_res) {
+  const int64_t L = (int64_t)NHn * nC;
+  for (int64_t l = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; l < L;
+       l += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < nsplit; ++k) s += part[(int64_t)k * L + l];
+    const int64_t kk = l / nC, cc = l % nC;
+    float* dst = kk < N ? d_pre + kk * nC : (kk < 2 * N ? d_post + (kk - N) * nC : d_res + (kk - 2 * N) * nC);
+    dst[cc] = s;
+  }
+}
+
+// One CTA per column v of a [B, stride] table: total[v] = sum_b tab[b, v]
+// (fixed order: thread-strided partials, then a fixed tree).
+__global__ void __launch_bounds__(256)
+    reduce_tokens_kernel(const float* __restrict__ tab, int64_t B, int stride,
+                         float* __restrict__ out) {
+  __shared__ float red[8];
+  const int v = blockIdx.x;
+  float s = 0.f;
+  for (int64_t b = threadIdx.x; b < B; b += blockDim.x) s += tab[b * stride + v];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += red[k];
+    out[v] = t;
+  }
+}
+
+// Scatter the token-reduced dynamic parameter gradients: tot = [dt(NH), dalpha(3)]
+template <int N>
+__global__ void scatter_dyn_param_grads_kernel(const float* __restrict__ tot,
+                                               float* __restrict__ gbp, float* __restrict__ gbq,
+                                               float* __restrict__ gbr, float* __restrict__ gap,
+                                               float* __restrict__ gaq, float* __restrict__ gar) {
+  constexpr int NH = L<N>::NH;
+  const int k = threadIdx.x;
+  if (k < N) gbp[k] = tot[k];
+  else if (k < 2 * N) gbq[k - N] = tot[k];
+  else if (k < NH) gbr[k - 2 * N] = tot[k];
+  if (k == 0) { *gap = tot[NH]; *gaq = tot[NH + 1]; *gar = tot[NH + 2]; }
+}
+
+// Static-H parameter gradients from the token totals [dt_pre, dt_post, gM].
+template <int N>
+__global__ void static_param_grads_kernel(const float* __restrict__ tot,
+                                          const float* __restrict__ H_res,
+                                          float* __restrict__ gHp, float* __restrict__ gHq,
+                                          float* __restrict__ gHr, int iters, float s_eps) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  for (int i = 0; i < N; ++i) { gHp[i] = tot[i]; gHq[i] = tot[N + i]; }
+  float e0[N * N], gm[N * N];
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) { e0[e] = expf(H_res[e]); gm[e] = tot[2 * N + e]; }
+  sk_backward<N>(e0, gm, iters, s_eps);
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) gHr[e] = gm[e] * e0[e];
+}
+
+// ---------------------------------------------------------------------------
+// Host-side planning
+// ---------------------------------------------------------------------------
+inline size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
+
+struct Carve {
+  char* base;
+  size_t off = 0;
+  explicit Carve(void* p) : base((char*)p) {}
+  float* take(size_t floats) {
+    float* p = base ? (float*)(base + off) : nullptr;
+    off += align_up(floats * sizeof(float));
+    return p;
+  }
+};
+
+int choose_ksplit(int64_t tiles, int64_t C, int sms) {
+  const int64_t max_ks = (C + 31) / 32;
+  int best = 1;
+  double best_eff = -1.0;
+  for (int ks = 1; ks <= 32 && ks <= max_ks; ++ks) {
+    const int64_t total = tiles * ks;
+    const int64_t waves = (total + sms - 1) / sms;
+    double eff = (double)total / (double)(waves * sms);
+    if (total < 2 * sms) eff *= (double)total / (2.0 * sms);  // too little parallelism
+    if (eff > best_eff + 0.02) { best_eff = eff; best = ks; }
+  }
+  return best;
+}
+
+int choose_gx_splits(int64_t tiles, int64_t B, int sms, int per_sm) {
+  const int64_t slots = (int64_t)sms * per_sm;
+  int best = 1;
+  double best_eff = -1.0;
+  const int64_t max_s = B < 1 ? 1 : (B < 1024 ? B : 1024);
+  for (int64_t s = 1; s <= max_s; ++s) {
+    const int64_t total = tiles * s;
+    const int64_t waves = (total + slots - 1) / slots;
+    double eff = (double)total / (double)(waves * slots);
+    if (waves > 8) break;
+    // prefer fewer splits (less partial traffic) unless clearly better balanced
+    if (eff > best_eff + 0.01) { best_eff = eff; best = (int)s; }
+  }
+  return best;
+}
+
+struct FwdPlan {
+  int ks, cps;
+  int64_t tiles;
+  size_t ppart, gpart, rec_tmp;
+};
+
+template <int N>
+FwdPlan plan_fwd(int64_t B, int64_t C) {
+  FwdPlan p;
+  p.tiles = (B + ProjCfg<N>::TT - 1) / ProjCfg<N>::TT;
+  p.ks = choose_ksplit(p.tiles, C, num_sms());
+  p.cps = (int)(((C + p.ks - 1) / p.ks + 31) / 32 * 32);
+  p.ks = (int)((C + p.cps - 1) / p.cps);
+  p.ppart = (size_t)p.ks * B * L<N>::NHP;
+  p.gpart = (size_t)p.ks * B * L<N>::NG;
+  p.rec_tmp = (size_t)B * L<N>::REC;
+  return p;
+}
+
+struct BwdPlan {
+  int ntiles, nsplit;
+  size_t stats, tokb, tokr, dphi, gw, tot;
+};
+
+template <int N, bool DYN>
+BwdPlan plan_bwd(int64_t B, int64_t C) {
+  BwdPlan p;
+  p.ntiles = (int)((C + GX_CW - 1) / GX_CW);
+  p.nsplit = choose_gx_splits(p.ntiles, B, num_sms(), N <= 4 ? 2 : 1);
+  p.stats = (size_t)B * L<N>::NS1;
+  p.tokb = (size_t)B * (DYN ? L<N>::TB : 4);
+  p.tokr = (size_t)B * (DYN ? L<N>::NR : L<N>::NRS);
+  p.dphi = DYN ? (size_t)p.nsplit * L<N>::NH * N * C : 0;
+  p.gw = (size_t)p.nsplit * C;
+  p.tot = (size_t)(DYN ? L<N>::NR : L<N>::NRS);
+  return p;
+}
+
+template <int N>
+size_t fwd_ws_bytes(int64_t B, int64_t C, bool need_rec) {
+  FwdPlan p = plan_fwd<N>(B, C);
+  Carve cv(nullptr);
+  cv.take(p.ppart);
+  cv.take(p.gpart);
+  if (need_rec) cv.take(p.rec_tmp);
+  return cv.off;
+}
+
+template <int N, bool DYN>
+size_t bwd_ws_bytes(int64_t B, int64_t C) {
+  BwdPlan p = plan_bwd<N, DYN>(B, C);
+  Carve cv(nullptr);
+  cv.take(p.stats); cv.take(p.tokb); cv.take(p.tokr); cv.take(p.dphi); cv.take(p.gw);
+  cv.take(p.tot);
+  if (!DYN) cv.take(L<N>::REC);
+  return cv.off;
+}
+
+inline unsigned grid_1d(int64_t n, int threads, int64_t cap = 1 << 30) {
+  int64_t g = (n + threads - 1) / threads;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return (unsigned)g;
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+template <int N>
+int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float* pq,
+                    const float* pr, const float* ap, const float* aq, const float* ar,
+                    const float* bp, const float* bq, const float* br, float* out,
+                    float* token_state, int64_t B, int64_t C, int iters, float s_eps,
+                    float r_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
+  const bool need_rec = token_state == nullptr;
+  const size_t need = fwd_ws_bytes<N>(B, C, need_rec);
+  MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
+              "mhc_layer_fwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
+  FwdPlan p = plan_fwd<N>(B, C);
+  Carve cv(ws);
+  float* ppart = cv.take(p.ppart);
+  float* gpart = cv.take(p.gpart);
+  float* rec = need_rec ? cv.take(p.rec_tmp) : token_state;
+
+  using P = ProjCfg<N>;
+  const size_t smem = (size_t)P::SMEM_FLOATS * sizeof(float);
+  // Opt in to > 48 KB of dynamic shared memory (cheap, idempotent, per device).
+  cudaFuncSetAttribute(proj_stats_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem);
+  { ProfScope _ps("proj_stats", s); proj_stats_kernel<N><<<dim3((unsigned)p.tiles, (unsigned)p.ks), 256, smem, s>>>(
+      x, pp, pq, pr, ppart, gpart, B, C, p.cps); }
+  int rc = check_launch("mhc_layer_fwd_dynamic/proj_stats");
+  if (rc) return rc;
+  { ProfScope _ps("token_fwd", s); token_fwd_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(ppart, gpart, p.ks, ap, aq, ar, bp, bq, br,
+                                                     rec, B, C, iters, s_eps, r_eps); }
+  rc = check_launch("mhc_layer_fwd_dynamic/token_fwd");
+  if (rc) return rc;
+  const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(out) && aligned16(w);
+  const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
+  if (vec)
+    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, true><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C); }
+  else
+    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, false><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C); }
+  return check_launch("mhc_layer_fwd_dynamic/stream_fwd");
+}
+
+template <int N>
+int run_bwd_dynamic(const float* g, const float* x, const float* w, const float* pp,
+                    const float* pq, const float* pr, const float* ap, const float* aq,
+                    const float* ar, const float* br, const float* rec, float* gx, float* gw,
+                    float* gpp, float* gpq, float* gpr, float* gap, float* gaq, float* gar,
+                    float* gbp, float* gbq, float* gbr, int64_t B, int64_t C, int iters,
+                    float s_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
+  const size_t need = bwd_ws_bytes<N, true>(B, C);
+  MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
+              "mhc_layer_bwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
+  BwdPlan p = plan_bwd<N, true>(B, C);
+  Carve cv(ws);
+  float* stats = cv.take(p.stats);
+  float* tokb = cv.take(p.tokb);
+  float* tokr = cv.take(p.tokr);
+  float* dphi = cv.take(p.dphi);
+  float* gwp = cv.take(p.gw);
+  float* tot = cv.take(p.tot);
+  const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(w);
+  const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
+  if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  int rc = check_launch("mhc_layer_bwd_dynamic/bwd_stats");
+  if (rc) return rc;
+  { ProfScope _ps("token_bwd", s); token_bwd_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, rec, ap, aq, ar, br, tokb, tokr, B,
+                                                     C, iters, s_eps); }
+  rc = check_launch("mhc_layer_bwd_dynamic/token_bwd");
+  if (rc) return rc;
+  { ProfScope _ps("grad_x", s); grad_x_kernel<N, true><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
+      g, x, w, pp, pq, pr, rec, L<N>::REC, tokb, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
+  rc = check_launch("mhc_layer_bwd_dynamic/grad_x");
+  if (rc) return rc;
+  const int64_t nC = (int64_t)N * C;
+  { ProfScope _ps("reduce_dphi", s); reduce_dphi_kernel<<<grid_1d((int64_t)L<N>::NH * nC, 256, 4096), 256, 0, s>>>(
+      dphi, p.nsplit, L<N>::NH, N, nC, gpp, gpq, gpr); }
+  { ProfScope _ps("reduce_splits", s); reduce_splits_kernel<<<grid_1d(C, 256, 4096), 256, 0, s>>>(gwp, p.nsplit, C, gw); }
+  { ProfScope _ps("reduce_tokens", s); reduce_tokens_kernel<<<L<N>::NR, 256, 0, s>>>(tokr, B, L<N>::NR, tot); }
+  { ProfScope _ps("scatter_dyn_param_grads", s); scatter_dyn_param_grads_kernel<N><<<1, 128, 0, s>>>(tot, gbp, gbq, gbr, gap, gaq, gar); }
+  return check_launch("mhc_layer_bwd_dynamic/reduce");
+}
+
+template <int N, typename T>
+int run_fwd_static(const T* x, const float* w, const float* Hp, const float* Hq, const float* Hr,
+                   T* out, float* rms, int64_t B, int64_t C, int iters, float s_eps, float r_eps,
+                   void* ws, size_t ws_bytes, cudaStream_t s) {
+  MHC_REQUIRE(ws != nullptr && ws_bytes >= align_up(L<N>::REC * sizeof(float)),
+              MHC_ERR_WORKSPACE, "mhc_layer_fwd_static: workspace too small");
+  float* rec = (float*)ws;
+  { ProfScope _ps("static_prep", s); static_prep_kernel<N><<<1, 32, 0, s>>>(Hp, Hq, Hr, rec, iters, s_eps); }
+  int rc = check_launch("mhc_layer_fwd_static/prep");
+  if (rc) return rc;
+  const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(out) && aligned16(w);
+  const int64_t q = (C / 4 + 255) / 256;  // quads per thread
+  const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
+  if (B == 0) return MHC_OK;
+  if (vec && q <= 1) { ProfScope _ps("static_fwd", s); static_fwd_kernel<N, 1, T><<<grid, 256, 0, s>>>(x, w, rec, rms, out, B, C, r_eps); }
+  else if (vec && q <= 2) { ProfScope _ps("static_fwd", s); static_fwd_kernel<N, 2, T><<<grid, 256, 0, s>>>(x, w, rec, rms, out, B, C, r_eps); }
+  else if (vec && q <= 4) { ProfScope _ps("static_fwd", s); static_fwd_kernel<N, 4, T><<<grid, 256, 0, s>>>(x, w, rec, rms, out, B, C, r_eps); }
+  else if (vec && q <= 8 && N <= 4) { ProfScope _ps("static_fwd", s); static_fwd_kernel<N, (N <= 4 ? 8 : 4), T><<<grid, 256, 0, s>>>(x, w, rec, rms, out, B, C, r_eps); }
+  else { ProfScope _ps("static_fwd_generic", s); static_fwd_generic_kernel<N, T><<<grid, 256, 0, s>>>(x, w, rec, rms, out, B, C, r_eps); }
+  return check_launch("mhc_layer_fwd_static");
+}
+
+template <int N>
+int run_bwd_static(const float* g, const float* x, const float* w, const float* Hp,
+                   const float* Hq, const float* Hr, const float* rms, float* gx, float* gw,
+                   float* gHp, float* gHq, float* gHr, int64_t B, int64_t C, int iters,
+                   float s_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
+  const size_t need = bwd_ws_bytes<N, false>(B, C);
+  MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
+              "mhc_layer_bwd_static: workspace of %zu bytes required, got %zu", need, ws_bytes);
+  BwdPlan p = plan_bwd<N, false>(B, C);
+  Carve cv(ws);
+  float* stats = cv.take(p.stats);
+  float* tokb = cv.take(p.tokb);
+  float* tokr = cv.take(p.tokr);
+  cv.take(p.dphi);
+  float* gwp = cv.take(p.gw);
+  float* tot = cv.take(p.tot);
+  float* rec = cv.take(L<N>::REC);
+  { ProfScope _ps("static_prep", s); static_prep_kernel<N><<<1, 32, 0, s>>>(Hp, Hq, Hr, rec, iters, s_eps); }
+  const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(w);
+  const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
+  if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  int rc = check_launch("mhc_layer_bwd_static/bwd_stats");
+  if (rc) return rc;
+  { ProfScope _ps("token_bwd_static", s); token_bwd_static_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, rec, rms, tokb, tokr, B, C); }
+  { ProfScope _ps("grad_x", s); grad_x_kernel<N, false><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
+      g, x, w, nullptr, nullptr, nullptr, rec, 0, tokb, gx, nullptr, gwp, B, C, p.ntiles,
+      p.nsplit); }
+  rc = check_launch("mhc_layer_bwd_static/grad_x");
+  if (rc) return rc;
+  { ProfScope _ps("reduce_splits", s); reduce_splits_kernel<<<grid_1d(C, 256, 4096), 256, 0, s>>>(gwp, p.nsplit, C, gw); }
+  { ProfScope _ps("reduce_tokens", s); reduce_tokens_kernel<<<L<N>::NRS, 256, 0, s>>>(tokr, B, L<N>::NRS, tot); }
+  { ProfScope _ps("static_param_grads", s); static_param_grads_kernel<N><<<1, 32, 0, s>>>(tot, Hr, gHp, gHq, gHr, iters, s_eps); }
+  return check_launch("mhc_layer_bwd_static/reduce");
+}
+
+int check_layer_args(const char* what, int64_t B, int n, int64_t C, int iters, float s_eps,
+                     float r_eps) {
+  MHC_REQUIRE(B >= 0, MHC_ERR_INVALID_ARG, "%s: batch must be >= 0", what);
+  MHC_REQUIRE(C >= 1, MHC_ERR_INVALID_ARG, "%s: hidden_dim must be >= 1", what);
+  MHC_REQUIRE(n >= 1 && n <= 8, MHC_ERR_UNSUPPORTED, "%s: expansion_rate n must be in [1, 8], got %d",
+              what, n);
+  MHC_REQUIRE(iters >= 0, MHC_ERR_INVALID_ARG, "%s: sinkhorn_iters must be >= 0", what);
+  MHC_REQUIRE(s_eps >= 0.f && r_eps >= 0.f, MHC_ERR_INVALID_ARG, "%s: eps must be >= 0", what);
+  MHC_REQUIRE((int64_t)n * C < (1LL << 31), MHC_ERR_UNSUPPORTED, "%s: n*C too large", what);
+  return MHC_OK;
+}
+
+}  // namespace
+}  // namespace mhc
+
+using namespace mhc;
+
+#define MHC_DISPATCH_N(n, CALL)          \
+  switch (n) {                           \
+    case 1: { constexpr int NN = 1; return CALL; } \
+    case 2: { constexpr int NN = 2; return CALL; } \
+    case 3: { constexpr int NN = 3; return CALL; } \
+    case 4: { constexpr int NN = 4; return CALL; } \
+    case 5: { constexpr int NN = 5; return CALL; } \
+    case 6: { constexpr int NN = 6; return CALL; } \
+    case 7: { constexpr int NN = 7; return CALL; } \
+    case 8: { constexpr int NN = 8; return CALL; } \
+    default: return fail(MHC_ERR_UNSUPPORTED, "expansion_rate %d unsupported", n); \
+  }
+
+extern "C" int32_t mhc_token_state_stride(int32_t n) { return rec_stride(n); }
+
+extern "C" size_t mhc_layer_fwd_dynamic_workspace_bytes(int64_t batch, int32_t n,
+                                                        int64_t hidden) {
+  if (batch <= 0 || hidden <= 0 || n < 1 || n > 8) return 0;
+  switch (n) {
+    case 1: return fwd_ws_bytes<1>(batch, hidden, true);
+    case 2: return fwd_ws_bytes<2>(batch, hidden, true);
+    case 3: return fwd_ws_bytes<3>(batch, hidden, true);
+    case 4: return fwd_ws_bytes<4>(batch, hidden, true);
+    case 5: return fwd_ws_bytes<5>(batch, hidden, true);
+    case 6: return fwd_ws_bytes<6>(batch, hidden, true);
+    case 7: return fwd_ws_bytes<7>(batch, hidden, true);
+    default: return fwd_ws_bytes<8>(batch, hidden, true);
+  }
+}
+
+extern "C" int mhc_layer_fwd_dynamic(const float* x, const float* rmsnorm_weight,
+                                     const float* phi_pre, const float* phi_post,
+                                     const float* phi_res, const float* alpha_pre,
+                                     const float* alpha_post, const float* alpha_res,
+                                     const float* b_pre, const float* b_post, const float* b_res,
+                                     float* out, float* token_state, int64_t batch, int32_t n,
+                                     int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
+                                     float rmsnorm_eps, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  int rc = check_layer_args("mhc_layer_fwd_dynamic", batch, n, hidden, sinkhorn_iters,
+                            sinkhorn_eps, rmsnorm_eps);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(rmsnorm_weight); MHC_REQUIRE_PTR(phi_pre);
+  MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res); MHC_REQUIRE_PTR(alpha_pre);
+  MHC_REQUIRE_PTR(alpha_post); MHC_REQUIRE_PTR(alpha_res); MHC_REQUIRE_PTR(b_pre);
+  MHC_REQUIRE_PTR(b_post); MHC_REQUIRE_PTR(b_res); MHC_REQUIRE_PTR(out);
+  if (batch == 0) return MHC_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  MHC_DISPATCH_N(n, (run_fwd_dynamic<NN>(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
+                                         alpha_post, alpha_res, b_pre, b_post, b_res, out,
+                                         token_state, batch, hidden, sinkhorn_iters,
+                                         sinkhorn_eps, rmsnorm_eps, workspace, workspace_bytes, s)));
+}
+
+extern "C" size_t mhc_layer_bwd_dynamic_workspace_bytes(int64_t batch, int32_t n,
+                                                        int64_t hidden) {
+  if (batch <= 0 || hidden <= 0 || n < 1 || n > 8) return 0;
+  switch (n) {
+    case 1: return bwd_ws_bytes<1, true>(batch, hidden);
+    case 2: return bwd_ws_bytes<2, true>(batch, hidden);
+    case 3: return bwd_ws_bytes<3, true>(batch, hidden);
+    case 4: return bwd_ws_bytes<4, true>(batch, hidden);
+    case 5: return bwd_ws_bytes<5, true>(batch, hidden);
+    case 6: return bwd_ws_bytes<6, true>(batch, hidden);
+    case 7: return bwd_ws_bytes<7, true>(batch, hidden);
+    default: return bwd_ws_bytes<8, true>(batch, hidden);
+  }
+}
+
+extern "C" int mhc_layer_bwd_dynamic(
+    const float* grad_out, const float* x, const float* rmsnorm_weight, const float* phi_pre,
+    const float* phi_post, const float* phi_res, const float* alpha_pre, const float* alpha_post,
+    const float* alpha_res, const float* b_pre, const float* b_post, const float* b_res,
+    const float* token_state, float* grad_x, float* grad_rmsnorm_weight, float* grad_phi_pre,
+    float* grad_phi_post, float* grad_phi_res, float* grad_alpha_pre, float* grad_alpha_post,
+    float* grad_alpha_res, float* grad_b_pre, float* grad_b_post, float* grad_b_res,
+    int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
+    float rmsnorm_eps, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)b_pre; (void)b_post;
+  int rc = check_layer_args("mhc_layer_bwd_dynamic", batch, n, hidden, sinkhorn_iters,
+                            sinkhorn_eps, rmsnorm_eps);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(grad_out); MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(rmsnorm_weight);
+  MHC_REQUIRE_PTR(phi_pre); MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res);
+  MHC_REQUIRE_PTR(alpha_pre); MHC_REQUIRE_PTR(alpha_post); MHC_REQUIRE_PTR(alpha_res);
+  MHC_REQUIRE_PTR(b_res); MHC_REQUIRE_PTR(token_state); MHC_REQUIRE_PTR(grad_x);
+  MHC_REQUIRE_PTR(grad_rmsnorm_weight); MHC_REQUIRE_PTR(grad_phi_pre);
+  MHC_REQUIRE_PTR(grad_phi_post); MHC_REQUIRE_PTR(grad_phi_res); MHC_REQUIRE_PTR(grad_alpha_pre);
+  MHC_REQUIRE_PTR(grad_alpha_post); MHC_REQUIRE_PTR(grad_alpha_res);
+  MHC_REQUIRE_PTR(grad_b_pre); MHC_REQUIRE_PTR(grad_b_post); MHC_REQUIRE_PTR(grad_b_res);
+  MHC_REQUIRE(batch > 0, MHC_ERR_INVALID_ARG, "mhc_layer_bwd_dynamic: batch must be > 0");
+  cudaStream_t s = (cudaStream_t)stream;
+  MHC_DISPATCH_N(n, (run_bwd_dynamic<NN>(grad_out, x, rmsnorm_weight, phi_pre, phi_post, phi_res,
+                                         alpha_pre, alpha_post, alpha_res, b_res, token_state,
+                                         grad_x, grad_rmsnorm_weight, grad_phi_pre, grad_phi_post,
+                                         grad_phi_res, grad_alpha_pre, grad_alpha_post,
+                                         grad_alpha_res, grad_b_pre, grad_b_post, grad_b_res,
+                                         batch, hidden, sinkhorn_iters, sinkhorn_eps, workspace,
+                                         workspace_bytes, s)));
+}
+
+extern "C" size_t mhc_layer_static_workspace_bytes(int64_t batch, int32_t n, int64_t hidden) {
+  if (hidden <= 0 || n < 1 || n > 8) return 0;
+  if (batch < 1) batch = 1;
+  switch (n) {
+    case 1: return bwd_ws_bytes<1, false>(batch, hidden);
+    case 2: return bwd_ws_bytes<2, false>(batch, hidden);
+    case 3: return bwd_ws_bytes<3, false>(batch, hidden);
+    case 4: return bwd_ws_bytes<4, false>(batch, hidden);
+    case 5: return bwd_ws_bytes<5, false>(batch, hidden);
+    case 6: return bwd_ws_bytes<6, false>(batch, hidden);
+    case 7: return bwd_ws_bytes<7, false>(batch, hidden);
+    default: return bwd_ws_bytes<8, false>(batch, hidden);
+  }
+}
+
+template <typename T>
+static int fwd_static_entry(const T* x, const float* w, const float* Hp, const float* Hq,
+                            const float* Hr, T* out, float* rms, int64_t batch, int32_t n,
+                            int64_t hidden, int32_t iters, float s_eps, float r_eps, void* ws,
+                            size_t ws_bytes, void* stream) {
+  int rc = check_layer_args("mhc_layer_fwd_static", batch, n, hidden, iters, s_eps, r_eps);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(w); MHC_REQUIRE_PTR(Hp); MHC_REQUIRE_PTR(Hq);
+  MHC_REQUIRE_PTR(Hr); MHC_REQUIRE_PTR(out);
+  cudaStream_t s = (cudaStream_t)stream;
+  MHC_DISPATCH_N(n, (run_fwd_static<NN, T>(x, w, Hp, Hq, Hr, out, rms, batch, hidden, iters,
+                                           s_eps, r_eps, ws, ws_bytes, s)));
+}
+
+extern "C" int mhc_layer_fwd_static_f32(const float* x, const float* rmsnorm_weight,
+                                        const float* H_pre, const float* H_post,
+                                        const float* H_res, float* out, float* rms,
+                                        int64_t batch, int32_t n, int64_t hidden,
+                                        int32_t sinkhorn_iters, float sinkhorn_eps,
+                                        float rmsnorm_eps, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  return fwd_static_entry<float>(x, rmsnorm_weight, H_pre, H_post, H_res, out, rms, batch, n,
+                                 hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace,
+                                 workspace_bytes, stream);
+}
+
+extern "C" int mhc_layer_fwd_static_bf16(const void* x, const float* rmsnorm_weight,
+                                         const float* H_pre, const float* H_post,
+                                         const float* H_res, void* out, float* rms,
+                                         int64_t batch, int32_t n, int64_t hidden,
+                                         int32_t sinkhorn_iters, float sinkhorn_eps,
+                                         float rmsnorm_eps, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  return fwd_static_entry<__nv_bfloat16>((const __nv_bfloat16*)x, rmsnorm_weight, H_pre, H_post,
+                                         H_res, (__nv_bfloat16*)out, rms, batch, n, hidden,
+                                         sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace,
+                                         workspace_bytes, stream);
+}
+
+extern "C" int mhc_layer_bwd_static(const float* grad_out, const float* x,
+                                    const float* rmsnorm_weight, const float* H_pre,
+                                    const float* H_post, const float* H_res, const float* rms,
+                                    float* grad_x, float* grad_rmsnorm_weight, float* grad_H_pre,
+                                    float* grad_H_post, float* grad_H_res, int64_t batch,
+                                    int32_t n, int64_t hidden, int32_t sinkhorn_iters,
+                                    float sinkhorn_eps, float rmsnorm_eps, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  int rc = check_layer_args("mhc_layer_bwd_static", batch, n, hidden, sinkhorn_iters,
+                            sinkhorn_eps, rmsnorm_eps);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(grad_out); MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(rmsnorm_weight);
+  MHC_REQUIRE_PTR(H_pre); MHC_REQUIRE_PTR(H_post); MHC_REQUIRE_PTR(H_res); MHC_REQUIRE_PTR(rms);
+  MHC_REQUIRE_PTR(grad_x); MHC_REQUIRE_PTR(grad_rmsnorm_weight); MHC_REQUIRE_PTR(grad_H_pre);
+  MHC_REQUIRE_PTR(grad_H_post); MHC_REQUIRE_PTR(grad_H_res);
+  MHC_REQUIRE(batch > 0, MHC_ERR_INVALID_ARG, "mhc_layer_bwd_static: batch must be > 0");
+  cudaStream_t s = (cudaStream_t)stream;
+  MHC_DISPATCH_N(n, (run_bwd_static<NN>(grad_out, x, rmsnorm_weight, H_pre, H_post, H_res, rms,
+                                        grad_x, grad_rmsnorm_weight, grad_H_pre, grad_H_post,
+                                        grad_H_res, batch, hidden, sinkhorn_iters, sinkhorn_eps,
+                                        workspace, workspace_bytes, s)));
+}

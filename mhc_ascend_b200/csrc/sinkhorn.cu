@@ -1,0 +1,220 @@
+// Standalone batched Sinkhorn-Knopp (forward and reverse mode).
+//
+// Replaces the Ascend kernels of sinkhorn_knopp.cpp (fwd :118-665, bwd
+// :856-1814) behind sinkhorn_knopp_fwd / sinkhorn_knopp_bwd
+// (bindings.cpp:155-231).  Layout: [batch, n, n] fp32 row-major.
+//   n <= 8 : one matrix per thread, all n*n entries in registers.
+//   n <= 32: one matrix per warp, lane j owns column j; row sums are warp
+//            reductions; the per-iteration denominators for the reverse pass
+//            live in shared memory.
+#include "common.cuh"
+#include "sinkhorn.cuh"
+
+namespace mhc {
+namespace {
+
+template <int N>
+__global__ void __launch_bounds__(128) sk_fwd_thread_kernel(const float* __restrict__ inp,
+                                                            float* __restrict__ out,
+                                                            int64_t batch, int iters, float eps) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  float a[N * N];
+  const float* src = inp + b * (N * N);
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) a[e] = src[e];
+  sk_forward<N>(a, iters, eps);
+  float* dst = out + b * (N * N);
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) dst[e] = a[e];
+}
+
+template <int N>
+__global__ void __launch_bounds__(128) sk_bwd_thread_kernel(const float* __restrict__ grad_out,
+                                                            const float* __restrict__ inp,
+                                                            float* __restrict__ grad_inp,
+                                                            int64_t batch, int iters, float eps) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  float x0[N * N], g[N * N];
+  const float* src = inp + b * (N * N);
+  const float* gsrc = grad_out + b * (N * N);
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) {
+    x0[e] = src[e];
+    g[e] = gsrc[e];
+  }
+  sk_backward<N>(x0, g, iters, eps);
+  float* dst = grad_inp + b * (N * N);
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) dst[e] = g[e];
+}
+
+constexpr int WARPS_PER_BLOCK = 4;
+
+// One matrix per warp, lane j holds column j (rows 0..n-1), n <= 32.
+__device__ __forceinline__ void warp_sk_step(float (&a)[32], int n, int lane, float eps,
+                                             float* dr, float* dc) {
+  const bool active = lane < n;
+  for (int i = 0; i < n; ++i) {
+    const float s = warp_sum(active ? a[i] : 0.f);
+    const float d = s + eps;
+    if (dr && lane == 0) dr[i] = d;
+    if (active) a[i] = a[i] / d;
+  }
+  float s = 0.f;
+  for (int i = 0; i < n; ++i) s += a[i];
+  const float d = s + eps;
+  if (dc && active) dc[lane] = d;
+  if (active)
+    for (int i = 0; i < n; ++i) a[i] = a[i] / d;
+}
+
+__global__ void __launch_bounds__(WARPS_PER_BLOCK * 32)
+    sk_fwd_warp_kernel(const float* __restrict__ inp, float* __restrict__ out, int64_t batch,
+                       int n, int iters, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t b = (int64_t)blockIdx.x * WARPS_PER_BLOCK + (threadIdx.x >> 5);
+  if (b >= batch) return;
+  float a[32];
+  const float* src = inp + b * n * n;
+  for (int i = 0; i < n; ++i) a[i] = lane < n ? src[i * n + lane] : 0.f;
+  for (int t = 0; t < iters; ++t) warp_sk_step(a, n, lane, eps, nullptr, nullptr);
+  float* dst = out + b * n * n;
+  if (lane < n)
+    for (int i = 0; i < n; ++i) dst[i * n + lane] = a[i];
+}
+
+__global__ void __launch_bounds__(WARPS_PER_BLOCK * 32)
+    sk_bwd_warp_kernel(const float* __restrict__ grad_out, const float* __restrict__ inp,
+                       float* __restrict__ grad_inp, int64_t batch, int n, int iters,
+                       float eps) {
+  __shared__ float s_dr[WARPS_PER_BLOCK][SK_SEG][32];
+  __shared__ float s_dc[WARPS_PER_BLOCK][SK_SEG][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t b = (int64_t)blockIdx.x * WARPS_PER_BLOCK + w;
+  if (b >= batch) return;
+  const bool active = lane < n;
+  float g[32], z[32];
+  const float* src = inp + b * n * n;
+  const float* gsrc = grad_out + b * n * n;
+  for (int i = 0; i < n; ++i) g[i] = active ? gsrc[i * n + lane] : 0.f;
+  int seg_end = iters;
+  while (seg_end > 0) {
+    const int seg_start = seg_end > SK_SEG ? seg_end - SK_SEG : 0;
+    for (int i = 0; i < n; ++i) z[i] = active ? src[i * n + lane] : 0.f;
+    for (int t = 0; t < seg_start; ++t) warp_sk_step(z, n, lane, eps, nullptr, nullptr);
+    for (int t = seg_start; t < seg_end; ++t)
+      warp_sk_step(z, n, lane, eps, s_dr[w][t - seg_start], s_dc[w][t - seg_start]);
+    __syncwarp();
+    for (int t = seg_end - 1; t >= seg_start; --t) {
+      // column step
+      const float dcj = active ? s_dc[w][t - seg_start][lane] : 1.f;
+      float s = 0.f;
+      for (int i = 0; i < n; ++i) s += g[i] * z[i];
+      for (int i = 0; i < n; ++i) {
+        g[i] = active ? (g[i] - s) / dcj : 0.f;
+        z[i] = z[i] * dcj;
+      }
+      // row step
+      for (int i = 0; i < n; ++i) {
+        const float d = s_dr[w][t - seg_start][i];
+        const float si = warp_sum(active ? g[i] * z[i] : 0.f);
+        g[i] = active ? (g[i] - si) / d : 0.f;
+        z[i] = z[i] * d;
+      }
+    }
+    __syncwarp();
+    seg_end = seg_start;
+  }
+  float* dst = grad_inp + b * n * n;
+  if (active)
+    for (int i = 0; i < n; ++i) dst[i * n + lane] = g[i];
+}
+
+template <int N>
+int launch_thread_fwd(const float* inp, float* out, int64_t batch, int iters, float eps,
+                      cudaStream_t s) {
+  const int threads = 128;
+  const int64_t blocks = (batch + threads - 1) / threads;
+  sk_fwd_thread_kernel<N><<<(unsigned)blocks, threads, 0, s>>>(inp, out, batch, iters, eps);
+  return check_launch("sinkhorn_knopp_fwd");
+}
+
+template <int N>
+int launch_thread_bwd(const float* go, const float* inp, float* gi, int64_t batch, int iters,
+                      float eps, cudaStream_t s) {
+  const int threads = 128;
+  const int64_t blocks = (batch + threads - 1) / threads;
+  sk_bwd_thread_kernel<N><<<(unsigned)blocks, threads, 0, s>>>(go, inp, gi, batch, iters, eps);
+  return check_launch("sinkhorn_knopp_bwd");
+}
+
+int validate(const void* a, const void* b, int64_t batch, int n, int iters, float eps) {
+  MHC_REQUIRE(a != nullptr && b != nullptr, MHC_ERR_INVALID_ARG, "sinkhorn_knopp: NULL pointer");
+  MHC_REQUIRE(batch >= 0, MHC_ERR_INVALID_ARG, "sinkhorn_knopp: batch must be >= 0, got %lld",
+              (long long)batch);
+  MHC_REQUIRE(n >= 1 && n <= 32, MHC_ERR_UNSUPPORTED,
+              "sinkhorn_knopp: matrix size n must be in [1, 32], got %d", n);
+  MHC_REQUIRE(iters >= 0, MHC_ERR_INVALID_ARG, "sinkhorn_knopp: num_iters must be >= 0, got %d",
+              iters);
+  MHC_REQUIRE(eps >= 0.f, MHC_ERR_INVALID_ARG, "sinkhorn_knopp: eps must be >= 0");
+  MHC_REQUIRE(batch <= (int64_t)INT32_MAX * 32, MHC_ERR_UNSUPPORTED, "sinkhorn_knopp: batch too large");
+  return MHC_OK;
+}
+
+}  // namespace
+}  // namespace mhc
+
+using namespace mhc;
+
+extern "C" int mhc_sinkhorn_knopp_fwd(const float* inp, float* out, int64_t batch, int32_t n,
+                                      int32_t num_iters, float eps, void* stream) {
+  int rc = validate(inp, out, batch, n, num_iters, eps);
+  if (rc) return rc;
+  if (batch == 0) return MHC_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (n) {
+    case 1: return launch_thread_fwd<1>(inp, out, batch, num_iters, eps, s);
+    case 2: return launch_thread_fwd<2>(inp, out, batch, num_iters, eps, s);
+    case 3: return launch_thread_fwd<3>(inp, out, batch, num_iters, eps, s);
+    case 4: return launch_thread_fwd<4>(inp, out, batch, num_iters, eps, s);
+    case 5: return launch_thread_fwd<5>(inp, out, batch, num_iters, eps, s);
+    case 6: return launch_thread_fwd<6>(inp, out, batch, num_iters, eps, s);
+    case 7: return launch_thread_fwd<7>(inp, out, batch, num_iters, eps, s);
+    case 8: return launch_thread_fwd<8>(inp, out, batch, num_iters, eps, s);
+    default: {
+      const int64_t blocks = (batch + WARPS_PER_BLOCK - 1) / WARPS_PER_BLOCK;
+      sk_fwd_warp_kernel<<<(unsigned)blocks, WARPS_PER_BLOCK * 32, 0, s>>>(inp, out, batch, n,
+                                                                           num_iters, eps);
+      return check_launch("sinkhorn_knopp_fwd");
+    }
+  }
+}
+
+extern "C" int mhc_sinkhorn_knopp_bwd(const float* grad_out, const float* inp, const float* out,
+                                      float* grad_inp, int64_t batch, int32_t n,
+                                      int32_t num_iters, float eps, void* stream) {
+  (void)out;
+  int rc = validate(grad_out, grad_inp, batch, n, num_iters, eps);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(inp);
+  if (batch == 0) return MHC_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (n) {
+    case 1: return launch_thread_bwd<1>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
+    case 2: return launch_thread_bwd<2>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
+    case 3: return launch_thread_bwd<3>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
+    case 4: return launch_thread_bwd<4>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
+    case 5: return launch_thread_bwd<5>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
+    case 6: return launch_thread_bwd<6>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
+    case 7: return launch_thread_bwd<7>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
+    case 8: return launch_thread_bwd<8>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
+    default: {
+      const int64_t blocks = (batch + WARPS_PER_BLOCK - 1) / WARPS_PER_BLOCK;
+      sk_bwd_warp_kernel<<<(unsigned)blocks, WARPS_PER_BLOCK * 32, 0, s>>>(
+          grad_out, inp, grad_inp, batch, n, num_iters, eps);
+      return check_launch("sinkhorn_knopp_bwd");
+    }
+  }
+}

@@ -1,0 +1,37 @@
+"""Shared test helpers: golden fixtures and tolerance checks."""
+import os
+
+import numpy as np
+import torch
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+# Tolerance of the reference's fp32 formulation, as stated by the north star.
+RTOL = 1e-4
+ATOL = 1e-5
+
+
+def golden(name):
+    with np.load(os.path.join(GOLDEN, name + ".npz")) as z:
+        return {k: torch.from_numpy(np.array(z[k])) for k in z.files}
+
+
+def close(actual, expected, rtol=RTOL, atol=ATOL, what=""):
+    a = actual.detach().double().cpu()
+    e = expected.detach().double().cpu()
+    assert a.shape == e.shape, f"{what}: shape {tuple(a.shape)} != {tuple(e.shape)}"
+    err = (a - e).abs()
+    bound = atol + rtol * e.abs()
+    bad = err > bound
+    if bad.any():
+        idx = int(torch.argmax((err - bound).reshape(-1)))
+        raise AssertionError(
+            f"{what}: {int(bad.sum())}/{a.numel()} elements outside rtol={rtol} atol={atol}; "
+            f"worst at flat index {idx}: actual={a.reshape(-1)[idx].item():.8g} "
+            f"expected={e.reshape(-1)[idx].item():.8g} max_abs_err={err.max().item():.3g}")
+
+
+def rel_err(actual, expected):
+    a = actual.detach().double().cpu()
+    e = expected.detach().double().cpu()
+    return ((a - e).norm() / e.norm().clamp_min(1e-30)).item()

@@ -1,0 +1,201 @@
+"""Fused mHC layer parity (dynamic and static H, forward and backward) with the
+reference formulation: golden fixtures, the CPU oracle at random shapes, and
+size-independent properties at the BASELINE full sizes."""
+import pytest
+import torch
+
+import mhc_ascend_b200 as mhc
+from oracle import mhc_oracle as O
+from tests.helpers import close, golden, rel_err
+
+pytestmark = pytest.mark.gpu
+
+KEYS = {"rmsnorm_weight": "w", "phi_pre": "phi_pre", "phi_post": "phi_post", "phi_res": "phi_res",
+        "alpha_pre": "alpha_pre", "alpha_post": "alpha_post", "alpha_res": "alpha_res",
+        "b_pre": "b_pre", "b_post": "b_post", "b_res": "b_res"}
+
+
+def make_layer(params, n, C, dev, iters=20, s_eps=1e-8, r_eps=1e-5):
+    layer = mhc.MHCLayer(hidden_dim=C, expansion_rate=n, num_sinkhorn_iters=iters,
+                         sinkhorn_eps=s_eps, rmsnorm_eps=r_eps).to(dev)
+    with torch.no_grad():
+        for k, v in params.items():
+            getattr(layer, k).copy_(v.reshape(getattr(layer, k).shape))
+    return layer
+
+
+def run_layer(layer, x, grad_out=None):
+    x = x.clone().requires_grad_(True)
+    out = layer(x)
+    if grad_out is None:
+        (out ** 2).sum().backward()
+    else:
+        out.backward(grad_out)
+    grads = {"x": x.grad}
+    grads.update({k: p.grad for k, p in layer.named_parameters()})
+    return out.detach(), grads
+
+
+@pytest.mark.parametrize("case", ["dynamic_cfg1_B32_n4_C256", "dynamic_strong_B8_n4_C64",
+                                  "dynamic_strong_B4_n8_C32", "dynamic_strong_B6_n2_C100"])
+def test_dynamic_golden(cuda, case):
+    z = golden(case)
+    B, n, C = z["x"].shape
+    layer = make_layer({k: z[v] for k, v in KEYS.items()}, n, C, cuda)
+    g = z["grad_out"].to(cuda) if "grad_out" in z else None
+    out, grads = run_layer(layer, z["x"].to(cuda), g)
+    close(out, z["out"], what="out")
+    close(grads["x"], z["grad_x"], what="grad_x")
+    for k, v in KEYS.items():
+        close(grads[k], z["grad_" + v], what="grad_" + k)
+
+
+def oracle_case(B, n, C, seed, alpha=0.01, bias_std=0.0, weight=None):
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, n, C, generator=gen)
+    params = O.make_dynamic_params(n, C, gen, alpha=alpha, bias_std=bias_std, weight=weight)
+    grad = torch.randn(B, n, C, generator=gen)
+    return x, params, grad
+
+
+@pytest.mark.parametrize("B,n,C,alpha,bias", [
+    (64, 4, 4096, 0.01, 0.0),     # BASELINE shape family (cfg3 channels)
+    (37, 4, 4096, 1.0, 1.0),      # strong gating, token count not a tile multiple
+    (5, 4, 4097, 0.5, 0.5),       # C not a multiple of 4: scalar paths
+    (3, 8, 256, 0.5, 0.5),
+    (11, 2, 100, 1.0, 1.0),
+    (6, 3, 96, 1.0, 1.0),
+    (4, 1, 64, 1.0, 1.0),
+    (2, 6, 72, 0.5, 0.5),
+    (1, 4, 32, 1.0, 1.0),         # single token
+])
+def test_dynamic_vs_oracle(cuda, B, n, C, alpha, bias):
+    x, params, grad = oracle_case(B, n, C, seed=B * 7 + n * 13 + C, alpha=alpha, bias_std=bias,
+                                  weight="rand")
+    ro, rg = O.dynamic_fwd_bwd(x.double(), {k: v.double() for k, v in params.items()},
+                               grad.double())
+    layer = make_layer(params, n, C, cuda)
+    out, grads = run_layer(layer, x.to(cuda), grad.to(cuda))
+    close(out, ro, what="out")
+    close(grads["x"], rg["x"], what="grad_x")
+    for k in KEYS:
+        close(grads[k], rg[k], what="grad_" + k)
+
+
+def test_dynamic_inference_matches_training_forward(cuda):
+    x, params, _ = oracle_case(16, 4, 512, seed=5, alpha=1.0, bias_std=1.0)
+    layer = make_layer(params, 4, 512, cuda)
+    xd = x.to(cuda)
+    out_train = layer(xd)
+    layer.eval()
+    with torch.no_grad():
+        out_inf = layer(xd)
+    assert torch.equal(out_train.detach(), out_inf)
+
+
+def test_dynamic_backward_is_deterministic(cuda):
+    x, params, grad = oracle_case(512, 4, 1024, seed=9)
+    layer = make_layer(params, 4, 1024, cuda)
+    _, g1 = run_layer(layer, x.to(cuda), grad.to(cuda))
+    layer.zero_grad()
+    _, g2 = run_layer(layer, x.to(cuda), grad.to(cuda))
+    for k in g1:
+        assert torch.equal(g1[k], g2[k]), k
+
+
+def test_dynamic_cfg3_full_size(cuda):
+    """BASELINE cfg3: B=8192, n=4, C=4096.  The CPU oracle runs the whole batch
+    (a few seconds); additionally the parameter gradients are linear in the
+    batch: grads(full) == grads(first half) + grads(second half)."""
+    B, n, C = 8192, 4, 4096
+    x, params, grad = oracle_case(B, n, C, seed=0)
+    layer = make_layer(params, n, C, cuda)
+    xd, gd = x.to(cuda), grad.to(cuda)
+    out, grads = run_layer(layer, xd, gd)
+    ro, rg = O.dynamic_fwd_bwd(x, params, grad)
+    close(out, ro, what="out")
+    close(grads["x"], rg["x"], what="grad_x")
+    for k in KEYS:
+        close(grads[k], rg[k], what="grad_" + k)
+    halves = []
+    for sl in (slice(0, B // 2), slice(B // 2, B)):
+        layer.zero_grad()
+        _, gh = run_layer(layer, xd[sl], gd[sl])
+        halves.append(gh)
+    for k in KEYS:
+        close(halves[0][k] + halves[1][k], grads[k], what="linearity " + k)
+
+
+def test_static_golden(cuda):
+    z = golden("static_B16_n4_C128")
+    layer = mhc.MHCLayer(hidden_dim=128, expansion_rate=4, use_dynamic_h=False).to(cuda)
+    with torch.no_grad():
+        layer.rmsnorm_weight.copy_(z["w"])
+        layer.H_pre.copy_(z["H_pre"])
+        layer.H_post.copy_(z["H_post"])
+        layer.H_res.copy_(z["H_res"])
+    out, grads = run_layer(layer, z["x"].to(cuda))
+    close(out, z["out"], what="out")
+    close(grads["x"], z["grad_x"], what="grad_x")
+    close(grads["rmsnorm_weight"], z["grad_w"], what="grad_w")
+    for k in ("H_pre", "H_post", "H_res"):
+        close(grads[k], z["grad_" + k], what=k)
+
+
+@pytest.mark.parametrize("B,n,C", [(64, 4, 4096), (7, 4, 7168), (3, 8, 100), (5, 2, 4097),
+                                   (2, 4, 20000)])
+def test_static_vs_oracle(cuda, B, n, C):
+    gen = torch.Generator().manual_seed(B + C)
+    x = torch.randn(B, n, C, generator=gen)
+    Hp, Hq, Hr = (torch.randn(n, generator=gen), torch.randn(n, generator=gen),
+                  torch.randn(n, n, generator=gen))
+    w = torch.rand(C, generator=gen) + 0.5
+    grad = torch.randn(B, n, C, generator=gen)
+    ro, rg = O.static_fwd_bwd(x.double(), w.double(), Hp.double(), Hq.double(), Hr.double(),
+                              grad.double())
+    layer = mhc.MHCLayer(hidden_dim=C, expansion_rate=n, use_dynamic_h=False).to(cuda)
+    with torch.no_grad():
+        layer.rmsnorm_weight.copy_(w); layer.H_pre.copy_(Hp)
+        layer.H_post.copy_(Hq); layer.H_res.copy_(Hr)
+    out, grads = run_layer(layer, x.to(cuda), grad.to(cuda))
+    close(out, ro, what="out")
+    close(grads["x"], rg["x"], what="grad_x")
+    for k in ("rmsnorm_weight", "H_pre", "H_post", "H_res"):
+        close(grads[k], rg[k], what=k)
+    layer.eval()
+    with torch.no_grad():
+        close(layer(x.to(cuda)), ro, what="inference out")
+
+
+def test_static_bf16_io(cuda):
+    """bf16 storage, fp32 arithmetic: compare with the oracle on the same
+    bf16-rounded input; the only extra error is the bf16 rounding of the output
+    (relative 2^-9), so the stated tolerance is rtol 8e-3 / atol 1e-2."""
+    B, n, C = 256, 4, 4096
+    gen = torch.Generator().manual_seed(4)
+    x = torch.randn(B, n, C, generator=gen).bfloat16()
+    Hp, Hq, Hr = torch.randn(n, generator=gen), torch.randn(n, generator=gen), torch.randn(n, n, generator=gen)
+    layer = mhc.MHCLayer(hidden_dim=C, expansion_rate=n, use_dynamic_h=False, bf16_io=True).to(cuda)
+    with torch.no_grad():
+        layer.H_pre.copy_(Hp); layer.H_post.copy_(Hq); layer.H_res.copy_(Hr)
+    layer.eval()
+    with torch.no_grad():
+        out = layer(x.to(cuda))
+    assert out.dtype == torch.bfloat16
+    ro = O.mhc_layer_static(x.double(), torch.ones(C, dtype=torch.float64), Hp.double(),
+                            Hq.double(), Hr.double())
+    close(out.float(), ro, rtol=8e-3, atol=1e-2, what="bf16 out")
+
+
+def test_residual_wrapper(cuda):
+    B, T, C, n = 2, 5, 64, 4
+    gen = torch.Generator().manual_seed(3)
+    r, b = torch.randn(B, T, C, generator=gen), torch.randn(B, T, C, generator=gen)
+    w = mhc.replace_residual_with_mhc(hidden_dim=C, expansion_rate=n).to(cuda)
+    out = w(r.to(cuda), b.to(cuda))
+    streams, _ = O.residual_wrapper_pack(r.double(), b.double(), n)
+    params = {k: p.detach().cpu().double() for k, p in w.mhc.named_parameters()}
+    ref = O.mhc_layer_dynamic(streams, *[params[k] for k in O.DYNAMIC_PARAM_ORDER]).mean(dim=1)
+    close(out, ref.reshape(B, T, C), what="wrapper out")
+    out.sum().backward()
+    assert w.mhc.phi_res.grad is not None and torch.isfinite(w.mhc.phi_res.grad).all()
