@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(128)
   }
 #pragma unroll
   for (int e = 0; e < N * N; ++e) m[e] = expf((ar * p[2 * N + e]) * inv_h + b_res[e]);
-  sk_forward<N>(m, iters, s_eps);
+  sk_forward<N, float>(m, iters, s_eps);
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < N; ++i)
@@ -512,7 +512,7 @@ __global__ void static_prep_kernel(const float* __restrict__ H_pre,
   float m[N * N];
 #pragma unroll
   for (int e = 0; e < N * N; ++e) m[e] = expf(H_res[e]);
-  sk_forward<N>(m, iters, s_eps);
+  sk_forward<N, float>(m, iters, s_eps);
   for (int e = 0; e < Lc::REC; ++e) rec[e] = 0.f;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
@@ -528,18 +528,20 @@ __global__ void static_prep_kernel(const float* __restrict__ H_pre,
 //   One CTA (128 threads) per token, float4 over channel quads when VEC.
 // ---------------------------------------------------------------------------
 template <int V>
-__device__ __forceinline__ void block_reduce_to_global(float (&acc)[V], float* smem,
-                                                       float* __restrict__ dst) {
+__device__ __forceinline__ void block_reduce_to_global(double (&acc)[V], double* smem,
+                                                       double* __restrict__ dst) {
   // smem: [nwarps][V]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
   for (int v = 0; v < V; ++v) {
-    const float s = warp_sum(acc[v]);
+    double s = acc[v];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if (lane == 0) smem[warp * V + v] = s;
   }
   __syncthreads();
   for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    float s = 0.f;
+    double s = 0.0;
     for (int w = 0; w < nw; ++w) s += smem[w * V + v];
     dst[v] = s;
   }
@@ -549,32 +551,40 @@ __device__ __forceinline__ void block_reduce_to_global(float (&acc)[V], float* s
 template <int N, bool VEC>
 __global__ void __launch_bounds__(128)
     bwd_stats_kernel(const float* __restrict__ g, const float* __restrict__ x,
-                     const float* __restrict__ w, float* __restrict__ stats, int64_t B,
+                     const float* __restrict__ w, double* __restrict__ stats, int64_t B,
                      int64_t C) {
+  // Moments are accumulated in fp64: products of fp32 inputs are exact in
+  // fp64, and the closed-form backward subtracts nearly equal moments (the
+  // RMSNorm backward removes the radial component), which amplifies fp32
+  // accumulation error by ~ the ratio |A_i| / |gh_i| (hundreds at cfg3).
   using Lc = L<N>;
-  constexpr int NS1 = Lc::NS1, NG = Lc::NG;
-  __shared__ float red[4 * NS1];
+  constexpr int NS1 = Lc::NS1;
+  __shared__ double red[4 * NS1];
   for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
-    float acc[NS1];
+    double acc[NS1];
 #pragma unroll
-    for (int v = 0; v < NS1; ++v) acc[v] = 0.f;
+    for (int v = 0; v < NS1; ++v) acc[v] = 0.0;
     const float* gb = g + b * N * C;
     const float* xb = x + b * N * C;
-    auto accum = [&](const float (&gv)[N], const float (&xv)[N], float wv) {
+    auto accum = [&](const float (&gf)[N], const float (&xf)[N], float wf) {
+      double gv[N], xv[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) { gv[i] = gf[i]; xv[i] = xf[i]; }
+      const double wv = wf;
 #pragma unroll
       for (int i = 0; i < N; ++i) {
-        const float gw = gv[i] * wv;
+        const double gw = gv[i] * wv;
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-          acc[i * N + j] = fmaf(gv[i], xv[j], acc[i * N + j]);
-          acc[N * N + i * N + j] = fmaf(gw, xv[j], acc[N * N + i * N + j]);
+          acc[i * N + j] = fma(gv[i], xv[j], acc[i * N + j]);
+          acc[N * N + i * N + j] = fma(gw, xv[j], acc[N * N + i * N + j]);
         }
       }
       int e = 2 * N * N;
 #pragma unroll
       for (int i = 0; i < N; ++i)
 #pragma unroll
-        for (int j = i; j < N; ++j) { acc[e] = fmaf(xv[i], xv[j], acc[e]); ++e; }
+        for (int j = i; j < N; ++j) { acc[e] = fma(xv[i], xv[j], acc[e]); ++e; }
     };
     if (VEC) {
       for (int64_t q = threadIdx.x; q < C / 4; q += blockDim.x) {
@@ -612,131 +622,129 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---------------------------------------------------------------------------
-// Backward 2 (dynamic): per-token closed-form scalars, one thread per token.
-//   With W = g diag(w) x^T, G = x x^T, gM = g x^T (sums over c):
+// Backward 2 (dynamic): per-token closed-form scalars, one thread per token,
+// in fp64.  With W = g diag(w) x^T, G = x x^T, gM = g x^T (sums over c):
 //     ghp_i = (W h)_i / r                     (= sum_c g_i y)
 //     dot   = hp^T W h                        (= sum_c gy w x_agg)
 //     A_i   = (W^T hp)_i                      (= sum_c gy w x_i)
 //     Q_i   = (G h)_i                         (= sum_c x_agg x_i)
 //     beta  = dot / (C r^3);  gh_i = A_i / r - beta Q_i   (= sum_c gx_agg x_i)
-//   then the gate derivatives, Sinkhorn reverse on gM, and the projection
+//   then the gate derivatives, the Sinkhorn reverse on gM, and the projection
 //   backward: d_p = dt alpha / rms_h, coef = -(sum dt alpha p) / (rms_h^3 nC).
 // ---------------------------------------------------------------------------
 template <int N>
 __global__ void __launch_bounds__(128)
-    token_bwd_kernel(const float* __restrict__ stats, const float* __restrict__ rec,
+    token_bwd_kernel(const double* __restrict__ stats, const float* __restrict__ rec,
                      const float* __restrict__ a_pre, const float* __restrict__ a_post,
                      const float* __restrict__ a_res, const float* __restrict__ b_res,
-                     float* __restrict__ tokb, float* __restrict__ tokr, int64_t B, int64_t C,
+                     float* __restrict__ tokb, double* __restrict__ tokr, int64_t B, int64_t C,
                      int iters, float s_eps) {
   using Lc = L<N>;
   constexpr int NH = Lc::NH, NS1 = Lc::NS1;
   const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
-  const float* st = stats + b * NS1;
+  const double* st = stats + b * NS1;
   const float* rc = rec + b * Lc::REC;
-  const float rms_h = rc[0], r = rc[1];
-  const float inv_h = 1.f / rms_h, inv_r = 1.f / r;
-  float h[N], hp[N];
+  const double rms_h = rc[0], r = rc[1];
+  const double inv_h = 1.0 / rms_h, inv_r = 1.0 / r;
+  double h[N], hp[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) { h[i] = rc[Lc::OFF_H + i]; hp[i] = rc[Lc::OFF_HP + i]; }
-  float dt[NH];
-  float dot = 0.f;
+  double dt[NH];
+  double dot = 0.0;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    float wh = 0.f;
+    double wh = 0.0;
 #pragma unroll
-    for (int j = 0; j < N; ++j) wh = fmaf(st[N * N + i * N + j], h[j], wh);
-    dot = fmaf(hp[i], wh, dot);
-    const float ghp = wh * inv_r;
-    dt[N + i] = ghp * hp[i] * (1.f - 0.5f * hp[i]);
+    for (int j = 0; j < N; ++j) wh = fma(st[N * N + i * N + j], h[j], wh);
+    dot = fma(hp[i], wh, dot);
+    dt[N + i] = wh * inv_r * hp[i] * (1.0 - 0.5 * hp[i]);
   }
-  const float beta = dot / ((float)C * r * r * r);
+  const double beta = dot / ((double)C * r * r * r);
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    float A = 0.f, Q = 0.f;
+    double A = 0.0, Q = 0.0;
 #pragma unroll
-    for (int k = 0; k < N; ++k) A = fmaf(hp[k], st[N * N + k * N + i], A);
+    for (int k = 0; k < N; ++k) A = fma(hp[k], st[N * N + k * N + i], A);
 #pragma unroll
-    for (int j = 0; j < N; ++j) Q = fmaf(st[2 * N * N + gram_index(i, j, N)], h[j], Q);
-    const float gh = A * inv_r - beta * Q;
-    dt[i] = gh * h[i] * (1.f - h[i]);
+    for (int j = 0; j < N; ++j) Q = fma(st[2 * N * N + gram_index(i, j, N)], h[j], Q);
+    dt[i] = (A * inv_r - beta * Q) * h[i] * (1.0 - h[i]);
   }
-  const float ap = *a_pre, aq = *a_post, ar = *a_res;
-  float e0[N * N], gm[N * N];
+  const double ap = *a_pre, aq = *a_post, ar = *a_res;
+  double e0[N * N], gm[N * N];
 #pragma unroll
   for (int e = 0; e < N * N; ++e) {
-    e0[e] = expf((ar * rc[Lc::OFF_P + 2 * N + e]) * inv_h + b_res[e]);
+    e0[e] = exp((ar * (double)rc[Lc::OFF_P + 2 * N + e]) * inv_h + (double)b_res[e]);
     gm[e] = st[e];
   }
-  sk_backward<N>(e0, gm, iters, s_eps);
+  sk_backward<N, double>(e0, gm, iters, (double)s_eps);
 #pragma unroll
   for (int e = 0; e < N * N; ++e) dt[2 * N + e] = gm[e] * e0[e];
   float* tb = tokb + b * Lc::TB;
-  float* tr = tokr + b * Lc::NR;
-  float s = 0.f, da0 = 0.f, da1 = 0.f, da2 = 0.f;
+  double* tr = tokr + b * Lc::NR;
+  double s = 0.0, da0 = 0.0, da1 = 0.0, da2 = 0.0;
 #pragma unroll
   for (int k = 0; k < NH; ++k) {
-    const float a = k < N ? ap : (k < 2 * N ? aq : ar);
-    const float pk = rc[Lc::OFF_P + k];
-    tb[4 + k] = dt[k] * a * inv_h;
-    s = fmaf(dt[k] * a, pk, s);
-    const float dak = dt[k] * pk * inv_h;
+    const double a = k < N ? ap : (k < 2 * N ? aq : ar);
+    const double pk = rc[Lc::OFF_P + k];
+    tb[4 + k] = (float)(dt[k] * a * inv_h);
+    s = fma(dt[k] * a, pk, s);
+    const double dak = dt[k] * pk * inv_h;
     if (k < N) da0 += dak; else if (k < 2 * N) da1 += dak; else da2 += dak;
     tr[k] = dt[k];
   }
 #pragma unroll
   for (int k = NH; k < Lc::NHP; ++k) tb[4 + k] = 0.f;
-  tb[0] = beta;
-  tb[1] = inv_r;
-  tb[2] = -s * inv_h * inv_h * inv_h / (float)(N * C);
+  tb[0] = (float)beta;
+  tb[1] = (float)inv_r;
+  tb[2] = (float)(-s * inv_h * inv_h * inv_h / (double)(N * C));
   tb[3] = 0.f;
   tr[NH + 0] = da0;
   tr[NH + 1] = da1;
   tr[NH + 2] = da2;
 }
 
-// Static-H per-token scalars: beta, inv_r for grad_x, and per-token gate
-// gradients (dt_pre, dt_post) and gM for the reductions over the batch.
+// Static-H per-token scalars (fp64): beta, inv_r for grad_x, and per-token
+// gate gradients (dt_pre, dt_post) and gM for the reductions over the batch.
 template <int N>
 __global__ void __launch_bounds__(128)
-    token_bwd_static_kernel(const float* __restrict__ stats, const float* __restrict__ rec,
+    token_bwd_static_kernel(const double* __restrict__ stats, const float* __restrict__ rec,
                             const float* __restrict__ rms, float* __restrict__ tokb,
-                            float* __restrict__ tokr, int64_t B, int64_t C) {
+                            double* __restrict__ tokr, int64_t B, int64_t C) {
   using Lc = L<N>;
   constexpr int NS1 = Lc::NS1;
   const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
-  const float* st = stats + b * NS1;
-  const float r = rms[b], inv_r = 1.f / r;
-  float h[N], hp[N];
+  const double* st = stats + b * NS1;
+  const double r = rms[b], inv_r = 1.0 / r;
+  double h[N], hp[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) { h[i] = rec[Lc::OFF_H + i]; hp[i] = rec[Lc::OFF_HP + i]; }
-  float* tr = tokr + b * Lc::NRS;
-  float dot = 0.f;
+  double* tr = tokr + b * Lc::NRS;
+  double dot = 0.0;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    float wh = 0.f;
+    double wh = 0.0;
 #pragma unroll
-    for (int j = 0; j < N; ++j) wh = fmaf(st[N * N + i * N + j], h[j], wh);
-    dot = fmaf(hp[i], wh, dot);
-    tr[N + i] = wh * inv_r * hp[i] * (1.f - 0.5f * hp[i]);
+    for (int j = 0; j < N; ++j) wh = fma(st[N * N + i * N + j], h[j], wh);
+    dot = fma(hp[i], wh, dot);
+    tr[N + i] = wh * inv_r * hp[i] * (1.0 - 0.5 * hp[i]);
   }
-  const float beta = dot / ((float)C * r * r * r);
+  const double beta = dot / ((double)C * r * r * r);
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    float A = 0.f, Q = 0.f;
+    double A = 0.0, Q = 0.0;
 #pragma unroll
-    for (int k = 0; k < N; ++k) A = fmaf(hp[k], st[N * N + k * N + i], A);
+    for (int k = 0; k < N; ++k) A = fma(hp[k], st[N * N + k * N + i], A);
 #pragma unroll
-    for (int j = 0; j < N; ++j) Q = fmaf(st[2 * N * N + gram_index(i, j, N)], h[j], Q);
-    tr[i] = (A * inv_r - beta * Q) * h[i] * (1.f - h[i]);
+    for (int j = 0; j < N; ++j) Q = fma(st[2 * N * N + gram_index(i, j, N)], h[j], Q);
+    tr[i] = (A * inv_r - beta * Q) * h[i] * (1.0 - h[i]);
   }
 #pragma unroll
   for (int e = 0; e < N * N; ++e) tr[2 * N + e] = st[e];
   float* tb = tokb + b * 4;
-  tb[0] = beta;
-  tb[1] = inv_r;
+  tb[0] = (float)beta;
+  tb[1] = (float)inv_r;
   tb[2] = 0.f;
   tb[3] = 0.f;
 }
@@ -883,20 +891,21 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// One CTA per column v of a [B, stride] table: total[v] = sum_b tab[b, v]
+// One CTA per column v of a [B, stride] fp64 table: total[v] = sum_b tab[b, v]
 // (fixed order: thread-strided partials, then a fixed tree).
 __global__ void __launch_bounds__(256)
-    reduce_tokens_kernel(const float* __restrict__ tab, int64_t B, int stride,
-                         float* __restrict__ out) {
-  __shared__ float red[8];
+    reduce_tokens_kernel(const double* __restrict__ tab, int64_t B, int stride,
+                         double* __restrict__ out) {
+  __shared__ double red[8];
   const int v = blockIdx.x;
-  float s = 0.f;
+  double s = 0.0;
   for (int64_t b = threadIdx.x; b < B; b += blockDim.x) s += tab[b * stride + v];
-  s = warp_sum(s);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
   __syncthreads();
   if (threadIdx.x == 0) {
-    float t = 0.f;
+    double t = 0.0;
     for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += red[k];
     out[v] = t;
   }
@@ -904,32 +913,33 @@ __global__ void __launch_bounds__(256)
 
 // Scatter the token-reduced dynamic parameter gradients: tot = [dt(NH), dalpha(3)]
 template <int N>
-__global__ void scatter_dyn_param_grads_kernel(const float* __restrict__ tot,
+__global__ void scatter_dyn_param_grads_kernel(const double* __restrict__ tot,
                                                float* __restrict__ gbp, float* __restrict__ gbq,
                                                float* __restrict__ gbr, float* __restrict__ gap,
                                                float* __restrict__ gaq, float* __restrict__ gar) {
   constexpr int NH = L<N>::NH;
   const int k = threadIdx.x;
-  if (k < N) gbp[k] = tot[k];
-  else if (k < 2 * N) gbq[k - N] = tot[k];
-  else if (k < NH) gbr[k - 2 * N] = tot[k];
-  if (k == 0) { *gap = tot[NH]; *gaq = tot[NH + 1]; *gar = tot[NH + 2]; }
+  if (k < N) gbp[k] = (float)tot[k];
+  else if (k < 2 * N) gbq[k - N] = (float)tot[k];
+  else if (k < NH) gbr[k - 2 * N] = (float)tot[k];
+  if (k == 0) { *gap = (float)tot[NH]; *gaq = (float)tot[NH + 1]; *gar = (float)tot[NH + 2]; }
 }
 
-// Static-H parameter gradients from the token totals [dt_pre, dt_post, gM].
+// Static-H parameter gradients from the token totals [dt_pre, dt_post, gM]:
+// the Sinkhorn reverse runs once on the batch-summed gM (M is shared).
 template <int N>
-__global__ void static_param_grads_kernel(const float* __restrict__ tot,
+__global__ void static_param_grads_kernel(const double* __restrict__ tot,
                                           const float* __restrict__ H_res,
                                           float* __restrict__ gHp, float* __restrict__ gHq,
                                           float* __restrict__ gHr, int iters, float s_eps) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  for (int i = 0; i < N; ++i) { gHp[i] = tot[i]; gHq[i] = tot[N + i]; }
-  float e0[N * N], gm[N * N];
+  for (int i = 0; i < N; ++i) { gHp[i] = (float)tot[i]; gHq[i] = (float)tot[N + i]; }
+  double e0[N * N], gm[N * N];
 #pragma unroll
-  for (int e = 0; e < N * N; ++e) { e0[e] = expf(H_res[e]); gm[e] = tot[2 * N + e]; }
-  sk_backward<N>(e0, gm, iters, s_eps);
+  for (int e = 0; e < N * N; ++e) { e0[e] = exp((double)H_res[e]); gm[e] = tot[2 * N + e]; }
+  sk_backward<N, double>(e0, gm, iters, (double)s_eps);
 #pragma unroll
-  for (int e = 0; e < N * N; ++e) gHr[e] = gm[e] * e0[e];
+  for (int e = 0; e < N * N; ++e) gHr[e] = (float)(gm[e] * e0[e]);
 }
 
 // ---------------------------------------------------------------------------
@@ -1007,12 +1017,12 @@ BwdPlan plan_bwd(int64_t B, int64_t C) {
   BwdPlan p;
   p.ntiles = (int)((C + GX_CW - 1) / GX_CW);
   p.nsplit = choose_gx_splits(p.ntiles, B, num_sms(), N <= 4 ? 2 : 1);
-  p.stats = (size_t)B * L<N>::NS1;
+  p.stats = (size_t)B * L<N>::NS1 * 2;  // fp64
   p.tokb = (size_t)B * (DYN ? L<N>::TB : 4);
-  p.tokr = (size_t)B * (DYN ? L<N>::NR : L<N>::NRS);
+  p.tokr = (size_t)B * (DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
   p.dphi = DYN ? (size_t)p.nsplit * L<N>::NH * N * C : 0;
   p.gw = (size_t)p.nsplit * C;
-  p.tot = (size_t)(DYN ? L<N>::NR : L<N>::NRS);
+  p.tot = (size_t)(DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
   return p;
 }
 
@@ -1096,12 +1106,12 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
               "mhc_layer_bwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
   BwdPlan p = plan_bwd<N, true>(B, C);
   Carve cv(ws);
-  float* stats = cv.take(p.stats);
+  double* stats = (double*)cv.take(p.stats);
   float* tokb = cv.take(p.tokb);
-  float* tokr = cv.take(p.tokr);
+  double* tokr = (double*)cv.take(p.tokr);
   float* dphi = cv.take(p.dphi);
   float* gwp = cv.take(p.gw);
-  float* tot = cv.take(p.tot);
+  double* tot = (double*)cv.take(p.tot);
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(w);
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
   if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
@@ -1157,12 +1167,12 @@ int run_bwd_static(const float* g, const float* x, const float* w, const float* 
               "mhc_layer_bwd_static: workspace of %zu bytes required, got %zu", need, ws_bytes);
   BwdPlan p = plan_bwd<N, false>(B, C);
   Carve cv(ws);
-  float* stats = cv.take(p.stats);
+  double* stats = (double*)cv.take(p.stats);
   float* tokb = cv.take(p.tokb);
-  float* tokr = cv.take(p.tokr);
+  double* tokr = (double*)cv.take(p.tokr);
   cv.take(p.dphi);
   float* gwp = cv.take(p.gw);
-  float* tot = cv.take(p.tot);
+  double* tot = (double*)cv.take(p.tot);
   float* rec = cv.take(L<N>::REC);
   { ProfScope _ps("static_prep", s); static_prep_kernel<N><<<1, 32, 0, s>>>(Hp, Hq, Hr, rec, iters, s_eps); }
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(w);

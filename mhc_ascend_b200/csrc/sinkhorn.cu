@@ -23,7 +23,7 @@ __global__ void __launch_bounds__(128) sk_fwd_thread_kernel(const float* __restr
   const float* src = inp + b * (N * N);
 #pragma unroll
   for (int e = 0; e < N * N; ++e) a[e] = src[e];
-  sk_forward<N>(a, iters, eps);
+  sk_forward<N, float>(a, iters, eps);
   float* dst = out + b * (N * N);
 #pragma unroll
   for (int e = 0; e < N * N; ++e) dst[e] = a[e];
@@ -44,7 +44,12 @@ __global__ void __launch_bounds__(128) sk_bwd_thread_kernel(const float* __restr
     x0[e] = src[e];
     g[e] = gsrc[e];
   }
-  sk_backward<N>(x0, g, iters, eps);
+  double xd[N * N], gd[N * N];
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) { xd[e] = x0[e]; gd[e] = g[e]; }
+  sk_backward<N, double>(xd, gd, iters, (double)eps);
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) g[e] = (float)gd[e];
   float* dst = grad_inp + b * (N * N);
 #pragma unroll
   for (int e = 0; e < N * N; ++e) dst[e] = g[e];
@@ -85,17 +90,44 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32)
     for (int i = 0; i < n; ++i) dst[i * n + lane] = a[i];
 }
 
-__global__ void __launch_bounds__(WARPS_PER_BLOCK * 32)
+// Reverse mode runs in fp64 (the doubly-stochastic projection cancels the
+// row/column-constant part of the incoming gradient).
+constexpr int BWD_WARPS = 2;
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void warp_sk_step_d(double (&a)[32], int n, int lane, double eps,
+                                               double* dr, double* dc) {
+  const bool active = lane < n;
+  for (int i = 0; i < n; ++i) {
+    const double d = warp_sum_d(active ? a[i] : 0.0) + eps;
+    if (dr && lane == 0) dr[i] = d;
+    if (active) a[i] = a[i] / d;
+  }
+  double s = 0.0;
+  for (int i = 0; i < n; ++i) s += a[i];
+  const double d = s + eps;
+  if (dc && active) dc[lane] = d;
+  if (active)
+    for (int i = 0; i < n; ++i) a[i] = a[i] / d;
+}
+
+__global__ void __launch_bounds__(BWD_WARPS * 32)
     sk_bwd_warp_kernel(const float* __restrict__ grad_out, const float* __restrict__ inp,
                        float* __restrict__ grad_inp, int64_t batch, int n, int iters,
-                       float eps) {
-  __shared__ float s_dr[WARPS_PER_BLOCK][SK_SEG][32];
-  __shared__ float s_dc[WARPS_PER_BLOCK][SK_SEG][32];
+                       float eps_f) {
+  __shared__ double s_dr[BWD_WARPS][SK_SEG][32];
+  __shared__ double s_dc[BWD_WARPS][SK_SEG][32];
+  const double eps = eps_f;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int64_t b = (int64_t)blockIdx.x * WARPS_PER_BLOCK + w;
+  const int64_t b = (int64_t)blockIdx.x * BWD_WARPS + w;
   if (b >= batch) return;
   const bool active = lane < n;
-  float g[32], z[32];
+  double g[32], z[32];
   const float* src = inp + b * n * n;
   const float* gsrc = grad_out + b * n * n;
   for (int i = 0; i < n; ++i) g[i] = active ? gsrc[i * n + lane] : 0.f;
@@ -103,24 +135,24 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32)
   while (seg_end > 0) {
     const int seg_start = seg_end > SK_SEG ? seg_end - SK_SEG : 0;
     for (int i = 0; i < n; ++i) z[i] = active ? src[i * n + lane] : 0.f;
-    for (int t = 0; t < seg_start; ++t) warp_sk_step(z, n, lane, eps, nullptr, nullptr);
+    for (int t = 0; t < seg_start; ++t) warp_sk_step_d(z, n, lane, eps, nullptr, nullptr);
     for (int t = seg_start; t < seg_end; ++t)
-      warp_sk_step(z, n, lane, eps, s_dr[w][t - seg_start], s_dc[w][t - seg_start]);
+      warp_sk_step_d(z, n, lane, eps, s_dr[w][t - seg_start], s_dc[w][t - seg_start]);
     __syncwarp();
     for (int t = seg_end - 1; t >= seg_start; --t) {
       // column step
-      const float dcj = active ? s_dc[w][t - seg_start][lane] : 1.f;
-      float s = 0.f;
+      const double dcj = active ? s_dc[w][t - seg_start][lane] : 1.0;
+      double s = 0.0;
       for (int i = 0; i < n; ++i) s += g[i] * z[i];
       for (int i = 0; i < n; ++i) {
-        g[i] = active ? (g[i] - s) / dcj : 0.f;
+        g[i] = active ? (g[i] - s) / dcj : 0.0;
         z[i] = z[i] * dcj;
       }
       // row step
       for (int i = 0; i < n; ++i) {
-        const float d = s_dr[w][t - seg_start][i];
-        const float si = warp_sum(active ? g[i] * z[i] : 0.f);
-        g[i] = active ? (g[i] - si) / d : 0.f;
+        const double d = s_dr[w][t - seg_start][i];
+        const double si = warp_sum_d(active ? g[i] * z[i] : 0.0);
+        g[i] = active ? (g[i] - si) / d : 0.0;
         z[i] = z[i] * d;
       }
     }
@@ -129,7 +161,7 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32)
   }
   float* dst = grad_inp + b * n * n;
   if (active)
-    for (int i = 0; i < n; ++i) dst[i * n + lane] = g[i];
+    for (int i = 0; i < n; ++i) dst[i * n + lane] = (float)g[i];
 }
 
 template <int N>
@@ -211,8 +243,8 @@ extern "C" int mhc_sinkhorn_knopp_bwd(const float* grad_out, const float* inp, c
     case 7: return launch_thread_bwd<7>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
     case 8: return launch_thread_bwd<8>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
     default: {
-      const int64_t blocks = (batch + WARPS_PER_BLOCK - 1) / WARPS_PER_BLOCK;
-      sk_bwd_warp_kernel<<<(unsigned)blocks, WARPS_PER_BLOCK * 32, 0, s>>>(
+      const int64_t blocks = (batch + BWD_WARPS - 1) / BWD_WARPS;
+      sk_bwd_warp_kernel<<<(unsigned)blocks, BWD_WARPS * 32, 0, s>>>(
           grad_out, inp, grad_inp, batch, n, num_iters, eps);
       return check_launch("sinkhorn_knopp_bwd");
     }

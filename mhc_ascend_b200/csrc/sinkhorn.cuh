@@ -23,75 +23,92 @@ namespace mhc {
 
 constexpr int SK_SEG = 32;
 
-template <int N>
-__device__ __forceinline__ void sk_step(float (&a)[N * N], float eps, float* dr, float* dc) {
+// One iteration (row step, then column step).  T = float divides like the
+// reference formulation (A / (sum + eps)); T = double (backward replays)
+// multiplies by the reciprocal.  dr/dc (optional) receive the denominators.
+template <int N, typename T>
+__device__ __forceinline__ void sk_step(T (&a)[N * N], T eps, T* dr, T* dc) {
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    float s = 0.f;
+    T s = 0;
 #pragma unroll
     for (int j = 0; j < N; ++j) s += a[i * N + j];
-    const float d = s + eps;
+    const T d = s + eps;
     if (dr) dr[i] = d;
+    if (sizeof(T) == 8) {
+      const T inv = T(1) / d;
 #pragma unroll
-    for (int j = 0; j < N; ++j) a[i * N + j] = a[i * N + j] / d;
+      for (int j = 0; j < N; ++j) a[i * N + j] *= inv;
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j) a[i * N + j] = a[i * N + j] / d;
+    }
   }
 #pragma unroll
   for (int j = 0; j < N; ++j) {
-    float s = 0.f;
+    T s = 0;
 #pragma unroll
     for (int i = 0; i < N; ++i) s += a[i * N + j];
-    const float d = s + eps;
+    const T d = s + eps;
     if (dc) dc[j] = d;
+    if (sizeof(T) == 8) {
+      const T inv = T(1) / d;
 #pragma unroll
-    for (int i = 0; i < N; ++i) a[i * N + j] = a[i * N + j] / d;
+      for (int i = 0; i < N; ++i) a[i * N + j] *= inv;
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) a[i * N + j] = a[i * N + j] / d;
+    }
   }
 }
 
-template <int N>
-__device__ __forceinline__ void sk_forward(float (&a)[N * N], int iters, float eps) {
-  for (int t = 0; t < iters; ++t) sk_step<N>(a, eps, nullptr, nullptr);
+template <int N, typename T>
+__device__ __forceinline__ void sk_forward(T (&a)[N * N], int iters, T eps) {
+  for (int t = 0; t < iters; ++t) sk_step<N, T>(a, eps, nullptr, nullptr);
 }
 
 // g: on entry dL/d(output), on exit dL/d(input).  x0 is the forward input.
-template <int N>
-__device__ __forceinline__ void sk_backward(const float (&x0)[N * N], float (&g)[N * N],
-                                            int iters, float eps) {
-  float dr[SK_SEG * N], dc[SK_SEG * N];
+template <int N, typename T>
+__device__ __forceinline__ void sk_backward(const T (&x0)[N * N], T (&g)[N * N], int iters,
+                                            T eps) {
+  T dr[SK_SEG * N], dc[SK_SEG * N];
   int seg_end = iters;
   while (seg_end > 0) {
     const int seg_start = seg_end > SK_SEG ? seg_end - SK_SEG : 0;
-    float z[N * N];
+    T z[N * N];
 #pragma unroll
     for (int e = 0; e < N * N; ++e) z[e] = x0[e];
-    for (int t = 0; t < seg_start; ++t) sk_step<N>(z, eps, nullptr, nullptr);
+    for (int t = 0; t < seg_start; ++t) sk_step<N, T>(z, eps, nullptr, nullptr);
     for (int t = seg_start; t < seg_end; ++t)
-      sk_step<N>(z, eps, dr + (t - seg_start) * N, dc + (t - seg_start) * N);
+      sk_step<N, T>(z, eps, dr + (t - seg_start) * N, dc + (t - seg_start) * N);
     for (int t = seg_end - 1; t >= seg_start; --t) {
-      const float* drt = dr + (t - seg_start) * N;
-      const float* dct = dc + (t - seg_start) * N;
+      const T* drt = dr + (t - seg_start) * N;
+      const T* dct = dc + (t - seg_start) * N;
       // column step: Z = Y / dc
 #pragma unroll
       for (int j = 0; j < N; ++j) {
-        const float d = dct[j];
-        float s = 0.f;
+        const T d = dct[j];
+        const T inv = T(1) / d;
+        T s = 0;
 #pragma unroll
         for (int i = 0; i < N; ++i) s += g[i * N + j] * z[i * N + j];
 #pragma unroll
         for (int i = 0; i < N; ++i) {
-          g[i * N + j] = (g[i * N + j] - s) / d;
+          g[i * N + j] = (g[i * N + j] - s) * inv;
           z[i * N + j] = z[i * N + j] * d;  // now Y_t
         }
       }
       // row step: Y = X / dr
 #pragma unroll
       for (int i = 0; i < N; ++i) {
-        const float d = drt[i];
-        float s = 0.f;
+        const T d = drt[i];
+        const T inv = T(1) / d;
+        T s = 0;
 #pragma unroll
         for (int j = 0; j < N; ++j) s += g[i * N + j] * z[i * N + j];
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-          g[i * N + j] = (g[i * N + j] - s) / d;
+          g[i * N + j] = (g[i * N + j] - s) * inv;
           z[i * N + j] = z[i * N + j] * d;  // now Z_{t-1}
         }
       }

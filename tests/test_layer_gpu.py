@@ -6,7 +6,7 @@ import torch
 
 import mhc_ascend_b200 as mhc
 from oracle import mhc_oracle as O
-from tests.helpers import close, golden, rel_err
+from tests.helpers import close, close_ref, golden, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -44,10 +44,12 @@ def test_dynamic_golden(cuda, case):
     layer = make_layer({k: z[v] for k, v in KEYS.items()}, n, C, cuda)
     g = z["grad_out"].to(cuda) if "grad_out" in z else None
     out, grads = run_layer(layer, z["x"].to(cuda), g)
-    close(out, z["out"], what="out")
-    close(grads["x"], z["grad_x"], what="grad_x")
+    ro, rg = O.dynamic_fwd_bwd(z["x"].double(), {k: z[v].double() for k, v in KEYS.items()},
+                               z["grad_out"].double() if "grad_out" in z else None)
+    close_ref(out, z["out"], ro, what="out")
+    close_ref(grads["x"], z["grad_x"], rg["x"], what="grad_x")
     for k, v in KEYS.items():
-        close(grads[k], z["grad_" + v], what="grad_" + k)
+        close_ref(grads[k], z["grad_" + v], rg[k], what="grad_" + k)
 
 
 def oracle_case(B, n, C, seed, alpha=0.01, bias_std=0.0, weight=None):
@@ -135,11 +137,13 @@ def test_static_golden(cuda):
         layer.H_post.copy_(z["H_post"])
         layer.H_res.copy_(z["H_res"])
     out, grads = run_layer(layer, z["x"].to(cuda))
-    close(out, z["out"], what="out")
-    close(grads["x"], z["grad_x"], what="grad_x")
-    close(grads["rmsnorm_weight"], z["grad_w"], what="grad_w")
+    ro, rg = O.static_fwd_bwd(z["x"].double(), z["w"].double(), z["H_pre"].double(),
+                              z["H_post"].double(), z["H_res"].double())
+    close_ref(out, z["out"], ro, what="out")
+    close_ref(grads["x"], z["grad_x"], rg["x"], what="grad_x")
+    close_ref(grads["rmsnorm_weight"], z["grad_w"], rg["rmsnorm_weight"], what="grad_w")
     for k in ("H_pre", "H_post", "H_res"):
-        close(grads[k], z["grad_" + k], what=k)
+        close_ref(grads[k], z["grad_" + k], rg[k], what=k)
 
 
 @pytest.mark.parametrize("B,n,C", [(64, 4, 4096), (7, 4, 7168), (3, 8, 100), (5, 2, 4097),

@@ -6,7 +6,7 @@ import torch
 import mhc_ascend_b200 as mhc
 from mhc_ascend_b200 import ops
 from oracle import mhc_oracle as O
-from tests.helpers import close, golden
+from tests.helpers import close, close_ref, golden
 
 pytestmark = pytest.mark.gpu
 
@@ -23,8 +23,11 @@ def _grad_of(fn, inputs, grad, dev):
 def test_sinkhorn_golden(cuda, case):
     z = golden(case)
     out, (g,) = _grad_of(lambda a: mhc.sinkhorn_knopp(a, 20, 1e-8), [z["inp"]], z["grad"], cuda)
-    close(out, z["out"], what="sinkhorn out")
-    close(g, z["grad_inp"], what="sinkhorn grad")
+    ref = z["inp"].double().requires_grad_(True)
+    ro = O.sinkhorn_knopp(ref, 20, 1e-8)
+    ro.backward(z["grad"].double())
+    close_ref(out, z["out"], ro, what="sinkhorn out")
+    close_ref(g, z["grad_inp"], ref.grad, what="sinkhorn grad")
 
 
 @pytest.mark.parametrize("B,N,iters", [(65536, 4, 20), (1, 4, 20), (7, 3, 50), (5, 32, 20),
@@ -51,9 +54,12 @@ def test_sinkhorn_doubly_stochastic_full_size(cuda):
 def test_rmsnorm_golden(cuda):
     z = golden("rmsnorm_B16_C4096")
     out, (gx, gw) = _grad_of(lambda a, w: mhc.rmsnorm(a, w, 1e-5), [z["x"], z["w"]], z["grad"], cuda)
-    close(out, z["out"], what="rmsnorm out")
-    close(gx, z["grad_x"], what="rmsnorm grad_x")
-    close(gw, z["grad_w"], what="rmsnorm grad_w")
+    rx, rw = z["x"].double().requires_grad_(True), z["w"].double().requires_grad_(True)
+    ro = O.rmsnorm(rx, rw, 1e-5)
+    ro.backward(z["grad"].double())
+    close_ref(out, z["out"], ro, what="rmsnorm out")
+    close_ref(gx, z["grad_x"], rx.grad, what="rmsnorm grad_x")
+    close_ref(gw, z["grad_w"], rw.grad, what="rmsnorm grad_w")
 
 
 @pytest.mark.parametrize("B,C", [(1024, 4096), (3, 100), (1, 4097)])
