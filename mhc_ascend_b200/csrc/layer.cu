@@ -636,20 +636,41 @@ template <int N>
 __global__ void __launch_bounds__(128)
     token_bwd_kernel(const double* __restrict__ stats, const float* __restrict__ rec,
                      const float* __restrict__ a_pre, const float* __restrict__ a_post,
-                     const float* __restrict__ a_res, const float* __restrict__ b_res,
+                     const float* __restrict__ a_res, const float* __restrict__ b_pre,
+                     const float* __restrict__ b_post, const float* __restrict__ b_res,
                      float* __restrict__ tokb, double* __restrict__ tokr, int64_t B, int64_t C,
-                     int iters, float s_eps) {
+                     int iters, float s_eps, float r_eps) {
   using Lc = L<N>;
   constexpr int NH = Lc::NH, NS1 = Lc::NS1;
   const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const double* st = stats + b * NS1;
   const float* rc = rec + b * Lc::REC;
-  const double rms_h = rc[0], r = rc[1];
-  const double inv_h = 1.0 / rms_h, inv_r = 1.0 / r;
+  const double* G = st + 2 * N * N;
+  // The H_pre gradient is the small difference of two large moments (the
+  // RMSNorm backward removes the radial part of the upstream gradient), so it
+  // is sensitive to the exact gate values: recompute rms_h, h, hp and r in
+  // fp64 from the saved projections p and this pass's fp64 Gram matrix
+  // instead of reusing the fp32 values of the forward record.
+  double tr_g = 0.0;
+#pragma unroll
+  for (int i = 0; i < N; ++i) tr_g += G[gram_index(i, i, N)];
+  const double rms_h = sqrt(tr_g / (double)(N * C) + (double)r_eps);
+  const double inv_h = 1.0 / rms_h;
+  const double ap = *a_pre, aq = *a_post, ar = *a_res;
   double h[N], hp[N];
 #pragma unroll
-  for (int i = 0; i < N; ++i) { h[i] = rc[Lc::OFF_H + i]; hp[i] = rc[Lc::OFF_HP + i]; }
+  for (int i = 0; i < N; ++i) {
+    h[i] = 1.0 / (1.0 + exp(-((ap * (double)rc[Lc::OFF_P + i]) * inv_h + (double)b_pre[i])));
+    hp[i] = 2.0 / (1.0 + exp(-((aq * (double)rc[Lc::OFF_P + N + i]) * inv_h + (double)b_post[i])));
+  }
+  double q = 0.0;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) q += h[i] * h[j] * G[gram_index(i, j, N)];
+  const double r = sqrt(q / (double)C + (double)r_eps);
+  const double inv_r = 1.0 / r;
   double dt[NH];
   double dot = 0.0;
 #pragma unroll
@@ -670,7 +691,6 @@ __global__ void __launch_bounds__(128)
     for (int j = 0; j < N; ++j) Q = fma(st[2 * N * N + gram_index(i, j, N)], h[j], Q);
     dt[i] = (A * inv_r - beta * Q) * h[i] * (1.0 - h[i]);
   }
-  const double ap = *a_pre, aq = *a_post, ar = *a_res;
   double e0[N * N], gm[N * N];
 #pragma unroll
   for (int e = 0; e < N * N; ++e) {
@@ -708,18 +728,29 @@ __global__ void __launch_bounds__(128)
 // gate gradients (dt_pre, dt_post) and gM for the reductions over the batch.
 template <int N>
 __global__ void __launch_bounds__(128)
-    token_bwd_static_kernel(const double* __restrict__ stats, const float* __restrict__ rec,
-                            const float* __restrict__ rms, float* __restrict__ tokb,
-                            double* __restrict__ tokr, int64_t B, int64_t C) {
+    token_bwd_static_kernel(const double* __restrict__ stats, const float* __restrict__ H_pre,
+                            const float* __restrict__ H_post, float* __restrict__ tokb,
+                            double* __restrict__ tokr, int64_t B, int64_t C, float r_eps) {
   using Lc = L<N>;
   constexpr int NS1 = Lc::NS1;
   const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const double* st = stats + b * NS1;
-  const double r = rms[b], inv_r = 1.0 / r;
+  const double* G = st + 2 * N * N;
+  // gates and r in fp64 (see token_bwd_kernel for why)
   double h[N], hp[N];
 #pragma unroll
-  for (int i = 0; i < N; ++i) { h[i] = rec[Lc::OFF_H + i]; hp[i] = rec[Lc::OFF_HP + i]; }
+  for (int i = 0; i < N; ++i) {
+    h[i] = 1.0 / (1.0 + exp(-(double)H_pre[i]));
+    hp[i] = 2.0 / (1.0 + exp(-(double)H_post[i]));
+  }
+  double q = 0.0;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) q += h[i] * h[j] * G[gram_index(i, j, N)];
+  const double r = sqrt(q / (double)C + (double)r_eps);
+  const double inv_r = 1.0 / r;
   double* tr = tokr + b * Lc::NRS;
   double dot = 0.0;
 #pragma unroll
@@ -1097,10 +1128,11 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
 template <int N>
 int run_bwd_dynamic(const float* g, const float* x, const float* w, const float* pp,
                     const float* pq, const float* pr, const float* ap, const float* aq,
-                    const float* ar, const float* br, const float* rec, float* gx, float* gw,
-                    float* gpp, float* gpq, float* gpr, float* gap, float* gaq, float* gar,
-                    float* gbp, float* gbq, float* gbr, int64_t B, int64_t C, int iters,
-                    float s_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
+                    const float* ar, const float* bp, const float* bq, const float* br,
+                    const float* rec, float* gx, float* gw, float* gpp, float* gpq, float* gpr,
+                    float* gap, float* gaq, float* gar, float* gbp, float* gbq, float* gbr,
+                    int64_t B, int64_t C, int iters, float s_eps, float r_eps, void* ws,
+                    size_t ws_bytes, cudaStream_t s) {
   const size_t need = bwd_ws_bytes<N, true>(B, C);
   MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
               "mhc_layer_bwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
@@ -1118,8 +1150,8 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
   int rc = check_launch("mhc_layer_bwd_dynamic/bwd_stats");
   if (rc) return rc;
-  { ProfScope _ps("token_bwd", s); token_bwd_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, rec, ap, aq, ar, br, tokb, tokr, B,
-                                                     C, iters, s_eps); }
+  { ProfScope _ps("token_bwd", s); token_bwd_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, rec, ap, aq, ar, bp, bq, br, tokb,
+                                                     tokr, B, C, iters, s_eps, r_eps); }
   rc = check_launch("mhc_layer_bwd_dynamic/token_bwd");
   if (rc) return rc;
   { ProfScope _ps("grad_x", s); grad_x_kernel<N, true><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
@@ -1161,7 +1193,7 @@ template <int N>
 int run_bwd_static(const float* g, const float* x, const float* w, const float* Hp,
                    const float* Hq, const float* Hr, const float* rms, float* gx, float* gw,
                    float* gHp, float* gHq, float* gHr, int64_t B, int64_t C, int iters,
-                   float s_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
+                   float s_eps, float r_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
   const size_t need = bwd_ws_bytes<N, false>(B, C);
   MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
               "mhc_layer_bwd_static: workspace of %zu bytes required, got %zu", need, ws_bytes);
@@ -1181,7 +1213,7 @@ int run_bwd_static(const float* g, const float* x, const float* w, const float* 
   else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
   int rc = check_launch("mhc_layer_bwd_static/bwd_stats");
   if (rc) return rc;
-  { ProfScope _ps("token_bwd_static", s); token_bwd_static_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, rec, rms, tokb, tokr, B, C); }
+  { ProfScope _ps("token_bwd_static", s); token_bwd_static_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, Hp, Hq, tokb, tokr, B, C, r_eps); }
   { ProfScope _ps("grad_x", s); grad_x_kernel<N, false><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
       g, x, w, nullptr, nullptr, nullptr, rec, 0, tokb, gx, nullptr, gwp, B, C, p.ntiles,
       p.nsplit); }
@@ -1288,14 +1320,14 @@ extern "C" int mhc_layer_bwd_dynamic(
     float* grad_alpha_res, float* grad_b_pre, float* grad_b_post, float* grad_b_res,
     int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
     float rmsnorm_eps, void* workspace, size_t workspace_bytes, void* stream) {
-  (void)b_pre; (void)b_post;
   int rc = check_layer_args("mhc_layer_bwd_dynamic", batch, n, hidden, sinkhorn_iters,
                             sinkhorn_eps, rmsnorm_eps);
   if (rc) return rc;
   MHC_REQUIRE_PTR(grad_out); MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(rmsnorm_weight);
   MHC_REQUIRE_PTR(phi_pre); MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res);
   MHC_REQUIRE_PTR(alpha_pre); MHC_REQUIRE_PTR(alpha_post); MHC_REQUIRE_PTR(alpha_res);
-  MHC_REQUIRE_PTR(b_res); MHC_REQUIRE_PTR(token_state); MHC_REQUIRE_PTR(grad_x);
+  MHC_REQUIRE_PTR(b_pre); MHC_REQUIRE_PTR(b_post); MHC_REQUIRE_PTR(b_res);
+  MHC_REQUIRE_PTR(token_state); MHC_REQUIRE_PTR(grad_x);
   MHC_REQUIRE_PTR(grad_rmsnorm_weight); MHC_REQUIRE_PTR(grad_phi_pre);
   MHC_REQUIRE_PTR(grad_phi_post); MHC_REQUIRE_PTR(grad_phi_res); MHC_REQUIRE_PTR(grad_alpha_pre);
   MHC_REQUIRE_PTR(grad_alpha_post); MHC_REQUIRE_PTR(grad_alpha_res);
@@ -1303,12 +1335,12 @@ extern "C" int mhc_layer_bwd_dynamic(
   MHC_REQUIRE(batch > 0, MHC_ERR_INVALID_ARG, "mhc_layer_bwd_dynamic: batch must be > 0");
   cudaStream_t s = (cudaStream_t)stream;
   MHC_DISPATCH_N(n, (run_bwd_dynamic<NN>(grad_out, x, rmsnorm_weight, phi_pre, phi_post, phi_res,
-                                         alpha_pre, alpha_post, alpha_res, b_res, token_state,
-                                         grad_x, grad_rmsnorm_weight, grad_phi_pre, grad_phi_post,
-                                         grad_phi_res, grad_alpha_pre, grad_alpha_post,
-                                         grad_alpha_res, grad_b_pre, grad_b_post, grad_b_res,
-                                         batch, hidden, sinkhorn_iters, sinkhorn_eps, workspace,
-                                         workspace_bytes, s)));
+                                         alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
+                                         token_state, grad_x, grad_rmsnorm_weight, grad_phi_pre,
+                                         grad_phi_post, grad_phi_res, grad_alpha_pre,
+                                         grad_alpha_post, grad_alpha_res, grad_b_pre, grad_b_post,
+                                         grad_b_res, batch, hidden, sinkhorn_iters, sinkhorn_eps,
+                                         rmsnorm_eps, workspace, workspace_bytes, s)));
 }
 
 extern "C" size_t mhc_layer_static_workspace_bytes(int64_t batch, int32_t n, int64_t hidden) {
@@ -1385,5 +1417,5 @@ extern "C" int mhc_layer_bwd_static(const float* grad_out, const float* x,
   MHC_DISPATCH_N(n, (run_bwd_static<NN>(grad_out, x, rmsnorm_weight, H_pre, H_post, H_res, rms,
                                         grad_x, grad_rmsnorm_weight, grad_H_pre, grad_H_post,
                                         grad_H_res, batch, hidden, sinkhorn_iters, sinkhorn_eps,
-                                        workspace, workspace_bytes, s)));
+                                        rmsnorm_eps, workspace, workspace_bytes, s)));
 }
