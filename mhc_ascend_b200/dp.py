@@ -4,7 +4,7 @@ The mHC layer is independent per token, so data parallelism shards the token
 (batch) dimension across GPUs and needs exactly one exchange per step: a sum
 of the parameter gradients (phi_pre/post/res, rmsnorm_weight, alpha x3,
 b x3 -- about 1.6 MB at n=4, C=4096).  ``GradBucket`` packs them into one
-flat fp32 buffer in a fixed parameter order and all-reduces it with a single
+flat buffer (fp32 for the layer's parameters) in a fixed parameter order and all-reduces it with a single
 collective (NCCL over NVLink on GPUs, gloo on CPU), then scatters the result
 back.  The reference has no multi-device support (single-NPU library).
 """
@@ -24,11 +24,14 @@ class GradBucket:
         self.params: List[torch.nn.Parameter] = [p for p in params if p.requires_grad]
         self.average = average
         self.numel = sum(p.numel() for p in self.params)
+        dtypes = {p.dtype for p in self.params}
+        # one dtype for the whole bucket: the parameters' own when uniform
+        self.dtype = dtypes.pop() if len(dtypes) == 1 else torch.float32
         self._flat: Optional[torch.Tensor] = None
 
     def _buffer(self, device):
         if self._flat is None or self._flat.device != device:
-            self._flat = torch.empty(self.numel, dtype=torch.float32, device=device)
+            self._flat = torch.empty(self.numel, dtype=self.dtype, device=device)
         return self._flat
 
     def pack(self) -> torch.Tensor:
