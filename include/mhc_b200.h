@@ -154,6 +154,27 @@ MHC_API int mhc_layer_fwd_dynamic(const float* x, const float* rmsnorm_weight, c
                           int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference.  Same as mhc_layer_fwd_dynamic, for
+ * callers that cannot provide a workspace (no device allocator of their own,
+ * device memory fixed at start-up, or a path that must not call cudaMalloc /
+ * cudaFree because they can synchronise the device): the scratch comes from
+ * a 16 MiB array in the library's device image, which every GPU that loads
+ * the library holds until the process exits.  Requests needing more than
+ * 16 MiB (mhc_layer_fwd_dynamic_workspace_bytes > 16 MiB, e.g. more than
+ * ~30k tokens at n=4, C=4096) return MHC_ERR_UNSUPPORTED.  The first call on a
+ * device looks up the array's device address (make it before any stream
+ * capture).  All calls on a device share the array: calls whose kernels may
+ * overlap on the GPU race and must be serialised by the caller. */
+MHC_API int mhc_layer_fwd_dynamic_noalloc(const float* x, const float* rmsnorm_weight,
+                                          const float* phi_pre, const float* phi_post,
+                                          const float* phi_res, const float* alpha_pre,
+                                          const float* alpha_post, const float* alpha_res,
+                                          const float* b_pre, const float* b_post,
+                                          const float* b_res, float* out, float* token_state,
+                                          int64_t batch, int32_t n, int64_t hidden,
+                                          int32_t sinkhorn_iters, float sinkhorn_eps,
+                                          float rmsnorm_eps, void* stream);
+
 /* replaces mhc_layer_bwd_dynamic (bindings.cpp:600-874).  All parameter
  * gradients are written (not accumulated); they are fixed-order reductions
  * over the batch, so results are bitwise reproducible run to run. */
