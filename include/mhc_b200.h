@@ -219,6 +219,15 @@ MHC_API int mhc_layer_bwd_static(const float* grad_out, const float* x, const fl
                          size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Device error word.  No counterpart in the reference.  Kernels that wait on
+ * asynchronous copies (TMA + mbarrier) bound every wait; a wait that runs out
+ * sets this word to nonzero and the kernel abandons its work (its outputs are
+ * then incomplete) instead of hanging the GPU.  Reads the word (synchronous
+ * copy from the device) and optionally resets it to zero.
+ * ------------------------------------------------------------------------- */
+MHC_API int mhc_device_error_word(int32_t* value, int32_t reset);
+
+/* ---------------------------------------------------------------------------
  * Kernel timing (tracing).  No counterpart in the reference, which times
  * whole calls from Python (benchmark.py:156-269).  While enabled, every kernel
  * this library launches is bracketed by two CUDA events on its own stream;

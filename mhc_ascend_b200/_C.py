@@ -57,9 +57,17 @@ SIGNATURES = {
                                   [_P] * 7 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
     "mhc_layer_bwd_static": (ctypes.c_int,
                              [_P] * 12 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
+    "mhc_device_error_word": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
     "mhc_profile_enable": (ctypes.c_int, [ctypes.c_int]),
     "mhc_profile_report": (ctypes.c_int, [ctypes.c_char_p, _SZ]),
 }
+
+
+def device_error_word(reset: bool = False) -> int:
+    """Nonzero if a bounded device-side wait ran out (the kernel gave up)."""
+    v = ctypes.c_int32(0)
+    check(load().mhc_device_error_word(ctypes.byref(v), 1 if reset else 0), "mhc_device_error_word")
+    return v.value
 
 
 def profile_enable(on: bool) -> None:

@@ -29,6 +29,7 @@
 //         partials) -> reduce_* (fixed-order sums over splits / tokens)
 #include "common.cuh"
 #include "sinkhorn.cuh"
+#include "tma.cuh"
 #include <cuda_bf16.h>
 
 namespace mhc {
@@ -46,7 +47,9 @@ struct L {
   static constexpr int REC = (REC_RAW + 3) / 4 * 4;
   static constexpr int OFF_H = 2, OFF_HP = 2 + N, OFF_M = 2 + 2 * N, OFF_P = 2 + 2 * N + N * N;
   static constexpr int NS1 = 2 * N * N + NG;             // bwd moments: gM, W, G
-  static constexpr int TB = 4 + NHP;                      // bwd per-token: beta, inv_r, coef, -, d_p
+  // bwd per-token row read by grad_x: beta, inv_r, coef, -, d_p[NHP], h[N], hp[N], M[N*N]
+  static constexpr int OFF_TH = 4 + NHP, OFF_THP = OFF_TH + N, OFF_TM = OFF_THP + N;
+  static constexpr int TB = (OFF_TM + N * N + 3) / 4 * 4;
   static constexpr int NR = NH + 3;                       // bwd per-token reduce: dt, dalpha
   static constexpr int NRS = 2 * N + N * N;               // static per-token reduce: dt_pre, dt_post, gM
 };
@@ -188,6 +191,149 @@ __global__ void __launch_bounds__(256, 1)
   }
 
   // reduce over the 32 lanes (channels) and write this split's partials
+#pragma unroll
+  for (int t = 0; t < TPW; ++t) {
+    const int64_t tok = t0 + t;
+#pragma unroll
+    for (int k = 0; k < NHP; ++k) {
+      const float v = warp_sum(acc[t][k]);
+      if (lane == (k & 31) && tok < B) ppart[((int64_t)split * B + tok) * NHP + k] = v;
+    }
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const float v = warp_sum(gacc[t][g]);
+      if (lane == (g & 31) && tok < B) gpart[((int64_t)split * B + tok) * NG + g] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward 1, TMA-pipelined (n <= 4, C % 4 == 0, 16-byte aligned x): the same
+// split-K projection + Gram as proj_stats_kernel, with the x chunk
+// [32 tokens x n streams][32 channels] and the transposed phi chunk
+// [32 channels][PROW] brought into a PJT_STAGES-deep ring by TMA.  phiT is
+// phi rearranged per channel: phiT[c][i*NHP + k] = phi_k[i*C + c], rows padded
+// to PROW = n*NHP + 4 floats so the per-lane float4 reads hit distinct banks.
+// ---------------------------------------------------------------------------
+constexpr int PJT_STAGES = 4;
+
+template <int N>
+struct PjtCfg {
+  static constexpr int NHP = L<N>::NHP;
+  static constexpr int PROW = N * NHP + 4;
+  static constexpr int TT = 32;                           // tokens per CTA
+  static constexpr int XF = TT * N * 32;                  // x floats per stage
+  static constexpr int PF = 32 * PROW;                    // phiT floats per stage
+  static constexpr uint32_t STAGE_BYTES = (XF + PF) * 4;
+  static constexpr size_t SMEM = (size_t)PJT_STAGES * STAGE_BYTES + 128 + 64;
+};
+
+template <int N>
+__global__ void phi_transpose_kernel(const float* __restrict__ pp, const float* __restrict__ pq,
+                                     const float* __restrict__ pr, float* __restrict__ phiT,
+                                     int64_t C) {
+  using P = PjtCfg<N>;
+  constexpr int NH = L<N>::NH, NHP = L<N>::NHP;
+  const int64_t total = C * P::PROW;
+  const int64_t nC = (int64_t)N * C;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = e / P::PROW;
+    const int f = (int)(e % P::PROW);
+    float v = 0.f;
+    if (f < N * NHP) {
+      const int i = f / NHP, k = f % NHP;
+      if (k < NH) v = phi_row(pp, pq, pr, k, N, nC)[(int64_t)i * C + c];
+    }
+    phiT[e] = v;
+  }
+}
+
+template <int N>
+__global__ void __launch_bounds__(256, 1)
+    proj_stats_tma_kernel(const __grid_constant__ CUtensorMap xmap,
+                          const __grid_constant__ CUtensorMap pmap, float* __restrict__ ppart,
+                          float* __restrict__ gpart, int64_t B, int64_t C, int cps) {
+  using Lc = L<N>;
+  using P = PjtCfg<N>;
+  constexpr int NHP = Lc::NHP, NG = Lc::NG, TPW = 4, PROW = P::PROW;
+  extern __shared__ unsigned char smem_raw[];
+  float* ring = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + PJT_STAGES * (P::XF + P::PF));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t tile_t0 = (int64_t)blockIdx.x * P::TT;
+  const int64_t t0 = tile_t0 + warp * TPW;
+  const int split = blockIdx.y;
+  const int64_t c_begin = (int64_t)split * cps;
+  const int64_t c_end = c_begin + cps < C ? c_begin + cps : C;
+  const int nchunks = c_begin < c_end ? (int)((c_end - c_begin + 31) / 32) : 0;
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&xmap);
+    prefetch_tmap(&pmap);
+    for (int st = 0; st < PJT_STAGES; ++st) mbar_init(&bars[st], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int k) {
+    const int slot = k % PJT_STAGES;
+    float* base = ring + slot * (P::XF + P::PF);
+    const int cc = (int)(c_begin + 32 * k);
+    mbar_expect_tx(&bars[slot], P::STAGE_BYTES);
+    tma_load_2d(base, &xmap, cc, (int)(tile_t0 * N), &bars[slot]);
+    tma_load_2d(base + P::XF, &pmap, 0, cc, &bars[slot]);
+  };
+  if (threadIdx.x == 0)
+    for (int k = 0; k < PJT_STAGES && k < nchunks; ++k) issue(k);
+
+  float acc[TPW][NHP];
+  float gacc[TPW][NG];
+#pragma unroll
+  for (int t = 0; t < TPW; ++t) {
+#pragma unroll
+    for (int k = 0; k < NHP; ++k) acc[t][k] = 0.f;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) gacc[t][g] = 0.f;
+  }
+  for (int k = 0; k < nchunks; ++k) {
+    const int slot = k % PJT_STAGES;
+    const bool ok = mbar_wait(&bars[slot], (uint32_t)((k / PJT_STAGES) & 1));
+    if (__syncthreads_or(!ok)) return;
+    const float* xs = ring + slot * (P::XF + P::PF);
+    const float* row = xs + P::XF + lane * PROW;
+    float xv[TPW][N];
+#pragma unroll
+    for (int t = 0; t < TPW; ++t)
+#pragma unroll
+      for (int i = 0; i < N; ++i) xv[t][i] = xs[((warp * TPW + t) * N + i) * 32 + lane];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+#pragma unroll
+      for (int k4 = 0; k4 < NHP / 4; ++k4) {
+        const float4 f = *reinterpret_cast<const float4*>(row + i * NHP + 4 * k4);
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          acc[t][4 * k4 + 0] = fmaf(xv[t][i], f.x, acc[t][4 * k4 + 0]);
+          acc[t][4 * k4 + 1] = fmaf(xv[t][i], f.y, acc[t][4 * k4 + 1]);
+          acc[t][4 * k4 + 2] = fmaf(xv[t][i], f.z, acc[t][4 * k4 + 2]);
+          acc[t][4 * k4 + 3] = fmaf(xv[t][i], f.w, acc[t][4 * k4 + 3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TPW; ++t) {
+      int g = 0;
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int j = i; j < N; ++j) {
+          gacc[t][g] = fmaf(xv[t][i], xv[t][j], gacc[t][g]);
+          ++g;
+        }
+    }
+    __syncthreads();  // slot consumed: refill it
+    if (threadIdx.x == 0 && k + PJT_STAGES < nchunks) issue(k + PJT_STAGES);
+  }
 #pragma unroll
   for (int t = 0; t < TPW; ++t) {
     const int64_t tok = t0 + t;
@@ -719,6 +865,15 @@ __global__ void __launch_bounds__(128)
   tb[1] = (float)inv_r;
   tb[2] = (float)(-s * inv_h * inv_h * inv_h / (double)(N * C));
   tb[3] = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    tb[Lc::OFF_TH + i] = (float)h[i];
+    tb[Lc::OFF_THP + i] = (float)hp[i];
+  }
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) tb[Lc::OFF_TM + e] = rc[Lc::OFF_M + e];
+#pragma unroll
+  for (int e = Lc::OFF_TM + N * N; e < Lc::TB; ++e) tb[e] = 0.f;
   tr[NH + 0] = da0;
   tr[NH + 1] = da1;
   tr[NH + 2] = da2;
@@ -729,7 +884,8 @@ __global__ void __launch_bounds__(128)
 template <int N>
 __global__ void __launch_bounds__(128)
     token_bwd_static_kernel(const double* __restrict__ stats, const float* __restrict__ H_pre,
-                            const float* __restrict__ H_post, float* __restrict__ tokb,
+                            const float* __restrict__ H_post, const float* __restrict__ rec,
+                            float* __restrict__ tokb,
                             double* __restrict__ tokr, int64_t B, int64_t C, float r_eps) {
   using Lc = L<N>;
   constexpr int NS1 = Lc::NS1;
@@ -773,11 +929,22 @@ __global__ void __launch_bounds__(128)
   }
 #pragma unroll
   for (int e = 0; e < N * N; ++e) tr[2 * N + e] = st[e];
-  float* tb = tokb + b * 4;
+  float* tb = tokb + b * Lc::TB;
   tb[0] = (float)beta;
   tb[1] = (float)inv_r;
   tb[2] = 0.f;
   tb[3] = 0.f;
+#pragma unroll
+  for (int k = 0; k < Lc::NHP; ++k) tb[4 + k] = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    tb[Lc::OFF_TH + i] = (float)h[i];
+    tb[Lc::OFF_THP + i] = (float)hp[i];
+  }
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) tb[Lc::OFF_TM + e] = rec[Lc::OFF_M + e];
+#pragma unroll
+  for (int e = Lc::OFF_TM + N * N; e < Lc::TB; ++e) tb[e] = 0.f;
 }
 
 // ---------------------------------------------------------------------------
@@ -797,16 +964,13 @@ __global__ void __launch_bounds__(GX_CW* N)
     grad_x_kernel(const float* __restrict__ g, const float* __restrict__ x,
                   const float* __restrict__ w, const float* __restrict__ phi_pre,
                   const float* __restrict__ phi_post, const float* __restrict__ phi_res,
-                  const float* __restrict__ rec, int rec_stride, const float* __restrict__ tokb,
-                  float* __restrict__ gx, float* __restrict__ dphi_part,
+                  const float* __restrict__ tokb, float* __restrict__ gx,
+                  float* __restrict__ dphi_part,
                   float* __restrict__ gw_part, int64_t B, int64_t C, int ntiles, int nsplit) {
   using Lc = L<N>;
   constexpr int NH = Lc::NH, NHP = Lc::NHP;
-  constexpr int TBS = DYN ? Lc::TB : 4;      // per-token tokb stride
-  constexpr int SREC = 2 * N + N * N;        // h, hp, M
-  constexpr int STOK = TBS + SREC;           // smem floats per staged token
-  __shared__ __align__(16) float s_tok[GX_TB][STOK + (4 - (STOK & 3)) % 4];
-  constexpr int SSTR = STOK + (4 - (STOK & 3)) % 4;
+  constexpr int TBS = Lc::TB;                // per-token row
+  __shared__ __align__(16) float s_tok[GX_TB][TBS];
   const int tile = blockIdx.x % ntiles;
   const int split = blockIdx.x / ntiles;
   const int i = threadIdx.x / GX_CW;
@@ -833,13 +997,9 @@ __global__ void __launch_bounds__(GX_CW* N)
   for (int64_t t0 = tb0; t0 < tb1; t0 += GX_TB) {
     const int nt = (int)((tb1 - t0) < GX_TB ? (tb1 - t0) : GX_TB);
     __syncthreads();
-    for (int e = threadIdx.x; e < nt * STOK; e += blockDim.x) {
-      const int tt = e / STOK, f = e % STOK;
-      const int64_t tok = t0 + tt;
-      float v;
-      if (f < TBS) v = tokb[tok * TBS + f];
-      else v = rec[tok * rec_stride + Lc::OFF_H + (f - TBS)];
-      s_tok[tt][f] = v;
+    for (int e = threadIdx.x; e < nt * TBS; e += blockDim.x) {
+      const int tt = e / TBS, f = e % TBS;
+      s_tok[tt][f] = tokb[(t0 + tt) * TBS + f];
     }
     __syncthreads();
     if (!cval) continue;
@@ -847,9 +1007,9 @@ __global__ void __launch_bounds__(GX_CW* N)
       const int64_t tok = t0 + tt;
       const float* st = s_tok[tt];
       const float beta = st[0], inv_r = st[1];
-      const float* h = st + TBS;
-      const float* hp = h + N;
-      const float* m = hp + N;
+      const float* h = st + Lc::OFF_TH;
+      const float* hp = st + Lc::OFF_THP;
+      const float* m = st + Lc::OFF_TM;
       const float* gb = g + tok * nC + c;
       const float* xb = x + tok * nC + c;
       float gv[N], xv[N];
@@ -885,6 +1045,151 @@ __global__ void __launch_bounds__(GX_CW* N)
       if (i == 0) gwacc = fmaf(gy * xa, inv_r, gwacc);
     }
   }
+  if (cval) {
+    if (DYN) {
+#pragma unroll
+      for (int k = 0; k < NH; ++k) dphi_part[((int64_t)split * NH + k) * nC + col] = dph[k];
+    }
+    if (i == 0) gw_part[(int64_t)split * C + c] = gwacc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward 3, TMA-pipelined (n <= 4, C % 4 == 0, 16-byte aligned tensors):
+// same math and thread mapping as grad_x_kernel, but batches of GXT_TB tokens
+// of grad_out, x and the per-token rows are brought into a GXT_STAGES-deep
+// shared-memory ring by TMA (one elected thread issues the copies, an
+// mbarrier per slot tracks arrival), so the bytes in flight no longer depend
+// on how many warps are resident.
+// ---------------------------------------------------------------------------
+constexpr int GXT_TB = 8;      // tokens per stage
+constexpr int GXT_STAGES = 4;
+
+template <int N>
+struct GxtCfg {
+  static constexpr int ROWS = GXT_TB * N;                    // g / x rows per stage
+  static constexpr int TILE_FLOATS = ROWS * GX_CW;           // one of g / x
+  static constexpr int TOK_FLOATS = GXT_TB * L<N>::TB;
+  static constexpr int STAGE_FLOATS = 2 * TILE_FLOATS + TOK_FLOATS;
+  static constexpr uint32_t STAGE_BYTES = STAGE_FLOATS * 4;
+  static constexpr size_t SMEM = (size_t)GXT_STAGES * STAGE_BYTES + 128 + 64;
+};
+
+template <int N, bool DYN>
+__global__ void __launch_bounds__(GX_CW* N)
+    grad_x_tma_kernel(const __grid_constant__ CUtensorMap gmap,
+                      const __grid_constant__ CUtensorMap xmap,
+                      const __grid_constant__ CUtensorMap tmap, const float* __restrict__ w,
+                      const float* __restrict__ phi_pre, const float* __restrict__ phi_post,
+                      const float* __restrict__ phi_res, float* __restrict__ gx,
+                      float* __restrict__ dphi_part, float* __restrict__ gw_part, int64_t B,
+                      int64_t C, int ntiles, int nsplit) {
+  using Lc = L<N>;
+  using Cf = GxtCfg<N>;
+  constexpr int NH = Lc::NH, NHP = Lc::NHP, TBS = Lc::TB;
+  extern __shared__ unsigned char smem_raw[];
+  float* ring = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + GXT_STAGES * Cf::STAGE_FLOATS);
+
+  const int tile = blockIdx.x % ntiles;
+  const int split = blockIdx.x / ntiles;
+  const int i = threadIdx.x / GX_CW;
+  const int cl = threadIdx.x % GX_CW;
+  const int64_t c = (int64_t)tile * GX_CW + cl;
+  const bool cval = c < C;
+  const int64_t nC = (int64_t)N * C;
+  const int64_t col = (int64_t)i * C + c;
+  const int64_t tb0 = B * split / nsplit, tb1 = B * (split + 1) / nsplit;
+  const int nbatch = (int)((tb1 - tb0 + GXT_TB - 1) / GXT_TB);
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&gmap);
+    prefetch_tmap(&xmap);
+    prefetch_tmap(&tmap);
+    for (int st = 0; st < GXT_STAGES; ++st) mbar_init(&bars[st], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int j) {
+    const int slot = j % GXT_STAGES;
+    float* base = ring + slot * Cf::STAGE_FLOATS;
+    const int t0 = (int)(tb0 + (int64_t)j * GXT_TB);
+    mbar_expect_tx(&bars[slot], Cf::STAGE_BYTES);
+    tma_load_2d(base, &gmap, tile * GX_CW, t0 * N, &bars[slot]);
+    tma_load_2d(base + Cf::TILE_FLOATS, &xmap, tile * GX_CW, t0 * N, &bars[slot]);
+    tma_load_2d(base + 2 * Cf::TILE_FLOATS, &tmap, 0, t0, &bars[slot]);
+  };
+  if (threadIdx.x == 0)
+    for (int j = 0; j < GXT_STAGES && j < nbatch; ++j) issue(j);
+
+  float phi[DYN ? NHP : 1];
+  float dph[DYN ? NHP : 1];
+  if (DYN) {
+#pragma unroll
+    for (int k = 0; k < NHP; ++k) {
+      phi[k] = (k < NH && cval) ? __ldg(phi_row(phi_pre, phi_post, phi_res, k, N, nC) + col) : 0.f;
+      dph[k] = 0.f;
+    }
+  }
+  const float wc = cval ? w[c] : 0.f;
+  float gwacc = 0.f;
+  bool failed = false;
+
+  for (int j = 0; j < nbatch; ++j) {
+    const int slot = j % GXT_STAGES;
+    const bool ok = mbar_wait(&bars[slot], (uint32_t)((j / GXT_STAGES) & 1));
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    const float* gs = ring + slot * Cf::STAGE_FLOATS;
+    const float* xs = gs + Cf::TILE_FLOATS;
+    const float* ts = xs + Cf::TILE_FLOATS;
+    const int64_t t0 = tb0 + (int64_t)j * GXT_TB;
+    const int nt = (int)((tb1 - t0) < GXT_TB ? (tb1 - t0) : GXT_TB);
+    if (cval) {
+      for (int tt = 0; tt < nt; ++tt) {
+        const int64_t tok = t0 + tt;
+        const float* st = ts + tt * TBS;
+        const float beta = st[0], inv_r = st[1];
+        const float* h = st + Lc::OFF_TH;
+        const float* hp = st + Lc::OFF_THP;
+        const float* m = st + Lc::OFF_TM;
+        float gv[N], xv[N];
+#pragma unroll
+        for (int jj = 0; jj < N; ++jj) {
+          gv[jj] = gs[(tt * N + jj) * GX_CW + cl];
+          xv[jj] = xs[(tt * N + jj) * GX_CW + cl];
+        }
+        float gy = 0.f, xa = 0.f, mix = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < N; ++jj) {
+          gy = fmaf(hp[jj], gv[jj], gy);
+          xa = fmaf(h[jj], xv[jj], xa);
+          mix = fmaf(m[jj * N + i], gv[jj], mix);
+        }
+        const float xi = xv[i];
+        float acc = mix + h[i] * (gy * wc * inv_r - xa * beta);
+        if (DYN) {
+          const float coef = st[2];
+          const float* dp = st + 4;
+          float2 a2 = make_float2(0.f, 0.f);
+          const float2 x2 = make_float2(xi, xi);
+#pragma unroll
+          for (int k = 0; k < NHP; k += 2) {
+            const float2 d2 = *reinterpret_cast<const float2*>(dp + k);
+            a2 = __ffma2_rn(d2, make_float2(phi[k], phi[k + 1]), a2);
+            float2 q2 = __ffma2_rn(d2, x2, make_float2(dph[k], dph[k + 1]));
+            dph[k] = q2.x;
+            dph[k + 1] = q2.y;
+          }
+          acc += (a2.x + a2.y) + coef * xi;
+        }
+        __stcs(gx + tok * nC + col, acc);
+        if (i == 0) gwacc = fmaf(gy * xa, inv_r, gwacc);
+      }
+    }
+    __syncthreads();  // slot fully consumed: refill it
+    if (threadIdx.x == 0 && j + GXT_STAGES < nbatch) issue(j + GXT_STAGES);
+  }
+  if (failed) return;
   if (cval) {
     if (DYN) {
 #pragma unroll
@@ -1022,7 +1327,7 @@ int choose_gx_splits(int64_t tiles, int64_t B, int sms, int per_sm) {
 struct FwdPlan {
   int ks, cps;
   int64_t tiles;
-  size_t ppart, gpart, rec_tmp;
+  size_t ppart, gpart, rec_tmp, phiT;
 };
 
 template <int N>
@@ -1035,6 +1340,7 @@ FwdPlan plan_fwd(int64_t B, int64_t C) {
   p.ppart = (size_t)p.ks * B * L<N>::NHP;
   p.gpart = (size_t)p.ks * B * L<N>::NG;
   p.rec_tmp = (size_t)B * L<N>::REC;
+  p.phiT = N <= 4 ? (size_t)C * PjtCfg<(N <= 4 ? N : 4)>::PROW : 0;
   return p;
 }
 
@@ -1049,7 +1355,7 @@ BwdPlan plan_bwd(int64_t B, int64_t C) {
   p.ntiles = (int)((C + GX_CW - 1) / GX_CW);
   p.nsplit = choose_gx_splits(p.ntiles, B, num_sms(), N <= 4 ? 2 : 1);
   p.stats = (size_t)B * L<N>::NS1 * 2;  // fp64
-  p.tokb = (size_t)B * (DYN ? L<N>::TB : 4);
+  p.tokb = (size_t)B * L<N>::TB;
   p.tokr = (size_t)B * (DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
   p.dphi = DYN ? (size_t)p.nsplit * L<N>::NH * N * C : 0;
   p.gw = (size_t)p.nsplit * C;
@@ -1063,6 +1369,7 @@ size_t fwd_ws_bytes(int64_t B, int64_t C, bool need_rec) {
   Carve cv(nullptr);
   cv.take(p.ppart);
   cv.take(p.gpart);
+  cv.take(p.phiT);
   if (need_rec) cv.take(p.rec_tmp);
   return cv.off;
 }
@@ -1084,6 +1391,31 @@ inline unsigned grid_1d(int64_t n, int threads, int64_t cap = 1 << 30) {
   return (unsigned)g;
 }
 
+// Launch the TMA-pipelined grad_x when the layout allows it; false -> caller
+// uses the generic kernel.
+template <int N, bool DYN>
+bool launch_grad_x_tma(const float* g, const float* x, const float* w, const float* pp,
+                       const float* pq, const float* pr, const float* tokb, float* gx,
+                       float* dphi, float* gwp, int64_t B, int64_t C, const BwdPlan& p,
+                       cudaStream_t s) {
+  if constexpr (N > 4) {
+    return false;
+  } else {
+    using Cf = GxtCfg<N>;
+    CUtensorMap gmap, xmap, tmap;
+    if (C % 4 != 0 || !aligned16(g) || !aligned16(x) || !aligned16(tokb)) return false;
+    if (!make_tmap_2d_f32(&gmap, g, (uint64_t)B * N, C, C, Cf::ROWS, GX_CW) ||
+        !make_tmap_2d_f32(&xmap, x, (uint64_t)B * N, C, C, Cf::ROWS, GX_CW) ||
+        !make_tmap_2d_f32(&tmap, tokb, B, L<N>::TB, L<N>::TB, GXT_TB, L<N>::TB))
+      return false;
+    cudaFuncSetAttribute(grad_x_tma_kernel<N, DYN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)Cf::SMEM);
+    { ProfScope _ps("grad_x", s); grad_x_tma_kernel<N, DYN><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, Cf::SMEM, s>>>(
+        gmap, xmap, tmap, w, pp, pq, pr, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
+    return true;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
@@ -1101,16 +1433,36 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
   Carve cv(ws);
   float* ppart = cv.take(p.ppart);
   float* gpart = cv.take(p.gpart);
+  float* phiT = cv.take(p.phiT);
   float* rec = need_rec ? cv.take(p.rec_tmp) : token_state;
 
-  using P = ProjCfg<N>;
-  const size_t smem = (size_t)P::SMEM_FLOATS * sizeof(float);
-  // Opt in to > 48 KB of dynamic shared memory (cheap, idempotent, per device).
-  cudaFuncSetAttribute(proj_stats_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       (int)smem);
-  { ProfScope _ps("proj_stats", s); proj_stats_kernel<N><<<dim3((unsigned)p.tiles, (unsigned)p.ks), 256, smem, s>>>(
-      x, pp, pq, pr, ppart, gpart, B, C, p.cps); }
-  int rc = check_launch("mhc_layer_fwd_dynamic/proj_stats");
+  int rc = MHC_OK;
+  bool done = false;
+  if constexpr (N <= 4) {
+    // TMA-pipelined projection when the layout allows it.
+    using PT = PjtCfg<N>;
+    CUtensorMap xmap, pmap;
+    if (C % 4 == 0 && aligned16(x) && aligned16(phiT) &&
+        make_tmap_2d_f32(&xmap, x, (uint64_t)B * N, C, C, PT::TT * N, 32) &&
+        make_tmap_2d_f32(&pmap, phiT, C, PT::PROW, PT::PROW, 32, PT::PROW)) {
+      { ProfScope _ps("phi_transpose", s); phi_transpose_kernel<N><<<grid_1d(C * PT::PROW, 256, 2048), 256, 0, s>>>(pp, pq, pr, phiT, C); }
+      cudaFuncSetAttribute(proj_stats_tma_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)PT::SMEM);
+      { ProfScope _ps("proj_stats", s); proj_stats_tma_kernel<N><<<dim3((unsigned)p.tiles, (unsigned)p.ks), 256, PT::SMEM, s>>>(
+          xmap, pmap, ppart, gpart, B, C, p.cps); }
+      done = true;
+    }
+  }
+  if (!done) {
+    using P = ProjCfg<N>;
+    const size_t smem = (size_t)P::SMEM_FLOATS * sizeof(float);
+    // Opt in to > 48 KB of dynamic shared memory (cheap, idempotent, per device).
+    cudaFuncSetAttribute(proj_stats_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    { ProfScope _ps("proj_stats", s); proj_stats_kernel<N><<<dim3((unsigned)p.tiles, (unsigned)p.ks), 256, smem, s>>>(
+        x, pp, pq, pr, ppart, gpart, B, C, p.cps); }
+  }
+  rc = check_launch("mhc_layer_fwd_dynamic/proj_stats");
   if (rc) return rc;
   { ProfScope _ps("token_fwd", s); token_fwd_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(ppart, gpart, p.ks, ap, aq, ar, bp, bq, br,
                                                      rec, B, C, iters, s_eps, r_eps); }
@@ -1154,8 +1506,9 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
                                                      tokr, B, C, iters, s_eps, r_eps); }
   rc = check_launch("mhc_layer_bwd_dynamic/token_bwd");
   if (rc) return rc;
-  { ProfScope _ps("grad_x", s); grad_x_kernel<N, true><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
-      g, x, w, pp, pq, pr, rec, L<N>::REC, tokb, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
+  if (!launch_grad_x_tma<N, true>(g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p, s))
+    { ProfScope _ps("grad_x", s); grad_x_kernel<N, true><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
+        g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
   rc = check_launch("mhc_layer_bwd_dynamic/grad_x");
   if (rc) return rc;
   const int64_t nC = (int64_t)N * C;
@@ -1213,10 +1566,11 @@ int run_bwd_static(const float* g, const float* x, const float* w, const float* 
   else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
   int rc = check_launch("mhc_layer_bwd_static/bwd_stats");
   if (rc) return rc;
-  { ProfScope _ps("token_bwd_static", s); token_bwd_static_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, Hp, Hq, tokb, tokr, B, C, r_eps); }
-  { ProfScope _ps("grad_x", s); grad_x_kernel<N, false><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
-      g, x, w, nullptr, nullptr, nullptr, rec, 0, tokb, gx, nullptr, gwp, B, C, p.ntiles,
-      p.nsplit); }
+  { ProfScope _ps("token_bwd_static", s); token_bwd_static_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, Hp, Hq, rec, tokb, tokr, B, C, r_eps); }
+  if (!launch_grad_x_tma<N, false>(g, x, w, nullptr, nullptr, nullptr, tokb, gx, nullptr, gwp, B,
+                                   C, p, s))
+    { ProfScope _ps("grad_x", s); grad_x_kernel<N, false><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
+        g, x, w, nullptr, nullptr, nullptr, tokb, gx, nullptr, gwp, B, C, p.ntiles, p.nsplit); }
   rc = check_launch("mhc_layer_bwd_static/grad_x");
   if (rc) return rc;
   { ProfScope _ps("reduce_splits", s); reduce_splits_kernel<<<grid_1d(C, 256, 4096), 256, 0, s>>>(gwp, p.nsplit, C, gw); }
@@ -1418,4 +1772,20 @@ extern "C" int mhc_layer_bwd_static(const float* grad_out, const float* x,
                                         grad_x, grad_rmsnorm_weight, grad_H_pre, grad_H_post,
                                         grad_H_res, batch, hidden, sinkhorn_iters, sinkhorn_eps,
                                         rmsnorm_eps, workspace, workspace_bytes, s)));
+}
+
+extern "C" int mhc_device_error_word(int32_t* value, int32_t reset) {
+  MHC_REQUIRE_PTR(value);
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_mhc_device_error, sizeof(int));
+  if (e != cudaSuccess)
+    return fail(MHC_ERR_CUDA, "mhc_device_error_word: %s", cudaGetErrorString(e));
+  *value = v;
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_mhc_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess)
+      return fail(MHC_ERR_CUDA, "mhc_device_error_word: %s", cudaGetErrorString(e));
+  }
+  return MHC_OK;
 }

@@ -203,3 +203,13 @@ def test_residual_wrapper(cuda):
     close(out, ref.reshape(B, T, C), what="wrapper out")
     out.sum().backward()
     assert w.mhc.phi_res.grad is not None and torch.isfinite(w.mhc.phi_res.grad).all()
+
+
+def test_no_device_wait_timed_out(cuda):
+    """The TMA-pipelined kernels bound every mbarrier wait; none may have run out."""
+    from mhc_ascend_b200 import _C
+    x, params, grad = oracle_case(333, 4, 4096, seed=21)
+    layer = make_layer(params, 4, 4096, cuda)
+    run_layer(layer, x.to(cuda), grad.to(cuda))
+    torch.cuda.synchronize()
+    assert _C.device_error_word(reset=True) == 0
