@@ -47,7 +47,7 @@ struct L {
   static constexpr int REC = (REC_RAW + 3) / 4 * 4;
   static constexpr int OFF_H = 2, OFF_HP = 2 + N, OFF_M = 2 + 2 * N, OFF_P = 2 + 2 * N + N * N;
   static constexpr int NS1 = 2 * N * N + NG;             // bwd moments: gM, W, G
-  // bwd per-token row read by grad_x: beta, inv_r, coef, -, d_p[NHP], h[N], hp[N], M[N*N]
+  // bwd per-token row read by grad_x: beta, inv_r, coef, -, d_p[NHP], h[N], hp[N], M^T[N*N]
   static constexpr int OFF_TH = 4 + NHP, OFF_THP = OFF_TH + N, OFF_TM = OFF_THP + N;
   static constexpr int TB = (OFF_TM + N * N + 3) / 4 * 4;
   static constexpr int NR = NH + 3;                       // bwd per-token reduce: dt, dalpha
@@ -249,14 +249,16 @@ __global__ void phi_transpose_kernel(const float* __restrict__ pp, const float* 
   }
 }
 
+constexpr int PJT_THREADS = 512;  // 16 warps x 2 tokens
+
 template <int N>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(PJT_THREADS, 1)
     proj_stats_tma_kernel(const __grid_constant__ CUtensorMap xmap,
                           const __grid_constant__ CUtensorMap pmap, float* __restrict__ ppart,
                           float* __restrict__ gpart, int64_t B, int64_t C, int cps) {
   using Lc = L<N>;
   using P = PjtCfg<N>;
-  constexpr int NHP = Lc::NHP, NG = Lc::NG, TPW = 4, PROW = P::PROW;
+  constexpr int NHP = Lc::NHP, NG = Lc::NG, TPW = P::TT / (PJT_THREADS / 32), PROW = P::PROW;
   extern __shared__ unsigned char smem_raw[];
   float* ring = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + PJT_STAGES * (P::XF + P::PF));
@@ -695,7 +697,7 @@ __device__ __forceinline__ void block_reduce_to_global(double (&acc)[V], double*
 }
 
 template <int N, bool VEC>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, 4)
     bwd_stats_kernel(const float* __restrict__ g, const float* __restrict__ x,
                      const float* __restrict__ w, double* __restrict__ stats, int64_t B,
                      int64_t C) {
@@ -733,27 +735,23 @@ __global__ void __launch_bounds__(128)
         for (int j = i; j < N; ++j) { acc[e] = fma(xv[i], xv[j], acc[e]); ++e; }
     };
     if (VEC) {
-      for (int64_t q = threadIdx.x; q < C / 4; q += blockDim.x) {
-        float4 g4[N], x4[N];
+      // float2 per stream: keeps the live load registers low enough for
+      // 4 CTAs (16 warps) per SM next to the 42 fp64 accumulators.
+      for (int64_t q = threadIdx.x; q < C / 2; q += blockDim.x) {
+        float2 g2[N], x2[N];
 #pragma unroll
         for (int i = 0; i < N; ++i) {
-          g4[i] = __ldg(reinterpret_cast<const float4*>(gb + i * C) + q);
-          x4[i] = __ldg(reinterpret_cast<const float4*>(xb + i * C) + q);
+          g2[i] = __ldcs(reinterpret_cast<const float2*>(gb + i * C) + q);
+          x2[i] = __ldcs(reinterpret_cast<const float2*>(xb + i * C) + q);
         }
-        const float4 w4 = __ldg(reinterpret_cast<const float4*>(w) + q);
+        const float2 w2 = __ldg(reinterpret_cast<const float2*>(w) + q);
         float gv[N], xv[N];
 #pragma unroll
-        for (int i = 0; i < N; ++i) { gv[i] = g4[i].x; xv[i] = x4[i].x; }
-        accum(gv, xv, w4.x);
+        for (int i = 0; i < N; ++i) { gv[i] = g2[i].x; xv[i] = x2[i].x; }
+        accum(gv, xv, w2.x);
 #pragma unroll
-        for (int i = 0; i < N; ++i) { gv[i] = g4[i].y; xv[i] = x4[i].y; }
-        accum(gv, xv, w4.y);
-#pragma unroll
-        for (int i = 0; i < N; ++i) { gv[i] = g4[i].z; xv[i] = x4[i].z; }
-        accum(gv, xv, w4.z);
-#pragma unroll
-        for (int i = 0; i < N; ++i) { gv[i] = g4[i].w; xv[i] = x4[i].w; }
-        accum(gv, xv, w4.w);
+        for (int i = 0; i < N; ++i) { gv[i] = g2[i].y; xv[i] = x2[i].y; }
+        accum(gv, xv, w2.y);
       }
     } else {
       for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
@@ -871,7 +869,7 @@ __global__ void __launch_bounds__(128)
     tb[Lc::OFF_THP + i] = (float)hp[i];
   }
 #pragma unroll
-  for (int e = 0; e < N * N; ++e) tb[Lc::OFF_TM + e] = rc[Lc::OFF_M + e];
+  for (int e = 0; e < N * N; ++e) tb[Lc::OFF_TM + (e % N) * N + e / N] = rc[Lc::OFF_M + e];
 #pragma unroll
   for (int e = Lc::OFF_TM + N * N; e < Lc::TB; ++e) tb[e] = 0.f;
   tr[NH + 0] = da0;
@@ -942,7 +940,7 @@ __global__ void __launch_bounds__(128)
     tb[Lc::OFF_THP + i] = (float)hp[i];
   }
 #pragma unroll
-  for (int e = 0; e < N * N; ++e) tb[Lc::OFF_TM + e] = rec[Lc::OFF_M + e];
+  for (int e = 0; e < N * N; ++e) tb[Lc::OFF_TM + (e % N) * N + e / N] = rec[Lc::OFF_M + e];
 #pragma unroll
   for (int e = Lc::OFF_TM + N * N; e < Lc::TB; ++e) tb[e] = 0.f;
 }
@@ -1020,7 +1018,7 @@ __global__ void __launch_bounds__(GX_CW* N)
       for (int j = 0; j < N; ++j) {
         gy = fmaf(hp[j], gv[j], gy);
         xa = fmaf(h[j], xv[j], xa);
-        mix = fmaf(m[j * N + i], gv[j], mix);
+        mix = fmaf(m[i * N + j], gv[j], mix);
       }
       const float xi = xv[i];
       float acc = mix + h[i] * (gy * wc * inv_r - xa * beta);
@@ -1145,13 +1143,30 @@ __global__ void __launch_bounds__(GX_CW* N)
     const int64_t t0 = tb0 + (int64_t)j * GXT_TB;
     const int nt = (int)((tb1 - t0) < GXT_TB ? (tb1 - t0) : GXT_TB);
     if (cval) {
+#pragma unroll 2
       for (int tt = 0; tt < nt; ++tt) {
         const int64_t tok = t0 + tt;
         const float* st = ts + tt * TBS;
-        const float beta = st[0], inv_r = st[1];
-        const float* h = st + Lc::OFF_TH;
-        const float* hp = st + Lc::OFF_THP;
-        const float* m = st + Lc::OFF_TM;
+        float beta, inv_r, coef, h[N], hp[N], mc[N];
+        if constexpr (N == 4) {
+          // per-token scalars as float4 broadcasts (row layout is 16-byte aligned at n = 4)
+          const float4 s0 = *reinterpret_cast<const float4*>(st);
+          const float4 h4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TH);
+          const float4 q4 = *reinterpret_cast<const float4*>(st + Lc::OFF_THP);
+          const float4 m4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TM + i * N);
+          beta = s0.x; inv_r = s0.y; coef = s0.z;
+          h[0] = h4.x; h[1] = h4.y; h[2] = h4.z; h[3] = h4.w;
+          hp[0] = q4.x; hp[1] = q4.y; hp[2] = q4.z; hp[3] = q4.w;
+          mc[0] = m4.x; mc[1] = m4.y; mc[2] = m4.z; mc[3] = m4.w;
+        } else {
+          beta = st[0]; inv_r = st[1]; coef = st[2];
+#pragma unroll
+          for (int jj = 0; jj < N; ++jj) {
+            h[jj] = st[Lc::OFF_TH + jj];
+            hp[jj] = st[Lc::OFF_THP + jj];
+            mc[jj] = st[Lc::OFF_TM + i * N + jj];
+          }
+        }
         float gv[N], xv[N];
 #pragma unroll
         for (int jj = 0; jj < N; ++jj) {
@@ -1163,22 +1178,26 @@ __global__ void __launch_bounds__(GX_CW* N)
         for (int jj = 0; jj < N; ++jj) {
           gy = fmaf(hp[jj], gv[jj], gy);
           xa = fmaf(h[jj], xv[jj], xa);
-          mix = fmaf(m[jj * N + i], gv[jj], mix);
+          mix = fmaf(mc[jj], gv[jj], mix);
         }
         const float xi = xv[i];
         float acc = mix + h[i] * (gy * wc * inv_r - xa * beta);
         if (DYN) {
-          const float coef = st[2];
-          const float* dp = st + 4;
+          const float4* dp4 = reinterpret_cast<const float4*>(st + 4);
           float2 a2 = make_float2(0.f, 0.f);
           const float2 x2 = make_float2(xi, xi);
 #pragma unroll
-          for (int k = 0; k < NHP; k += 2) {
-            const float2 d2 = *reinterpret_cast<const float2*>(dp + k);
-            a2 = __ffma2_rn(d2, make_float2(phi[k], phi[k + 1]), a2);
-            float2 q2 = __ffma2_rn(d2, x2, make_float2(dph[k], dph[k + 1]));
+          for (int k = 0; k < NHP; k += 4) {
+            const float4 d4 = dp4[k / 4];
+            const float2 da = make_float2(d4.x, d4.y), db = make_float2(d4.z, d4.w);
+            a2 = __ffma2_rn(da, make_float2(phi[k], phi[k + 1]), a2);
+            a2 = __ffma2_rn(db, make_float2(phi[k + 2], phi[k + 3]), a2);
+            float2 q2 = __ffma2_rn(da, x2, make_float2(dph[k], dph[k + 1]));
             dph[k] = q2.x;
             dph[k + 1] = q2.y;
+            q2 = __ffma2_rn(db, x2, make_float2(dph[k + 2], dph[k + 3]));
+            dph[k + 2] = q2.x;
+            dph[k + 3] = q2.y;
           }
           acc += (a2.x + a2.y) + coef * xi;
         }
@@ -1196,6 +1215,240 @@ __global__ void __launch_bounds__(GX_CW* N)
       for (int k = 0; k < NH; ++k) dphi_part[((int64_t)split * NH + k) * nC + col] = dph[k];
     }
     if (i == 0) gw_part[(int64_t)split * C + c] = gwacc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward 3 for n = 4 (C % 64 == 0, aligned): tile-blocked grad_x.
+//   CTA = 64 channels x 4 streams = 256 columns (col = i*64 + cl), 256
+//   threads, a contiguous token range, TMA ring of 8-token stages.  Per stage:
+//   (E) one thread per (token, channel): the local terms of all 4 streams,
+//       sum_j M[j,i] g_j + h_i (gy w / r - x_agg beta) + coef x_i -> smem;
+//   (C1) thread tile 2 tokens x 4 columns: + sum_k d_p[t,k] phi[k,col]
+//       (phi slice resident in smem, d_p pre-duplicated into (d, d) pairs for
+//       FFMA2), then a 16-byte store of grad_x;
+//   (C2) thread tile 6 outputs x 4 columns: dphi[k,col] += d_p[t,k] x[t,col]
+//       accumulated in registers over the whole token range.
+//   Two CTA barriers per stage: arrival (which also frees the previous slot
+//   for refilling) and E -> C.
+//   Each scalar and each operand is loaded once per use site instead of once
+//   per output element.
+// ---------------------------------------------------------------------------
+constexpr int GX4_STAGES = 3;
+
+struct Gx4Cfg {
+  static constexpr int N = 4, CW = 64, COLS = N * CW, TOK = 8, TB = L<4>::TB;
+  static constexpr int TILE = TOK * COLS;                 // g or x floats per stage
+  static constexpr int STAGE = 2 * TILE + TOK * TB;
+  static constexpr uint32_t STAGE_BYTES = STAGE * 4;
+  static constexpr int NHP = L<4>::NHP;                   // 24
+  // ring | phi[NHP][COLS] | gxl[TOK][COLS] | dpk[NHP][TOK](d,d) | dpt[TOK][NHP](d,d) | gw[8][CW] | bars
+  static constexpr size_t SMEM = ((size_t)GX4_STAGES * STAGE + NHP * COLS + TOK * COLS +
+                                  4 * NHP * TOK + 8 * CW) * 4 + GX4_STAGES * 8 + 128;
+};
+
+template <bool DYN>
+__global__ void __launch_bounds__(256, 2)
+    grad_x4_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
+                   const __grid_constant__ CUtensorMap tmap, const float* __restrict__ w,
+                   const float* __restrict__ phi_pre, const float* __restrict__ phi_post,
+                   const float* __restrict__ phi_res, float* __restrict__ gx,
+                   float* __restrict__ dphi_part, float* __restrict__ gw_part, int64_t B,
+                   int64_t C, int ntiles, int nsplit) {
+  using F = Gx4Cfg;
+  using Lc = L<4>;
+  constexpr int N = 4, CW = F::CW, COLS = F::COLS, NHP = F::NHP, TB = F::TB;
+  extern __shared__ unsigned char smem_raw[];
+  float* ring = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  float* phiS = ring + GX4_STAGES * F::STAGE;
+  float* gxl = phiS + NHP * COLS;
+  float* dpk = gxl + F::TOK * COLS;        // [k][tok] pairs (d, d)
+  float* dpt = dpk + 2 * NHP * F::TOK;     // [tok][k] pairs (d, d)
+  float* gwS = dpt + 2 * NHP * F::TOK;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gwS + 8 * CW);
+
+  const int tid = threadIdx.x;
+  const int tile = blockIdx.x % ntiles;
+  const int split = blockIdx.x / ntiles;
+  const int64_t c0 = (int64_t)tile * CW;
+  const int64_t nC = (int64_t)N * C;
+  const int64_t tb0 = B * split / nsplit, tb1 = B * (split + 1) / nsplit;
+  const int nbatch = (int)((tb1 - tb0 + F::TOK - 1) / F::TOK);
+
+  if (tid == 0) {
+    prefetch_tmap(&gmap);
+    prefetch_tmap(&xmap);
+    prefetch_tmap(&tmap);
+    for (int st = 0; st < GX4_STAGES; ++st) mbar_init(&bars[st], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int j) {
+    const int slot = j % GX4_STAGES;
+    float* base = ring + slot * F::STAGE;
+    const int t0 = (int)(tb0 + (int64_t)j * F::TOK);
+    mbar_expect_tx(&bars[slot], F::STAGE_BYTES);
+    tma_load_2d(base, &gmap, (int)c0, t0 * N, &bars[slot]);
+    tma_load_2d(base + F::TILE, &xmap, (int)c0, t0 * N, &bars[slot]);
+    tma_load_2d(base + 2 * F::TILE, &tmap, 0, t0, &bars[slot]);
+  };
+  if (tid == 0)
+    for (int j = 0; j < GX4_STAGES && j < nbatch; ++j) issue(j);
+
+  // resident phi slice: phiS[k][i*64 + cl] = phi_k[i*C + c0 + cl]
+  if (DYN) {
+    for (int e = tid; e < NHP * COLS; e += blockDim.x) {
+      const int k = e / COLS, col = e % COLS;
+      const int i = col / CW, cl = col % CW;
+      phiS[e] = k < Lc::NH ? __ldg(phi_row(phi_pre, phi_post, phi_res, k, N, nC) + (int64_t)i * C + c0 + cl)
+                           : 0.f;
+    }
+  }
+  // (E) mapping: token te = tid / 32, channels ce and ce + 32
+  const int te = tid >> 5, ce = tid & 31;
+  const float w0 = __ldg(w + c0 + ce), w1 = __ldg(w + c0 + ce + 32);
+  float gw0 = 0.f, gw1 = 0.f;
+  // (C1) mapping: tokens 2*tg, 2*tg+1; columns 4*cg .. 4*cg+3
+  // (C2) mapping: outputs 6*tg .. 6*tg+5; columns 4*cg .. 4*cg+3
+  const int tg = tid >> 6, cg = tid & 63;
+  const int ci = (4 * cg) / CW, ccl = (4 * cg) % CW;   // stream and channel of the column quad
+  float dph[6][4];
+#pragma unroll
+  for (int a = 0; a < 6; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) dph[a][b] = 0.f;
+  __syncthreads();
+
+  bool failed = false;
+  for (int j = 0; j < nbatch; ++j) {
+    const int slot = j % GX4_STAGES;
+    const bool ok = mbar_wait(&bars[slot], (uint32_t)((j / GX4_STAGES) & 1));
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    // every thread is past stage j-1: its slot can be refilled
+    if (tid == 0 && j >= 1 && j - 1 + GX4_STAGES < nbatch) issue(j - 1 + GX4_STAGES);
+    const float* gs = ring + slot * F::STAGE;
+    const float* xs = gs + F::TILE;
+    const float* ts = xs + F::TILE;
+    const int64_t t0 = tb0 + (int64_t)j * F::TOK;
+    const int nt = (int)((tb1 - t0) < F::TOK ? (tb1 - t0) : F::TOK);
+
+    // d_p of the stage, duplicated into (d, d) pairs for FFMA2, in both orders
+    if (DYN && tid < NHP * F::TOK) {
+      const int tt = tid / NHP, k = tid % NHP;
+      const float d = ts[tt * TB + 4 + k];
+      *reinterpret_cast<float2*>(dpk + 2 * (k * F::TOK + tt)) = make_float2(d, d);
+      *reinterpret_cast<float2*>(dpt + 2 * (tt * NHP + k)) = make_float2(d, d);
+    }
+    // (E) local terms, all 4 streams of channels ce and ce+32 of token te
+    if (te < nt) {
+      const float* st = ts + te * TB;
+      const float4 s0 = *reinterpret_cast<const float4*>(st);
+      const float4 h4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TH);
+      const float4 q4 = *reinterpret_cast<const float4*>(st + Lc::OFF_THP);
+      const float h[4] = {h4.x, h4.y, h4.z, h4.w};
+      const float hq[4] = {q4.x, q4.y, q4.z, q4.w};
+      float mt[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 m4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TM + 4 * i);
+        mt[i][0] = m4.x; mt[i][1] = m4.y; mt[i][2] = m4.z; mt[i][3] = m4.w;
+      }
+      const float beta = s0.x, inv_r = s0.y, coef = DYN ? s0.z : 0.f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int cl = ce + 32 * half;
+        float gv[4], xv[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          gv[jj] = gs[(te * 4 + jj) * CW + cl];
+          xv[jj] = xs[(te * 4 + jj) * CW + cl];
+        }
+        float gy = 0.f, xa = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) { gy = fmaf(hq[jj], gv[jj], gy); xa = fmaf(h[jj], xv[jj], xa); }
+        const float wc = half ? w1 : w0;
+        const float agg = gy * wc * inv_r - xa * beta;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float mix = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) mix = fmaf(mt[i][jj], gv[jj], mix);
+          gxl[te * COLS + i * CW + cl] = mix + h[i] * agg + coef * xv[i];
+        }
+        const float gwv = gy * xa * inv_r;
+        if (half) gw1 += gwv; else gw0 += gwv;
+      }
+    }
+    __syncthreads();
+
+    // (C1) grad_x = local + d_p . phi for tokens 2tg, 2tg+1 and columns 4cg..4cg+3
+    {
+      const int ta = 2 * tg;
+      float4 acc0 = *reinterpret_cast<const float4*>(gxl + ta * COLS + 4 * cg);
+      float4 acc1 = *reinterpret_cast<const float4*>(gxl + (ta + 1) * COLS + 4 * cg);
+      if (DYN) {
+        float2 a0l = make_float2(acc0.x, acc0.y), a0h = make_float2(acc0.z, acc0.w);
+        float2 a1l = make_float2(acc1.x, acc1.y), a1h = make_float2(acc1.z, acc1.w);
+#pragma unroll
+        for (int k = 0; k < NHP; ++k) {
+          const float4 d = *reinterpret_cast<const float4*>(dpk + 2 * (k * F::TOK + ta));
+          const float4 p = *reinterpret_cast<const float4*>(phiS + k * COLS + 4 * cg);
+          const float2 pl = make_float2(p.x, p.y), ph = make_float2(p.z, p.w);
+          const float2 d0 = make_float2(d.x, d.y), d1 = make_float2(d.z, d.w);
+          a0l = __ffma2_rn(d0, pl, a0l);
+          a0h = __ffma2_rn(d0, ph, a0h);
+          a1l = __ffma2_rn(d1, pl, a1l);
+          a1h = __ffma2_rn(d1, ph, a1h);
+        }
+        acc0 = make_float4(a0l.x, a0l.y, a0h.x, a0h.y);
+        acc1 = make_float4(a1l.x, a1l.y, a1h.x, a1h.y);
+      }
+      float* dst = gx + (t0 + ta) * nC + (int64_t)ci * C + c0 + ccl;
+      if (ta < nt) __stcs(reinterpret_cast<float4*>(dst), acc0);
+      if (ta + 1 < nt) __stcs(reinterpret_cast<float4*>(dst + nC), acc1);
+    }
+    // (C2) dphi[6tg.., 4cg..] += d_p[t, k] x[t, col]
+    if (DYN) {
+      for (int tt = 0; tt < nt; ++tt) {
+        const float4 x4 = *reinterpret_cast<const float4*>(xs + (tt * 4 + ci) * CW + ccl);
+        const float2 xl = make_float2(x4.x, x4.y), xh = make_float2(x4.z, x4.w);
+        const float4* dp = reinterpret_cast<const float4*>(dpt + 2 * (tt * NHP + 6 * tg));
+#pragma unroll
+        for (int a2 = 0; a2 < 3; ++a2) {
+          const float4 d = dp[a2];
+          const float2 da = make_float2(d.x, d.y), db = make_float2(d.z, d.w);
+          float2 r;
+          r = __ffma2_rn(da, xl, make_float2(dph[2 * a2][0], dph[2 * a2][1]));
+          dph[2 * a2][0] = r.x; dph[2 * a2][1] = r.y;
+          r = __ffma2_rn(da, xh, make_float2(dph[2 * a2][2], dph[2 * a2][3]));
+          dph[2 * a2][2] = r.x; dph[2 * a2][3] = r.y;
+          r = __ffma2_rn(db, xl, make_float2(dph[2 * a2 + 1][0], dph[2 * a2 + 1][1]));
+          dph[2 * a2 + 1][0] = r.x; dph[2 * a2 + 1][1] = r.y;
+          r = __ffma2_rn(db, xh, make_float2(dph[2 * a2 + 1][2], dph[2 * a2 + 1][3]));
+          dph[2 * a2 + 1][2] = r.x; dph[2 * a2 + 1][3] = r.y;
+        }
+      }
+    }
+  }
+  if (failed) return;
+  if (DYN) {
+#pragma unroll
+    for (int a = 0; a < 6; ++a) {
+      const int k = 6 * tg + a;
+      if (k < Lc::NH)
+        *reinterpret_cast<float4*>(dphi_part + ((int64_t)split * Lc::NH + k) * nC + (int64_t)ci * C + c0 + ccl) =
+            make_float4(dph[a][0], dph[a][1], dph[a][2], dph[a][3]);
+    }
+  }
+  // grad_w: reduce the 8 token lanes that share a channel (fixed order)
+  gwS[te * CW + ce] = gw0;
+  gwS[te * CW + ce + 32] = gw1;
+  __syncthreads();
+  if (tid < CW) {
+    float sacc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sacc += gwS[k * CW + tid];
+    gw_part[(int64_t)split * C + c0 + tid] = sacc;
   }
 }
 
@@ -1401,6 +1654,21 @@ bool launch_grad_x_tma(const float* g, const float* x, const float* w, const flo
   if constexpr (N > 4) {
     return false;
   } else {
+    if constexpr (N == 4) {
+      using F = Gx4Cfg;
+      CUtensorMap gm, xm, tm;
+      if (C % 64 == 0 && aligned16(g) && aligned16(x) && aligned16(tokb) && aligned16(gx) &&
+          (!DYN || aligned16(dphi)) &&
+          make_tmap_2d_f32(&gm, g, (uint64_t)B * N, C, C, F::TOK * N, F::CW) &&
+          make_tmap_2d_f32(&xm, x, (uint64_t)B * N, C, C, F::TOK * N, F::CW) &&
+          make_tmap_2d_f32(&tm, tokb, B, L<N>::TB, L<N>::TB, F::TOK, L<N>::TB)) {
+        cudaFuncSetAttribute(grad_x4_kernel<DYN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)F::SMEM);
+        { ProfScope _ps("grad_x", s); grad_x4_kernel<DYN><<<(unsigned)(p.ntiles * p.nsplit), 256, F::SMEM, s>>>(
+            gm, xm, tm, w, pp, pq, pr, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
+        return true;
+      }
+    }
     using Cf = GxtCfg<N>;
     CUtensorMap gmap, xmap, tmap;
     if (C % 4 != 0 || !aligned16(g) || !aligned16(x) || !aligned16(tokb)) return false;
@@ -1448,7 +1716,7 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
       { ProfScope _ps("phi_transpose", s); phi_transpose_kernel<N><<<grid_1d(C * PT::PROW, 256, 2048), 256, 0, s>>>(pp, pq, pr, phiT, C); }
       cudaFuncSetAttribute(proj_stats_tma_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)PT::SMEM);
-      { ProfScope _ps("proj_stats", s); proj_stats_tma_kernel<N><<<dim3((unsigned)p.tiles, (unsigned)p.ks), 256, PT::SMEM, s>>>(
+      { ProfScope _ps("proj_stats", s); proj_stats_tma_kernel<N><<<dim3((unsigned)p.tiles, (unsigned)p.ks), PJT_THREADS, PT::SMEM, s>>>(
           xmap, pmap, ppart, gpart, B, C, p.cps); }
       done = true;
     }
