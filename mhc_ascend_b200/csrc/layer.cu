@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(PJT_THREADS, 1)
   }
   for (int k = 0; k < nchunks; ++k) {
     const int slot = k % PJT_STAGES;
-    const bool ok = mbar_wait(&bars[slot], (uint32_t)((k / PJT_STAGES) & 1));
+    const bool ok = threadIdx.x == 0 ? mbar_wait(&bars[slot], (uint32_t)((k / PJT_STAGES) & 1)) : true;
     if (__syncthreads_or(!ok)) return;
     const float* xs = ring + slot * (P::XF + P::PF);
     const float* row = xs + P::XF + lane * PROW;
@@ -1135,7 +1135,7 @@ __global__ void __launch_bounds__(GX_CW* N)
 
   for (int j = 0; j < nbatch; ++j) {
     const int slot = j % GXT_STAGES;
-    const bool ok = mbar_wait(&bars[slot], (uint32_t)((j / GXT_STAGES) & 1));
+    const bool ok = threadIdx.x == 0 ? mbar_wait(&bars[slot], (uint32_t)((j / GXT_STAGES) & 1)) : true;
     if (__syncthreads_or(!ok)) { failed = true; break; }
     const float* gs = ring + slot * Cf::STAGE_FLOATS;
     const float* xs = gs + Cf::TILE_FLOATS;
@@ -1219,32 +1219,63 @@ __global__ void __launch_bounds__(GX_CW* N)
 }
 
 // ---------------------------------------------------------------------------
-// Backward 3 for n = 4 (C % 64 == 0, aligned): tile-blocked grad_x.
-//   CTA = 64 channels x 4 streams = 256 columns (col = i*64 + cl), 256
-//   threads, a contiguous token range, TMA ring of 8-token stages.  Per stage:
-//   (E) one thread per (token, channel): the local terms of all 4 streams,
-//       sum_j M[j,i] g_j + h_i (gy w / r - x_agg beta) + coef x_i -> smem;
-//   (C1) thread tile 2 tokens x 4 columns: + sum_k d_p[t,k] phi[k,col]
-//       (phi slice resident in smem, d_p pre-duplicated into (d, d) pairs for
-//       FFMA2), then a 16-byte store of grad_x;
-//   (C2) thread tile 6 outputs x 4 columns: dphi[k,col] += d_p[t,k] x[t,col]
-//       accumulated in registers over the whole token range.
-//   Two CTA barriers per stage: arrival (which also frees the previous slot
-//   for refilling) and E -> C.
-//   Each scalar and each operand is loaded once per use site instead of once
-//   per output element.
+// 3xTF32 tensor-core helpers (m16n8k8, fp32 accumulate).  x = hi + lo with
+// hi = tf32(x) (round to nearest) and lo = tf32(x - hi); a product is taken
+// as hi*hi + hi*lo + lo*hi, which keeps ~fp32 accuracy (the dropped lo*lo
+// term is below 2^-22 relative).
 // ---------------------------------------------------------------------------
-constexpr int GX4_STAGES = 3;
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_rna(x);
+  lo = tf32_rna(x - __uint_as_float(hi));
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// d += (a_hi + a_lo)(b_hi + b_lo), small terms first
+__device__ __forceinline__ void mma_3xtf32(float (&d)[4], const uint32_t (&ah)[4],
+                                           const uint32_t (&al)[4], uint32_t bh0, uint32_t bh1,
+                                           uint32_t bl0, uint32_t bl1) {
+  mma_tf32(d, al, bh0, bh1);
+  mma_tf32(d, ah, bl0, bl1);
+  mma_tf32(d, ah, bh0, bh1);
+}
+
+// ---------------------------------------------------------------------------
+// Backward 3 for n = 4 (C % 64 == 0, aligned): grad_x with tensor-core
+// contractions.
+//   CTA = 64 channels x 4 streams = 256 columns (col = i*64 + cl), 256
+//   threads (8 warps, warp w owns columns 32w..32w+31), a contiguous token
+//   range, TMA ring of 16-token stages.  Per stage:
+//   (E) one thread per (token, channel): local terms of all 4 streams,
+//       sum_j M[j,i] g_j + h_i (gy w / r - x_agg beta) + coef x_i -> smem,
+//       and the stage's d_p split into tf32 hi/lo -> smem;
+//   (C1) grad_x[tok, col] = local + (D_p[16 x 24] . Phi[24 x col]) with
+//       mma.sync m16n8k8 3xTF32; the Phi fragments of the warp's columns stay
+//       in registers for the whole token range;
+//   (C2) dphi^T[col x k] += X^T[col x 16 tok] . D_p[16 tok x 24], same
+//       instruction, accumulators persistent in registers.
+// ---------------------------------------------------------------------------
+constexpr int GX4_STAGES = 2;
 
 struct Gx4Cfg {
-  static constexpr int N = 4, CW = 64, COLS = N * CW, TOK = 8, TB = L<4>::TB;
+  static constexpr int N = 4, CW = 64, COLS = N * CW, TOK = 16, TB = L<4>::TB;
   static constexpr int TILE = TOK * COLS;                 // g or x floats per stage
   static constexpr int STAGE = 2 * TILE + TOK * TB;
   static constexpr uint32_t STAGE_BYTES = STAGE * 4;
   static constexpr int NHP = L<4>::NHP;                   // 24
-  // ring | phi[NHP][COLS] | gxl[TOK][COLS] | dpk[NHP][TOK](d,d) | dpt[TOK][NHP](d,d) | gw[8][CW] | bars
-  static constexpr size_t SMEM = ((size_t)GX4_STAGES * STAGE + NHP * COLS + TOK * COLS +
-                                  4 * NHP * TOK + 8 * CW) * 4 + GX4_STAGES * 8 + 128;
+  // ring | gxl[TOK][COLS] | dph[TOK][NHP] | dpl[TOK][NHP] | gw[TOK/2][CW] | bars
+  static constexpr size_t SMEM = ((size_t)GX4_STAGES * STAGE + TOK * COLS + 2 * TOK * NHP +
+                                  (TOK / 2) * CW) * 4 + GX4_STAGES * 8 + 128;
 };
 
 template <bool DYN>
@@ -1257,23 +1288,23 @@ __global__ void __launch_bounds__(256, 2)
                    int64_t C, int ntiles, int nsplit) {
   using F = Gx4Cfg;
   using Lc = L<4>;
-  constexpr int N = 4, CW = F::CW, COLS = F::COLS, NHP = F::NHP, TB = F::TB;
+  constexpr int N = 4, CW = F::CW, COLS = F::COLS, NHP = F::NHP, TB = F::TB, TOK = F::TOK;
   extern __shared__ unsigned char smem_raw[];
   float* ring = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  float* phiS = ring + GX4_STAGES * F::STAGE;
-  float* gxl = phiS + NHP * COLS;
-  float* dpk = gxl + F::TOK * COLS;        // [k][tok] pairs (d, d)
-  float* dpt = dpk + 2 * NHP * F::TOK;     // [tok][k] pairs (d, d)
-  float* gwS = dpt + 2 * NHP * F::TOK;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(gwS + 8 * CW);
+  float* gxl = ring + GX4_STAGES * F::STAGE;
+  uint32_t* dph_s = reinterpret_cast<uint32_t*>(gxl + TOK * COLS);   // [tok][k] hi
+  uint32_t* dpl_s = dph_s + TOK * NHP;                               // [tok][k] lo
+  float* gwS = reinterpret_cast<float*>(dpl_s + TOK * NHP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gwS + (TOK / 2) * CW);
 
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g8 = lane >> 2, t4 = lane & 3;
   const int tile = blockIdx.x % ntiles;
   const int split = blockIdx.x / ntiles;
   const int64_t c0 = (int64_t)tile * CW;
   const int64_t nC = (int64_t)N * C;
   const int64_t tb0 = B * split / nsplit, tb1 = B * (split + 1) / nsplit;
-  const int nbatch = (int)((tb1 - tb0 + F::TOK - 1) / F::TOK);
+  const int nbatch = (int)((tb1 - tb0 + TOK - 1) / TOK);
 
   if (tid == 0) {
     prefetch_tmap(&gmap);
@@ -1286,7 +1317,7 @@ __global__ void __launch_bounds__(256, 2)
   auto issue = [&](int j) {
     const int slot = j % GX4_STAGES;
     float* base = ring + slot * F::STAGE;
-    const int t0 = (int)(tb0 + (int64_t)j * F::TOK);
+    const int t0 = (int)(tb0 + (int64_t)j * TOK);
     mbar_expect_tx(&bars[slot], F::STAGE_BYTES);
     tma_load_2d(base, &gmap, (int)c0, t0 * N, &bars[slot]);
     tma_load_2d(base + F::TILE, &xmap, (int)c0, t0 * N, &bars[slot]);
@@ -1295,154 +1326,175 @@ __global__ void __launch_bounds__(256, 2)
   if (tid == 0)
     for (int j = 0; j < GX4_STAGES && j < nbatch; ++j) issue(j);
 
-  // resident phi slice: phiS[k][i*64 + cl] = phi_k[i*C + c0 + cl]
-  if (DYN) {
-    for (int e = tid; e < NHP * COLS; e += blockDim.x) {
-      const int k = e / COLS, col = e % COLS;
-      const int i = col / CW, cl = col % CW;
-      phiS[e] = k < Lc::NH ? __ldg(phi_row(phi_pre, phi_post, phi_res, k, N, nC) + (int64_t)i * C + c0 + cl)
-                           : 0.f;
-    }
-  }
-  // (E) mapping: token te = tid / 32, channels ce and ce + 32
-  const int te = tid >> 5, ce = tid & 31;
+  // warp columns: stream wi, channels wc0 .. wc0+31 of the tile
+  const int wi = warp >> 1, wc0 = (warp & 1) * 32;
+  // (C1) B fragments: Phi[k][col] for n-tile nt (8 columns), k-step ks
+  uint32_t bph[4][3][2], bpl[4][3][2];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int ks = 0; ks < 3; ++ks)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int k = 8 * ks + t4 + 4 * h;
+        float v = 0.f;
+        if (DYN && k < Lc::NH)
+          v = __ldg(phi_row(phi_pre, phi_post, phi_res, k, N, nC) + (int64_t)wi * C + c0 + wc0 + 8 * nt + g8);
+        split_tf32(v, bph[nt][ks][h], bpl[nt][ks][h]);
+      }
+  // (C2) accumulators: dphi^T rows = columns (2 m-tiles of 16), cols = k (3 n-tiles of 8)
+  float acc2[2][3][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc2[mt][nt][e] = 0.f;
+  // (E) mapping: tokens ee and ee + 8, channels ce and ce + 32
+  const int ee = tid >> 5, ce = tid & 31;
   const float w0 = __ldg(w + c0 + ce), w1 = __ldg(w + c0 + ce + 32);
   float gw0 = 0.f, gw1 = 0.f;
-  // (C1) mapping: tokens 2*tg, 2*tg+1; columns 4*cg .. 4*cg+3
-  // (C2) mapping: outputs 6*tg .. 6*tg+5; columns 4*cg .. 4*cg+3
-  const int tg = tid >> 6, cg = tid & 63;
-  const int ci = (4 * cg) / CW, ccl = (4 * cg) % CW;   // stream and channel of the column quad
-  float dph[6][4];
-#pragma unroll
-  for (int a = 0; a < 6; ++a)
-#pragma unroll
-    for (int b = 0; b < 4; ++b) dph[a][b] = 0.f;
-  __syncthreads();
 
   bool failed = false;
   for (int j = 0; j < nbatch; ++j) {
     const int slot = j % GX4_STAGES;
-    const bool ok = mbar_wait(&bars[slot], (uint32_t)((j / GX4_STAGES) & 1));
+    // one thread polls the barrier; the others park at the CTA barrier
+    const bool ok = tid == 0 ? mbar_wait(&bars[slot], (uint32_t)((j / GX4_STAGES) & 1)) : true;
     if (__syncthreads_or(!ok)) { failed = true; break; }
     // every thread is past stage j-1: its slot can be refilled
     if (tid == 0 && j >= 1 && j - 1 + GX4_STAGES < nbatch) issue(j - 1 + GX4_STAGES);
     const float* gs = ring + slot * F::STAGE;
     const float* xs = gs + F::TILE;
     const float* ts = xs + F::TILE;
-    const int64_t t0 = tb0 + (int64_t)j * F::TOK;
-    const int nt = (int)((tb1 - t0) < F::TOK ? (tb1 - t0) : F::TOK);
+    const int64_t t0 = tb0 + (int64_t)j * TOK;
+    const int nt_ = (int)((tb1 - t0) < TOK ? (tb1 - t0) : TOK);
 
-    // d_p of the stage, duplicated into (d, d) pairs for FFMA2, in both orders
-    if (DYN && tid < NHP * F::TOK) {
-      const int tt = tid / NHP, k = tid % NHP;
-      const float d = ts[tt * TB + 4 + k];
-      *reinterpret_cast<float2*>(dpk + 2 * (k * F::TOK + tt)) = make_float2(d, d);
-      *reinterpret_cast<float2*>(dpt + 2 * (tt * NHP + k)) = make_float2(d, d);
-    }
-    // (E) local terms, all 4 streams of channels ce and ce+32 of token te
-    if (te < nt) {
-      const float* st = ts + te * TB;
-      const float4 s0 = *reinterpret_cast<const float4*>(st);
-      const float4 h4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TH);
-      const float4 q4 = *reinterpret_cast<const float4*>(st + Lc::OFF_THP);
-      const float h[4] = {h4.x, h4.y, h4.z, h4.w};
-      const float hq[4] = {q4.x, q4.y, q4.z, q4.w};
-      float mt[4][4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 m4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TM + 4 * i);
-        mt[i][0] = m4.x; mt[i][1] = m4.y; mt[i][2] = m4.z; mt[i][3] = m4.w;
+    // d_p of the stage in tf32 hi/lo; tokens beyond the range contribute 0
+    if (DYN) {
+      for (int e = tid; e < TOK * NHP; e += 256) {
+        const int tt = e / NHP, k = e % NHP;
+        const float d = tt < nt_ ? ts[tt * TB + 4 + k] : 0.f;
+        split_tf32(d, dph_s[e], dpl_s[e]);
       }
-      const float beta = s0.x, inv_r = s0.y, coef = DYN ? s0.z : 0.f;
+    }
+    // (E) local terms
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int cl = ce + 32 * half;
-        float gv[4], xv[4];
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          gv[jj] = gs[(te * 4 + jj) * CW + cl];
-          xv[jj] = xs[(te * 4 + jj) * CW + cl];
-        }
-        float gy = 0.f, xa = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) { gy = fmaf(hq[jj], gv[jj], gy); xa = fmaf(h[jj], xv[jj], xa); }
-        const float wc = half ? w1 : w0;
-        const float agg = gy * wc * inv_r - xa * beta;
+    for (int r = 0; r < 2; ++r) {
+      const int te = ee + 8 * r;
+      if (te < nt_) {
+        const float* st = ts + te * TB;
+        const float4 s0 = *reinterpret_cast<const float4*>(st);
+        const float4 h4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TH);
+        const float4 q4 = *reinterpret_cast<const float4*>(st + Lc::OFF_THP);
+        const float h[4] = {h4.x, h4.y, h4.z, h4.w};
+        const float hq[4] = {q4.x, q4.y, q4.z, q4.w};
+        float mt[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          float mix = 0.f;
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) mix = fmaf(mt[i][jj], gv[jj], mix);
-          gxl[te * COLS + i * CW + cl] = mix + h[i] * agg + coef * xv[i];
+          const float4 m4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TM + 4 * i);
+          mt[i][0] = m4.x; mt[i][1] = m4.y; mt[i][2] = m4.z; mt[i][3] = m4.w;
         }
-        const float gwv = gy * xa * inv_r;
-        if (half) gw1 += gwv; else gw0 += gwv;
+        const float beta = s0.x, inv_r = s0.y, coef = DYN ? s0.z : 0.f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int cl = ce + 32 * half;
+          float gv[4], xv[4];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            gv[jj] = gs[(te * 4 + jj) * CW + cl];
+            xv[jj] = xs[(te * 4 + jj) * CW + cl];
+          }
+          float gy = 0.f, xa = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) { gy = fmaf(hq[jj], gv[jj], gy); xa = fmaf(h[jj], xv[jj], xa); }
+          const float wc = half ? w1 : w0;
+          const float agg = gy * wc * inv_r - xa * beta;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float mix = 0.f;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) mix = fmaf(mt[i][jj], gv[jj], mix);
+            gxl[te * COLS + i * CW + cl] = mix + h[i] * agg + coef * xv[i];
+          }
+          const float gwv = gy * xa * inv_r;
+          if (half) gw1 += gwv; else gw0 += gwv;
+        }
       }
     }
     __syncthreads();
 
-    // (C1) grad_x = local + d_p . phi for tokens 2tg, 2tg+1 and columns 4cg..4cg+3
-    {
-      const int ta = 2 * tg;
-      float4 acc0 = *reinterpret_cast<const float4*>(gxl + ta * COLS + 4 * cg);
-      float4 acc1 = *reinterpret_cast<const float4*>(gxl + (ta + 1) * COLS + 4 * cg);
-      if (DYN) {
-        float2 a0l = make_float2(acc0.x, acc0.y), a0h = make_float2(acc0.z, acc0.w);
-        float2 a1l = make_float2(acc1.x, acc1.y), a1h = make_float2(acc1.z, acc1.w);
-#pragma unroll
-        for (int k = 0; k < NHP; ++k) {
-          const float4 d = *reinterpret_cast<const float4*>(dpk + 2 * (k * F::TOK + ta));
-          const float4 p = *reinterpret_cast<const float4*>(phiS + k * COLS + 4 * cg);
-          const float2 pl = make_float2(p.x, p.y), ph = make_float2(p.z, p.w);
-          const float2 d0 = make_float2(d.x, d.y), d1 = make_float2(d.z, d.w);
-          a0l = __ffma2_rn(d0, pl, a0l);
-          a0h = __ffma2_rn(d0, ph, a0h);
-          a1l = __ffma2_rn(d1, pl, a1l);
-          a1h = __ffma2_rn(d1, ph, a1h);
-        }
-        acc0 = make_float4(a0l.x, a0l.y, a0h.x, a0h.y);
-        acc1 = make_float4(a1l.x, a1l.y, a1h.x, a1h.y);
-      }
-      float* dst = gx + (t0 + ta) * nC + (int64_t)ci * C + c0 + ccl;
-      if (ta < nt) __stcs(reinterpret_cast<float4*>(dst), acc0);
-      if (ta + 1 < nt) __stcs(reinterpret_cast<float4*>(dst + nC), acc1);
-    }
-    // (C2) dphi[6tg.., 4cg..] += d_p[t, k] x[t, col]
+    // (C1) grad_x: 4 n-tiles of 8 columns, rows = the 16 tokens
+    uint32_t ah[3][4], al[3][4];
     if (DYN) {
-      for (int tt = 0; tt < nt; ++tt) {
-        const float4 x4 = *reinterpret_cast<const float4*>(xs + (tt * 4 + ci) * CW + ccl);
-        const float2 xl = make_float2(x4.x, x4.y), xh = make_float2(x4.z, x4.w);
-        const float4* dp = reinterpret_cast<const float4*>(dpt + 2 * (tt * NHP + 6 * tg));
 #pragma unroll
-        for (int a2 = 0; a2 < 3; ++a2) {
-          const float4 d = dp[a2];
-          const float2 da = make_float2(d.x, d.y), db = make_float2(d.z, d.w);
-          float2 r;
-          r = __ffma2_rn(da, xl, make_float2(dph[2 * a2][0], dph[2 * a2][1]));
-          dph[2 * a2][0] = r.x; dph[2 * a2][1] = r.y;
-          r = __ffma2_rn(da, xh, make_float2(dph[2 * a2][2], dph[2 * a2][3]));
-          dph[2 * a2][2] = r.x; dph[2 * a2][3] = r.y;
-          r = __ffma2_rn(db, xl, make_float2(dph[2 * a2 + 1][0], dph[2 * a2 + 1][1]));
-          dph[2 * a2 + 1][0] = r.x; dph[2 * a2 + 1][1] = r.y;
-          r = __ffma2_rn(db, xh, make_float2(dph[2 * a2 + 1][2], dph[2 * a2 + 1][3]));
-          dph[2 * a2 + 1][2] = r.x; dph[2 * a2 + 1][3] = r.y;
+      for (int ks = 0; ks < 3; ++ks) {
+        const int k0 = 8 * ks + t4;
+        ah[ks][0] = dph_s[g8 * NHP + k0];       al[ks][0] = dpl_s[g8 * NHP + k0];
+        ah[ks][1] = dph_s[(g8 + 8) * NHP + k0]; al[ks][1] = dpl_s[(g8 + 8) * NHP + k0];
+        ah[ks][2] = dph_s[g8 * NHP + k0 + 4];   al[ks][2] = dpl_s[g8 * NHP + k0 + 4];
+        ah[ks][3] = dph_s[(g8 + 8) * NHP + k0 + 4]; al[ks][3] = dpl_s[(g8 + 8) * NHP + k0 + 4];
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int colw = wi * CW + wc0 + 8 * nt + 2 * t4;   // column in the tile
+      float d[4];
+      const float2 top = *reinterpret_cast<const float2*>(gxl + g8 * COLS + colw);
+      const float2 bot = *reinterpret_cast<const float2*>(gxl + (g8 + 8) * COLS + colw);
+      d[0] = top.x; d[1] = top.y; d[2] = bot.x; d[3] = bot.y;
+      if (DYN) {
+#pragma unroll
+        for (int ks = 0; ks < 3; ++ks)
+          mma_3xtf32(d, ah[ks], al[ks], bph[nt][ks][0], bph[nt][ks][1], bpl[nt][ks][0], bpl[nt][ks][1]);
+      }
+      float* dst = gx + (t0 + g8) * nC + (int64_t)wi * C + c0 + wc0 + 8 * nt + 2 * t4;
+      if (g8 < nt_) __stcs(reinterpret_cast<float2*>(dst), make_float2(d[0], d[1]));
+      if (g8 + 8 < nt_) __stcs(reinterpret_cast<float2*>(dst + 8 * nC), make_float2(d[2], d[3]));
+    }
+    // (C2) dphi^T += X^T . D_p over the 16 tokens (2 k-steps of 8 tokens)
+    if (DYN) {
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        const int tk = 8 * ks + t4;
+        uint32_t bh[3][2], bl[3][2];
+#pragma unroll
+        for (int nt = 0; nt < 3; ++nt) {
+          bh[nt][0] = dph_s[tk * NHP + 8 * nt + g8];       bl[nt][0] = dpl_s[tk * NHP + 8 * nt + g8];
+          bh[nt][1] = dph_s[(tk + 4) * NHP + 8 * nt + g8]; bl[nt][1] = dpl_s[(tk + 4) * NHP + 8 * nt + g8];
+        }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          const int cl = wc0 + 16 * mt + g8;   // channel of fragment row g8 (row g8+8 -> cl+8)
+          uint32_t xh[4], xl[4];
+          split_tf32(xs[(tk * 4 + wi) * CW + cl], xh[0], xl[0]);
+          split_tf32(xs[(tk * 4 + wi) * CW + cl + 8], xh[1], xl[1]);
+          split_tf32(xs[((tk + 4) * 4 + wi) * CW + cl], xh[2], xl[2]);
+          split_tf32(xs[((tk + 4) * 4 + wi) * CW + cl + 8], xh[3], xl[3]);
+#pragma unroll
+          for (int nt = 0; nt < 3; ++nt)
+            mma_3xtf32(acc2[mt][nt], xh, xl, bh[nt][0], bh[nt][1], bl[nt][0], bl[nt][1]);
         }
       }
     }
   }
   if (failed) return;
   if (DYN) {
+    // acc2[mt][nt]: rows = channels wc0+16mt+g8 (+8), cols = k 8nt+2t4 (+1)
 #pragma unroll
-    for (int a = 0; a < 6; ++a) {
-      const int k = 6 * tg + a;
-      if (k < Lc::NH)
-        *reinterpret_cast<float4*>(dphi_part + ((int64_t)split * Lc::NH + k) * nC + (int64_t)ci * C + c0 + ccl) =
-            make_float4(dph[a][0], dph[a][1], dph[a][2], dph[a][3]);
-    }
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = 8 * nt + 2 * t4 + (e & 1);
+          const int cl = wc0 + 16 * mt + g8 + (e >> 1) * 8;
+          if (k < Lc::NH)
+            dphi_part[((int64_t)split * Lc::NH + k) * nC + (int64_t)wi * C + c0 + cl] = acc2[mt][nt][e];
+        }
   }
   // grad_w: reduce the 8 token lanes that share a channel (fixed order)
-  gwS[te * CW + ce] = gw0;
-  gwS[te * CW + ce + 32] = gw1;
+  gwS[ee * CW + ce] = gw0;
+  gwS[ee * CW + ce + 32] = gw1;
   __syncthreads();
   if (tid < CW) {
     float sacc = 0.f;
