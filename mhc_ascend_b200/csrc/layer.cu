@@ -737,6 +737,7 @@ __global__ void __launch_bounds__(128, 4)
     if (VEC) {
       // float2 per stream: keeps the live load registers low enough for
       // 4 CTAs (16 warps) per SM next to the 42 fp64 accumulators.
+#pragma unroll 2
       for (int64_t q = threadIdx.x; q < C / 2; q += blockDim.x) {
         float2 g2[N], x2[N];
 #pragma unroll
@@ -1235,7 +1236,9 @@ __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) 
 }
 __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
-  asm volatile(
+  // not volatile: a pure function of its operands, so the compiler may
+  // interleave independent mma chains
+  asm(
       "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -1281,7 +1284,8 @@ struct Gx4Cfg {
 template <bool DYN>
 __global__ void __launch_bounds__(256, 2)
     grad_x4_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
-                   const __grid_constant__ CUtensorMap tmap, const float* __restrict__ w,
+                   const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap omap,
+                   const float* __restrict__ w,
                    const float* __restrict__ phi_pre, const float* __restrict__ phi_post,
                    const float* __restrict__ phi_res, float* __restrict__ gx,
                    float* __restrict__ dphi_part, float* __restrict__ gw_part, int64_t B,
@@ -1358,8 +1362,13 @@ __global__ void __launch_bounds__(256, 2)
   bool failed = false;
   for (int j = 0; j < nbatch; ++j) {
     const int slot = j % GX4_STAGES;
-    // one thread polls the barrier; the others park at the CTA barrier
-    const bool ok = tid == 0 ? mbar_wait(&bars[slot], (uint32_t)((j / GX4_STAGES) & 1)) : true;
+    // one thread polls the barrier (after the previous grad_x store has read
+    // gxl); the others park at the CTA barrier
+    bool ok = true;
+    if (tid == 0) {
+      bulk_wait_read0();
+      ok = mbar_wait(&bars[slot], (uint32_t)((j / GX4_STAGES) & 1));
+    }
     if (__syncthreads_or(!ok)) { failed = true; break; }
     // every thread is past stage j-1: its slot can be refilled
     if (tid == 0 && j >= 1 && j - 1 + GX4_STAGES < nbatch) issue(j - 1 + GX4_STAGES);
@@ -1435,21 +1444,47 @@ __global__ void __launch_bounds__(256, 2)
         ah[ks][3] = dph_s[(g8 + 8) * NHP + k0 + 4]; al[ks][3] = dpl_s[(g8 + 8) * NHP + k0 + 4];
       }
     }
+    float d1[4][4];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
       const int colw = wi * CW + wc0 + 8 * nt + 2 * t4;   // column in the tile
-      float d[4];
       const float2 top = *reinterpret_cast<const float2*>(gxl + g8 * COLS + colw);
       const float2 bot = *reinterpret_cast<const float2*>(gxl + (g8 + 8) * COLS + colw);
-      d[0] = top.x; d[1] = top.y; d[2] = bot.x; d[3] = bot.y;
-      if (DYN) {
+      d1[nt][0] = top.x; d1[nt][1] = top.y; d1[nt][2] = bot.x; d1[nt][3] = bot.y;
+    }
+    if (DYN) {
+      // k-step outer, n-tile inner: consecutive mma are independent
 #pragma unroll
-        for (int ks = 0; ks < 3; ++ks)
-          mma_3xtf32(d, ah[ks], al[ks], bph[nt][ks][0], bph[nt][ks][1], bpl[nt][ks][0], bpl[nt][ks][1]);
+      for (int ks = 0; ks < 3; ++ks) {
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) mma_tf32(d1[nt], al[ks], bph[nt][ks][0], bph[nt][ks][1]);
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) mma_tf32(d1[nt], ah[ks], bpl[nt][ks][0], bpl[nt][ks][1]);
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) mma_tf32(d1[nt], ah[ks], bph[nt][ks][0], bph[nt][ks][1]);
       }
-      float* dst = gx + (t0 + g8) * nC + (int64_t)wi * C + c0 + wc0 + 8 * nt + 2 * t4;
-      if (g8 < nt_) __stcs(reinterpret_cast<float2*>(dst), make_float2(d[0], d[1]));
-      if (g8 + 8 < nt_) __stcs(reinterpret_cast<float2*>(dst + 8 * nC), make_float2(d[2], d[3]));
+    }
+    if (nt_ == TOK) {
+      // full stage: results back into gxl (same layout as the grad_x box), one TMA store
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int colw = wi * CW + wc0 + 8 * nt + 2 * t4;
+        *reinterpret_cast<float2*>(gxl + g8 * COLS + colw) = make_float2(d1[nt][0], d1[nt][1]);
+        *reinterpret_cast<float2*>(gxl + (g8 + 8) * COLS + colw) = make_float2(d1[nt][2], d1[nt][3]);
+      }
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tma_store_2d(&omap, gxl, (int)c0, (int)(t0 * N));
+        bulk_commit();
+      }
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        float* dst = gx + (t0 + g8) * nC + (int64_t)wi * C + c0 + wc0 + 8 * nt + 2 * t4;
+        if (g8 < nt_) __stcs(reinterpret_cast<float2*>(dst), make_float2(d1[nt][0], d1[nt][1]));
+        if (g8 + 8 < nt_) __stcs(reinterpret_cast<float2*>(dst + 8 * nC), make_float2(d1[nt][2], d1[nt][3]));
+      }
     }
     // (C2) dphi^T += X^T . D_p over the 16 tokens (2 k-steps of 8 tokens)
     if (DYN) {
@@ -1462,21 +1497,31 @@ __global__ void __launch_bounds__(256, 2)
           bh[nt][0] = dph_s[tk * NHP + 8 * nt + g8];       bl[nt][0] = dpl_s[tk * NHP + 8 * nt + g8];
           bh[nt][1] = dph_s[(tk + 4) * NHP + 8 * nt + g8]; bl[nt][1] = dpl_s[(tk + 4) * NHP + 8 * nt + g8];
         }
+        uint32_t xh[2][4], xl[2][4];
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
           const int cl = wc0 + 16 * mt + g8;   // channel of fragment row g8 (row g8+8 -> cl+8)
-          uint32_t xh[4], xl[4];
-          split_tf32(xs[(tk * 4 + wi) * CW + cl], xh[0], xl[0]);
-          split_tf32(xs[(tk * 4 + wi) * CW + cl + 8], xh[1], xl[1]);
-          split_tf32(xs[((tk + 4) * 4 + wi) * CW + cl], xh[2], xl[2]);
-          split_tf32(xs[((tk + 4) * 4 + wi) * CW + cl + 8], xh[3], xl[3]);
-#pragma unroll
-          for (int nt = 0; nt < 3; ++nt)
-            mma_3xtf32(acc2[mt][nt], xh, xl, bh[nt][0], bh[nt][1], bl[nt][0], bl[nt][1]);
+          split_tf32(xs[(tk * 4 + wi) * CW + cl], xh[mt][0], xl[mt][0]);
+          split_tf32(xs[(tk * 4 + wi) * CW + cl + 8], xh[mt][1], xl[mt][1]);
+          split_tf32(xs[((tk + 4) * 4 + wi) * CW + cl], xh[mt][2], xl[mt][2]);
+          split_tf32(xs[((tk + 4) * 4 + wi) * CW + cl + 8], xh[mt][3], xl[mt][3]);
         }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 3; ++nt) mma_tf32(acc2[mt][nt], xl[mt], bh[nt][0], bh[nt][1]);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 3; ++nt) mma_tf32(acc2[mt][nt], xh[mt], bl[nt][0], bl[nt][1]);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 3; ++nt) mma_tf32(acc2[mt][nt], xh[mt], bh[nt][0], bh[nt][1]);
       }
     }
   }
+  if (tid == 0) bulk_wait0();  // grad_x stores complete before the CTA's smem goes away
   if (failed) return;
   if (DYN) {
     // acc2[mt][nt]: rows = channels wc0+16mt+g8 (+8), cols = k 8nt+2t4 (+1)
@@ -1502,6 +1547,590 @@ __global__ void __launch_bounds__(256, 2)
     for (int k = 0; k < 8; ++k) sacc += gwS[k * CW + tid];
     gw_part[(int64_t)split * C + c0 + tid] = sacc;
   }
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 (UMMA) helpers: kind::tf32, operands in shared memory in the
+// K-major "interleaved" (no swizzle) layout -- 8 rows x 16 bytes core
+// matrices -- accumulators in tensor memory.
+// ---------------------------------------------------------------------------
+// byte offset of element (row r, k) in an R-row K-major operand
+__host__ __device__ __forceinline__ uint32_t umma_kmaj_off(int r, int k, int R) {
+  return (uint32_t)((k >> 2) * (R >> 3) * 128 + (r >> 3) * 128 + (r & 7) * 16 + (k & 3) * 4);
+}
+// smem matrix descriptor: start address, leading (K-chunk) and stride (8-row
+// group) byte offsets, sm100 descriptor version, no swizzle
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
+}
+// descriptor of K-step s (k in [8s, 8s+8)) of an R-row operand, rows from rb
+__device__ __forceinline__ uint64_t umma_desc_k(uint32_t base, int R, int s, int rb) {
+  return umma_desc(base + (uint32_t)(2 * s * (R >> 3) * 128 + (rb >> 3) * 128), (uint32_t)((R >> 3) * 128), 128);
+}
+// instruction descriptor: D f32, A/B tf32, both K-major, M x N
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// 32 lanes x 16 columns of fp32 from tensor memory (this warp's lane quadrant)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// ---------------------------------------------------------------------------
+// Forward 1 on tcgen05: projection p = x_flat . phi^T and the per-token Gram
+// matrix of the n streams, for n <= 4 (C % 4 == 0, x 16-byte aligned).
+//   CTA = 128 tokens (one M=128 MMA tile) x one split of the channels,
+//   warp-specialised: warp 0 issues TMA, warp 1 issues MMAs, warps 2..9
+//   (two threads per token, one per half of a 128-byte row) prepare operands.
+//   A stage is one stream x 32 channels: x[128 tokens x 32] and
+//   phi_hi / phi_lo[NB rows x 32] (phi split once per call), K-major in the
+//   128-byte-swizzled layout that TMA writes directly.  The compute threads
+//   rewrite their row as tf32 hi in place plus tf32 lo in a second buffer
+//   (keeping the swizzled offsets), keep the values of the n streams of a
+//   channel block in registers and accumulate the Gram entries; the MMA warp
+//   then adds x_lo.phi_hi + x_hi.phi_lo + x_hi.phi_hi (3xTF32) into tensor
+//   memory and frees the stage with tcgen05.commit.  Barriers per stage:
+//   full (TMA bytes), ready (8 compute warps), empty (MMA commit).
+// ---------------------------------------------------------------------------
+template <int N>
+struct PumCfg {
+  static constexpr int NH = L<N>::NH, NHP = L<N>::NHP, NG = L<N>::NG;
+  static constexpr int NB = (NH + 15) / 16 * 16;           // MMA N (padded phi rows)
+  static constexpr int TCOLS = 32;
+  static constexpr int TOK = 128, CH = 32, THREADS = 320;
+  static constexpr uint32_t XB = TOK * CH * 4;             // x tile of one stage
+  static constexpr uint32_t PB = NB * CH * 4;              // phi tile of one stage
+  static constexpr uint32_t SLOT = 2 * XB + 2 * PB;        // x/hi, lo, phi_hi, phi_lo
+  static constexpr uint32_t OFF_LO = XB, OFF_PH = 2 * XB, OFF_PL = 2 * XB + PB;
+  static constexpr uint32_t TX = XB + 2 * PB;              // bytes TMA brings per stage
+  static constexpr int STAGES = (200 * 1024) / SLOT < 8 ? (200 * 1024) / SLOT : 8;
+  static constexpr uint32_t OFF_GX = STAGES * SLOT;        // Gram exchange [128][NG]
+  static constexpr uint32_t OFF_BAR = OFF_GX + TOK * NG * 4;
+  static constexpr size_t SMEM = OFF_BAR + (3 * STAGES + 1) * 8 + 16 + 1024;
+  static_assert(NB <= 32, "one 32-column accumulator");
+  static_assert(XB % 1024 == 0 && PB % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+};
+
+// phi_hi / phi_lo [NB rows x nC]: rows k < NH hold phi_k split into tf32 hi +
+// tf32 lo, the padding rows are zero.
+template <int N>
+__global__ void phi_split_kernel(const float* __restrict__ pp, const float* __restrict__ pq,
+                                 const float* __restrict__ pr, float* __restrict__ ph,
+                                 float* __restrict__ pl, int64_t C) {
+  using P = PumCfg<N>;
+  const int64_t nC = (int64_t)N * C;
+  const int64_t total = (int64_t)P::NB * nC;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int k = (int)(e / nC);
+    const float v = k < P::NH ? phi_row(pp, pq, pr, k, N, nC)[e % nC] : 0.f;
+    uint32_t hi, lo;
+    split_tf32(v, hi, lo);
+    ph[e] = __uint_as_float(hi);
+    pl[e] = __uint_as_float(lo);
+  }
+}
+
+// smem descriptor of a K-major, 128-byte-swizzled operand (8-row groups
+// 1024 B apart); the start may advance by 32 B per K-step inside the atom
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Bounded mbarrier wait that also gives up once another role of the CTA has
+// raised the abort word.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity,
+                                                   const volatile int* abort_word) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 255) == 255 && *abort_word) return false;
+  }
+  atomicExch(&g_mhc_device_error, 1);
+  return false;
+}
+
+template <int N>
+__global__ void __launch_bounds__(320, 1)
+    proj_umma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap hmap,
+                     const __grid_constant__ CUtensorMap lmap, float* __restrict__ ppart,
+                     float* __restrict__ gpart, int64_t B, int64_t C, int cps) {
+  using P = PumCfg<N>;
+  constexpr int NG = P::NG, NHP = P::NHP, S = P::STAGES;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* gx_s = reinterpret_cast<float*>(sm + P::OFF_GX);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + P::OFF_BAR);
+  uint64_t* ready = full + S;
+  uint64_t* empty = ready + S;
+  uint64_t* done = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t sbase = smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t t0 = (int64_t)blockIdx.x * P::TOK;
+  const int split = blockIdx.y;
+  const int64_t c_begin = (int64_t)split * cps;
+  const int64_t c_end = c_begin + cps < C ? c_begin + cps : C;
+  const int nblocks = c_begin < c_end ? (int)((c_end - c_begin + P::CH - 1) / P::CH) : 0;
+  const int nchunks = nblocks * N;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(P::TCOLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 32) {
+    prefetch_tmap(&xmap);
+    prefetch_tmap(&hmap);
+    prefetch_tmap(&lmap);
+    for (int st = 0; st < S; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&ready[st], 8);
+      mbar_init(&empty[st], 1);
+    }
+    mbar_init(done, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int k = 0; k < nchunks; ++k) {
+        const int slot = k % S;
+        if (k >= S && !mbar_wait_or_abort(&empty[slot], (uint32_t)(((k / S) - 1) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        issued = k + 1;
+        unsigned char* base = sm + slot * P::SLOT;
+        const int c = (int)(c_begin + (int64_t)(k / N) * P::CH);
+        const int i = k % N;
+        mbar_expect_tx(&full[slot], P::TX);
+        tma_load_3d(base, &xmap, c, i, (int)t0, &full[slot]);
+        tma_load_3d(base + P::OFF_PH, &hmap, c, i, 0, &full[slot]);
+        tma_load_3d(base + P::OFF_PL, &lmap, c, i, 0, &full[slot]);
+      }
+      // no copy may still be landing when the CTA exits (bounded)
+      for (int q = issued > S ? issued - S : 0; q < issued; ++q)
+        mbar_wait(&full[q % S], (uint32_t)((q / S) & 1));
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t ID = umma_idesc_tf32(128, P::NB);
+      for (int k = 0; k < nchunks; ++k) {
+        const int slot = k % S;
+        if (!mbar_wait_or_abort(&ready[slot], (uint32_t)((k / S) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sb = sbase + slot * P::SLOT;
+#pragma unroll
+        for (int st = 0; st < P::CH / 8; ++st) {
+          const uint64_t ah = umma_desc_sw128(sb + 32 * st);
+          const uint64_t al = umma_desc_sw128(sb + P::OFF_LO + 32 * st);
+          const uint64_t bh = umma_desc_sw128(sb + P::OFF_PH + 32 * st);
+          const uint64_t bl = umma_desc_sw128(sb + P::OFF_PL + 32 * st);
+          umma_tf32(tmem, al, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
+          umma_tf32(tmem, ah, bl, ID, 1u);
+          umma_tf32(tmem, ah, bh, ID, 1u);
+        }
+        umma_commit(&empty[slot]);
+      }
+      umma_commit(done);
+    }
+  } else {
+    // ---------------- operand preparation + Gram ----------------
+    const int cw = warp - 2;               // 0..7
+    const int h = cw >> 2;                 // half of the 128-byte row
+    const int r = 32 * (warp & 3) + lane;  // token row = tensor-memory lane
+    const uint32_t rowoff = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    uint32_t choff[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) choff[j] = rowoff + (uint32_t)((((4 * h + j) ^ (r & 7))) * 16);
+    float gacc[NG];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) gacc[g] = 0.f;
+    bool ok = true;
+    for (int b = 0; b < nblocks && ok; ++b) {
+      float v[N][16];
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int k = b * N + i;
+        const int slot = k % S;
+        unsigned char* base = sm + slot * P::SLOT;
+        if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word)) {
+          *abort_word = 1;
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 a = *reinterpret_cast<const float4*>(base + choff[j]);
+          v[i][4 * j + 0] = a.x; v[i][4 * j + 1] = a.y; v[i][4 * j + 2] = a.z; v[i][4 * j + 3] = a.w;
+          uint4 hi, lo;
+          split_tf32(a.x, hi.x, lo.x); split_tf32(a.y, hi.y, lo.y);
+          split_tf32(a.z, hi.z, lo.z); split_tf32(a.w, hi.w, lo.w);
+          *reinterpret_cast<uint4*>(base + choff[j]) = hi;
+          *reinterpret_cast<uint4*>(base + P::OFF_LO + choff[j]) = lo;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[slot]);
+      }
+      if (!ok) break;
+      int g = 0;
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int j = i; j < N; ++j) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) gacc[g] = fmaf(v[i][q], v[j][q], gacc[g]);
+          ++g;
+        }
+    }
+    // results: D columns [16h, 16h + 16) of this token, Gram halves summed
+    bool have = ok && nchunks > 0 && mbar_wait_or_abort(done, 0u, abort_word);
+    have = __all_sync(0xffffffffu, have);
+    tc_fence_after();
+    const int64_t tok = t0 + r;
+    if (16 * h < NHP) {
+      float d[16];
+      if (have) {
+        tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 16 * h, d);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) d[e] = 0.f;
+      }
+      if (tok < B && (have || nchunks == 0)) {
+        float* pd = ppart + ((int64_t)split * B + tok) * NHP + 16 * h;
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (16 * h + e < NHP) pd[e] = d[e];
+      }
+    }
+    if (h == 1) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g) gx_s[r * NG + g] = gacc[g];
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (h == 0 && tok < B && (have || nchunks == 0)) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g)
+        gpart[((int64_t)split * B + tok) * NG + g] = gacc[g] + gx_s[r * NG + g];
+    }
+  }
+  // the MMA issuer drains its last batch before tensor memory is released
+  if (warp == 1 && lane == 0 && nchunks > 0) mbar_wait_or_abort(done, 0u, abort_word);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P::TCOLS));
+}
+
+// ---------------------------------------------------------------------------
+// Backward 3 for n = 4 on tcgen05 (dynamic H, C % 32 == 0, aligned).
+//   CTA = 32 channels x 4 streams = 128 columns (col = i*32 + cl) = one
+//   M=128 MMA tile, 128 threads (one warpgroup), two CTAs per SM so that one
+//   CTA's tensor-core round trip overlaps the other's elementwise work; a
+//   contiguous token range; TMA ring of 16-token stages.  Per stage:
+//   (E)  thread = (4 consecutive tokens, one channel): local terms of the 4
+//        streams -> smem; x of its tokens -> the X^T operand (tf32 hi/lo);
+//        d_p split into tf32 hi/lo operands;
+//   (MMA) one thread issues, 3xTF32 each:
+//        D1[col x tok] = Phi^T[col x 24] . D_p^T          (M=128, N=16)
+//        D2[col x k]  += X^T[col x 16 tok] . D_p[16 x 32] (M=128, N=32)
+//        Phi^T (hi/lo) is resident in smem; D1, D2 live in tensor memory;
+//   (epilogue) thread = column (warp w = stream w): grad_x = D1 + local term.
+//   After the range: D2 -> this split's dphi partial.
+// ---------------------------------------------------------------------------
+// The tcgen05 grad_x below is parity-exact but, with its per-stage MMA round
+// trip, slower than the mma.sync kernel on B200; it is kept selectable for
+// the warp-specialised rewrite.
+constexpr bool kGradXTcgen05 = false;
+
+struct Gx5Cfg {
+  static constexpr int CW = 32, COLS = 128, TOK = 16, TB = L<4>::TB, NHP = 24, KP = 32;
+  static constexpr int STAGES = 2, THREADS = 128;
+  static constexpr int TILE = TOK * COLS;
+  static constexpr int STAGE = 2 * TILE + TOK * TB;              // floats
+  static constexpr uint32_t STAGE_BYTES = STAGE * 4;
+  static constexpr uint32_t OFF_RING = 0;
+  static constexpr uint32_t OFF_A1H = OFF_RING + STAGES * STAGE_BYTES;   // Phi^T [128][24]
+  static constexpr uint32_t OFF_A1L = OFF_A1H + COLS * NHP * 4;
+  static constexpr uint32_t OFF_A2H = OFF_A1L + COLS * NHP * 4;          // X^T [128][16]
+  static constexpr uint32_t OFF_A2L = OFF_A2H + COLS * TOK * 4;
+  static constexpr uint32_t OFF_B1H = OFF_A2L + COLS * TOK * 4;          // D_p [16][24]
+  static constexpr uint32_t OFF_B1L = OFF_B1H + TOK * NHP * 4;
+  static constexpr uint32_t OFF_B2H = OFF_B1L + TOK * NHP * 4;           // D_p^T [32][16]
+  static constexpr uint32_t OFF_B2L = OFF_B2H + KP * TOK * 4;
+  static constexpr uint32_t OFF_GXL = OFF_B2L + KP * TOK * 4;            // local terms [16][128]
+  static constexpr uint32_t OFF_GW = OFF_GXL + TOK * COLS * 4;           // [4][32]
+  static constexpr uint32_t OFF_BAR = OFF_GW + 4 * CW * 4;               // STAGES + 1 mbarriers
+  static constexpr uint32_t OFF_TMEM = OFF_BAR + (STAGES + 1) * 8;
+  static constexpr size_t SMEM = OFF_TMEM + 16 + 128;
+  static constexpr uint32_t TMEM_COLS = 64;   // D1: cols [0,16), D2: [32,64)
+};
+
+__global__ void __launch_bounds__(128, 2)
+    grad_x5_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
+                   const __grid_constant__ CUtensorMap tmap, const float* __restrict__ w,
+                   const float* __restrict__ phi_pre, const float* __restrict__ phi_post,
+                   const float* __restrict__ phi_res, float* __restrict__ gx,
+                   float* __restrict__ dphi_part, float* __restrict__ gw_part, int64_t B,
+                   int64_t C, int ntiles, int nsplit) {
+  using F = Gx5Cfg;
+  using Lc = L<4>;
+  constexpr int N = 4, CW = F::CW, COLS = F::COLS, NHP = F::NHP, TB = F::TB, TOK = F::TOK;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  float* ring = reinterpret_cast<float*>(sm + F::OFF_RING);
+  float* gxl = reinterpret_cast<float*>(sm + F::OFF_GXL);
+  float* gwS = reinterpret_cast<float*>(sm + F::OFF_GW);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + F::OFF_BAR);
+  uint64_t* mma_bar = bars + F::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + F::OFF_TMEM);
+  const uint32_t sbase = smem_u32(sm);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tile = blockIdx.x % ntiles;
+  const int split = blockIdx.x / ntiles;
+  const int64_t c0 = (int64_t)tile * CW;
+  const int64_t nC = (int64_t)N * C;
+  const int64_t tb0 = B * split / nsplit, tb1 = B * (split + 1) / nsplit;
+  const int nbatch = (int)((tb1 - tb0 + TOK - 1) / TOK);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(F::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    prefetch_tmap(&gmap);
+    prefetch_tmap(&xmap);
+    prefetch_tmap(&tmap);
+    for (int st = 0; st <= F::STAGES; ++st) mbar_init(&bars[st], 1);
+    fence_mbar_init();
+  }
+  // resident operand Phi^T (hi/lo) and the zero rows k = 24..31 of D_p^T
+  for (int e = tid; e < COLS * NHP; e += F::THREADS) {
+    const int k = e / COLS, col = e % COLS;
+    const int i = col / CW, cl = col % CW;
+    const float v = k < Lc::NH ? __ldg(phi_row(phi_pre, phi_post, phi_res, k, N, nC) + (int64_t)i * C + c0 + cl) : 0.f;
+    uint32_t hi, lo;
+    split_tf32(v, hi, lo);
+    const uint32_t off = umma_kmaj_off(col, k, COLS);
+    *reinterpret_cast<uint32_t*>(sm + F::OFF_A1H + off) = hi;
+    *reinterpret_cast<uint32_t*>(sm + F::OFF_A1L + off) = lo;
+  }
+  for (int e = tid; e < (F::KP - NHP) * TOK; e += F::THREADS) {
+    const int k = NHP + e / TOK, tt = e % TOK;
+    const uint32_t off = umma_kmaj_off(k, tt, F::KP);
+    *reinterpret_cast<uint32_t*>(sm + F::OFF_B2H + off) = 0u;
+    *reinterpret_cast<uint32_t*>(sm + F::OFF_B2L + off) = 0u;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto issue = [&](int j) {
+    const int slot = j % F::STAGES;
+    float* base = ring + slot * F::STAGE;
+    const int t0 = (int)(tb0 + (int64_t)j * TOK);
+    mbar_expect_tx(&bars[slot], F::STAGE_BYTES);
+    tma_load_2d(base, &gmap, (int)c0, t0 * N, &bars[slot]);
+    tma_load_2d(base + F::TILE, &xmap, (int)c0, t0 * N, &bars[slot]);
+    tma_load_2d(base + 2 * F::TILE, &tmap, 0, t0, &bars[slot]);
+  };
+  if (tid == 0)
+    for (int j = 0; j < F::STAGES && j < nbatch; ++j) issue(j);
+
+  // (E) mapping: tokens 4*warp .. 4*warp+3, channel = lane
+  const int ecl = lane;
+  const float wc = __ldg(w + c0 + ecl);
+  float gwacc = 0.f;
+  // epilogue mapping: TMEM lane quadrant = warp -> column 32*warp + lane = (stream warp, channel lane)
+
+  constexpr uint32_t ID1 = umma_idesc_tf32(128, TOK);
+  constexpr uint32_t ID2 = umma_idesc_tf32(128, F::KP);
+  bool failed = false;
+  for (int j = 0; j < nbatch; ++j) {
+    const int slot = j % F::STAGES;
+    bool ok = true;
+    if (tid == 0) ok = mbar_wait(&bars[slot], (uint32_t)((j / F::STAGES) & 1));
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    if (tid == 0 && j >= 1 && j - 1 + F::STAGES < nbatch) issue(j - 1 + F::STAGES);
+    const float* gs = ring + slot * F::STAGE;
+    const float* xs = gs + F::TILE;
+    const float* ts = xs + F::TILE;
+    const int64_t t0 = tb0 + (int64_t)j * TOK;
+    const int nt = (int)((tb1 - t0) < TOK ? (tb1 - t0) : TOK);
+
+    // d_p operands (tokens beyond the range contribute zero)
+    for (int e = tid; e < TOK * NHP; e += F::THREADS) {
+      const int tt = e / NHP, k = e % NHP;
+      const float d = tt < nt ? ts[tt * TB + 4 + k] : 0.f;
+      uint32_t hi, lo;
+      split_tf32(d, hi, lo);
+      const uint32_t o1 = umma_kmaj_off(tt, k, TOK), o2 = umma_kmaj_off(k, tt, F::KP);
+      *reinterpret_cast<uint32_t*>(sm + F::OFF_B1H + o1) = hi;
+      *reinterpret_cast<uint32_t*>(sm + F::OFF_B1L + o1) = lo;
+      *reinterpret_cast<uint32_t*>(sm + F::OFF_B2H + o2) = hi;
+      *reinterpret_cast<uint32_t*>(sm + F::OFF_B2L + o2) = lo;
+    }
+    // (E) local terms + X^T operand
+    {
+      float xq[4][4];   // [stream][token]
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int tt = 4 * warp + u;
+        float gv[4], xv[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          gv[jj] = gs[(tt * 4 + jj) * CW + ecl];
+          xv[jj] = xs[(tt * 4 + jj) * CW + ecl];
+          xq[jj][u] = xv[jj];
+        }
+        if (tt < nt) {
+          const float* st = ts + tt * TB;
+          const float4 s0 = *reinterpret_cast<const float4*>(st);
+          const float4 h4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TH);
+          const float4 q4 = *reinterpret_cast<const float4*>(st + Lc::OFF_THP);
+          const float h[4] = {h4.x, h4.y, h4.z, h4.w};
+          const float hq[4] = {q4.x, q4.y, q4.z, q4.w};
+          float gy = 0.f, xa = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) { gy = fmaf(hq[jj], gv[jj], gy); xa = fmaf(h[jj], xv[jj], xa); }
+          const float agg = gy * wc * s0.y - xa * s0.x;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 m4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TM + 4 * i);
+            const float mix = m4.x * gv[0] + m4.y * gv[1] + m4.z * gv[2] + m4.w * gv[3];
+            gxl[tt * COLS + i * CW + ecl] = mix + h[i] * agg + s0.z * xv[i];
+          }
+          gwacc = fmaf(gy * xa, s0.y, gwacc);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 hi, lo;
+        split_tf32(xq[i][0], hi.x, lo.x);
+        split_tf32(xq[i][1], hi.y, lo.y);
+        split_tf32(xq[i][2], hi.z, lo.z);
+        split_tf32(xq[i][3], hi.w, lo.w);
+        const uint32_t off = umma_kmaj_off(i * CW + ecl, 4 * warp, COLS);
+        *reinterpret_cast<uint4*>(sm + F::OFF_A2H + off) = hi;
+        *reinterpret_cast<uint4*>(sm + F::OFF_A2L + off) = lo;
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+#pragma unroll
+      for (int s = 0; s < 3; ++s) {
+        const uint64_t ah = umma_desc_k(sbase + F::OFF_A1H, COLS, s, 0);
+        const uint64_t al = umma_desc_k(sbase + F::OFF_A1L, COLS, s, 0);
+        const uint64_t bh = umma_desc_k(sbase + F::OFF_B1H, TOK, s, 0);
+        const uint64_t bl = umma_desc_k(sbase + F::OFF_B1L, TOK, s, 0);
+        umma_tf32(tmem, al, bh, ID1, s > 0);
+        umma_tf32(tmem, ah, bl, ID1, 1);
+        umma_tf32(tmem, ah, bh, ID1, 1);
+      }
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        const uint64_t ah = umma_desc_k(sbase + F::OFF_A2H, COLS, s, 0);
+        const uint64_t al = umma_desc_k(sbase + F::OFF_A2L, COLS, s, 0);
+        const uint64_t bh = umma_desc_k(sbase + F::OFF_B2H, F::KP, s, 0);
+        const uint64_t bl = umma_desc_k(sbase + F::OFF_B2L, F::KP, s, 0);
+        umma_tf32(tmem + 32, al, bh, ID2, (j > 0 || s > 0) ? 1u : 0u);
+        umma_tf32(tmem + 32, ah, bl, ID2, 1);
+        umma_tf32(tmem + 32, ah, bh, ID2, 1);
+      }
+      umma_commit(mma_bar);
+    }
+    ok = true;
+    if (tid == 0) ok = mbar_wait(mma_bar, (uint32_t)(j & 1));
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    tc_fence_after();
+    // epilogue: grad_x = D1 + local term; thread = column (stream warp, channel lane)
+    {
+      float v[16];
+      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16), v);
+      float* dst = gx + t0 * nC + (int64_t)warp * C + c0 + lane;
+#pragma unroll
+      for (int tt = 0; tt < TOK; ++tt)
+        if (tt < nt) __stcs(dst + tt * nC, v[tt] + gxl[tt * COLS + warp * CW + lane]);
+    }
+    tc_fence_before();
+  }
+  if (!failed) {
+    // dphi partial of this split from D2 (rows = columns, cols = k)
+    float a[16], b[16];
+    if (nbatch > 0) {
+      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + 32, a);
+      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + 48, b);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) { a[q] = 0.f; b[q] = 0.f; }
+    }
+    float* dst = dphi_part + (int64_t)split * Lc::NH * nC + (int64_t)warp * C + c0 + lane;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) dst[(int64_t)k * nC] = a[k];
+#pragma unroll
+    for (int k = 16; k < Lc::NH; ++k) dst[(int64_t)k * nC] = b[k - 16];
+    gwS[warp * CW + ecl] = gwacc;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (!failed && tid < CW) {
+    float sacc = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) sacc += gwS[q * CW + tid];
+    gw_part[(int64_t)split * C + c0 + tid] = sacc;
+  }
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(F::TMEM_COLS));
 }
 
 // out[l] = sum_s part[s * L + l]   (fixed order over splits)
@@ -1632,6 +2261,8 @@ int choose_gx_splits(int64_t tiles, int64_t B, int sms, int per_sm) {
 struct FwdPlan {
   int ks, cps;
   int64_t tiles;
+  int uks, ucps;     // splits of the tensor-core projection (n <= 4, C % 8 == 0)
+  int64_t utiles;
   size_t ppart, gpart, rec_tmp, phiT;
 };
 
@@ -1642,15 +2273,28 @@ FwdPlan plan_fwd(int64_t B, int64_t C) {
   p.ks = choose_ksplit(p.tiles, C, num_sms());
   p.cps = (int)(((C + p.ks - 1) / p.ks + 31) / 32 * 32);
   p.ks = (int)((C + p.cps - 1) / p.cps);
-  p.ppart = (size_t)p.ks * B * L<N>::NHP;
-  p.gpart = (size_t)p.ks * B * L<N>::NG;
+  int mks = p.ks;
+  p.uks = 0; p.ucps = 0; p.utiles = 0;
+  size_t uphi = 0;
+  if (N <= 4 && C % 4 == 0) {
+    p.utiles = (B + 127) / 128;
+    int ks = choose_ksplit(p.utiles, C, num_sms());
+    p.ucps = (int)(((C + ks - 1) / ks + 31) / 32 * 32);
+    p.uks = (int)((C + p.ucps - 1) / p.ucps);
+    if (p.uks > mks) mks = p.uks;
+    uphi = (size_t)2 * PumCfg<(N <= 4 ? N : 4)>::NB * N * C;
+  }
+  p.ppart = (size_t)mks * B * L<N>::NHP;
+  p.gpart = (size_t)mks * B * L<N>::NG;
   p.rec_tmp = (size_t)B * L<N>::REC;
   p.phiT = N <= 4 ? (size_t)C * PjtCfg<(N <= 4 ? N : 4)>::PROW : 0;
+  if (uphi > p.phiT) p.phiT = uphi;
   return p;
 }
 
 struct BwdPlan {
   int ntiles, nsplit;
+  int nsplit5;  // splits of the 32-channel tensor-core grad_x (n = 4, dynamic H)
   size_t stats, tokb, tokr, dphi, gw, tot;
 };
 
@@ -1659,11 +2303,13 @@ BwdPlan plan_bwd(int64_t B, int64_t C) {
   BwdPlan p;
   p.ntiles = (int)((C + GX_CW - 1) / GX_CW);
   p.nsplit = choose_gx_splits(p.ntiles, B, num_sms(), N <= 4 ? 2 : 1);
+  p.nsplit5 = (N == 4 && DYN) ? choose_gx_splits((C + 31) / 32, B, num_sms(), 2) : 0;
+  const int64_t msplit = p.nsplit > p.nsplit5 ? p.nsplit : p.nsplit5;
   p.stats = (size_t)B * L<N>::NS1 * 2;  // fp64
   p.tokb = (size_t)B * L<N>::TB;
   p.tokr = (size_t)B * (DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
-  p.dphi = DYN ? (size_t)p.nsplit * L<N>::NH * N * C : 0;
-  p.gw = (size_t)p.nsplit * C;
+  p.dphi = DYN ? (size_t)msplit * L<N>::NH * N * C : 0;
+  p.gw = (size_t)msplit * C;
   p.tot = (size_t)(DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
   return p;
 }
@@ -1702,22 +2348,40 @@ template <int N, bool DYN>
 bool launch_grad_x_tma(const float* g, const float* x, const float* w, const float* pp,
                        const float* pq, const float* pr, const float* tokb, float* gx,
                        float* dphi, float* gwp, int64_t B, int64_t C, const BwdPlan& p,
-                       cudaStream_t s) {
+                       int* nsplit_used, cudaStream_t s) {
+  *nsplit_used = p.nsplit;
   if constexpr (N > 4) {
     return false;
   } else {
+    if constexpr (N == 4 && DYN && kGradXTcgen05) {
+      using F5 = Gx5Cfg;
+      CUtensorMap gm, xm, tm;
+      const int nt5 = (int)(C / F5::CW);
+      const int ns5 = p.nsplit5;
+      if (C % F5::CW == 0 && aligned16(g) && aligned16(x) && aligned16(tokb) &&
+          make_tmap_2d_f32(&gm, g, (uint64_t)B * N, C, C, F5::TOK * N, F5::CW) &&
+          make_tmap_2d_f32(&xm, x, (uint64_t)B * N, C, C, F5::TOK * N, F5::CW) &&
+          make_tmap_2d_f32(&tm, tokb, B, L<N>::TB, L<N>::TB, F5::TOK, L<N>::TB)) {
+        cudaFuncSetAttribute(grad_x5_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F5::SMEM);
+        { ProfScope _ps("grad_x", s); grad_x5_kernel<<<(unsigned)(nt5 * ns5), F5::THREADS, F5::SMEM, s>>>(
+            gm, xm, tm, w, pp, pq, pr, gx, dphi, gwp, B, C, nt5, ns5); }
+        *nsplit_used = ns5;
+        return true;
+      }
+    }
     if constexpr (N == 4) {
       using F = Gx4Cfg;
-      CUtensorMap gm, xm, tm;
+      CUtensorMap gm, xm, tm, om;
       if (C % 64 == 0 && aligned16(g) && aligned16(x) && aligned16(tokb) && aligned16(gx) &&
           (!DYN || aligned16(dphi)) &&
           make_tmap_2d_f32(&gm, g, (uint64_t)B * N, C, C, F::TOK * N, F::CW) &&
+          make_tmap_2d_f32(&om, gx, (uint64_t)B * N, C, C, F::TOK * N, F::CW) &&
           make_tmap_2d_f32(&xm, x, (uint64_t)B * N, C, C, F::TOK * N, F::CW) &&
           make_tmap_2d_f32(&tm, tokb, B, L<N>::TB, L<N>::TB, F::TOK, L<N>::TB)) {
         cudaFuncSetAttribute(grad_x4_kernel<DYN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)F::SMEM);
         { ProfScope _ps("grad_x", s); grad_x4_kernel<DYN><<<(unsigned)(p.ntiles * p.nsplit), 256, F::SMEM, s>>>(
-            gm, xm, tm, w, pp, pq, pr, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
+            gm, xm, tm, om, w, pp, pq, pr, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
         return true;
       }
     }
@@ -1758,7 +2422,28 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
 
   int rc = MHC_OK;
   bool done = false;
+  int ks = p.ks;
   if constexpr (N <= 4) {
+    // tcgen05 projection: phi split once into tf32 hi/lo rows, x streamed by TMA.
+    using PU = PumCfg<N>;
+    const int64_t nC = (int64_t)N * C;
+    float* ph = phiT;
+    float* pl = phiT + (size_t)PU::NB * nC;
+    CUtensorMap xmap, hmap, lmap;
+    const uint64_t cs = (uint64_t)C * 4, rs = (uint64_t)nC * 4;
+    if (p.uks > 0 && B > 0 && aligned16(x) && aligned16(ph) && aligned16(pl) &&
+        make_tmap_3d_f32(&xmap, x, C, N, B, cs, rs, PU::CH, 1, PU::TOK, CU_TENSOR_MAP_SWIZZLE_128B) &&
+        make_tmap_3d_f32(&hmap, ph, C, N, PU::NB, cs, rs, PU::CH, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B) &&
+        make_tmap_3d_f32(&lmap, pl, C, N, PU::NB, cs, rs, PU::CH, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B)) {
+      { ProfScope _ps("phi_split", s); phi_split_kernel<N><<<grid_1d(PU::NB * nC, 256, 2048), 256, 0, s>>>(pp, pq, pr, ph, pl, C); }
+      cudaFuncSetAttribute(proj_umma_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PU::SMEM);
+      { ProfScope _ps("proj_stats", s); proj_umma_kernel<N><<<dim3((unsigned)p.utiles, (unsigned)p.uks), PU::THREADS, PU::SMEM, s>>>(
+          xmap, hmap, lmap, ppart, gpart, B, C, p.ucps); }
+      ks = p.uks;
+      done = true;
+    }
+  }
+  if constexpr (N <= 4) if (!done) {
     // TMA-pipelined projection when the layout allows it.
     using PT = PjtCfg<N>;
     CUtensorMap xmap, pmap;
@@ -1784,7 +2469,7 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
   }
   rc = check_launch("mhc_layer_fwd_dynamic/proj_stats");
   if (rc) return rc;
-  { ProfScope _ps("token_fwd", s); token_fwd_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(ppart, gpart, p.ks, ap, aq, ar, bp, bq, br,
+  { ProfScope _ps("token_fwd", s); token_fwd_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(ppart, gpart, ks, ap, aq, ar, bp, bq, br,
                                                      rec, B, C, iters, s_eps, r_eps); }
   rc = check_launch("mhc_layer_fwd_dynamic/token_fwd");
   if (rc) return rc;
@@ -1826,15 +2511,16 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
                                                      tokr, B, C, iters, s_eps, r_eps); }
   rc = check_launch("mhc_layer_bwd_dynamic/token_bwd");
   if (rc) return rc;
-  if (!launch_grad_x_tma<N, true>(g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p, s))
+  int nsplit = p.nsplit;
+  if (!launch_grad_x_tma<N, true>(g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p, &nsplit, s))
     { ProfScope _ps("grad_x", s); grad_x_kernel<N, true><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
         g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
   rc = check_launch("mhc_layer_bwd_dynamic/grad_x");
   if (rc) return rc;
   const int64_t nC = (int64_t)N * C;
   { ProfScope _ps("reduce_dphi", s); reduce_dphi_kernel<<<grid_1d((int64_t)L<N>::NH * nC, 256, 4096), 256, 0, s>>>(
-      dphi, p.nsplit, L<N>::NH, N, nC, gpp, gpq, gpr); }
-  { ProfScope _ps("reduce_splits", s); reduce_splits_kernel<<<grid_1d(C, 256, 4096), 256, 0, s>>>(gwp, p.nsplit, C, gw); }
+      dphi, nsplit, L<N>::NH, N, nC, gpp, gpq, gpr); }
+  { ProfScope _ps("reduce_splits", s); reduce_splits_kernel<<<grid_1d(C, 256, 4096), 256, 0, s>>>(gwp, nsplit, C, gw); }
   { ProfScope _ps("reduce_tokens", s); reduce_tokens_kernel<<<L<N>::NR, 256, 0, s>>>(tokr, B, L<N>::NR, tot); }
   { ProfScope _ps("scatter_dyn_param_grads", s); scatter_dyn_param_grads_kernel<N><<<1, 128, 0, s>>>(tot, gbp, gbq, gbr, gap, gaq, gar); }
   return check_launch("mhc_layer_bwd_dynamic/reduce");
@@ -1887,8 +2573,9 @@ int run_bwd_static(const float* g, const float* x, const float* w, const float* 
   int rc = check_launch("mhc_layer_bwd_static/bwd_stats");
   if (rc) return rc;
   { ProfScope _ps("token_bwd_static", s); token_bwd_static_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, Hp, Hq, rec, tokb, tokr, B, C, r_eps); }
+  int nsplit = p.nsplit;
   if (!launch_grad_x_tma<N, false>(g, x, w, nullptr, nullptr, nullptr, tokb, gx, nullptr, gwp, B,
-                                   C, p, s))
+                                   C, p, &nsplit, s))
     { ProfScope _ps("grad_x", s); grad_x_kernel<N, false><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
         g, x, w, nullptr, nullptr, nullptr, tokb, gx, nullptr, gwp, B, C, p.ntiles, p.nsplit); }
   rc = check_launch("mhc_layer_bwd_static/grad_x");

@@ -42,10 +42,11 @@ inline EncodeTiledFn encode_tiled_fn() {
 }
 
 // 2D fp32 tensor map over a row-major matrix rows x cols (row stride in
-// elements, a multiple of 4), box box_rows x box_cols, no swizzle; elements
-// outside the matrix read as zero.  Returns false on failure.
+// elements, a multiple of 4), box box_rows x box_cols, optional shared-memory
+// swizzle; elements outside the matrix read as zero.  Returns false on failure.
 inline bool make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                             uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols) {
+                             uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols,
+                             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {cols, rows};
@@ -53,7 +54,26 @@ inline bool make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, 
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// 3D fp32 tensor map: dims (d0 innermost, d1, d2), byte strides of d1 and d2
+// (multiples of 16), box (b0, b1, b2), optional swizzle; out-of-range
+// elements read as zero.  Returns false on failure.
+inline bool make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                             uint32_t b0, uint32_t b1, uint32_t b2,
+                             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -103,6 +123,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// plain arrive (no transaction bytes)
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 3D tiled TMA load: box at (c0, c1, c2) of the map into dst (this CTA's smem).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 2D tiled TMA load: box at (col, row) of the map into dst (this CTA's smem).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int col, int row,
                                             uint64_t* bar) {
@@ -111,6 +146,28 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(col), "r"(row), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 2D tiled TMA store: this CTA's smem tile -> box at (col, row) of the map.
+// Completion is tracked with the bulk async-group of the issuing thread.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int col,
+                                             int row) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(col), "r"(row)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until the issuing thread's bulk stores have finished reading smem
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// wait until the issuing thread's bulk stores are complete
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// make this thread's generic-proxy smem writes visible to the async proxy
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
