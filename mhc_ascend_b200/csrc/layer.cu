@@ -1627,7 +1627,7 @@ struct PumCfg {
   static constexpr uint32_t SLOT = 2 * XB + 2 * PB;        // x/hi, lo, phi_hi, phi_lo
   static constexpr uint32_t OFF_LO = XB, OFF_PH = 2 * XB, OFF_PL = 2 * XB + PB;
   static constexpr uint32_t TX = XB + 2 * PB;              // bytes TMA brings per stage
-  static constexpr int STAGES = (200 * 1024) / SLOT < 8 ? (200 * 1024) / SLOT : 8;
+  static constexpr int STAGES = 2;                        // two CTAs per SM
   static constexpr uint32_t OFF_GX = STAGES * SLOT;        // Gram exchange [128][NG]
   static constexpr uint32_t OFF_BAR = OFF_GX + TOK * NG * 4;
   static constexpr size_t SMEM = OFF_BAR + (3 * STAGES + 1) * 8 + 16 + 1024;
@@ -1683,7 +1683,7 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
 }
 
 template <int N>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(320, 2)
     proj_umma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap hmap,
                      const __grid_constant__ CUtensorMap lmap, float* __restrict__ ppart,
                      float* __restrict__ gpart, int64_t B, int64_t C, int cps) {
@@ -1819,13 +1819,17 @@ __global__ void __launch_bounds__(320, 1)
         if (lane == 0) mbar_arrive(&ready[slot]);
       }
       if (!ok) break;
+      // Gram of this block first, then the running sum: the rounding error
+      // grows with the number of blocks, not of channels
       int g = 0;
 #pragma unroll
       for (int i = 0; i < N; ++i)
 #pragma unroll
         for (int j = i; j < N; ++j) {
+          float blk = v[i][0] * v[j][0];
 #pragma unroll
-          for (int q = 0; q < 16; ++q) gacc[g] = fmaf(v[i][q], v[j][q], gacc[g]);
+          for (int q = 1; q < 16; ++q) blk = fmaf(v[i][q], v[j][q], blk);
+          gacc[g] += blk;
           ++g;
         }
     }
@@ -2242,6 +2246,24 @@ int choose_ksplit(int64_t tiles, int64_t C, int sms) {
   return best;
 }
 
+// Channel splits of the tensor-core projection: minimise waves x (32-channel
+// blocks per CTA + a fixed per-CTA cost), at most 1024 channels per split.
+int choose_proj_splits(int64_t tiles, int64_t C, int slots) {
+  const int64_t nblk = (C + 31) / 32;
+  int64_t lo = (C + 1023) / 1024;
+  if (lo < 1) lo = 1;
+  const int64_t hi = nblk < 64 ? nblk : 64;
+  int best = (int)lo;
+  double best_cost = 1e300;
+  for (int64_t ks = lo; ks <= hi || ks == lo; ++ks) {
+    const int64_t waves = (tiles * ks + slots - 1) / slots;
+    const int64_t blocks = (nblk + ks - 1) / ks;
+    const double cost = (double)waves * (double)(blocks + 3);
+    if (cost < best_cost) { best_cost = cost; best = (int)ks; }
+  }
+  return best;
+}
+
 int choose_gx_splits(int64_t tiles, int64_t B, int sms, int per_sm) {
   const int64_t slots = (int64_t)sms * per_sm;
   int best = 1;
@@ -2278,7 +2300,7 @@ FwdPlan plan_fwd(int64_t B, int64_t C) {
   size_t uphi = 0;
   if (N <= 4 && C % 4 == 0) {
     p.utiles = (B + 127) / 128;
-    int ks = choose_ksplit(p.utiles, C, num_sms());
+    const int ks = choose_proj_splits(p.utiles, C, 2 * num_sms());
     p.ucps = (int)(((C + ks - 1) / ks + 31) / 32 * 32);
     p.uks = (int)((C + p.ucps - 1) / p.ucps);
     if (p.uks > mks) mks = p.uks;
