@@ -1599,6 +1599,36 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
 }
+// 32 lanes x 8 columns of fp32 from tensor memory (this warp's lane quadrant)
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// 32 lanes x 16 columns of 32-bit values into tensor memory (this warp's lane quadrant)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// D (tmem) (+)= A (tmem, M lanes x 8 columns) . B (smem descriptor)^T, kind::tf32
+__device__ __forceinline__ void umma_tf32_at(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 // ---------------------------------------------------------------------------
 // Forward 1 on tcgen05: projection p = x_flat . phi^T and the per-token Gram
@@ -1886,6 +1916,407 @@ __global__ void __launch_bounds__(320, 2)
 //        Phi^T (hi/lo) is resident in smem; D1, D2 live in tensor memory;
 //   (epilogue) thread = column (warp w = stream w): grad_x = D1 + local term.
 //   After the range: D2 -> this split's dphi partial.
+// ---------------------------------------------------------------------------
+// Backward 3 for n = 4, dynamic H, on tcgen05 with warp specialisation.
+//   CTA = 32 channels x 4 streams = 128 columns (col = 32 i + c) = one M=128
+//   MMA tile, a contiguous range of 16-token blocks; 27 warps: warp 0 TMA,
+//   warp 1 issues D1, warps 2..17 "E" (one token each, lane = channel, all
+//   four streams), warps 18..21 epilogue and warps 23..26 X^T (stream = the
+//   tensor-memory lane quadrant of the warp, lane = channel), warp 22 issues
+//   D2.  Per block j:
+//     TMA:  g, x [16 tokens x 4 streams x 32 channels] and the block's
+//           operand image (d_p split into tf32 hi/lo in both the B layout of
+//           D1 and of D2, plus the per-token scalars), written by
+//           gx_image_kernel in the exact K-major shared-memory layout;
+//     MMA:  D1[b] = Phi^T[col x 24] . D_p^T      (M=128, N=16, 3xTF32)
+//           D2   += X^T[col x 16 tok] . D_p      (M=128, N=32, 3xTF32)
+//           with Phi^T resident in shared memory, X^T (A of D2) and D1 in
+//           tensor memory, ND-deep;
+//     X^T:  x of the warp's stream split into tf32 hi/lo and stored into
+//           tensor memory (tcgen05.st: lane = column, column = token), which
+//           transposes for free and needs no proxy fence;
+//     E:    the local terms of all four streams into a shared buffer
+//           (overlapping the MMAs);
+//     epilogue: grad_x = D1 + local term, added in place in the local-term
+//           buffer (its [token][stream][channel] layout is the grad_x tile)
+//           and written with one TMA store.
+//   After the range: D2 -> this split's dphi partial, sum of gy.xa.inv_r ->
+//   this split's grad-w partial.
+// ---------------------------------------------------------------------------
+struct Gx6Cfg {
+  static constexpr int CW = 32, COLS = 128, TOK = 16, NH = 24, KP = 32;
+  static constexpr int SG = 6, SI = 6, ND = 4, E_WARPS = 16, TPE = 1, THREADS = 32 * (2 + E_WARPS + 4 + 1 + 4);
+  static constexpr int D2_WARP = 2 + E_WARPS + 4;          // issues the D2 MMAs
+  static constexpr int XT_WARP0 = D2_WARP + 1;             // first of the four X^T warps
+  // operand image of one 16-token block (floats)
+  static constexpr int IMG_B1H = 0, IMG_B1L = 384, IMG_B2H = 768, IMG_B2L = 1280, IMG_SC = 1792;
+  static constexpr int IMG_FLOATS = 2304;
+  static constexpr uint32_t IMG = IMG_FLOATS * 4;
+  static constexpr uint32_t GB = TOK * 4 * CW * 4;         // g (or x) tile bytes
+  static constexpr uint32_t OFF_IMG = SG * 2 * GB;         // g/x ring, then the image ring
+  static constexpr uint32_t OFF_A1H = OFF_IMG + SI * IMG;  // Phi^T [128 x 24]
+  static constexpr uint32_t OFF_A1L = OFF_A1H + COLS * NH * 4;
+  static constexpr uint32_t LOCB = TOK * COLS * 4;         // local terms [16 tokens][128 columns]
+  static constexpr uint32_t OFF_LOC = OFF_A1L + COLS * NH * 4;  // [ND buffers]
+  static constexpr uint32_t OFF_GW = OFF_LOC + ND * LOCB;  // grad-w partials [E warps][32]
+  static constexpr uint32_t OFF_BAR = OFF_GW + E_WARPS * CW * 4;
+  static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 1;
+  static constexpr size_t SMEM = OFF_BAR + NBAR * 8 + 16 + 128;
+  static constexpr uint32_t TMEM_COLS = 256;   // D1[b]: [16 b, +16); D2: [64, 96); X^T[b]: [128 + 32 b, +32) hi|lo
+  static constexpr uint32_t D2_COL = 64, XT_COL = 128;
+};
+
+// Operand image of each 16-token block from the per-token backward rows:
+// D_p hi/lo as the K-major [16 tokens x 24] B operand of D1 and as the
+// K-major [32 (k, zero-padded) x 16 tokens] B operand of D2, and 32 scalars
+// per token (beta, inv_r, coef, 0, h[4], h_post[4], M^T[16], 0[4]).  Tokens
+// past B are zero.
+__global__ void __launch_bounds__(128)
+    gx_image_kernel(const float* __restrict__ tokb, float* __restrict__ img, int64_t B, int64_t nblk) {
+  using Lc = L<4>;
+  using F = Gx6Cfg;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= nblk * F::TOK) return;
+  const bool live = t < B;
+  const float* tb = tokb + (live ? t : 0) * Lc::TB;
+  float* im = img + (t / F::TOK) * F::IMG_FLOATS;
+  const int tt = (int)(t % F::TOK);
+#pragma unroll
+  for (int k = 0; k < F::KP; ++k) {
+    const float d = (live && k < F::NH) ? tb[4 + k] : 0.f;
+    uint32_t hi, lo;
+    split_tf32(d, hi, lo);
+    if (k < F::NH) {
+      const uint32_t o1 = umma_kmaj_off(tt, k, F::TOK) / 4;
+      im[F::IMG_B1H + o1] = __uint_as_float(hi);
+      im[F::IMG_B1L + o1] = __uint_as_float(lo);
+    }
+    const uint32_t o2 = umma_kmaj_off(k, tt, F::KP) / 4;
+    im[F::IMG_B2H + o2] = __uint_as_float(hi);
+    im[F::IMG_B2L + o2] = __uint_as_float(lo);
+  }
+  float* sc = im + F::IMG_SC + tt * 32;
+  float v[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) v[e] = 0.f;
+  if (live) {
+    v[0] = tb[0]; v[1] = tb[1]; v[2] = tb[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { v[4 + i] = tb[Lc::OFF_TH + i]; v[8 + i] = tb[Lc::OFF_THP + i]; }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[12 + e] = tb[Lc::OFF_TM + e];
+  }
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(sc + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+}
+
+__global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
+    grad_x6_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
+                   const __grid_constant__ CUtensorMap omap, const float* __restrict__ img, const float* __restrict__ w,
+                   const float* __restrict__ phi_pre, const float* __restrict__ phi_post,
+                   const float* __restrict__ phi_res, float* __restrict__ gx,
+                   float* __restrict__ dphi_part, float* __restrict__ gw_part, int64_t B,
+                   int64_t C, int ntiles, int nsplit, int64_t nblk) {
+  using F = Gx6Cfg;
+  constexpr int SG = F::SG, SI = F::SI, ND = F::ND, CW = F::CW, COLS = F::COLS, TOK = F::TOK;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* gfull = reinterpret_cast<uint64_t*>(sm + F::OFF_BAR);
+  uint64_t* gfree = gfull + SG;
+  uint64_t* ifull = gfree + SG;
+  uint64_t* ifree = ifull + SI;
+  uint64_t* a2_ready = ifree + SI;
+  uint64_t* a2_free = a2_ready + ND;
+  uint64_t* d1_full = a2_free + ND;
+  uint64_t* d1_free = d1_full + ND;
+  uint64_t* loc_ready = d1_free + ND;
+  uint64_t* loc_free = loc_ready + ND;
+  uint64_t* d2_done = loc_free + ND;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d2_done + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t sbase = smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x % ntiles;
+  const int split = blockIdx.x / ntiles;
+  const int64_t c0 = (int64_t)tile * CW;
+  const int64_t nC = 4 * C;
+  const int64_t blk0 = nblk * split / nsplit, blk1 = nblk * (split + 1) / nsplit;
+  const int nb = (int)(blk1 - blk0);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(F::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 32) {
+    prefetch_tmap(&gmap);
+    prefetch_tmap(&xmap);
+    prefetch_tmap(&omap);
+    for (int st = 0; st < SG; ++st) { mbar_init(&gfull[st], 1); mbar_init(&gfree[st], F::E_WARPS + 4); }
+    for (int st = 0; st < SI; ++st) { mbar_init(&ifull[st], 1); mbar_init(&ifree[st], 2 + F::E_WARPS); }
+    for (int b = 0; b < ND; ++b) {
+      mbar_init(&a2_ready[b], 4);
+      mbar_init(&a2_free[b], 1);
+      mbar_init(&d1_full[b], 1);
+      mbar_init(&d1_free[b], 4);
+      mbar_init(&loc_ready[b], F::E_WARPS);
+      mbar_init(&loc_free[b], 1);
+    }
+    mbar_init(d2_done, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+  }
+  // resident Phi^T (hi/lo), K-major [128 columns x 24]
+  for (int e = tid; e < COLS * F::NH; e += F::THREADS) {
+    const int k = e / COLS, col = e % COLS;
+    const float v = __ldg(phi_row(phi_pre, phi_post, phi_res, k, 4, nC) + (int64_t)(col / CW) * C + c0 + col % CW);
+    uint32_t hi, lo;
+    split_tf32(v, hi, lo);
+    const uint32_t off = umma_kmaj_off(col, k, COLS);
+    *reinterpret_cast<uint32_t*>(sm + F::OFF_A1H + off) = hi;
+    *reinterpret_cast<uint32_t*>(sm + F::OFF_A1L + off) = lo;
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int gi = 0, ii = 0;
+      for (int j = 0; j < nb; ++j) {
+        const int sg = j % SG, si = j % SI;
+        if (j >= SG && !mbar_wait_or_abort(&gfree[sg], (uint32_t)(((j / SG) - 1) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        const int64_t blk = blk0 + j;
+        const int row = (int)(blk * TOK * 4);
+        unsigned char* gb = sm + sg * 2 * F::GB;
+        mbar_expect_tx(&gfull[sg], 2 * F::GB);
+        tma_load_2d(gb, &gmap, (int)c0, row, &gfull[sg]);
+        tma_load_2d(gb + F::GB, &xmap, (int)c0, row, &gfull[sg]);
+        gi = j + 1;
+        if (j >= SI && !mbar_wait_or_abort(&ifree[si], (uint32_t)(((j / SI) - 1) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        mbar_expect_tx(&ifull[si], F::IMG);
+        bulk_load(sm + F::OFF_IMG + si * F::IMG, img + blk * F::IMG_FLOATS, F::IMG, &ifull[si]);
+        ii = j + 1;
+      }
+      // no copy may still be landing when the CTA exits (bounded)
+      for (int q = gi > SG ? gi - SG : 0; q < gi; ++q) mbar_wait(&gfull[q % SG], (uint32_t)((q / SG) & 1));
+      for (int q = ii > SI ? ii - SI : 0; q < ii; ++q) mbar_wait(&ifull[q % SI], (uint32_t)((q / SI) & 1));
+    }
+  } else if (warp == 1) {
+    // ---------------- D1 issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t ID1 = umma_idesc_tf32(128, TOK);
+      for (int j = 0; j < nb; ++j) {
+        const int si = j % SI, b = j % ND;
+        if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { *abort_word = 1; break; }
+        if (j >= ND && !mbar_wait_or_abort(&d1_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t im = sbase + F::OFF_IMG + si * F::IMG;
+#pragma unroll
+        for (int ks = 0; ks < 3; ++ks) {
+          const uint64_t ah = umma_desc_k(sbase + F::OFF_A1H, COLS, ks, 0);
+          const uint64_t al = umma_desc_k(sbase + F::OFF_A1L, COLS, ks, 0);
+          const uint64_t bh = umma_desc_k(im + F::IMG_B1H * 4, TOK, ks, 0);
+          const uint64_t bl = umma_desc_k(im + F::IMG_B1L * 4, TOK, ks, 0);
+          umma_tf32(tmem + 16 * b, al, bh, ID1, ks > 0 ? 1u : 0u);
+          umma_tf32(tmem + 16 * b, ah, bl, ID1, 1u);
+          umma_tf32(tmem + 16 * b, ah, bh, ID1, 1u);
+        }
+        umma_commit(&d1_full[b]);
+        umma_commit(&ifree[si]);
+      }
+    }
+  } else if (warp == F::D2_WARP) {
+    // ---------------- D2 issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t ID2 = umma_idesc_tf32(128, F::KP);
+      for (int j = 0; j < nb; ++j) {
+        const int si = j % SI, b = j % ND;
+        if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { *abort_word = 1; break; }
+        if (!mbar_wait_or_abort(&a2_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { *abort_word = 1; break; }
+        tc_fence_after();
+        const uint32_t im = sbase + F::OFF_IMG + si * F::IMG;
+        const uint32_t a2 = tmem + F::XT_COL + 32 * b;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const uint32_t ah = a2 + 8 * ks, al = a2 + 16 + 8 * ks;
+          const uint64_t bh = umma_desc_k(im + F::IMG_B2H * 4, F::KP, ks, 0);
+          const uint64_t bl = umma_desc_k(im + F::IMG_B2L * 4, F::KP, ks, 0);
+          umma_tf32_at(tmem + F::D2_COL, al, bh, ID2, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_tf32_at(tmem + F::D2_COL, ah, bl, ID2, 1u);
+          umma_tf32_at(tmem + F::D2_COL, ah, bh, ID2, 1u);
+        }
+        umma_commit(&a2_free[b]);
+        umma_commit(&ifree[si]);
+      }
+      umma_commit(d2_done);
+    }
+  } else if (warp >= F::XT_WARP0) {
+    // ---------------- X^T operand into tensor memory ----------------
+    const int q = warp & 3;                  // stream = tensor-memory lane quadrant
+    for (int j = 0; j < nb; ++j) {
+      const int sg = j % SG, b = j % ND;
+      if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { *abort_word = 1; break; }
+      const float* xs = reinterpret_cast<const float*>(sm + sg * 2 * F::GB) + F::GB / 4;
+      float xv[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) xv[t] = xs[(t * 4 + q) * CW + lane];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&gfree[sg]);
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) split_tf32(xv[t], hi[t], lo[t]);
+      if (j >= ND && !mbar_wait_or_abort(&a2_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) { *abort_word = 1; break; }
+      tc_fence_after();
+      const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + F::XT_COL + 32 * b;
+      tmem_st16(ta, hi);
+      tmem_st16(ta + 16, lo);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a2_ready[b]);
+    }
+  } else {
+    const int64_t c = c0 + lane;
+    float* locs = reinterpret_cast<float*>(sm + F::OFF_LOC);
+    float* gws = reinterpret_cast<float*>(sm + F::OFF_GW);
+    bool ok = true;
+    constexpr int TPE = F::TPE;
+    if (warp < 2 + F::E_WARPS) {
+      // ---------------- E: X^T operand and local terms ----------------
+      const int e = warp - 2;                // tokens TPE e .. TPE e + TPE - 1
+      const float wc = __ldg(w + c);
+      float gwacc = 0.f;
+      for (int j = 0; j < nb; ++j) {
+        const int sg = j % SG, si = j % SI, b = j % ND;
+        if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { ok = false; break; }
+        const float* gs = reinterpret_cast<const float*>(sm + sg * 2 * F::GB);
+        const float* xs = gs + F::GB / 4;
+        float gv[TPE][4], xv[TPE][4];        // [token][stream]
+#pragma unroll
+        for (int u = 0; u < TPE; ++u)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            gv[u][jj] = gs[((TPE * e + u) * 4 + jj) * CW + lane];
+            xv[u][jj] = xs[((TPE * e + u) * 4 + jj) * CW + lane];
+          }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&gfree[sg]);   // g, x now live in registers
+        if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { ok = false; break; }
+        const float* sc = reinterpret_cast<const float*>(sm + F::OFF_IMG + si * F::IMG) + F::IMG_SC;
+        // local terms of the four streams
+        if (j >= ND && !mbar_wait_or_abort(&loc_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) { ok = false; break; }
+        float* lb = locs + b * (F::LOCB / 4);
+#pragma unroll
+        for (int u = 0; u < TPE; ++u) {
+          const int t = TPE * e + u;
+          const float* st = sc + t * 32;
+          const float4 s0 = *reinterpret_cast<const float4*>(st);
+          const float4 h4 = *reinterpret_cast<const float4*>(st + 4);
+          const float4 q4 = *reinterpret_cast<const float4*>(st + 8);
+          const float gy = q4.x * gv[u][0] + q4.y * gv[u][1] + q4.z * gv[u][2] + q4.w * gv[u][3];
+          const float xa = h4.x * xv[u][0] + h4.y * xv[u][1] + h4.z * xv[u][2] + h4.w * xv[u][3];
+          const float agg = gy * wc * s0.y - xa * s0.x;
+          const float hh[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 m4 = *reinterpret_cast<const float4*>(st + 12 + 4 * i);
+            const float mix = m4.x * gv[u][0] + m4.y * gv[u][1] + m4.z * gv[u][2] + m4.w * gv[u][3];
+            lb[t * COLS + i * CW + lane] = mix + hh[i] * agg + s0.z * xv[u][i];
+          }
+          gwacc = fmaf(gy * xa, s0.y, gwacc);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&loc_ready[b]);
+          mbar_arrive(&ifree[si]);
+        }
+      }
+      gws[e * CW + lane] = gwacc;
+    } else {
+      // ---------------- epilogue: grad_x = D1 + local term ----------------
+      const int i = warp & 3;                // stream = tensor-memory lane quadrant
+      const bool leader = warp == 2 + F::E_WARPS && lane == 0;
+      for (int j = 0; j < nb; ++j) {
+        const int b = j % ND;
+        if (!mbar_wait_or_abort(&d1_full[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
+        tc_fence_after();
+        float d[16];
+        tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + 16 * b, d);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&d1_free[b]);
+        if (!mbar_wait_or_abort(&loc_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
+        float* lb = locs + b * (F::LOCB / 4) + i * CW + lane;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) lb[t * COLS] += d[t];
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (leader) {
+          tma_store_2d(&omap, locs + b * (F::LOCB / 4), (int)c0, (int)((blk0 + j) * TOK * 4));
+          bulk_commit();
+          // the previous block's buffer may be refilled once its store has read it
+          if (j > 0) {
+            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            mbar_arrive(&loc_free[(j - 1) % ND]);
+          }
+        }
+      }
+      if (leader) {
+        bulk_wait0();
+        if (ok && nb > 0) mbar_arrive(&loc_free[(nb - 1) % ND]);
+      }
+    }
+    if (!ok) *abort_word = 1;
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * (F::E_WARPS + 4)) : "memory");
+    ok = *abort_word == 0;
+    if (warp >= 2 + F::E_WARPS) {
+      const int i = warp & 3;
+      bool have = ok && nb > 0 && mbar_wait_or_abort(d2_done, 0u, abort_word);
+      have = __all_sync(0xffffffffu, have);
+      const bool write = have || (ok && nb == 0);
+      tc_fence_after();
+      float a[16], bb[16];
+      if (have) {
+        tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + F::D2_COL, a);
+        tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + F::D2_COL + 16, bb);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) { a[q] = 0.f; bb[q] = 0.f; }
+      }
+      if (write) {
+        float* dd = dphi_part + (int64_t)split * F::NH * nC + (int64_t)i * C + c;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) dd[(int64_t)k * nC] = a[k];
+#pragma unroll
+        for (int k = 16; k < F::NH; ++k) dd[(int64_t)k * nC] = bb[k - 16];
+        if (i == 0) {
+          float gsum = 0.f;
+#pragma unroll
+          for (int q = 0; q < F::E_WARPS; ++q) gsum += gws[q * CW + lane];
+          gw_part[(int64_t)split * C + c] = gsum;
+        }
+      }
+    }
+  }
+  if (warp == F::D2_WARP && lane == 0 && nb > 0) mbar_wait_or_abort(d2_done, 0u, abort_word);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(F::TMEM_COLS));
+}
+
 // ---------------------------------------------------------------------------
 // The tcgen05 grad_x below is parity-exact but, with its per-stage MMA round
 // trip, slower than the mma.sync kernel on B200; it is kept selectable for
@@ -2317,6 +2748,9 @@ FwdPlan plan_fwd(int64_t B, int64_t C) {
 struct BwdPlan {
   int ntiles, nsplit;
   int nsplit5;  // splits of the 32-channel tensor-core grad_x (n = 4, dynamic H)
+  int64_t nblk6;  // 16-token blocks of the warp-specialised grad_x (n = 4, dynamic H)
+  int nsplit6;
+  size_t img;
   size_t stats, tokb, tokr, dphi, gw, tot;
 };
 
@@ -2326,7 +2760,11 @@ BwdPlan plan_bwd(int64_t B, int64_t C) {
   p.ntiles = (int)((C + GX_CW - 1) / GX_CW);
   p.nsplit = choose_gx_splits(p.ntiles, B, num_sms(), N <= 4 ? 2 : 1);
   p.nsplit5 = (N == 4 && DYN) ? choose_gx_splits((C + 31) / 32, B, num_sms(), 2) : 0;
-  const int64_t msplit = p.nsplit > p.nsplit5 ? p.nsplit : p.nsplit5;
+  p.nblk6 = (N == 4 && DYN) ? (B + Gx6Cfg::TOK - 1) / Gx6Cfg::TOK : 0;
+  p.nsplit6 = (N == 4 && DYN && p.nblk6 > 0) ? choose_gx_splits((C + 31) / 32, p.nblk6, num_sms(), 1) : 0;
+  p.img = (size_t)p.nblk6 * Gx6Cfg::IMG_FLOATS;
+  int64_t msplit = p.nsplit > p.nsplit5 ? p.nsplit : p.nsplit5;
+  if (p.nsplit6 > msplit) msplit = p.nsplit6;
   p.stats = (size_t)B * L<N>::NS1 * 2;  // fp64
   p.tokb = (size_t)B * L<N>::TB;
   p.tokr = (size_t)B * (DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
@@ -2353,6 +2791,7 @@ size_t bwd_ws_bytes(int64_t B, int64_t C) {
   Carve cv(nullptr);
   cv.take(p.stats); cv.take(p.tokb); cv.take(p.tokr); cv.take(p.dphi); cv.take(p.gw);
   cv.take(p.tot);
+  cv.take(p.img);
   if (!DYN) cv.take(L<N>::REC);
   return cv.off;
 }
@@ -2523,6 +2962,7 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   float* dphi = cv.take(p.dphi);
   float* gwp = cv.take(p.gw);
   double* tot = (double*)cv.take(p.tot);
+  float* img = cv.take(p.img);
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(w);
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
   if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
@@ -2534,7 +2974,25 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   rc = check_launch("mhc_layer_bwd_dynamic/token_bwd");
   if (rc) return rc;
   int nsplit = p.nsplit;
-  if (!launch_grad_x_tma<N, true>(g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p, &nsplit, s))
+  bool gx_done = false;
+  if constexpr (N == 4) {
+    // warp-specialised tensor-core grad_x
+    using F6 = Gx6Cfg;
+    CUtensorMap gm, xm, om;
+    if (p.nsplit6 > 0 && C % F6::CW == 0 && aligned16(g) && aligned16(x) && aligned16(img) && aligned16(gx) &&
+        make_tmap_2d_f32(&gm, g, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW) &&
+        make_tmap_2d_f32(&xm, x, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW) &&
+        make_tmap_2d_f32(&om, gx, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW)) {
+      { ProfScope _ps("gx_image", s); gx_image_kernel<<<grid_1d(p.nblk6 * F6::TOK, 128), 128, 0, s>>>(tokb, img, B, p.nblk6); }
+      cudaFuncSetAttribute(grad_x6_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F6::SMEM);
+      const int nt6 = (int)(C / F6::CW);
+      { ProfScope _ps("grad_x", s); grad_x6_kernel<<<(unsigned)(nt6 * p.nsplit6), F6::THREADS, F6::SMEM, s>>>(
+          gm, xm, om, img, w, pp, pq, pr, gx, dphi, gwp, B, C, nt6, p.nsplit6, p.nblk6); }
+      nsplit = p.nsplit6;
+      gx_done = true;
+    }
+  }
+  if (!gx_done && !launch_grad_x_tma<N, true>(g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p, &nsplit, s))
     { ProfScope _ps("grad_x", s); grad_x_kernel<N, true><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
         g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
   rc = check_launch("mhc_layer_bwd_dynamic/grad_x");

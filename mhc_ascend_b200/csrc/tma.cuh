@@ -138,6 +138,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 1D bulk copy global -> this CTA's smem (addresses 16-byte aligned, bytes a
+// multiple of 16), completion counted on the mbarrier.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 2D tiled TMA load: box at (col, row) of the map into dst (this CTA's smem).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int col, int row,
                                             uint64_t* bar) {
