@@ -1902,21 +1902,6 @@ __global__ void __launch_bounds__(320, 2)
 }
 
 // ---------------------------------------------------------------------------
-// Backward 3 for n = 4 on tcgen05 (dynamic H, C % 32 == 0, aligned).
-//   CTA = 32 channels x 4 streams = 128 columns (col = i*32 + cl) = one
-//   M=128 MMA tile, 128 threads (one warpgroup), two CTAs per SM so that one
-//   CTA's tensor-core round trip overlaps the other's elementwise work; a
-//   contiguous token range; TMA ring of 16-token stages.  Per stage:
-//   (E)  thread = (4 consecutive tokens, one channel): local terms of the 4
-//        streams -> smem; x of its tokens -> the X^T operand (tf32 hi/lo);
-//        d_p split into tf32 hi/lo operands;
-//   (MMA) one thread issues, 3xTF32 each:
-//        D1[col x tok] = Phi^T[col x 24] . D_p^T          (M=128, N=16)
-//        D2[col x k]  += X^T[col x 16 tok] . D_p[16 x 32] (M=128, N=32)
-//        Phi^T (hi/lo) is resident in smem; D1, D2 live in tensor memory;
-//   (epilogue) thread = column (warp w = stream w): grad_x = D1 + local term.
-//   After the range: D2 -> this split's dphi partial.
-// ---------------------------------------------------------------------------
 // Backward 3 for n = 4, dynamic H, on tcgen05 with warp specialisation.
 //   CTA = 32 channels x 4 streams = 128 columns (col = 32 i + c) = one M=128
 //   MMA tile, a contiguous range of 16-token blocks; 27 warps: warp 0 TMA,
@@ -2317,257 +2302,6 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(F::TMEM_COLS));
 }
 
-// ---------------------------------------------------------------------------
-// The tcgen05 grad_x below is parity-exact but, with its per-stage MMA round
-// trip, slower than the mma.sync kernel on B200; it is kept selectable for
-// the warp-specialised rewrite.
-constexpr bool kGradXTcgen05 = false;
-
-struct Gx5Cfg {
-  static constexpr int CW = 32, COLS = 128, TOK = 16, TB = L<4>::TB, NHP = 24, KP = 32;
-  static constexpr int STAGES = 2, THREADS = 128;
-  static constexpr int TILE = TOK * COLS;
-  static constexpr int STAGE = 2 * TILE + TOK * TB;              // floats
-  static constexpr uint32_t STAGE_BYTES = STAGE * 4;
-  static constexpr uint32_t OFF_RING = 0;
-  static constexpr uint32_t OFF_A1H = OFF_RING + STAGES * STAGE_BYTES;   // Phi^T [128][24]
-  static constexpr uint32_t OFF_A1L = OFF_A1H + COLS * NHP * 4;
-  static constexpr uint32_t OFF_A2H = OFF_A1L + COLS * NHP * 4;          // X^T [128][16]
-  static constexpr uint32_t OFF_A2L = OFF_A2H + COLS * TOK * 4;
-  static constexpr uint32_t OFF_B1H = OFF_A2L + COLS * TOK * 4;          // D_p [16][24]
-  static constexpr uint32_t OFF_B1L = OFF_B1H + TOK * NHP * 4;
-  static constexpr uint32_t OFF_B2H = OFF_B1L + TOK * NHP * 4;           // D_p^T [32][16]
-  static constexpr uint32_t OFF_B2L = OFF_B2H + KP * TOK * 4;
-  static constexpr uint32_t OFF_GXL = OFF_B2L + KP * TOK * 4;            // local terms [16][128]
-  static constexpr uint32_t OFF_GW = OFF_GXL + TOK * COLS * 4;           // [4][32]
-  static constexpr uint32_t OFF_BAR = OFF_GW + 4 * CW * 4;               // STAGES + 1 mbarriers
-  static constexpr uint32_t OFF_TMEM = OFF_BAR + (STAGES + 1) * 8;
-  static constexpr size_t SMEM = OFF_TMEM + 16 + 128;
-  static constexpr uint32_t TMEM_COLS = 64;   // D1: cols [0,16), D2: [32,64)
-};
-
-__global__ void __launch_bounds__(128, 2)
-    grad_x5_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
-                   const __grid_constant__ CUtensorMap tmap, const float* __restrict__ w,
-                   const float* __restrict__ phi_pre, const float* __restrict__ phi_post,
-                   const float* __restrict__ phi_res, float* __restrict__ gx,
-                   float* __restrict__ dphi_part, float* __restrict__ gw_part, int64_t B,
-                   int64_t C, int ntiles, int nsplit) {
-  using F = Gx5Cfg;
-  using Lc = L<4>;
-  constexpr int N = 4, CW = F::CW, COLS = F::COLS, NHP = F::NHP, TB = F::TB, TOK = F::TOK;
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  float* ring = reinterpret_cast<float*>(sm + F::OFF_RING);
-  float* gxl = reinterpret_cast<float*>(sm + F::OFF_GXL);
-  float* gwS = reinterpret_cast<float*>(sm + F::OFF_GW);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + F::OFF_BAR);
-  uint64_t* mma_bar = bars + F::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + F::OFF_TMEM);
-  const uint32_t sbase = smem_u32(sm);
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int tile = blockIdx.x % ntiles;
-  const int split = blockIdx.x / ntiles;
-  const int64_t c0 = (int64_t)tile * CW;
-  const int64_t nC = (int64_t)N * C;
-  const int64_t tb0 = B * split / nsplit, tb1 = B * (split + 1) / nsplit;
-  const int nbatch = (int)((tb1 - tb0 + TOK - 1) / TOK);
-
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(F::TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  if (tid == 0) {
-    prefetch_tmap(&gmap);
-    prefetch_tmap(&xmap);
-    prefetch_tmap(&tmap);
-    for (int st = 0; st <= F::STAGES; ++st) mbar_init(&bars[st], 1);
-    fence_mbar_init();
-  }
-  // resident operand Phi^T (hi/lo) and the zero rows k = 24..31 of D_p^T
-  for (int e = tid; e < COLS * NHP; e += F::THREADS) {
-    const int k = e / COLS, col = e % COLS;
-    const int i = col / CW, cl = col % CW;
-    const float v = k < Lc::NH ? __ldg(phi_row(phi_pre, phi_post, phi_res, k, N, nC) + (int64_t)i * C + c0 + cl) : 0.f;
-    uint32_t hi, lo;
-    split_tf32(v, hi, lo);
-    const uint32_t off = umma_kmaj_off(col, k, COLS);
-    *reinterpret_cast<uint32_t*>(sm + F::OFF_A1H + off) = hi;
-    *reinterpret_cast<uint32_t*>(sm + F::OFF_A1L + off) = lo;
-  }
-  for (int e = tid; e < (F::KP - NHP) * TOK; e += F::THREADS) {
-    const int k = NHP + e / TOK, tt = e % TOK;
-    const uint32_t off = umma_kmaj_off(k, tt, F::KP);
-    *reinterpret_cast<uint32_t*>(sm + F::OFF_B2H + off) = 0u;
-    *reinterpret_cast<uint32_t*>(sm + F::OFF_B2L + off) = 0u;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  auto issue = [&](int j) {
-    const int slot = j % F::STAGES;
-    float* base = ring + slot * F::STAGE;
-    const int t0 = (int)(tb0 + (int64_t)j * TOK);
-    mbar_expect_tx(&bars[slot], F::STAGE_BYTES);
-    tma_load_2d(base, &gmap, (int)c0, t0 * N, &bars[slot]);
-    tma_load_2d(base + F::TILE, &xmap, (int)c0, t0 * N, &bars[slot]);
-    tma_load_2d(base + 2 * F::TILE, &tmap, 0, t0, &bars[slot]);
-  };
-  if (tid == 0)
-    for (int j = 0; j < F::STAGES && j < nbatch; ++j) issue(j);
-
-  // (E) mapping: tokens 4*warp .. 4*warp+3, channel = lane
-  const int ecl = lane;
-  const float wc = __ldg(w + c0 + ecl);
-  float gwacc = 0.f;
-  // epilogue mapping: TMEM lane quadrant = warp -> column 32*warp + lane = (stream warp, channel lane)
-
-  constexpr uint32_t ID1 = umma_idesc_tf32(128, TOK);
-  constexpr uint32_t ID2 = umma_idesc_tf32(128, F::KP);
-  bool failed = false;
-  for (int j = 0; j < nbatch; ++j) {
-    const int slot = j % F::STAGES;
-    bool ok = true;
-    if (tid == 0) ok = mbar_wait(&bars[slot], (uint32_t)((j / F::STAGES) & 1));
-    if (__syncthreads_or(!ok)) { failed = true; break; }
-    if (tid == 0 && j >= 1 && j - 1 + F::STAGES < nbatch) issue(j - 1 + F::STAGES);
-    const float* gs = ring + slot * F::STAGE;
-    const float* xs = gs + F::TILE;
-    const float* ts = xs + F::TILE;
-    const int64_t t0 = tb0 + (int64_t)j * TOK;
-    const int nt = (int)((tb1 - t0) < TOK ? (tb1 - t0) : TOK);
-
-    // d_p operands (tokens beyond the range contribute zero)
-    for (int e = tid; e < TOK * NHP; e += F::THREADS) {
-      const int tt = e / NHP, k = e % NHP;
-      const float d = tt < nt ? ts[tt * TB + 4 + k] : 0.f;
-      uint32_t hi, lo;
-      split_tf32(d, hi, lo);
-      const uint32_t o1 = umma_kmaj_off(tt, k, TOK), o2 = umma_kmaj_off(k, tt, F::KP);
-      *reinterpret_cast<uint32_t*>(sm + F::OFF_B1H + o1) = hi;
-      *reinterpret_cast<uint32_t*>(sm + F::OFF_B1L + o1) = lo;
-      *reinterpret_cast<uint32_t*>(sm + F::OFF_B2H + o2) = hi;
-      *reinterpret_cast<uint32_t*>(sm + F::OFF_B2L + o2) = lo;
-    }
-    // (E) local terms + X^T operand
-    {
-      float xq[4][4];   // [stream][token]
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int tt = 4 * warp + u;
-        float gv[4], xv[4];
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          gv[jj] = gs[(tt * 4 + jj) * CW + ecl];
-          xv[jj] = xs[(tt * 4 + jj) * CW + ecl];
-          xq[jj][u] = xv[jj];
-        }
-        if (tt < nt) {
-          const float* st = ts + tt * TB;
-          const float4 s0 = *reinterpret_cast<const float4*>(st);
-          const float4 h4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TH);
-          const float4 q4 = *reinterpret_cast<const float4*>(st + Lc::OFF_THP);
-          const float h[4] = {h4.x, h4.y, h4.z, h4.w};
-          const float hq[4] = {q4.x, q4.y, q4.z, q4.w};
-          float gy = 0.f, xa = 0.f;
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) { gy = fmaf(hq[jj], gv[jj], gy); xa = fmaf(h[jj], xv[jj], xa); }
-          const float agg = gy * wc * s0.y - xa * s0.x;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float4 m4 = *reinterpret_cast<const float4*>(st + Lc::OFF_TM + 4 * i);
-            const float mix = m4.x * gv[0] + m4.y * gv[1] + m4.z * gv[2] + m4.w * gv[3];
-            gxl[tt * COLS + i * CW + ecl] = mix + h[i] * agg + s0.z * xv[i];
-          }
-          gwacc = fmaf(gy * xa, s0.y, gwacc);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint4 hi, lo;
-        split_tf32(xq[i][0], hi.x, lo.x);
-        split_tf32(xq[i][1], hi.y, lo.y);
-        split_tf32(xq[i][2], hi.z, lo.z);
-        split_tf32(xq[i][3], hi.w, lo.w);
-        const uint32_t off = umma_kmaj_off(i * CW + ecl, 4 * warp, COLS);
-        *reinterpret_cast<uint4*>(sm + F::OFF_A2H + off) = hi;
-        *reinterpret_cast<uint4*>(sm + F::OFF_A2L + off) = lo;
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0) {
-#pragma unroll
-      for (int s = 0; s < 3; ++s) {
-        const uint64_t ah = umma_desc_k(sbase + F::OFF_A1H, COLS, s, 0);
-        const uint64_t al = umma_desc_k(sbase + F::OFF_A1L, COLS, s, 0);
-        const uint64_t bh = umma_desc_k(sbase + F::OFF_B1H, TOK, s, 0);
-        const uint64_t bl = umma_desc_k(sbase + F::OFF_B1L, TOK, s, 0);
-        umma_tf32(tmem, al, bh, ID1, s > 0);
-        umma_tf32(tmem, ah, bl, ID1, 1);
-        umma_tf32(tmem, ah, bh, ID1, 1);
-      }
-#pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        const uint64_t ah = umma_desc_k(sbase + F::OFF_A2H, COLS, s, 0);
-        const uint64_t al = umma_desc_k(sbase + F::OFF_A2L, COLS, s, 0);
-        const uint64_t bh = umma_desc_k(sbase + F::OFF_B2H, F::KP, s, 0);
-        const uint64_t bl = umma_desc_k(sbase + F::OFF_B2L, F::KP, s, 0);
-        umma_tf32(tmem + 32, al, bh, ID2, (j > 0 || s > 0) ? 1u : 0u);
-        umma_tf32(tmem + 32, ah, bl, ID2, 1);
-        umma_tf32(tmem + 32, ah, bh, ID2, 1);
-      }
-      umma_commit(mma_bar);
-    }
-    ok = true;
-    if (tid == 0) ok = mbar_wait(mma_bar, (uint32_t)(j & 1));
-    if (__syncthreads_or(!ok)) { failed = true; break; }
-    tc_fence_after();
-    // epilogue: grad_x = D1 + local term; thread = column (stream warp, channel lane)
-    {
-      float v[16];
-      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16), v);
-      float* dst = gx + t0 * nC + (int64_t)warp * C + c0 + lane;
-#pragma unroll
-      for (int tt = 0; tt < TOK; ++tt)
-        if (tt < nt) __stcs(dst + tt * nC, v[tt] + gxl[tt * COLS + warp * CW + lane]);
-    }
-    tc_fence_before();
-  }
-  if (!failed) {
-    // dphi partial of this split from D2 (rows = columns, cols = k)
-    float a[16], b[16];
-    if (nbatch > 0) {
-      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + 32, a);
-      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + 48, b);
-    } else {
-#pragma unroll
-      for (int q = 0; q < 16; ++q) { a[q] = 0.f; b[q] = 0.f; }
-    }
-    float* dst = dphi_part + (int64_t)split * Lc::NH * nC + (int64_t)warp * C + c0 + lane;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) dst[(int64_t)k * nC] = a[k];
-#pragma unroll
-    for (int k = 16; k < Lc::NH; ++k) dst[(int64_t)k * nC] = b[k - 16];
-    gwS[warp * CW + ecl] = gwacc;
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (!failed && tid < CW) {
-    float sacc = 0.f;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) sacc += gwS[q * CW + tid];
-    gw_part[(int64_t)split * C + c0 + tid] = sacc;
-  }
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(F::TMEM_COLS));
-}
-
 // out[l] = sum_s part[s * L + l]   (fixed order over splits)
 __global__ void __launch_bounds__(256)
     reduce_splits_kernel(const float* __restrict__ part, int nsplit, int64_t L,
@@ -2747,7 +2481,6 @@ FwdPlan plan_fwd(int64_t B, int64_t C) {
 
 struct BwdPlan {
   int ntiles, nsplit;
-  int nsplit5;  // splits of the 32-channel tensor-core grad_x (n = 4, dynamic H)
   int64_t nblk6;  // 16-token blocks of the warp-specialised grad_x (n = 4, dynamic H)
   int nsplit6;
   size_t img;
@@ -2759,11 +2492,10 @@ BwdPlan plan_bwd(int64_t B, int64_t C) {
   BwdPlan p;
   p.ntiles = (int)((C + GX_CW - 1) / GX_CW);
   p.nsplit = choose_gx_splits(p.ntiles, B, num_sms(), N <= 4 ? 2 : 1);
-  p.nsplit5 = (N == 4 && DYN) ? choose_gx_splits((C + 31) / 32, B, num_sms(), 2) : 0;
   p.nblk6 = (N == 4 && DYN) ? (B + Gx6Cfg::TOK - 1) / Gx6Cfg::TOK : 0;
   p.nsplit6 = (N == 4 && DYN && p.nblk6 > 0) ? choose_gx_splits((C + 31) / 32, p.nblk6, num_sms(), 1) : 0;
   p.img = (size_t)p.nblk6 * Gx6Cfg::IMG_FLOATS;
-  int64_t msplit = p.nsplit > p.nsplit5 ? p.nsplit : p.nsplit5;
+  int64_t msplit = p.nsplit;
   if (p.nsplit6 > msplit) msplit = p.nsplit6;
   p.stats = (size_t)B * L<N>::NS1 * 2;  // fp64
   p.tokb = (size_t)B * L<N>::TB;
@@ -2814,22 +2546,6 @@ bool launch_grad_x_tma(const float* g, const float* x, const float* w, const flo
   if constexpr (N > 4) {
     return false;
   } else {
-    if constexpr (N == 4 && DYN && kGradXTcgen05) {
-      using F5 = Gx5Cfg;
-      CUtensorMap gm, xm, tm;
-      const int nt5 = (int)(C / F5::CW);
-      const int ns5 = p.nsplit5;
-      if (C % F5::CW == 0 && aligned16(g) && aligned16(x) && aligned16(tokb) &&
-          make_tmap_2d_f32(&gm, g, (uint64_t)B * N, C, C, F5::TOK * N, F5::CW) &&
-          make_tmap_2d_f32(&xm, x, (uint64_t)B * N, C, C, F5::TOK * N, F5::CW) &&
-          make_tmap_2d_f32(&tm, tokb, B, L<N>::TB, L<N>::TB, F5::TOK, L<N>::TB)) {
-        cudaFuncSetAttribute(grad_x5_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F5::SMEM);
-        { ProfScope _ps("grad_x", s); grad_x5_kernel<<<(unsigned)(nt5 * ns5), F5::THREADS, F5::SMEM, s>>>(
-            gm, xm, tm, w, pp, pq, pr, gx, dphi, gwp, B, C, nt5, ns5); }
-        *nsplit_used = ns5;
-        return true;
-      }
-    }
     if constexpr (N == 4) {
       using F = Gx4Cfg;
       CUtensorMap gm, xm, tm, om;
