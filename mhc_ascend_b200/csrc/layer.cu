@@ -1619,6 +1619,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // D (tmem) (+)= A (tmem, M lanes x 8 columns) . B (smem descriptor)^T, kind::tf32
 __device__ __forceinline__ void umma_tf32_at(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
@@ -1633,34 +1638,36 @@ __device__ __forceinline__ void umma_tf32_at(uint32_t d_tmem, uint32_t a_tmem, u
 // ---------------------------------------------------------------------------
 // Forward 1 on tcgen05: projection p = x_flat . phi^T and the per-token Gram
 // matrix of the n streams, for n <= 4 (C % 4 == 0, x 16-byte aligned).
-//   CTA = 128 tokens (one M=128 MMA tile) x one split of the channels,
-//   warp-specialised: warp 0 issues TMA, warp 1 issues MMAs, warps 2..9
-//   (two threads per token, one per half of a 128-byte row) prepare operands.
-//   A stage is one stream x 32 channels: x[128 tokens x 32] and
-//   phi_hi / phi_lo[NB rows x 32] (phi split once per call), K-major in the
-//   128-byte-swizzled layout that TMA writes directly.  The compute threads
-//   rewrite their row as tf32 hi in place plus tf32 lo in a second buffer
-//   (keeping the swizzled offsets), keep the values of the n streams of a
-//   channel block in registers and accumulate the Gram entries; the MMA warp
-//   then adds x_lo.phi_hi + x_hi.phi_lo + x_hi.phi_hi (3xTF32) into tensor
-//   memory and frees the stage with tcgen05.commit.  Barriers per stage:
-//   full (TMA bytes), ready (8 compute warps), empty (MMA commit).
+//   CTA = 128 tokens (one M=128 MMA tile) x one split of the channels, two
+//   CTAs per SM, warp-specialised: warp 0 issues TMA, warp 1 issues MMAs,
+//   warps 2..9 (two threads per token, one per half of a 128-byte row)
+//   prepare the A operand.  A stage is one stream x 32 channels: x[128 tokens
+//   x 32] and phi_hi / phi_lo[NB rows x 32] (phi split once per call), both
+//   128-byte-swizzled as TMA writes them.  The operand threads read their
+//   token's row, keep the values of the n streams of a channel block in
+//   registers for the Gram entries, and store the row split into tf32 hi/lo
+//   into tensor memory with tcgen05.st (lane = token, column = channel: the
+//   A operand, no proxy fence); the MMA warp adds x_lo.phi_hi + x_hi.phi_lo +
+//   x_hi.phi_hi (3xTF32) into the accumulator in tensor memory.  Barriers:
+//   full (TMA bytes), empty (operand warps done with x + MMA done with phi),
+//   aready / afree per tensor-memory A buffer.
 // ---------------------------------------------------------------------------
 template <int N>
 struct PumCfg {
   static constexpr int NH = L<N>::NH, NHP = L<N>::NHP, NG = L<N>::NG;
   static constexpr int NB = (NH + 15) / 16 * 16;           // MMA N (padded phi rows)
-  static constexpr int TCOLS = 32;
   static constexpr int TOK = 128, CH = 32, THREADS = 320;
   static constexpr uint32_t XB = TOK * CH * 4;             // x tile of one stage
   static constexpr uint32_t PB = NB * CH * 4;              // phi tile of one stage
-  static constexpr uint32_t SLOT = 2 * XB + 2 * PB;        // x/hi, lo, phi_hi, phi_lo
-  static constexpr uint32_t OFF_LO = XB, OFF_PH = 2 * XB, OFF_PL = 2 * XB + PB;
-  static constexpr uint32_t TX = XB + 2 * PB;              // bytes TMA brings per stage
-  static constexpr int STAGES = 2;                        // two CTAs per SM
+  static constexpr uint32_t SLOT = XB + 2 * PB;            // x, phi_hi, phi_lo
+  static constexpr uint32_t OFF_PH = XB, OFF_PL = XB + PB;
+  static constexpr uint32_t TX = SLOT;                     // bytes TMA brings per stage
+  static constexpr int STAGES = 4, NA = 2;                 // smem stages, tensor-memory A buffers
+  static constexpr uint32_t TCOLS = 256;                   // D [0, 32); A[a] = [64 + 64 a, +64) hi|lo
+  static constexpr uint32_t ACOL = 64;
   static constexpr uint32_t OFF_GX = STAGES * SLOT;        // Gram exchange [128][NG]
   static constexpr uint32_t OFF_BAR = OFF_GX + TOK * NG * 4;
-  static constexpr size_t SMEM = OFF_BAR + (3 * STAGES + 1) * 8 + 16 + 1024;
+  static constexpr size_t SMEM = OFF_BAR + (2 * STAGES + 2 * NA + 1) * 8 + 16 + 1024;
   static_assert(NB <= 32, "one 32-column accumulator");
   static_assert(XB % 1024 == 0 && PB % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 };
@@ -1718,14 +1725,15 @@ __global__ void __launch_bounds__(320, 2)
                      const __grid_constant__ CUtensorMap lmap, float* __restrict__ ppart,
                      float* __restrict__ gpart, int64_t B, int64_t C, int cps) {
   using P = PumCfg<N>;
-  constexpr int NG = P::NG, NHP = P::NHP, S = P::STAGES;
+  constexpr int NG = P::NG, NHP = P::NHP, S = P::STAGES, NA = P::NA;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* gx_s = reinterpret_cast<float*>(sm + P::OFF_GX);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + P::OFF_BAR);
-  uint64_t* ready = full + S;
-  uint64_t* empty = ready + S;
-  uint64_t* done = empty + S;
+  uint64_t* empty = full + S;
+  uint64_t* aready = empty + S;
+  uint64_t* afree = aready + NA;
+  uint64_t* done = afree + NA;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t sbase = smem_u32(sm);
@@ -1748,8 +1756,11 @@ __global__ void __launch_bounds__(320, 2)
     prefetch_tmap(&lmap);
     for (int st = 0; st < S; ++st) {
       mbar_init(&full[st], 1);
-      mbar_init(&ready[st], 8);
-      mbar_init(&empty[st], 1);
+      mbar_init(&empty[st], 1 + 8);
+    }
+    for (int a = 0; a < NA; ++a) {
+      mbar_init(&aready[a], 8);
+      mbar_init(&afree[a], 1);
     }
     mbar_init(done, 1);
     *abort_word = 0;
@@ -1788,32 +1799,34 @@ __global__ void __launch_bounds__(320, 2)
     if (lane == 0) {
       constexpr uint32_t ID = umma_idesc_tf32(128, P::NB);
       for (int k = 0; k < nchunks; ++k) {
-        const int slot = k % S;
-        if (!mbar_wait_or_abort(&ready[slot], (uint32_t)((k / S) & 1), abort_word)) {
+        const int slot = k % S, a = k % NA;
+        if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word) ||
+            !mbar_wait_or_abort(&aready[a], (uint32_t)((k / NA) & 1), abort_word)) {
           *abort_word = 1;
           break;
         }
         tc_fence_after();
         const uint32_t sb = sbase + slot * P::SLOT;
+        const uint32_t at = tmem + P::ACOL + 64 * a;
 #pragma unroll
         for (int st = 0; st < P::CH / 8; ++st) {
-          const uint64_t ah = umma_desc_sw128(sb + 32 * st);
-          const uint64_t al = umma_desc_sw128(sb + P::OFF_LO + 32 * st);
           const uint64_t bh = umma_desc_sw128(sb + P::OFF_PH + 32 * st);
           const uint64_t bl = umma_desc_sw128(sb + P::OFF_PL + 32 * st);
-          umma_tf32(tmem, al, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
-          umma_tf32(tmem, ah, bl, ID, 1u);
-          umma_tf32(tmem, ah, bh, ID, 1u);
+          umma_tf32_at(tmem, at + 32 + 8 * st, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
+          umma_tf32_at(tmem, at + 8 * st, bl, ID, 1u);
+          umma_tf32_at(tmem, at + 8 * st, bh, ID, 1u);
         }
         umma_commit(&empty[slot]);
+        umma_commit(&afree[a]);
       }
       umma_commit(done);
     }
   } else {
-    // ---------------- operand preparation + Gram ----------------
+    // ---------------- A operand (tensor memory) + Gram ----------------
     const int cw = warp - 2;               // 0..7
     const int h = cw >> 2;                 // half of the 128-byte row
-    const int r = 32 * (warp & 3) + lane;  // token row = tensor-memory lane
+    const int qd = warp & 3;               // tensor-memory lane quadrant
+    const int r = 32 * qd + lane;          // token row = tensor-memory lane
     const uint32_t rowoff = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     uint32_t choff[4];
 #pragma unroll
@@ -1827,26 +1840,31 @@ __global__ void __launch_bounds__(320, 2)
 #pragma unroll
       for (int i = 0; i < N; ++i) {
         const int k = b * N + i;
-        const int slot = k % S;
-        unsigned char* base = sm + slot * P::SLOT;
-        if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word)) {
-          *abort_word = 1;
-          ok = false;
-          break;
-        }
+        const int slot = k % S, a = k % NA;
+        const unsigned char* base = sm + slot * P::SLOT;
+        if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word)) { ok = false; break; }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float4 a = *reinterpret_cast<const float4*>(base + choff[j]);
-          v[i][4 * j + 0] = a.x; v[i][4 * j + 1] = a.y; v[i][4 * j + 2] = a.z; v[i][4 * j + 3] = a.w;
-          uint4 hi, lo;
-          split_tf32(a.x, hi.x, lo.x); split_tf32(a.y, hi.y, lo.y);
-          split_tf32(a.z, hi.z, lo.z); split_tf32(a.w, hi.w, lo.w);
-          *reinterpret_cast<uint4*>(base + choff[j]) = hi;
-          *reinterpret_cast<uint4*>(base + P::OFF_LO + choff[j]) = lo;
+          const float4 q4 = *reinterpret_cast<const float4*>(base + choff[j]);
+          v[i][4 * j + 0] = q4.x; v[i][4 * j + 1] = q4.y; v[i][4 * j + 2] = q4.z; v[i][4 * j + 3] = q4.w;
         }
-        fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ready[slot]);
+        if (lane == 0) mbar_arrive(&empty[slot]);  // x of this stage now lives in registers
+        if (k >= NA && !mbar_wait_or_abort(&afree[a], (uint32_t)(((k / NA) - 1) & 1), abort_word)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + P::ACOL + 64 * a + 16 * h;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) split_tf32(v[i][8 * hf + e], hi[e], lo[e]);
+          tmem_st8(ta + 8 * hf, hi);
+          tmem_st8(ta + 32 + 8 * hf, lo);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aready[a]);
       }
       if (!ok) break;
       // Gram of this block first, then the running sum: the rounding error
@@ -1863,6 +1881,7 @@ __global__ void __launch_bounds__(320, 2)
           ++g;
         }
     }
+    if (!ok) *abort_word = 1;
     // results: D columns [16h, 16h + 16) of this token, Gram halves summed
     bool have = ok && nchunks > 0 && mbar_wait_or_abort(done, 0u, abort_word);
     have = __all_sync(0xffffffffu, have);
@@ -1871,7 +1890,7 @@ __global__ void __launch_bounds__(320, 2)
     if (16 * h < NHP) {
       float d[16];
       if (have) {
-        tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 16 * h, d);
+        tmem_ld16(tmem + ((uint32_t)(32 * qd) << 16) + 16 * h, d);
       } else {
 #pragma unroll
         for (int e = 0; e < 16; ++e) d[e] = 0.f;
