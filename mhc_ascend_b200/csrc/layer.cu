@@ -2547,6 +2547,10 @@ size_t bwd_ws_bytes(int64_t B, int64_t C) {
   return cv.off;
 }
 
+// Per-token kernels run one thread per token with long dependent fp64
+// chains; one-warp blocks spread a few thousand tokens over every SM.
+constexpr int kTokThreads = 32;
+
 inline unsigned grid_1d(int64_t n, int threads, int64_t cap = 1 << 30) {
   int64_t g = (n + threads - 1) / threads;
   if (g < 1) g = 1;
@@ -2665,7 +2669,7 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
   }
   rc = check_launch("mhc_layer_fwd_dynamic/proj_stats");
   if (rc) return rc;
-  { ProfScope _ps("token_fwd", s); token_fwd_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(ppart, gpart, ks, ap, aq, ar, bp, bq, br,
+  { ProfScope _ps("token_fwd", s); token_fwd_kernel<N><<<grid_1d(B, kTokThreads), kTokThreads, 0, s>>>(ppart, gpart, ks, ap, aq, ar, bp, bq, br,
                                                      rec, B, C, iters, s_eps, r_eps); }
   rc = check_launch("mhc_layer_fwd_dynamic/token_fwd");
   if (rc) return rc;
@@ -2704,7 +2708,7 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
   int rc = check_launch("mhc_layer_bwd_dynamic/bwd_stats");
   if (rc) return rc;
-  { ProfScope _ps("token_bwd", s); token_bwd_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, rec, ap, aq, ar, bp, bq, br, tokb,
+  { ProfScope _ps("token_bwd", s); token_bwd_kernel<N><<<grid_1d(B, kTokThreads), kTokThreads, 0, s>>>(stats, rec, ap, aq, ar, bp, bq, br, tokb,
                                                      tokr, B, C, iters, s_eps, r_eps); }
   rc = check_launch("mhc_layer_bwd_dynamic/token_bwd");
   if (rc) return rc;
@@ -2787,7 +2791,7 @@ int run_bwd_static(const float* g, const float* x, const float* w, const float* 
   else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
   int rc = check_launch("mhc_layer_bwd_static/bwd_stats");
   if (rc) return rc;
-  { ProfScope _ps("token_bwd_static", s); token_bwd_static_kernel<N><<<grid_1d(B, 128), 128, 0, s>>>(stats, Hp, Hq, rec, tokb, tokr, B, C, r_eps); }
+  { ProfScope _ps("token_bwd_static", s); token_bwd_static_kernel<N><<<grid_1d(B, kTokThreads), kTokThreads, 0, s>>>(stats, Hp, Hq, rec, tokb, tokr, B, C, r_eps); }
   int nsplit = p.nsplit;
   if (!launch_grad_x_tma<N, false>(g, x, w, nullptr, nullptr, nullptr, tokb, gx, nullptr, gwp, B,
                                    C, p, &nsplit, s))
