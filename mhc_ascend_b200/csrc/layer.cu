@@ -1923,17 +1923,17 @@ __global__ void __launch_bounds__(320, 2)
 // ---------------------------------------------------------------------------
 // Backward 3 for n = 4, dynamic H, on tcgen05 with warp specialisation.
 //   CTA = 32 channels x 4 streams = 128 columns (col = 32 i + c) = one M=128
-//   MMA tile, a contiguous range of 16-token blocks; 27 warps: warp 0 TMA,
-//   warp 1 issues D1, warps 2..17 "E" (one token each, lane = channel, all
+//   MMA tile, a contiguous range of 32-token blocks; 27 warps: warp 0 TMA,
+//   warp 1 issues D1, warps 2..17 "E" (two tokens each, lane = channel, all
 //   four streams), warps 18..21 epilogue and warps 23..26 X^T (stream = the
 //   tensor-memory lane quadrant of the warp, lane = channel), warp 22 issues
 //   D2.  Per block j:
-//     TMA:  g, x [16 tokens x 4 streams x 32 channels] and the block's
+//     TMA:  g, x [32 tokens x 4 streams x 32 channels] and the block's
 //           operand image (d_p split into tf32 hi/lo in both the B layout of
 //           D1 and of D2, plus the per-token scalars), written by
 //           gx_image_kernel in the exact K-major shared-memory layout;
-//     MMA:  D1[b] = Phi^T[col x 24] . D_p^T      (M=128, N=16, 3xTF32)
-//           D2   += X^T[col x 16 tok] . D_p      (M=128, N=32, 3xTF32)
+//     MMA:  D1[b] = Phi^T[col x 24] . D_p^T      (M=128, N=32, 3xTF32)
+//           D2   += X^T[col x 32 tok] . D_p      (M=128, N=32, 3xTF32)
 //           with Phi^T resident in shared memory, X^T (A of D2) and D1 in
 //           tensor memory, ND-deep;
 //     X^T:  x of the warp's stream split into tf32 hi/lo and stored into
@@ -1948,31 +1948,32 @@ __global__ void __launch_bounds__(320, 2)
 //   this split's grad-w partial.
 // ---------------------------------------------------------------------------
 struct Gx6Cfg {
-  static constexpr int CW = 32, COLS = 128, TOK = 16, NH = 24, KP = 32;
-  static constexpr int SG = 6, SI = 6, ND = 4, E_WARPS = 16, TPE = 1, THREADS = 32 * (2 + E_WARPS + 4 + 1 + 4);
+  static constexpr int CW = 32, COLS = 128, TOK = 32, NH = 24, KP = 32;
+  static constexpr int SG = 3, SI = 3, ND = 2, E_WARPS = 16, TPE = TOK / E_WARPS, THREADS = 32 * (2 + E_WARPS + 4 + 1 + 4);
   static constexpr int D2_WARP = 2 + E_WARPS + 4;          // issues the D2 MMAs
   static constexpr int XT_WARP0 = D2_WARP + 1;             // first of the four X^T warps
-  // operand image of one 16-token block (floats)
-  static constexpr int IMG_B1H = 0, IMG_B1L = 384, IMG_B2H = 768, IMG_B2L = 1280, IMG_SC = 1792;
-  static constexpr int IMG_FLOATS = 2304;
+  // operand image of one token block (floats)
+  static constexpr int IMG_B1H = 0, IMG_B1L = TOK * NH, IMG_B2H = 2 * TOK * NH, IMG_B2L = IMG_B2H + KP * TOK;
+  static constexpr int IMG_SC = IMG_B2L + KP * TOK, IMG_FLOATS = IMG_SC + TOK * 32;
   static constexpr uint32_t IMG = IMG_FLOATS * 4;
   static constexpr uint32_t GB = TOK * 4 * CW * 4;         // g (or x) tile bytes
   static constexpr uint32_t OFF_IMG = SG * 2 * GB;         // g/x ring, then the image ring
   static constexpr uint32_t OFF_A1H = OFF_IMG + SI * IMG;  // Phi^T [128 x 24]
   static constexpr uint32_t OFF_A1L = OFF_A1H + COLS * NH * 4;
-  static constexpr uint32_t LOCB = TOK * COLS * 4;         // local terms [16 tokens][128 columns]
+  static constexpr uint32_t LOCB = TOK * COLS * 4;         // local terms [tokens][128 columns]
   static constexpr uint32_t OFF_LOC = OFF_A1L + COLS * NH * 4;  // [ND buffers]
   static constexpr uint32_t OFF_GW = OFF_LOC + ND * LOCB;  // grad-w partials [E warps][32]
   static constexpr uint32_t OFF_BAR = OFF_GW + E_WARPS * CW * 4;
   static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 1;
   static constexpr size_t SMEM = OFF_BAR + NBAR * 8 + 16 + 128;
-  static constexpr uint32_t TMEM_COLS = 256;   // D1[b]: [16 b, +16); D2: [64, 96); X^T[b]: [128 + 32 b, +32) hi|lo
+  static constexpr uint32_t TMEM_COLS = 256;   // D1[b]: [TOK b, +TOK); D2: [64, 96); X^T[b]: [128 + 2 TOK b, +2 TOK) hi|lo
   static constexpr uint32_t D2_COL = 64, XT_COL = 128;
+  static_assert(ND * TOK <= 64 && XT_COL + 2 * TOK * ND <= TMEM_COLS && TOK % 16 == 0, "tensor-memory plan");
 };
 
-// Operand image of each 16-token block from the per-token backward rows:
-// D_p hi/lo as the K-major [16 tokens x 24] B operand of D1 and as the
-// K-major [32 (k, zero-padded) x 16 tokens] B operand of D2, and 32 scalars
+// Operand image of each token block from the per-token backward rows:
+// D_p hi/lo as the K-major [TOK tokens x 24] B operand of D1 and as the
+// K-major [32 (k, zero-padded) x TOK tokens] B operand of D2, and 32 scalars
 // per token (beta, inv_r, coef, 0, h[4], h_post[4], M^T[16], 0[4]).  Tokens
 // past B are zero.
 __global__ void __launch_bounds__(128)
@@ -2134,9 +2135,9 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
           const uint64_t al = umma_desc_k(sbase + F::OFF_A1L, COLS, ks, 0);
           const uint64_t bh = umma_desc_k(im + F::IMG_B1H * 4, TOK, ks, 0);
           const uint64_t bl = umma_desc_k(im + F::IMG_B1L * 4, TOK, ks, 0);
-          umma_tf32(tmem + 16 * b, al, bh, ID1, ks > 0 ? 1u : 0u);
-          umma_tf32(tmem + 16 * b, ah, bl, ID1, 1u);
-          umma_tf32(tmem + 16 * b, ah, bh, ID1, 1u);
+          umma_tf32(tmem + TOK * b, al, bh, ID1, ks > 0 ? 1u : 0u);
+          umma_tf32(tmem + TOK * b, ah, bl, ID1, 1u);
+          umma_tf32(tmem + TOK * b, ah, bh, ID1, 1u);
         }
         umma_commit(&d1_full[b]);
         umma_commit(&ifree[si]);
@@ -2152,10 +2153,10 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         if (!mbar_wait_or_abort(&a2_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { *abort_word = 1; break; }
         tc_fence_after();
         const uint32_t im = sbase + F::OFF_IMG + si * F::IMG;
-        const uint32_t a2 = tmem + F::XT_COL + 32 * b;
+        const uint32_t a2 = tmem + F::XT_COL + 2 * TOK * b;
 #pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const uint32_t ah = a2 + 8 * ks, al = a2 + 16 + 8 * ks;
+        for (int ks = 0; ks < TOK / 8; ++ks) {
+          const uint32_t ah = a2 + 8 * ks, al = a2 + TOK + 8 * ks;
           const uint64_t bh = umma_desc_k(im + F::IMG_B2H * 4, F::KP, ks, 0);
           const uint64_t bl = umma_desc_k(im + F::IMG_B2L * 4, F::KP, ks, 0);
           umma_tf32_at(tmem + F::D2_COL, al, bh, ID2, (j > 0 || ks > 0) ? 1u : 0u);
@@ -2174,19 +2175,22 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       const int sg = j % SG, b = j % ND;
       if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { *abort_word = 1; break; }
       const float* xs = reinterpret_cast<const float*>(sm + sg * 2 * F::GB) + F::GB / 4;
-      float xv[16];
+      float xv[TOK];
 #pragma unroll
-      for (int t = 0; t < 16; ++t) xv[t] = xs[(t * 4 + q) * CW + lane];
+      for (int t = 0; t < TOK; ++t) xv[t] = xs[(t * 4 + q) * CW + lane];
       __syncwarp();
       if (lane == 0) mbar_arrive(&gfree[sg]);
-      uint32_t hi[16], lo[16];
-#pragma unroll
-      for (int t = 0; t < 16; ++t) split_tf32(xv[t], hi[t], lo[t]);
       if (j >= ND && !mbar_wait_or_abort(&a2_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) { *abort_word = 1; break; }
       tc_fence_after();
-      const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + F::XT_COL + 32 * b;
-      tmem_st16(ta, hi);
-      tmem_st16(ta + 16, lo);
+      const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + F::XT_COL + 2 * TOK * b;
+#pragma unroll
+      for (int hf = 0; hf < TOK / 16; ++hf) {
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) split_tf32(xv[16 * hf + t], hi[t], lo[t]);
+        tmem_st16(ta + 16 * hf, hi);
+        tmem_st16(ta + TOK + 16 * hf, lo);
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -2256,16 +2260,19 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       for (int j = 0; j < nb; ++j) {
         const int b = j % ND;
         if (!mbar_wait_or_abort(&d1_full[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
+        if (!mbar_wait_or_abort(&loc_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
         tc_fence_after();
-        float d[16];
-        tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + 16 * b, d);
+        float* lb = locs + b * (F::LOCB / 4) + i * CW + lane;
+#pragma unroll
+        for (int hf = 0; hf < TOK / 16; ++hf) {
+          float d[16];
+          tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + TOK * b + 16 * hf, d);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) lb[(16 * hf + t) * COLS] += d[t];
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&d1_free[b]);
-        if (!mbar_wait_or_abort(&loc_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
-        float* lb = locs + b * (F::LOCB / 4) + i * CW + lane;
-#pragma unroll
-        for (int t = 0; t < 16; ++t) lb[t * COLS] += d[t];
         fence_proxy_async_smem();
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (leader) {
@@ -2500,7 +2507,7 @@ FwdPlan plan_fwd(int64_t B, int64_t C) {
 
 struct BwdPlan {
   int ntiles, nsplit;
-  int64_t nblk6;  // 16-token blocks of the warp-specialised grad_x (n = 4, dynamic H)
+  int64_t nblk6;  // token blocks of the warp-specialised grad_x (n = 4, dynamic H)
   int nsplit6;
   size_t img;
   size_t stats, tokb, tokr, dphi, gw, tot;
