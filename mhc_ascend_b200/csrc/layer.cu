@@ -1958,16 +1958,16 @@ struct Gx6Cfg {
   static constexpr uint32_t IMG = IMG_FLOATS * 4;
   static constexpr uint32_t GB = TOK * 4 * CW * 4;         // g (or x) tile bytes
   static constexpr uint32_t OFF_IMG = SG * 2 * GB;         // g/x ring, then the image ring
-  static constexpr uint32_t OFF_A1H = OFF_IMG + SI * IMG;  // Phi^T [128 x 24]
-  static constexpr uint32_t OFF_A1L = OFF_A1H + COLS * NH * 4;
   static constexpr uint32_t LOCB = TOK * COLS * 4;         // local terms [tokens][128 columns]
-  static constexpr uint32_t OFF_LOC = OFF_A1L + COLS * NH * 4;  // [ND buffers]
+  static constexpr uint32_t OFF_LOC = OFF_IMG + SI * IMG;  // [ND buffers]
   static constexpr uint32_t OFF_GW = OFF_LOC + ND * LOCB;  // grad-w partials [E warps][32]
   static constexpr uint32_t OFF_BAR = OFF_GW + E_WARPS * CW * 4;
-  static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 1;
+  static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 2;
   static constexpr size_t SMEM = OFF_BAR + NBAR * 8 + 16 + 128;
-  static constexpr uint32_t TMEM_COLS = 256;   // D1[b]: [TOK b, +TOK); D2: [64, 96); X^T[b]: [128 + 2 TOK b, +2 TOK) hi|lo
-  static constexpr uint32_t D2_COL = 64, XT_COL = 128;
+  // tensor memory: D1[b] [TOK b, +TOK); D2 [64, 96); Phi^T hi [96, 120), lo [128, 152);
+  // X^T[b] [256 + 2 TOK b, +2 TOK) hi|lo
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t D2_COL = 64, A1_COL = 96, A1L_COL = 128, XT_COL = 256;
   static_assert(ND * TOK <= 64 && XT_COL + 2 * TOK * ND <= TMEM_COLS && TOK % 16 == 0, "tensor-memory plan");
 };
 
@@ -2037,7 +2037,8 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
   uint64_t* loc_ready = d1_free + ND;
   uint64_t* loc_free = loc_ready + ND;
   uint64_t* d2_done = loc_free + ND;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d2_done + 1);
+  uint64_t* phi_ready = d2_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(phi_ready + 1);
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t sbase = smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -2068,20 +2069,10 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       mbar_init(&loc_free[b], 1);
     }
     mbar_init(d2_done, 1);
+    mbar_init(phi_ready, 4);
     *abort_word = 0;
     fence_mbar_init();
   }
-  // resident Phi^T (hi/lo), K-major [128 columns x 24]
-  for (int e = tid; e < COLS * F::NH; e += F::THREADS) {
-    const int k = e / COLS, col = e % COLS;
-    const float v = __ldg(phi_row(phi_pre, phi_post, phi_res, k, 4, nC) + (int64_t)(col / CW) * C + c0 + col % CW);
-    uint32_t hi, lo;
-    split_tf32(v, hi, lo);
-    const uint32_t off = umma_kmaj_off(col, k, COLS);
-    *reinterpret_cast<uint32_t*>(sm + F::OFF_A1H + off) = hi;
-    *reinterpret_cast<uint32_t*>(sm + F::OFF_A1L + off) = lo;
-  }
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -2120,7 +2111,8 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     // ---------------- D1 issuer ----------------
     if (lane == 0) {
       constexpr uint32_t ID1 = umma_idesc_tf32(128, TOK);
-      for (int j = 0; j < nb; ++j) {
+      if (nb > 0 && !mbar_wait_or_abort(phi_ready, 0u, abort_word)) *abort_word = 1;
+      for (int j = 0; j < nb && !*abort_word; ++j) {
         const int si = j % SI, b = j % ND;
         if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { *abort_word = 1; break; }
         if (j >= ND && !mbar_wait_or_abort(&d1_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) {
@@ -2131,13 +2123,12 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         const uint32_t im = sbase + F::OFF_IMG + si * F::IMG;
 #pragma unroll
         for (int ks = 0; ks < 3; ++ks) {
-          const uint64_t ah = umma_desc_k(sbase + F::OFF_A1H, COLS, ks, 0);
-          const uint64_t al = umma_desc_k(sbase + F::OFF_A1L, COLS, ks, 0);
+          const uint32_t ah = tmem + F::A1_COL + 8 * ks, al = tmem + F::A1L_COL + 8 * ks;
           const uint64_t bh = umma_desc_k(im + F::IMG_B1H * 4, TOK, ks, 0);
           const uint64_t bl = umma_desc_k(im + F::IMG_B1L * 4, TOK, ks, 0);
-          umma_tf32(tmem + TOK * b, al, bh, ID1, ks > 0 ? 1u : 0u);
-          umma_tf32(tmem + TOK * b, ah, bl, ID1, 1u);
-          umma_tf32(tmem + TOK * b, ah, bh, ID1, 1u);
+          umma_tf32_at(tmem + TOK * b, al, bh, ID1, ks > 0 ? 1u : 0u);
+          umma_tf32_at(tmem + TOK * b, ah, bl, ID1, 1u);
+          umma_tf32_at(tmem + TOK * b, ah, bh, ID1, 1u);
         }
         umma_commit(&d1_full[b]);
         umma_commit(&ifree[si]);
@@ -2171,6 +2162,26 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
   } else if (warp >= F::XT_WARP0) {
     // ---------------- X^T operand into tensor memory ----------------
     const int q = warp & 3;                  // stream = tensor-memory lane quadrant
+    {
+      // resident Phi^T (A of D1): lane = column (stream q, channel lane), column = k
+      const float* ph = nullptr;
+      uint32_t hi[24], lo[24];
+#pragma unroll
+      for (int k = 0; k < F::NH; ++k) {
+        ph = phi_row(phi_pre, phi_post, phi_res, k, 4, nC);
+        split_tf32(__ldg(ph + (int64_t)q * C + c0 + lane), hi[k], lo[k]);
+      }
+      const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16);
+#pragma unroll
+      for (int k8 = 0; k8 < 3; ++k8) {
+        tmem_st8(ta + F::A1_COL + 8 * k8, *reinterpret_cast<const uint32_t(*)[8]>(hi + 8 * k8));
+        tmem_st8(ta + F::A1L_COL + 8 * k8, *reinterpret_cast<const uint32_t(*)[8]>(lo + 8 * k8));
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(phi_ready);
+    }
     for (int j = 0; j < nb; ++j) {
       const int sg = j % SG, b = j % ND;
       if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { *abort_word = 1; break; }
