@@ -18,7 +18,7 @@
 //             (sum(xf^2) = trace G, sum_c x_agg^2 = h^T G h);
 //   backward: gM = g x^T, W = g diag(w) x^T and G again; from these every
 //             per-token scalar of the backward follows in closed form (see
-//             dyn_token_bwd_kernel).
+//             token_bwd_lanes_kernel).
 // So the forward reads x twice and writes out once; the backward reads g and
 // x twice and writes grad_x once; parameter gradients are fixed-order
 // reductions (no atomics: bitwise reproducible).
@@ -29,6 +29,7 @@
 //         partials) -> reduce_* (fixed-order sums over splits / tokens)
 #include "common.cuh"
 #include "sinkhorn.cuh"
+#include "sinkhorn_lanes.cuh"
 #include "tma.cuh"
 #include <cuda_bf16.h>
 
@@ -767,7 +768,9 @@ __global__ void __launch_bounds__(128, 4)
 }
 
 // ---------------------------------------------------------------------------
-// Backward 2 (dynamic): per-token closed-form scalars, one thread per token,
+// Backward 2 (dynamic): per-token closed-form scalars, one group of lanes per
+// token (the Sinkhorn reverse runs one matrix row per lane, the rest is
+// evaluated alike by every lane of the group and written by its first lane),
 // in fp64.  With W = g diag(w) x^T, G = x x^T, gM = g x^T (sums over c):
 //     ghp_i = (W h)_i / r                     (= sum_c g_i y)
 //     dot   = hp^T W h                        (= sum_c gy w x_agg)
@@ -779,7 +782,7 @@ __global__ void __launch_bounds__(128, 4)
 // ---------------------------------------------------------------------------
 template <int N>
 __global__ void __launch_bounds__(128)
-    token_bwd_kernel(const double* __restrict__ stats, const float* __restrict__ rec,
+    token_bwd_lanes_kernel(const double* __restrict__ stats, const float* __restrict__ rec,
                      const float* __restrict__ a_pre, const float* __restrict__ a_post,
                      const float* __restrict__ a_res, const float* __restrict__ b_pre,
                      const float* __restrict__ b_post, const float* __restrict__ b_res,
@@ -787,10 +790,17 @@ __global__ void __launch_bounds__(128)
                      int iters, float s_eps, float r_eps) {
   using Lc = L<N>;
   constexpr int NH = Lc::NH, NS1 = Lc::NS1;
-  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= B) return;
-  const double* st = stats + b * NS1;
-  const float* rc = rec + b * Lc::REC;
+  constexpr int LG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);  // lanes per token
+  const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = (int)(threadIdx.x & (LG - 1));
+  const int base = (int)(threadIdx.x & 31) & ~(LG - 1);
+  const int64_t b = gt / LG;
+  const bool live = b < B;
+  // every lane of the warp takes part in the shuffles: dead groups evaluate
+  // the last token and write nothing
+  const int64_t bb = live ? b : B - 1;
+  const double* st = stats + bb * NS1;
+  const float* rc = rec + bb * Lc::REC;
   const double* G = st + 2 * N * N;
   // The H_pre gradient is the small difference of two large moments (the
   // RMSNorm backward removes the radial part of the upstream gradient), so it
@@ -803,11 +813,15 @@ __global__ void __launch_bounds__(128)
   const double rms_h = sqrt(tr_g / (double)(N * C) + (double)r_eps);
   const double inv_h = 1.0 / rms_h;
   const double ap = *a_pre, aq = *a_post, ar = *a_res;
+  // gate `row` on this lane, then shared over the group
+  const int gi = row < N ? row : 0;
+  const double h_mine = 1.0 / (1.0 + exp(-((ap * (double)rc[Lc::OFF_P + gi]) * inv_h + (double)b_pre[gi])));
+  const double hp_mine = 2.0 / (1.0 + exp(-((aq * (double)rc[Lc::OFF_P + N + gi]) * inv_h + (double)b_post[gi])));
   double h[N], hp[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    h[i] = 1.0 / (1.0 + exp(-((ap * (double)rc[Lc::OFF_P + i]) * inv_h + (double)b_pre[i])));
-    hp[i] = 2.0 / (1.0 + exp(-((aq * (double)rc[Lc::OFF_P + N + i]) * inv_h + (double)b_post[i])));
+    h[i] = __shfl_sync(0xffffffffu, h_mine, base + i);
+    hp[i] = __shfl_sync(0xffffffffu, hp_mine, base + i);
   }
   double q = 0.0;
 #pragma unroll
@@ -836,15 +850,22 @@ __global__ void __launch_bounds__(128)
     for (int j = 0; j < N; ++j) Q = fma(st[2 * N * N + gram_index(i, j, N)], h[j], Q);
     dt[i] = (A * inv_r - beta * Q) * h[i] * (1.0 - h[i]);
   }
-  double e0[N * N], gm[N * N];
+  // Sinkhorn reverse with lane `row` of the group holding that row
+  double e0[N], gm[N];
 #pragma unroll
-  for (int e = 0; e < N * N; ++e) {
-    e0[e] = exp((ar * (double)rc[Lc::OFF_P + 2 * N + e]) * inv_h + (double)b_res[e]);
-    gm[e] = st[e];
+  for (int j = 0; j < N; ++j) {
+    e0[j] = row < N ? exp((ar * (double)rc[Lc::OFF_P + 2 * N + row * N + j]) * inv_h + (double)b_res[row * N + j]) : 0.0;
+    gm[j] = row < N ? st[row * N + j] : 0.0;
   }
-  sk_backward<N, double>(e0, gm, iters, (double)s_eps);
+  skl_backward<N, LG, double>(e0, gm, iters, (double)s_eps, row);
 #pragma unroll
-  for (int e = 0; e < N * N; ++e) dt[2 * N + e] = gm[e] * e0[e];
+  for (int rr = 0; rr < N; ++rr)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const double v = __shfl_sync(0xffffffffu, gm[j] * e0[j], base + rr);
+      dt[2 * N + rr * N + j] = v;
+    }
+  if (!live || row != 0) return;
   float* tb = tokb + b * Lc::TB;
   double* tr = tokr + b * Lc::NR;
   double s = 0.0, da0 = 0.0, da1 = 0.0, da2 = 0.0;
@@ -892,7 +913,7 @@ __global__ void __launch_bounds__(128)
   if (b >= B) return;
   const double* st = stats + b * NS1;
   const double* G = st + 2 * N * N;
-  // gates and r in fp64 (see token_bwd_kernel for why)
+  // gates and r in fp64 (see token_bwd_lanes_kernel for why)
   double h[N], hp[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) {
@@ -1244,14 +1265,6 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-// d += (a_hi + a_lo)(b_hi + b_lo), small terms first
-__device__ __forceinline__ void mma_3xtf32(float (&d)[4], const uint32_t (&ah)[4],
-                                           const uint32_t (&al)[4], uint32_t bh0, uint32_t bh1,
-                                           uint32_t bl0, uint32_t bl1) {
-  mma_tf32(d, al, bh0, bh1);
-  mma_tf32(d, ah, bl0, bl1);
-  mma_tf32(d, ah, bh0, bh1);
-}
 
 // ---------------------------------------------------------------------------
 // Backward 3 for n = 4 (C % 64 == 0, aligned): grad_x with tensor-core
@@ -1572,14 +1585,6 @@ __device__ __forceinline__ uint64_t umma_desc_k(uint32_t base, int R, int s, int
 __host__ __device__ constexpr uint32_t umma_idesc_tf32(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
-      : "memory");
-}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
@@ -1598,17 +1603,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-}
-// 32 lanes x 8 columns of fp32 from tensor memory (this warp's lane quadrant)
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-  uint32_t r[8];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[j]);
 }
 
 // 32 lanes x 16 columns of 32-bit values into tensor memory (this warp's lane quadrant)
@@ -2726,7 +2720,8 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
   int rc = check_launch("mhc_layer_bwd_dynamic/bwd_stats");
   if (rc) return rc;
-  { ProfScope _ps("token_bwd", s); token_bwd_kernel<N><<<grid_1d(B, kTokThreads), kTokThreads, 0, s>>>(stats, rec, ap, aq, ar, bp, bq, br, tokb,
+  constexpr int TG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);
+  if (B > 0) { ProfScope _ps("token_bwd", s); token_bwd_lanes_kernel<N><<<grid_1d(B * TG, 128), 128, 0, s>>>(stats, rec, ap, aq, ar, bp, bq, br, tokb,
                                                      tokr, B, C, iters, s_eps, r_eps); }
   rc = check_launch("mhc_layer_bwd_dynamic/token_bwd");
   if (rc) return rc;
