@@ -354,11 +354,12 @@ __global__ void __launch_bounds__(PJT_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Forward 2: per-token gates, Sinkhorn and RMS (one thread per token).
+// Forward 2: per-token gates, Sinkhorn and RMS (a group of lanes per token:
+// the Sinkhorn runs one row of M per lane, the rest is written by the first).
 // ---------------------------------------------------------------------------
 template <int N>
 __global__ void __launch_bounds__(128)
-    token_fwd_kernel(const float* __restrict__ ppart, const float* __restrict__ gpart, int ks,
+    token_fwd_lanes_kernel(const float* __restrict__ ppart, const float* __restrict__ gpart, int ks,
                      const float* __restrict__ a_pre, const float* __restrict__ a_post,
                      const float* __restrict__ a_res, const float* __restrict__ b_pre,
                      const float* __restrict__ b_post, const float* __restrict__ b_res,
@@ -366,8 +367,14 @@ __global__ void __launch_bounds__(128)
                      float r_eps) {
   using Lc = L<N>;
   constexpr int NH = Lc::NH, NHP = Lc::NHP, NG = Lc::NG;
-  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= B) return;
+  constexpr int LG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);  // lanes per token
+  const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = (int)(threadIdx.x & (LG - 1));
+  const int64_t bt = gt / LG;
+  const bool live = bt < B;
+  // every lane of the warp takes part in the shuffles: dead groups evaluate
+  // the last token and write nothing
+  const int64_t b = live ? bt : B - 1;
   float p[NH], G[NG];
 #pragma unroll
   for (int k = 0; k < NH; ++k) p[k] = 0.f;
@@ -387,22 +394,30 @@ __global__ void __launch_bounds__(128)
   const float rms_h = sqrtf(ss / (float)(N * C) + r_eps);
   const float inv_h = 1.f / rms_h;
   const float ap = *a_pre, aq = *a_post, ar = *a_res;
-  float h[N], hp[N], m[N * N];
+  float h[N], hp[N], m[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) {
     h[i] = sigmoidf_((ap * p[i]) * inv_h + b_pre[i]);
     hp[i] = 2.f * sigmoidf_((aq * p[N + i]) * inv_h + b_post[i]);
   }
+  // Sinkhorn with lane `row` of the group holding that row of M
 #pragma unroll
-  for (int e = 0; e < N * N; ++e) m[e] = expf((ar * p[2 * N + e]) * inv_h + b_res[e]);
-  sk_forward<N, float>(m, iters, s_eps);
+  for (int j = 0; j < N; ++j)
+    m[j] = row < N ? expf((ar * p[2 * N + row * N + j]) * inv_h + b_res[row * N + j]) : 0.f;
+  skl_forward<N, LG, float>(m, iters, s_eps, row);
+  if (!live) return;
+  float* o = rec + b * Lc::REC;
+  if (row < N) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) o[Lc::OFF_M + row * N + j] = m[j];
+  }
+  if (row != 0) return;
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < N; ++i)
 #pragma unroll
     for (int j = 0; j < N; ++j) q += h[i] * h[j] * G[gram_index(i, j, N)];
   const float r = sqrtf(fmaxf(q, 0.f) / (float)C + r_eps);
-  float* o = rec + b * Lc::REC;
   o[0] = rms_h;
   o[1] = r;
 #pragma unroll
@@ -410,8 +425,6 @@ __global__ void __launch_bounds__(128)
     o[Lc::OFF_H + i] = h[i];
     o[Lc::OFF_HP + i] = hp[i];
   }
-#pragma unroll
-  for (int e = 0; e < N * N; ++e) o[Lc::OFF_M + e] = m[e];
 #pragma unroll
   for (int k = 0; k < NH; ++k) o[Lc::OFF_P + k] = p[k];
 }
@@ -2681,7 +2694,7 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
   }
   rc = check_launch("mhc_layer_fwd_dynamic/proj_stats");
   if (rc) return rc;
-  { ProfScope _ps("token_fwd", s); token_fwd_kernel<N><<<grid_1d(B, kTokThreads), kTokThreads, 0, s>>>(ppart, gpart, ks, ap, aq, ar, bp, bq, br,
+  { constexpr int TG = N <= 2 ? 2 : (N <= 4 ? 4 : 8); ProfScope _ps("token_fwd", s); if (B > 0) token_fwd_lanes_kernel<N><<<grid_1d(B * TG, 128), 128, 0, s>>>(ppart, gpart, ks, ap, aq, ar, bp, bq, br,
                                                      rec, B, C, iters, s_eps, r_eps); }
   rc = check_launch("mhc_layer_fwd_dynamic/token_fwd");
   if (rc) return rc;
