@@ -139,6 +139,10 @@ MHC_API int mhc_fused_rmsnorm_matmul_bwd(const float* grad_out, const float* inp
  *   [2+n, 2+2n)       H_post_act = 2*sigmoid(H_post_tilde)
  *   [2+2n, 2+2n+n*n)  M          = Sinkhorn(exp(H_res_tilde))
  *   [2+2n+n*n, ...+n*n+2n)  raw projections p = x_flat @ phi^T (pre|post|res)
+ *   then, from the next even index, n(n+1)/2 doubles: the upper triangle of
+ *   the token's Gram matrix x x^T (row-major), accumulated in fp64 from exact
+ *   products; the record (and therefore the buffer) must be 8-byte aligned.
+ *   Stride at n = 4: 72 floats.
  * ------------------------------------------------------------------------- */
 MHC_API int32_t mhc_token_state_stride(int32_t n);
 

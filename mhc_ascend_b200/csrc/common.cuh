@@ -95,6 +95,12 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 __device__ __forceinline__ float sigmoidf_(float t) { return 1.0f / (1.0f + expf(-t)); }
 
 // Sum `V` per-lane values over the 32 lanes of a warp.  On return lane 0 holds

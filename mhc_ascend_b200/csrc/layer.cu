@@ -45,9 +45,13 @@ struct L {
   static constexpr int NHP = (NH + 3) / 4 * 4;           // padded to float4
   static constexpr int NG = N * (N + 1) / 2;             // Gram upper triangle
   static constexpr int REC_RAW = 2 + 2 * N + N * N + NH;  // token_state record
-  static constexpr int REC = (REC_RAW + 3) / 4 * 4;
+  // then the Gram matrix in fp64 (exact products), written by the dynamic
+  // stream_fwd for the backward, at an 8-byte offset
+  static constexpr int OFF_G64 = (REC_RAW + 1) / 2 * 2;
+  static constexpr int REC = (OFF_G64 + 2 * NG + 3) / 4 * 4;
   static constexpr int OFF_H = 2, OFF_HP = 2 + N, OFF_M = 2 + 2 * N, OFF_P = 2 + 2 * N + N * N;
-  static constexpr int NS1 = 2 * N * N + NG;             // bwd moments: gM, W, G
+  static constexpr int NS1 = 2 * N * N + NG;             // static bwd moments: gM, W, G
+  static constexpr int NSD = 2 * N * N;                  // dynamic bwd moments: gM, W
   // bwd per-token row read by grad_x: beta, inv_r, coef, -, d_p[NHP], h[N], hp[N], M^T[N*N]
   static constexpr int OFF_TH = 4 + NHP, OFF_THP = OFF_TH + N, OFF_TM = OFF_THP + N;
   static constexpr int TB = (OFF_TM + N * N + 3) / 4 * 4;
@@ -57,7 +61,8 @@ struct L {
 
 __host__ __device__ inline int rec_stride(int n) {
   const int raw = 2 + 2 * n + n * n + (n * n + 2 * n);
-  return (raw + 3) / 4 * 4;
+  const int og = (raw + 1) / 2 * 2;
+  return (og + n * (n + 1) + 3) / 4 * 4;
 }
 
 __device__ __forceinline__ int gram_index(int i, int j, int N) {
@@ -434,14 +439,18 @@ __global__ void __launch_bounds__(128)
 //   One CTA per token (grid-stride over tokens); per-token record in smem;
 //   rec_stride 0 = one shared record (static H) with per-token r from rms[].
 // ---------------------------------------------------------------------------
-template <int N, bool VEC>
+template <int N, bool VEC, bool GRAM>
 __global__ void __launch_bounds__(256)
     stream_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
                       const float* __restrict__ rec, int rec_stride,
                       const float* __restrict__ rms, float* __restrict__ out, int64_t B,
-                      int64_t C) {
+                      int64_t C, float* __restrict__ rec_w) {
+  // GRAM (dynamic H): also the token's Gram matrix in fp64 from exact
+  // products, for the backward -- FP64 work hidden under this HBM-bound pass.
   using Lc = L<N>;
+  constexpr int NG = Lc::NG;
   __shared__ float s_rec[Lc::REC];
+  __shared__ double s_g[GRAM ? 8 * NG : 1];
   for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
     __syncthreads();
     for (int e = threadIdx.x; e < Lc::REC; e += blockDim.x) s_rec[e] = rec[b * rec_stride + e];
@@ -453,11 +462,27 @@ __global__ void __launch_bounds__(256)
     const float* m = s_rec + Lc::OFF_M;
     const float* xb = x + b * N * C;
     float* ob = out + b * N * C;
+    double gacc[NG];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) gacc[g] = 0.0;
     if (VEC) {
       for (int64_t q = threadIdx.x; q < C / 4; q += blockDim.x) {
         float4 xv[N];
 #pragma unroll
         for (int j = 0; j < N; ++j) xv[j] = __ldcs(reinterpret_cast<const float4*>(xb + j * C) + q);
+        if (GRAM) {
+          int g = 0;
+#pragma unroll
+          for (int i = 0; i < N; ++i)
+#pragma unroll
+            for (int j = i; j < N; ++j) {
+              gacc[g] = fma((double)xv[i].x, (double)xv[j].x, gacc[g]);
+              gacc[g] = fma((double)xv[i].y, (double)xv[j].y, gacc[g]);
+              gacc[g] = fma((double)xv[i].z, (double)xv[j].z, gacc[g]);
+              gacc[g] = fma((double)xv[i].w, (double)xv[j].w, gacc[g]);
+              ++g;
+            }
+        }
         const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + q);
         float4 xa = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -486,6 +511,13 @@ __global__ void __launch_bounds__(256)
         float xv[N];
 #pragma unroll
         for (int j = 0; j < N; ++j) xv[j] = xb[j * C + c];
+        if (GRAM) {
+          int g = 0;
+#pragma unroll
+          for (int i = 0; i < N; ++i)
+#pragma unroll
+            for (int j = i; j < N; ++j) { gacc[g] = fma((double)xv[i], (double)xv[j], gacc[g]); ++g; }
+        }
         float xa = 0.f;
 #pragma unroll
         for (int j = 0; j < N; ++j) xa = fmaf(h[j], xv[j], xa);
@@ -497,6 +529,21 @@ __global__ void __launch_bounds__(256)
           for (int j = 0; j < N; ++j) o = fmaf(m[i * N + j], xv[j], o);
           ob[i * C + c] = o;
         }
+      }
+    }
+    if (GRAM) {
+      // block sum of the fp64 Gram entries, in a fixed order
+      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const double v = warp_sum_d(gacc[g]);
+        if (lane == 0) s_g[warp * NG + g] = v;
+      }
+      __syncthreads();
+      if (threadIdx.x < NG) {
+        double t = 0.0;
+        for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) t += s_g[wi * NG + threadIdx.x];
+        reinterpret_cast<double*>(rec_w + b * Lc::REC + Lc::OFF_G64)[threadIdx.x] = t;
       }
     }
   }
@@ -710,7 +757,7 @@ __device__ __forceinline__ void block_reduce_to_global(double (&acc)[V], double*
   __syncthreads();
 }
 
-template <int N, bool VEC>
+template <int N, bool VEC, bool WITH_G>
 __global__ void __launch_bounds__(128, 4)
     bwd_stats_kernel(const float* __restrict__ g, const float* __restrict__ x,
                      const float* __restrict__ w, double* __restrict__ stats, int64_t B,
@@ -720,7 +767,8 @@ __global__ void __launch_bounds__(128, 4)
   // RMSNorm backward removes the radial component), which amplifies fp32
   // accumulation error by ~ the ratio |A_i| / |gh_i| (hundreds at cfg3).
   using Lc = L<N>;
-  constexpr int NS1 = Lc::NS1;
+  // dynamic H: the forward saved the fp64 Gram matrix, only gM and W are needed
+  constexpr int NS1 = WITH_G ? Lc::NS1 : Lc::NSD;
   __shared__ double red[4 * NS1];
   for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
     double acc[NS1];
@@ -742,13 +790,41 @@ __global__ void __launch_bounds__(128, 4)
           acc[N * N + i * N + j] = fma(gw, xv[j], acc[N * N + i * N + j]);
         }
       }
-      int e = 2 * N * N;
+      if (WITH_G) {
+        int e = 2 * N * N;
 #pragma unroll
-      for (int i = 0; i < N; ++i)
+        for (int i = 0; i < N; ++i)
 #pragma unroll
-        for (int j = i; j < N; ++j) { acc[e] = fma(xv[i], xv[j], acc[e]); ++e; }
+          for (int j = i; j < N; ++j) { acc[e] = fma(xv[i], xv[j], acc[e]); ++e; }
+      }
     };
-    if (VEC) {
+    if (VEC && !WITH_G) {
+      // float4 per stream: with the Gram matrix left to the forward, 32
+      // accumulators leave room for twice the loads in flight.
+#pragma unroll 1
+      for (int64_t q = threadIdx.x; q < C / 4; q += blockDim.x) {
+        float4 g4[N], x4[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          g4[i] = __ldcs(reinterpret_cast<const float4*>(gb + i * C) + q);
+          x4[i] = __ldcs(reinterpret_cast<const float4*>(xb + i * C) + q);
+        }
+        const float4 w4 = __ldg(reinterpret_cast<const float4*>(w) + q);
+        float gv[N], xv[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) { gv[i] = g4[i].x; xv[i] = x4[i].x; }
+        accum(gv, xv, w4.x);
+#pragma unroll
+        for (int i = 0; i < N; ++i) { gv[i] = g4[i].y; xv[i] = x4[i].y; }
+        accum(gv, xv, w4.y);
+#pragma unroll
+        for (int i = 0; i < N; ++i) { gv[i] = g4[i].z; xv[i] = x4[i].z; }
+        accum(gv, xv, w4.z);
+#pragma unroll
+        for (int i = 0; i < N; ++i) { gv[i] = g4[i].w; xv[i] = x4[i].w; }
+        accum(gv, xv, w4.w);
+      }
+    } else if (VEC) {
       // float2 per stream: keeps the live load registers low enough for
       // 4 CTAs (16 warps) per SM next to the 42 fp64 accumulators.
 #pragma unroll 2
@@ -802,7 +878,7 @@ __global__ void __launch_bounds__(128)
                      float* __restrict__ tokb, double* __restrict__ tokr, int64_t B, int64_t C,
                      int iters, float s_eps, float r_eps) {
   using Lc = L<N>;
-  constexpr int NH = Lc::NH, NS1 = Lc::NS1;
+  constexpr int NH = Lc::NH, NSD = Lc::NSD;
   constexpr int LG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);  // lanes per token
   const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int row = (int)(threadIdx.x & (LG - 1));
@@ -812,13 +888,13 @@ __global__ void __launch_bounds__(128)
   // every lane of the warp takes part in the shuffles: dead groups evaluate
   // the last token and write nothing
   const int64_t bb = live ? b : B - 1;
-  const double* st = stats + bb * NS1;
+  const double* st = stats + bb * NSD;
   const float* rc = rec + bb * Lc::REC;
-  const double* G = st + 2 * N * N;
+  const double* G = reinterpret_cast<const double*>(rc + Lc::OFF_G64);  // fp64 Gram saved by the forward
   // The H_pre gradient is the small difference of two large moments (the
   // RMSNorm backward removes the radial part of the upstream gradient), so it
   // is sensitive to the exact gate values: recompute rms_h, h, hp and r in
-  // fp64 from the saved projections p and this pass's fp64 Gram matrix
+  // fp64 from the saved projections p and the forward's fp64 Gram matrix
   // instead of reusing the fp32 values of the forward record.
   double tr_g = 0.0;
 #pragma unroll
@@ -860,7 +936,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int k = 0; k < N; ++k) A = fma(hp[k], st[N * N + k * N + i], A);
 #pragma unroll
-    for (int j = 0; j < N; ++j) Q = fma(st[2 * N * N + gram_index(i, j, N)], h[j], Q);
+    for (int j = 0; j < N; ++j) Q = fma(G[gram_index(i, j, N)], h[j], Q);
     dt[i] = (A * inv_r - beta * Q) * h[i] * (1.0 - h[i]);
   }
   // Sinkhorn reverse with lane `row` of the group holding that row
@@ -2541,7 +2617,7 @@ BwdPlan plan_bwd(int64_t B, int64_t C) {
   p.img = (size_t)p.nblk6 * Gx6Cfg::IMG_FLOATS;
   int64_t msplit = p.nsplit;
   if (p.nsplit6 > msplit) msplit = p.nsplit6;
-  p.stats = (size_t)B * L<N>::NS1 * 2;  // fp64
+  p.stats = (size_t)B * (DYN ? L<N>::NSD : L<N>::NS1) * 2;  // fp64
   p.tokb = (size_t)B * L<N>::TB;
   p.tokr = (size_t)B * (DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
   p.dphi = DYN ? (size_t)msplit * L<N>::NH * N * C : 0;
@@ -2701,9 +2777,9 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(out) && aligned16(w);
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
   if (vec)
-    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, true><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C); }
+    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, true, true><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
   else
-    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, false><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C); }
+    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, false, true><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
   return check_launch("mhc_layer_fwd_dynamic/stream_fwd");
 }
 
@@ -2729,8 +2805,8 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   float* img = cv.take(p.img);
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(w);
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
-  if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
-  else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
   int rc = check_launch("mhc_layer_bwd_dynamic/bwd_stats");
   if (rc) return rc;
   constexpr int TG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);
@@ -2813,8 +2889,8 @@ int run_bwd_static(const float* g, const float* x, const float* w, const float* 
   { ProfScope _ps("static_prep", s); static_prep_kernel<N><<<1, 32, 0, s>>>(Hp, Hq, Hr, rec, iters, s_eps); }
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(w);
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
-  if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
-  else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true, true><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false, true><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
   int rc = check_launch("mhc_layer_bwd_static/bwd_stats");
   if (rc) return rc;
   { ProfScope _ps("token_bwd_static", s); token_bwd_static_kernel<N><<<grid_1d(B, kTokThreads), kTokThreads, 0, s>>>(stats, Hp, Hq, rec, tokb, tokr, B, C, r_eps); }

@@ -73,6 +73,6 @@ def test_workspace_queries():
     bwd = lib.mhc_layer_bwd_dynamic_workspace_bytes(8192, 4, 4096)
     assert 0 < fwd < 64 << 20
     assert 0 < bwd < 512 << 20
-    assert lib.mhc_token_state_stride(4) == 52
+    assert lib.mhc_token_state_stride(4) == 72  # 50 record floats + padding + fp64 Gram (10 doubles)
     assert lib.mhc_layer_static_workspace_bytes(65536, 4, 4096) > 0
     assert lib.mhc_rmsnorm_bwd_workspace_bytes(1024, 4096) >= 4096 * 4
