@@ -2776,10 +2776,15 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
   if (rc) return rc;
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(out) && aligned16(w);
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
-  if (vec)
+  // the fp64 Gram matrix is only needed when the record is kept for a backward
+  if (vec && !need_rec)
     { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, true, true><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
-  else
+  else if (vec)
+    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, true, false><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
+  else if (!need_rec)
     { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, false, true><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
+  else
+    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, false, false><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
   return check_launch("mhc_layer_fwd_dynamic/stream_fwd");
 }
 
