@@ -876,9 +876,10 @@ __global__ void __launch_bounds__(128)
                      const float* __restrict__ a_res, const float* __restrict__ b_pre,
                      const float* __restrict__ b_post, const float* __restrict__ b_res,
                      float* __restrict__ tokb, double* __restrict__ tokr, int64_t B, int64_t C,
-                     int iters, float s_eps, float r_eps) {
+                     int iters, float s_eps, float r_eps, unsigned int* __restrict__ counter) {
   using Lc = L<N>;
   constexpr int NH = Lc::NH, NSD = Lc::NSD;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;  // arrival counter of finish_dyn_bwd
   constexpr int LG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);  // lanes per token
   const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int row = (int)(threadIdx.x & (LG - 1));
@@ -1758,20 +1759,35 @@ struct PumCfg {
 // phi_hi / phi_lo [NB rows x nC]: rows k < NH hold phi_k split into tf32 hi +
 // tf32 lo, the padding rows are zero.
 template <int N>
-__global__ void phi_split_kernel(const float* __restrict__ pp, const float* __restrict__ pq,
-                                 const float* __restrict__ pr, float* __restrict__ ph,
-                                 float* __restrict__ pl, int64_t C) {
+__global__ void __launch_bounds__(256)
+    phi_split_kernel(const float* __restrict__ pp, const float* __restrict__ pq,
+                     const float* __restrict__ pr, float* __restrict__ ph,
+                     float* __restrict__ pl, int64_t C, bool vec) {
+  // blockIdx.y = row k; float4 columns when every row start is 16-byte aligned
   using P = PumCfg<N>;
   const int64_t nC = (int64_t)N * C;
-  const int64_t total = (int64_t)P::NB * nC;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int k = (int)(e / nC);
-    const float v = k < P::NH ? phi_row(pp, pq, pr, k, N, nC)[e % nC] : 0.f;
-    uint32_t hi, lo;
-    split_tf32(v, hi, lo);
-    ph[e] = __uint_as_float(hi);
-    pl[e] = __uint_as_float(lo);
+  const int k = blockIdx.y;
+  const float* src = k < P::NH ? phi_row(pp, pq, pr, k, N, nC) : nullptr;
+  float* dh = ph + (int64_t)k * nC;
+  float* dl = pl + (int64_t)k * nC;
+  if (vec) {
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nC / 4;
+         q += (int64_t)gridDim.x * blockDim.x) {
+      const float4 v = src ? __ldg(reinterpret_cast<const float4*>(src) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      uint4 hi, lo;
+      split_tf32(v.x, hi.x, lo.x); split_tf32(v.y, hi.y, lo.y);
+      split_tf32(v.z, hi.z, lo.z); split_tf32(v.w, hi.w, lo.w);
+      reinterpret_cast<uint4*>(dh)[q] = hi;
+      reinterpret_cast<uint4*>(dl)[q] = lo;
+    }
+  } else {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nC;
+         e += (int64_t)gridDim.x * blockDim.x) {
+      uint32_t hi, lo;
+      split_tf32(src ? src[e] : 0.f, hi, lo);
+      dh[e] = __uint_as_float(hi);
+      dl[e] = __uint_as_float(lo);
+    }
   }
 }
 
@@ -2434,21 +2450,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// dphi[k, :] = sum_s part[s, k, :] written straight into the three grad tensors
-__global__ void __launch_bounds__(256)
-    reduce_dphi_kernel(const float* __restrict__ part, int nsplit, int NHn, int N, int64_t nC,
-                       float* __restrict__ d_pre, float* __restrict__ d_post,
-                       float* __restrict__ d_res) {
-  const int64_t L = (int64_t)NHn * nC;
-  for (int64_t l = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; l < L;
-       l += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int k = 0; k < nsplit; ++k) s += part[(int64_t)k * L + l];
-    const int64_t kk = l / nC, cc = l % nC;
-    float* dst = kk < N ? d_pre + kk * nC : (kk < 2 * N ? d_post + (kk - N) * nC : d_res + (kk - 2 * N) * nC);
-    dst[cc] = s;
-  }
-}
 
 // One CTA per column v of a [B, stride] fp64 table: total[v] = sum_b tab[b, v]
 // (fixed order: thread-strided partials, then a fixed tree).
@@ -2470,18 +2471,79 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Scatter the token-reduced dynamic parameter gradients: tot = [dt(NH), dalpha(3)]
+
+// Tail of the dynamic backward in one launch.  Blocks [0, nb_dphi) sum the
+// dphi split partials into the three phi gradients, the next nb_gw blocks the
+// grad-w split partials, the last nb_tok blocks reduce the per-token rows
+// [B, NR] (dt, dalpha) to block partials; the last of those to finish sums
+// the partials in block order and scatters the bias / alpha gradients.  The
+// arrival counter is zeroed by token_bwd earlier on the same stream.  Every
+// sum runs in a fixed order (bitwise reproducible).
 template <int N>
-__global__ void scatter_dyn_param_grads_kernel(const double* __restrict__ tot,
-                                               float* __restrict__ gbp, float* __restrict__ gbq,
-                                               float* __restrict__ gbr, float* __restrict__ gap,
-                                               float* __restrict__ gaq, float* __restrict__ gar) {
-  constexpr int NH = L<N>::NH;
-  const int k = threadIdx.x;
-  if (k < N) gbp[k] = (float)tot[k];
-  else if (k < 2 * N) gbq[k - N] = (float)tot[k];
-  else if (k < NH) gbr[k - 2 * N] = (float)tot[k];
-  if (k == 0) { *gap = (float)tot[NH]; *gaq = (float)tot[NH + 1]; *gar = (float)tot[NH + 2]; }
+__global__ void __launch_bounds__(256)
+    finish_dyn_bwd_kernel(const float* __restrict__ dphi_part, const float* __restrict__ gw_part,
+                          int nsplit, int64_t C, float* __restrict__ d_pre,
+                          float* __restrict__ d_post, float* __restrict__ d_res,
+                          float* __restrict__ gw, const double* __restrict__ tokr, int64_t B,
+                          double* __restrict__ tok_part, unsigned int* __restrict__ counter,
+                          int nb_dphi, int nb_gw, int nb_tok, float* __restrict__ gbp,
+                          float* __restrict__ gbq, float* __restrict__ gbr, float* __restrict__ gap,
+                          float* __restrict__ gaq, float* __restrict__ gar) {
+  constexpr int NH = L<N>::NH, NR = L<N>::NR, RL = 256 / NR;
+  const int64_t nC = (int64_t)N * C;
+  const int bid = blockIdx.x, tid = threadIdx.x;
+  if (bid < nb_dphi) {
+    const int64_t Ld = (int64_t)NH * nC;
+    for (int64_t l = (int64_t)bid * 256 + tid; l < Ld; l += (int64_t)nb_dphi * 256) {
+      float sacc = 0.f;
+      for (int k = 0; k < nsplit; ++k) sacc += dphi_part[(int64_t)k * Ld + l];
+      const int64_t kk = l / nC, cc = l % nC;
+      float* dst = kk < N ? d_pre + kk * nC : (kk < 2 * N ? d_post + (kk - N) * nC : d_res + (kk - 2 * N) * nC);
+      dst[cc] = sacc;
+    }
+    return;
+  }
+  if (bid < nb_dphi + nb_gw) {
+    for (int64_t l = (int64_t)(bid - nb_dphi) * 256 + tid; l < C; l += (int64_t)nb_gw * 256) {
+      float sacc = 0.f;
+      for (int k = 0; k < nsplit; ++k) sacc += gw_part[(int64_t)k * C + l];
+      gw[l] = sacc;
+    }
+    return;
+  }
+  // token rows: thread = (column v, row lane rl), rows of this block's range
+  __shared__ double red[256];
+  __shared__ bool last;
+  const int kb = bid - nb_dphi - nb_gw;
+  const int64_t r0 = B * kb / nb_tok, r1 = B * (kb + 1) / nb_tok;
+  const int v = tid % NR, rl = tid / NR;
+  double sacc = 0.0;
+  if (rl < RL)
+    for (int64_t r = r0 + rl; r < r1; r += RL) sacc += tokr[r * NR + v];
+  red[tid] = sacc;
+  __syncthreads();
+  if (tid < NR) {
+    double t = 0.0;
+    for (int q = 0; q < RL; ++q) t += red[q * NR + tid];
+    tok_part[(int64_t)kb * NR + tid] = t;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(counter, 1u) == (unsigned)(nb_tok - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (tid < NR) {
+    double t = 0.0;
+    for (int q = 0; q < nb_tok; ++q) t += *(volatile const double*)(tok_part + (int64_t)q * NR + tid);
+    if (tid < N) gbp[tid] = (float)t;
+    else if (tid < 2 * N) gbq[tid - N] = (float)t;
+    else if (tid < NH) gbr[tid - 2 * N] = (float)t;
+    else if (tid == NH) *gap = (float)t;
+    else if (tid == NH + 1) *gaq = (float)t;
+    else *gar = (float)t;
+  }
+  if (tid == 0) *counter = 0u;
 }
 
 // Static-H parameter gradients from the token totals [dt_pre, dt_post, gM]:
@@ -2599,6 +2661,8 @@ FwdPlan plan_fwd(int64_t B, int64_t C) {
   return p;
 }
 
+constexpr int kTokPartBlocks = 64;
+
 struct BwdPlan {
   int ntiles, nsplit;
   int64_t nblk6;  // token blocks of the warp-specialised grad_x (n = 4, dynamic H)
@@ -2622,7 +2686,8 @@ BwdPlan plan_bwd(int64_t B, int64_t C) {
   p.tokr = (size_t)B * (DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
   p.dphi = DYN ? (size_t)msplit * L<N>::NH * N * C : 0;
   p.gw = (size_t)msplit * C;
-  p.tot = (size_t)(DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
+  // dynamic: per-block token partials of finish_dyn_bwd + its arrival counter
+  p.tot = DYN ? (size_t)kTokPartBlocks * L<N>::NR * 2 + 4 : (size_t)L<N>::NRS * 2;  // fp64
   return p;
 }
 
@@ -2736,7 +2801,11 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
         make_tmap_3d_f32(&xmap, x, C, N, B, cs, rs, PU::CH, 1, PU::TOK, CU_TENSOR_MAP_SWIZZLE_128B) &&
         make_tmap_3d_f32(&hmap, ph, C, N, PU::NB, cs, rs, PU::CH, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B) &&
         make_tmap_3d_f32(&lmap, pl, C, N, PU::NB, cs, rs, PU::CH, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B)) {
-      { ProfScope _ps("phi_split", s); phi_split_kernel<N><<<grid_1d(PU::NB * nC, 256, 2048), 256, 0, s>>>(pp, pq, pr, ph, pl, C); }
+      {
+        const bool pvec = nC % 4 == 0 && aligned16(pp) && aligned16(pq) && aligned16(pr);
+        ProfScope _ps("phi_split", s);
+        phi_split_kernel<N><<<dim3(grid_1d(pvec ? nC / 4 : nC, 256, 64), PU::NB), 256, 0, s>>>(pp, pq, pr, ph, pl, C, pvec);
+      }
       cudaFuncSetAttribute(proj_umma_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PU::SMEM);
       { ProfScope _ps("proj_stats", s); proj_umma_kernel<N><<<dim3((unsigned)p.utiles, (unsigned)p.uks), PU::THREADS, PU::SMEM, s>>>(
           xmap, hmap, lmap, ppart, gpart, B, C, p.ucps); }
@@ -2807,6 +2876,7 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   float* dphi = cv.take(p.dphi);
   float* gwp = cv.take(p.gw);
   double* tot = (double*)cv.take(p.tot);
+  unsigned int* counter = reinterpret_cast<unsigned int*>(tot + (size_t)kTokPartBlocks * L<N>::NR);
   float* img = cv.take(p.img);
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(w);
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
@@ -2816,7 +2886,8 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   if (rc) return rc;
   constexpr int TG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);
   if (B > 0) { ProfScope _ps("token_bwd", s); token_bwd_lanes_kernel<N><<<grid_1d(B * TG, 128), 128, 0, s>>>(stats, rec, ap, aq, ar, bp, bq, br, tokb,
-                                                     tokr, B, C, iters, s_eps, r_eps); }
+                                                     tokr, B, C, iters, s_eps, r_eps, counter); }
+  else cudaMemsetAsync(counter, 0, sizeof(unsigned int), s);
   rc = check_launch("mhc_layer_bwd_dynamic/token_bwd");
   if (rc) return rc;
   int nsplit = p.nsplit;
@@ -2844,11 +2915,15 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   rc = check_launch("mhc_layer_bwd_dynamic/grad_x");
   if (rc) return rc;
   const int64_t nC = (int64_t)N * C;
-  { ProfScope _ps("reduce_dphi", s); reduce_dphi_kernel<<<grid_1d((int64_t)L<N>::NH * nC, 256, 4096), 256, 0, s>>>(
-      dphi, nsplit, L<N>::NH, N, nC, gpp, gpq, gpr); }
-  { ProfScope _ps("reduce_splits", s); reduce_splits_kernel<<<grid_1d(C, 256, 4096), 256, 0, s>>>(gwp, nsplit, C, gw); }
-  { ProfScope _ps("reduce_tokens", s); reduce_tokens_kernel<<<L<N>::NR, 256, 0, s>>>(tokr, B, L<N>::NR, tot); }
-  { ProfScope _ps("scatter_dyn_param_grads", s); scatter_dyn_param_grads_kernel<N><<<1, 128, 0, s>>>(tot, gbp, gbq, gbr, gap, gaq, gar); }
+  {
+    const int nb_dphi = (int)grid_1d((int64_t)L<N>::NH * nC, 256, 4 * (int64_t)num_sms());
+    const int nb_gw = (int)grid_1d(C, 256, 64);
+    const int nb_tok = (int)(B / 128 < 1 ? 1 : (B / 128 < kTokPartBlocks ? B / 128 : kTokPartBlocks));
+    ProfScope _ps("finish", s);
+    finish_dyn_bwd_kernel<N><<<(unsigned)(nb_dphi + nb_gw + nb_tok), 256, 0, s>>>(
+        dphi, gwp, nsplit, C, gpp, gpq, gpr, gw, tokr, B, tot, counter, nb_dphi, nb_gw, nb_tok,
+        gbp, gbq, gbr, gap, gaq, gar);
+  }
   return check_launch("mhc_layer_bwd_dynamic/reduce");
 }
 
