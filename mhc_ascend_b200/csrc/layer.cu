@@ -65,6 +65,31 @@ __host__ __device__ inline int rec_stride(int n) {
   return (og + n * (n + 1) + 3) / 4 * 4;
 }
 
+// Layout of the warp-specialised n = 4 grad_x (kernel comment at grad_x6_kernel).
+struct Gx6Cfg {
+  static constexpr int CW = 32, COLS = 128, TOK = 32, NH = 24, KP = 32;
+  static constexpr int SG = 3, SI = 3, ND = 2, E_WARPS = 16, TPE = TOK / E_WARPS, THREADS = 32 * (2 + E_WARPS + 4 + 1 + 4);
+  static constexpr int D2_WARP = 2 + E_WARPS + 4;          // issues the D2 MMAs
+  static constexpr int XT_WARP0 = D2_WARP + 1;             // first of the four X^T warps
+  // operand image of one token block (floats)
+  static constexpr int IMG_B1H = 0, IMG_B1L = TOK * NH, IMG_B2H = 2 * TOK * NH, IMG_B2L = IMG_B2H + KP * TOK;
+  static constexpr int IMG_SC = IMG_B2L + KP * TOK, IMG_FLOATS = IMG_SC + TOK * 32;
+  static constexpr uint32_t IMG = IMG_FLOATS * 4;
+  static constexpr uint32_t GB = TOK * 4 * CW * 4;         // g (or x) tile bytes
+  static constexpr uint32_t OFF_IMG = SG * 2 * GB;         // g/x ring, then the image ring
+  static constexpr uint32_t LOCB = TOK * COLS * 4;         // local terms [tokens][128 columns]
+  static constexpr uint32_t OFF_LOC = OFF_IMG + SI * IMG;  // [ND buffers]
+  static constexpr uint32_t OFF_GW = OFF_LOC + ND * LOCB;  // grad-w partials [E warps][32]
+  static constexpr uint32_t OFF_BAR = OFF_GW + E_WARPS * CW * 4;
+  static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 2;
+  static constexpr size_t SMEM = OFF_BAR + NBAR * 8 + 16 + 128;
+  // tensor memory: D1[b] [TOK b, +TOK); D2 [64, 96); Phi^T hi [96, 120), lo [128, 152);
+  // X^T[b] [256 + 2 TOK b, +2 TOK) hi|lo
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t D2_COL = 64, A1_COL = 96, A1L_COL = 128, XT_COL = 256;
+  static_assert(ND * TOK <= 64 && XT_COL + 2 * TOK * ND <= TMEM_COLS && TOK % 16 == 0, "tensor-memory plan");
+};
+
 __device__ __forceinline__ int gram_index(int i, int j, int N) {
   // upper triangle, row-major: (0,0),(0,1)..(0,N-1),(1,1)...
   if (i > j) { int t = i; i = j; j = t; }
@@ -869,6 +894,51 @@ __global__ void __launch_bounds__(128, 4)
 //   then the gate derivatives, the Sinkhorn reverse on gM, and the projection
 //   backward: d_p = dt alpha / rms_h, coef = -(sum dt alpha p) / (rms_h^3 nC).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo);
+__host__ __device__ __forceinline__ uint32_t umma_kmaj_off(int r, int k, int R);
+
+// Operand image of each token block from the per-token backward rows:
+// D_p hi/lo as the K-major [TOK tokens x 24] B operand of D1 and as the
+// K-major [32 (k, zero-padded) x TOK tokens] B operand of D2, and 32 scalars
+// per token (beta, inv_r, coef, 0, h[4], h_post[4], M^T[16], 0[4]).  Tokens
+// past B are zero.
+__device__ __forceinline__ void gx_image_row(const float* __restrict__ tb, float* __restrict__ img,
+                                             int64_t t) {
+  // tb: the token's backward row, or nullptr for a padding token (zeros)
+  using Lc = L<4>;
+  using F = Gx6Cfg;
+  const bool live = tb != nullptr;
+  float* im = img + (t / F::TOK) * F::IMG_FLOATS;
+  const int tt = (int)(t % F::TOK);
+#pragma unroll
+  for (int k = 0; k < F::KP; ++k) {
+    const float d = (live && k < F::NH) ? tb[4 + k] : 0.f;
+    uint32_t hi, lo;
+    split_tf32(d, hi, lo);
+    if (k < F::NH) {
+      const uint32_t o1 = umma_kmaj_off(tt, k, F::TOK) / 4;
+      im[F::IMG_B1H + o1] = __uint_as_float(hi);
+      im[F::IMG_B1L + o1] = __uint_as_float(lo);
+    }
+    const uint32_t o2 = umma_kmaj_off(k, tt, F::KP) / 4;
+    im[F::IMG_B2H + o2] = __uint_as_float(hi);
+    im[F::IMG_B2L + o2] = __uint_as_float(lo);
+  }
+  float* sc = im + F::IMG_SC + tt * 32;
+  float v[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) v[e] = 0.f;
+  if (live) {
+    v[0] = tb[0]; v[1] = tb[1]; v[2] = tb[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { v[4 + i] = tb[Lc::OFF_TH + i]; v[8 + i] = tb[Lc::OFF_THP + i]; }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[12 + e] = tb[Lc::OFF_TM + e];
+  }
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(sc + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+}
+
 template <int N>
 __global__ void __launch_bounds__(128)
     token_bwd_lanes_kernel(const double* __restrict__ stats, const float* __restrict__ rec,
@@ -876,7 +946,8 @@ __global__ void __launch_bounds__(128)
                      const float* __restrict__ a_res, const float* __restrict__ b_pre,
                      const float* __restrict__ b_post, const float* __restrict__ b_res,
                      float* __restrict__ tokb, double* __restrict__ tokr, int64_t B, int64_t C,
-                     int iters, float s_eps, float r_eps, unsigned int* __restrict__ counter) {
+                     int iters, float s_eps, float r_eps, unsigned int* __restrict__ counter,
+                     float* __restrict__ img, int64_t img_tokens) {
   using Lc = L<N>;
   constexpr int NH = Lc::NH, NSD = Lc::NSD;
   if (blockIdx.x == 0 && threadIdx.x == 0) *counter = 0u;  // arrival counter of finish_dyn_bwd
@@ -955,7 +1026,12 @@ __global__ void __launch_bounds__(128)
       const double v = __shfl_sync(0xffffffffu, gm[j] * e0[j], base + rr);
       dt[2 * N + rr * N + j] = v;
     }
-  if (!live || row != 0) return;
+  if (row != 0) return;
+  if (!live) {
+    // padding tokens of the last operand-image block
+    if constexpr (N == 4) { if (img != nullptr && b < img_tokens) gx_image_row(nullptr, img, b); }
+    return;
+  }
   float* tb = tokb + b * Lc::TB;
   double* tr = tokr + b * Lc::NR;
   double s = 0.0, da0 = 0.0, da1 = 0.0, da2 = 0.0;
@@ -987,6 +1063,9 @@ __global__ void __launch_bounds__(128)
   tr[NH + 0] = da0;
   tr[NH + 1] = da1;
   tr[NH + 2] = da2;
+  if constexpr (N == 4) {
+    if (img != nullptr) gx_image_row(tb, img, b);
+  }
 }
 
 // Static-H per-token scalars (fp64): beta, inv_r for grad_x, and per-token
@@ -2046,73 +2125,7 @@ __global__ void __launch_bounds__(320, 2)
 //   After the range: D2 -> this split's dphi partial, sum of gy.xa.inv_r ->
 //   this split's grad-w partial.
 // ---------------------------------------------------------------------------
-struct Gx6Cfg {
-  static constexpr int CW = 32, COLS = 128, TOK = 32, NH = 24, KP = 32;
-  static constexpr int SG = 3, SI = 3, ND = 2, E_WARPS = 16, TPE = TOK / E_WARPS, THREADS = 32 * (2 + E_WARPS + 4 + 1 + 4);
-  static constexpr int D2_WARP = 2 + E_WARPS + 4;          // issues the D2 MMAs
-  static constexpr int XT_WARP0 = D2_WARP + 1;             // first of the four X^T warps
-  // operand image of one token block (floats)
-  static constexpr int IMG_B1H = 0, IMG_B1L = TOK * NH, IMG_B2H = 2 * TOK * NH, IMG_B2L = IMG_B2H + KP * TOK;
-  static constexpr int IMG_SC = IMG_B2L + KP * TOK, IMG_FLOATS = IMG_SC + TOK * 32;
-  static constexpr uint32_t IMG = IMG_FLOATS * 4;
-  static constexpr uint32_t GB = TOK * 4 * CW * 4;         // g (or x) tile bytes
-  static constexpr uint32_t OFF_IMG = SG * 2 * GB;         // g/x ring, then the image ring
-  static constexpr uint32_t LOCB = TOK * COLS * 4;         // local terms [tokens][128 columns]
-  static constexpr uint32_t OFF_LOC = OFF_IMG + SI * IMG;  // [ND buffers]
-  static constexpr uint32_t OFF_GW = OFF_LOC + ND * LOCB;  // grad-w partials [E warps][32]
-  static constexpr uint32_t OFF_BAR = OFF_GW + E_WARPS * CW * 4;
-  static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 2;
-  static constexpr size_t SMEM = OFF_BAR + NBAR * 8 + 16 + 128;
-  // tensor memory: D1[b] [TOK b, +TOK); D2 [64, 96); Phi^T hi [96, 120), lo [128, 152);
-  // X^T[b] [256 + 2 TOK b, +2 TOK) hi|lo
-  static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t D2_COL = 64, A1_COL = 96, A1L_COL = 128, XT_COL = 256;
-  static_assert(ND * TOK <= 64 && XT_COL + 2 * TOK * ND <= TMEM_COLS && TOK % 16 == 0, "tensor-memory plan");
-};
 
-// Operand image of each token block from the per-token backward rows:
-// D_p hi/lo as the K-major [TOK tokens x 24] B operand of D1 and as the
-// K-major [32 (k, zero-padded) x TOK tokens] B operand of D2, and 32 scalars
-// per token (beta, inv_r, coef, 0, h[4], h_post[4], M^T[16], 0[4]).  Tokens
-// past B are zero.
-__global__ void __launch_bounds__(128)
-    gx_image_kernel(const float* __restrict__ tokb, float* __restrict__ img, int64_t B, int64_t nblk) {
-  using Lc = L<4>;
-  using F = Gx6Cfg;
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= nblk * F::TOK) return;
-  const bool live = t < B;
-  const float* tb = tokb + (live ? t : 0) * Lc::TB;
-  float* im = img + (t / F::TOK) * F::IMG_FLOATS;
-  const int tt = (int)(t % F::TOK);
-#pragma unroll
-  for (int k = 0; k < F::KP; ++k) {
-    const float d = (live && k < F::NH) ? tb[4 + k] : 0.f;
-    uint32_t hi, lo;
-    split_tf32(d, hi, lo);
-    if (k < F::NH) {
-      const uint32_t o1 = umma_kmaj_off(tt, k, F::TOK) / 4;
-      im[F::IMG_B1H + o1] = __uint_as_float(hi);
-      im[F::IMG_B1L + o1] = __uint_as_float(lo);
-    }
-    const uint32_t o2 = umma_kmaj_off(k, tt, F::KP) / 4;
-    im[F::IMG_B2H + o2] = __uint_as_float(hi);
-    im[F::IMG_B2L + o2] = __uint_as_float(lo);
-  }
-  float* sc = im + F::IMG_SC + tt * 32;
-  float v[32];
-#pragma unroll
-  for (int e = 0; e < 32; ++e) v[e] = 0.f;
-  if (live) {
-    v[0] = tb[0]; v[1] = tb[1]; v[2] = tb[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) { v[4 + i] = tb[Lc::OFF_TH + i]; v[8 + i] = tb[Lc::OFF_THP + i]; }
-#pragma unroll
-    for (int e = 0; e < 16; ++e) v[12 + e] = tb[Lc::OFF_TM + e];
-  }
-#pragma unroll
-  for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(sc + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-}
 
 __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     grad_x6_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
@@ -2885,8 +2898,14 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   int rc = check_launch("mhc_layer_bwd_dynamic/bwd_stats");
   if (rc) return rc;
   constexpr int TG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);
-  if (B > 0) { ProfScope _ps("token_bwd", s); token_bwd_lanes_kernel<N><<<grid_1d(B * TG, 128), 128, 0, s>>>(stats, rec, ap, aq, ar, bp, bq, br, tokb,
-                                                     tokr, B, C, iters, s_eps, r_eps, counter); }
+  // the warp-specialised grad_x (n = 4) reads the operand image token_bwd writes
+  const bool use6 = N == 4 && p.nsplit6 > 0 && C % Gx6Cfg::CW == 0 && aligned16(g) && aligned16(x) &&
+                    aligned16(img) && aligned16(gx);
+  const int64_t img_tokens = use6 ? p.nblk6 * Gx6Cfg::TOK : 0;
+  const int64_t tb_tokens = B > img_tokens ? B : img_tokens;
+  if (B > 0) { ProfScope _ps("token_bwd", s); token_bwd_lanes_kernel<N><<<grid_1d(tb_tokens * TG, 128), 128, 0, s>>>(stats, rec, ap, aq, ar, bp, bq, br, tokb,
+                                                     tokr, B, C, iters, s_eps, r_eps, counter,
+                                                     use6 ? img : nullptr, img_tokens); }
   else cudaMemsetAsync(counter, 0, sizeof(unsigned int), s);
   rc = check_launch("mhc_layer_bwd_dynamic/token_bwd");
   if (rc) return rc;
@@ -2896,11 +2915,10 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
     // warp-specialised tensor-core grad_x
     using F6 = Gx6Cfg;
     CUtensorMap gm, xm, om;
-    if (p.nsplit6 > 0 && C % F6::CW == 0 && aligned16(g) && aligned16(x) && aligned16(img) && aligned16(gx) &&
+    if (use6 &&
         make_tmap_2d_f32(&gm, g, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW) &&
         make_tmap_2d_f32(&xm, x, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW) &&
         make_tmap_2d_f32(&om, gx, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW)) {
-      { ProfScope _ps("gx_image", s); gx_image_kernel<<<grid_1d(p.nblk6 * F6::TOK, 128), 128, 0, s>>>(tokb, img, B, p.nblk6); }
       cudaFuncSetAttribute(grad_x6_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F6::SMEM);
       const int nt6 = (int)(C / F6::CW);
       { ProfScope _ps("grad_x", s); grad_x6_kernel<<<(unsigned)(nt6 * p.nsplit6), F6::THREADS, F6::SMEM, s>>>(
