@@ -2109,7 +2109,7 @@ __global__ void __launch_bounds__(320, 2)
 //     TMA:  g, x [32 tokens x 4 streams x 32 channels] and the block's
 //           operand image (d_p split into tf32 hi/lo in both the B layout of
 //           D1 and of D2, plus the per-token scalars), written by
-//           gx_image_kernel in the exact K-major shared-memory layout;
+//           token_bwd (gx_image_row) in the exact K-major shared-memory layout;
 //     MMA:  D1[b] = Phi^T[col x 24] . D_p^T      (M=128, N=32, 3xTF32)
 //           D2   += X^T[col x 32 tok] . D_p      (M=128, N=32, 3xTF32)
 //           with Phi^T resident in shared memory, X^T (A of D2) and D1 in
