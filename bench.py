@@ -68,12 +68,13 @@ def algorithmic_bytes(mode, B, n, C):
     raise ValueError(mode)
 
 
-def kernel_bytes(name, B, n, C):
+def kernel_bytes(name, B, n, C, elem=4):
     """Algorithmic bytes per launch of the layer kernels (unique data a launch
-    must move: its inputs once and its outputs once)."""
+    must move: its inputs once and its outputs once); elem = bytes per element
+    of x / out (4 fp32, 2 bf16 I/O)."""
     nC = n * C
     NH = n * n + 2 * n
-    x = B * nC * 4
+    x = B * nC * elem
     return {
         "proj_stats": x + NH * nC * 4,
         "stream_fwd": 2 * x + C * 4,
@@ -350,14 +351,14 @@ def run_mine(args, world, rank, local):
     kernels = {}
     for name, (cnt, tot) in rep.items():
         avg = tot / cnt
-        kb = kernel_bytes(name, tokens, n, C)
+        kb = kernel_bytes(name, tokens, n, C, 2 if mode.endswith("bf16") else 4)
         kernels[name] = {"launches_per_step": cnt / prof_steps, "avg_ms": avg,
                          "share": tot / sum(t for _, t in rep.values()),
                          "gbs": (kb / (avg * 1e-3) / 1e9) if kb else None}
     dom = max(rep, key=lambda k: rep[k][1])
     peak, peak_kind = peaks()
     dom_avg = rep[dom][1] / rep[dom][0]
-    dom_bytes = kernel_bytes(dom, tokens, n, C)
+    dom_bytes = kernel_bytes(dom, tokens, n, C, 2 if mode.endswith("bf16") else 4)
     achieved = dom_bytes / (dom_avg * 1e-3) / 1e9 if dom_bytes else None
     traffic = None
     tf = os.path.join(ROOT, "profiles", "ncu_traffic.txt")

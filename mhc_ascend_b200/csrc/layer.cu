@@ -583,6 +583,12 @@ struct bf16x4 { __nv_bfloat162 a, b; };
 
 template <typename T> struct IO;
 template <> struct IO<float> {
+  // raw4: four elements as stored (kept in registers until used)
+  using raw4 = float4;
+  static __device__ __forceinline__ raw4 load_raw4(const float* p, int64_t q) {
+    return __ldcs(reinterpret_cast<const float4*>(p) + q);
+  }
+  static __device__ __forceinline__ float4 to_f4(raw4 r) { return r; }
   static __device__ __forceinline__ float4 load4(const float* p, int64_t q) {
     return __ldcs(reinterpret_cast<const float4*>(p) + q);
   }
@@ -591,6 +597,15 @@ template <> struct IO<float> {
   }
 };
 template <> struct IO<__nv_bfloat16> {
+  using raw4 = uint2;
+  static __device__ __forceinline__ raw4 load_raw4(const __nv_bfloat16* p, int64_t q) {
+    return __ldcs(reinterpret_cast<const uint2*>(p) + q);
+  }
+  static __device__ __forceinline__ float4 to_f4(raw4 u) {
+    // bf16 -> fp32 is a 16-bit shift
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+  }
   static __device__ __forceinline__ float4 load4(const __nv_bfloat16* p, int64_t q) {
     const uint2 u = __ldcs(reinterpret_cast<const uint2*>(p) + q);
     __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
@@ -608,7 +623,7 @@ template <> struct IO<__nv_bfloat16> {
 };
 
 template <int N, int QPT, typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, sizeof(T) == 2 ? 3 : 2)
     static_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
                       const float* __restrict__ rec, float* __restrict__ rms,
                       T* __restrict__ out, int64_t B, int64_t C, float r_eps) {
@@ -625,7 +640,7 @@ __global__ void __launch_bounds__(256)
   for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
     const T* xb = x + b * N * C;
     T* ob = out + b * N * C;
-    float4 xv[QPT][N];
+    typename IO<T>::raw4 xv[QPT][N];   // as stored: bf16 tokens take half the registers
     float4 xa[QPT];
     float sq = 0.f;
 #pragma unroll
@@ -634,11 +649,12 @@ __global__ void __launch_bounds__(256)
       xa[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (q < C4) {
 #pragma unroll
-        for (int j = 0; j < N; ++j) xv[u][j] = IO<T>::load4(xb + j * C, q);
+        for (int j = 0; j < N; ++j) xv[u][j] = IO<T>::load_raw4(xb + j * C, q);
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-          xa[u].x = fmaf(h[j], xv[u][j].x, xa[u].x); xa[u].y = fmaf(h[j], xv[u][j].y, xa[u].y);
-          xa[u].z = fmaf(h[j], xv[u][j].z, xa[u].z); xa[u].w = fmaf(h[j], xv[u][j].w, xa[u].w);
+          const float4 xf = IO<T>::to_f4(xv[u][j]);
+          xa[u].x = fmaf(h[j], xf.x, xa[u].x); xa[u].y = fmaf(h[j], xf.y, xa[u].y);
+          xa[u].z = fmaf(h[j], xf.z, xa[u].z); xa[u].w = fmaf(h[j], xf.w, xa[u].w);
         }
         sq += xa[u].x * xa[u].x + xa[u].y * xa[u].y + xa[u].z * xa[u].z + xa[u].w * xa[u].w;
       }
@@ -668,8 +684,9 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
           for (int j = 0; j < N; ++j) {
             const float mij = m[i * N + j];
-            o.x = fmaf(mij, xv[u][j].x, o.x); o.y = fmaf(mij, xv[u][j].y, o.y);
-            o.z = fmaf(mij, xv[u][j].z, o.z); o.w = fmaf(mij, xv[u][j].w, o.w);
+            const float4 xf = IO<T>::to_f4(xv[u][j]);
+            o.x = fmaf(mij, xf.x, o.x); o.y = fmaf(mij, xf.y, o.y);
+            o.z = fmaf(mij, xf.z, o.z); o.w = fmaf(mij, xf.w, o.w);
           }
           IO<T>::store4(ob + i * C, q, o);
         }
