@@ -158,6 +158,21 @@ MHC_API int mhc_layer_fwd_dynamic(const float* x, const float* rmsnorm_weight, c
                           int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* bf16 streams, an extension of mhc_layer_fwd_dynamic (the reference
+ * keeps bf16 intermediates, bindings.cpp:906): x and out are bf16, the
+ * parameters, token_state and all arithmetic fp32.  Needs n <= 4, hidden a
+ * multiple of 64 and 16-byte aligned x / out / rmsnorm_weight
+ * (MHC_ERR_UNSUPPORTED / MHC_ERR_ALIGNMENT otherwise).  Workspace as for
+ * mhc_layer_fwd_dynamic. */
+MHC_API int mhc_layer_fwd_dynamic_bf16(const void* x, const float* rmsnorm_weight,
+                          const float* phi_pre, const float* phi_post, const float* phi_res,
+                          const float* alpha_pre, const float* alpha_post,
+                          const float* alpha_res, const float* b_pre, const float* b_post,
+                          const float* b_res, void* out, float* token_state, int64_t batch,
+                          int32_t n, int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
+                          float rmsnorm_eps, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
 /* No counterpart in the reference.  Same as mhc_layer_fwd_dynamic, for
  * callers that cannot provide a workspace (no device allocator of their own,
  * device memory fixed at start-up, or a path that must not call cudaMalloc /
@@ -188,6 +203,24 @@ MHC_API int mhc_layer_bwd_dynamic(const float* grad_out, const float* x, const f
                           const float* alpha_pre, const float* alpha_post,
                           const float* alpha_res, const float* b_pre, const float* b_post,
                           const float* b_res, const float* token_state, float* grad_x,
+                          float* grad_rmsnorm_weight, float* grad_phi_pre,
+                          float* grad_phi_post, float* grad_phi_res, float* grad_alpha_pre,
+                          float* grad_alpha_post, float* grad_alpha_res, float* grad_b_pre,
+                          float* grad_b_post, float* grad_b_res, int64_t batch, int32_t n,
+                          int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
+                          float rmsnorm_eps, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* bf16 streams for the backward: grad_out, x and grad_x are bf16, every
+ * parameter gradient fp32 (arithmetic fp32, moments fp64 as in
+ * mhc_layer_bwd_dynamic).  Needs n == 4, hidden a multiple of 32 and 16-byte
+ * aligned tensors.  Workspace as for mhc_layer_bwd_dynamic. */
+MHC_API int mhc_layer_bwd_dynamic_bf16(const void* grad_out, const void* x,
+                          const float* rmsnorm_weight, const float* phi_pre,
+                          const float* phi_post, const float* phi_res,
+                          const float* alpha_pre, const float* alpha_post,
+                          const float* alpha_res, const float* b_pre, const float* b_post,
+                          const float* b_res, const float* token_state, void* grad_x,
                           float* grad_rmsnorm_weight, float* grad_phi_pre,
                           float* grad_phi_post, float* grad_phi_res, float* grad_alpha_pre,
                           float* grad_alpha_post, float* grad_alpha_res, float* grad_b_pre,

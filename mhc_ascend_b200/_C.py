@@ -47,9 +47,13 @@ SIGNATURES = {
                               [_P] * 13 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
     "mhc_layer_fwd_dynamic_noalloc": (ctypes.c_int,
                                       [_P] * 13 + [_I64, _I32, _I64, _I32, _F, _F, _P]),
+    "mhc_layer_fwd_dynamic_bf16": (ctypes.c_int,
+                                   [_P] * 13 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
     "mhc_layer_bwd_dynamic_workspace_bytes": (_SZ, [_I64, _I32, _I64]),
     "mhc_layer_bwd_dynamic": (ctypes.c_int,
                               [_P] * 24 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
+    "mhc_layer_bwd_dynamic_bf16": (ctypes.c_int,
+                                   [_P] * 24 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
     "mhc_layer_static_workspace_bytes": (_SZ, [_I64, _I32, _I64]),
     "mhc_layer_fwd_static_f32": (ctypes.c_int,
                                  [_P] * 7 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),

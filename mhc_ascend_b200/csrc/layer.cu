@@ -75,19 +75,28 @@ struct Gx6Cfg {
   static constexpr int IMG_B1H = 0, IMG_B1L = TOK * NH, IMG_B2H = 2 * TOK * NH, IMG_B2L = IMG_B2H + KP * TOK;
   static constexpr int IMG_SC = IMG_B2L + KP * TOK, IMG_FLOATS = IMG_SC + TOK * 32;
   static constexpr uint32_t IMG = IMG_FLOATS * 4;
-  static constexpr uint32_t GB = TOK * 4 * CW * 4;         // g (or x) tile bytes
-  static constexpr uint32_t OFF_IMG = SG * 2 * GB;         // g/x ring, then the image ring
   static constexpr uint32_t LOCB = TOK * COLS * 4;         // local terms [tokens][128 columns]
-  static constexpr uint32_t OFF_LOC = OFF_IMG + SI * IMG;  // [ND buffers]
-  static constexpr uint32_t OFF_GW = OFF_LOC + ND * LOCB;  // grad-w partials [E warps][32]
-  static constexpr uint32_t OFF_BAR = OFF_GW + E_WARPS * CW * 4;
   static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 2;
-  static constexpr size_t SMEM = OFF_BAR + NBAR * 8 + 16 + 128;
   // tensor memory: D1[b] [TOK b, +TOK); D2 [64, 96); Phi^T hi [96, 120), lo [128, 152);
   // X^T[b] [256 + 2 TOK b, +2 TOK) hi|lo
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t D2_COL = 64, A1_COL = 96, A1L_COL = 128, XT_COL = 256;
   static_assert(ND * TOK <= 64 && XT_COL + 2 * TOK * ND <= TMEM_COLS && TOK % 16 == 0, "tensor-memory plan");
+};
+
+// Shared-memory plan of grad_x6 for stream element type T (fp32 or bf16 I/O).
+template <typename T>
+struct Gx6S {
+  using F = Gx6Cfg;
+  static constexpr bool BF16 = sizeof(T) == 2;
+  static constexpr uint32_t GB = F::TOK * 4 * F::CW * sizeof(T);   // g (or x) tile bytes
+  static constexpr uint32_t OFF_IMG = F::SG * 2 * GB;              // g/x ring, then the image ring
+  static constexpr uint32_t OFF_LOC = OFF_IMG + F::SI * F::IMG;    // [ND buffers]
+  static constexpr uint32_t STGB = BF16 ? F::TOK * F::COLS * 2 : 0; // bf16 grad_x staging tile
+  static constexpr uint32_t OFF_STG = OFF_LOC + F::ND * F::LOCB;   // [ND buffers]
+  static constexpr uint32_t OFF_GW = OFF_STG + F::ND * STGB;       // grad-w partials [E warps][32]
+  static constexpr uint32_t OFF_BAR = OFF_GW + F::E_WARPS * F::CW * 4;
+  static constexpr size_t SMEM = OFF_BAR + F::NBAR * 8 + 16 + 128;
 };
 
 __device__ __forceinline__ int gram_index(int i, int j, int N) {
@@ -459,17 +468,62 @@ __global__ void __launch_bounds__(128)
   for (int k = 0; k < NH; ++k) o[Lc::OFF_P + k] = p[k];
 }
 
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> struct IO;
+template <> struct IO<float> {
+  // raw4: four elements as stored (kept in registers until used)
+  using raw4 = float4;
+  static __device__ __forceinline__ raw4 load_raw4(const float* p, int64_t q) {
+    return __ldcs(reinterpret_cast<const float4*>(p) + q);
+  }
+  static __device__ __forceinline__ float4 to_f4(raw4 r) { return r; }
+  static __device__ __forceinline__ float4 load4(const float* p, int64_t q) {
+    return __ldcs(reinterpret_cast<const float4*>(p) + q);
+  }
+  static __device__ __forceinline__ void store4(float* p, int64_t q, float4 v) {
+    __stcs(reinterpret_cast<float4*>(p) + q, v);
+  }
+};
+template <> struct IO<__nv_bfloat16> {
+  using raw4 = uint2;
+  static __device__ __forceinline__ raw4 load_raw4(const __nv_bfloat16* p, int64_t q) {
+    return __ldcs(reinterpret_cast<const uint2*>(p) + q);
+  }
+  static __device__ __forceinline__ float4 to_f4(raw4 u) {
+    // bf16 -> fp32 is a 16-bit shift
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+  }
+  static __device__ __forceinline__ float4 load4(const __nv_bfloat16* p, int64_t q) {
+    const uint2 u = __ldcs(reinterpret_cast<const uint2*>(p) + q);
+    __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+    __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+    float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  static __device__ __forceinline__ void store4(__nv_bfloat16* p, int64_t q, float4 v) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    __stcs(reinterpret_cast<uint2*>(p) + q, u);
+  }
+};
+
 // ---------------------------------------------------------------------------
 // Forward 3: out[i,c] = sum_j M_ij x[j,c] + hp_i * (w_c / r) * sum_j h_j x[j,c]
 //   One CTA per token (grid-stride over tokens); per-token record in smem;
 //   rec_stride 0 = one shared record (static H) with per-token r from rms[].
 // ---------------------------------------------------------------------------
-template <int N, bool VEC, bool GRAM>
+template <int N, bool VEC, bool GRAM, typename T = float>
 __global__ void __launch_bounds__(256)
-    stream_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+    stream_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
                       const float* __restrict__ rec, int rec_stride,
-                      const float* __restrict__ rms, float* __restrict__ out, int64_t B,
+                      const float* __restrict__ rms, T* __restrict__ out, int64_t B,
                       int64_t C, float* __restrict__ rec_w) {
+  static_assert(VEC || sizeof(T) == 4, "bf16 streams use the vector path");
   // GRAM (dynamic H): also the token's Gram matrix in fp64 from exact
   // products, for the backward -- FP64 work hidden under this HBM-bound pass.
   using Lc = L<N>;
@@ -485,8 +539,8 @@ __global__ void __launch_bounds__(256)
     const float* h = s_rec + Lc::OFF_H;
     const float* hp = s_rec + Lc::OFF_HP;
     const float* m = s_rec + Lc::OFF_M;
-    const float* xb = x + b * N * C;
-    float* ob = out + b * N * C;
+    const T* xb = x + b * N * C;
+    T* ob = out + b * N * C;
     double gacc[NG];
 #pragma unroll
     for (int g = 0; g < NG; ++g) gacc[g] = 0.0;
@@ -494,7 +548,7 @@ __global__ void __launch_bounds__(256)
       for (int64_t q = threadIdx.x; q < C / 4; q += blockDim.x) {
         float4 xv[N];
 #pragma unroll
-        for (int j = 0; j < N; ++j) xv[j] = __ldcs(reinterpret_cast<const float4*>(xb + j * C) + q);
+        for (int j = 0; j < N; ++j) xv[j] = IO<T>::load4(xb + j * C, q);
         if (GRAM) {
           int g = 0;
 #pragma unroll
@@ -528,10 +582,10 @@ __global__ void __launch_bounds__(256)
             o.x = fmaf(mij, xv[j].x, o.x); o.y = fmaf(mij, xv[j].y, o.y);
             o.z = fmaf(mij, xv[j].z, o.z); o.w = fmaf(mij, xv[j].w, o.w);
           }
-          __stcs(reinterpret_cast<float4*>(ob + i * C) + q, o);
+          IO<T>::store4(ob + i * C, q, o);
         }
       }
-    } else {
+    } else if constexpr (sizeof(T) == 4) {
       for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
         float xv[N];
 #pragma unroll
@@ -580,47 +634,6 @@ __global__ void __launch_bounds__(256)
 // and writes out.  T = float or __nv_bfloat16 (fp32 arithmetic either way).
 // ---------------------------------------------------------------------------
 struct bf16x4 { __nv_bfloat162 a, b; };
-
-template <typename T> struct IO;
-template <> struct IO<float> {
-  // raw4: four elements as stored (kept in registers until used)
-  using raw4 = float4;
-  static __device__ __forceinline__ raw4 load_raw4(const float* p, int64_t q) {
-    return __ldcs(reinterpret_cast<const float4*>(p) + q);
-  }
-  static __device__ __forceinline__ float4 to_f4(raw4 r) { return r; }
-  static __device__ __forceinline__ float4 load4(const float* p, int64_t q) {
-    return __ldcs(reinterpret_cast<const float4*>(p) + q);
-  }
-  static __device__ __forceinline__ void store4(float* p, int64_t q, float4 v) {
-    __stcs(reinterpret_cast<float4*>(p) + q, v);
-  }
-};
-template <> struct IO<__nv_bfloat16> {
-  using raw4 = uint2;
-  static __device__ __forceinline__ raw4 load_raw4(const __nv_bfloat16* p, int64_t q) {
-    return __ldcs(reinterpret_cast<const uint2*>(p) + q);
-  }
-  static __device__ __forceinline__ float4 to_f4(raw4 u) {
-    // bf16 -> fp32 is a 16-bit shift
-    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
-                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
-  }
-  static __device__ __forceinline__ float4 load4(const __nv_bfloat16* p, int64_t q) {
-    const uint2 u = __ldcs(reinterpret_cast<const uint2*>(p) + q);
-    __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
-    __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
-    float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
-    return make_float4(a.x, a.y, b.x, b.y);
-  }
-  static __device__ __forceinline__ void store4(__nv_bfloat16* p, int64_t q, float4 v) {
-    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-    uint2 u;
-    u.x = *reinterpret_cast<uint32_t*>(&lo);
-    u.y = *reinterpret_cast<uint32_t*>(&hi);
-    __stcs(reinterpret_cast<uint2*>(p) + q, u);
-  }
-};
 
 template <int N, int QPT, typename T>
 __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 3 : 2)
@@ -799,9 +812,9 @@ __device__ __forceinline__ void block_reduce_to_global(double (&acc)[V], double*
   __syncthreads();
 }
 
-template <int N, bool VEC, bool WITH_G>
+template <int N, bool VEC, bool WITH_G, typename T = float>
 __global__ void __launch_bounds__(128, 4)
-    bwd_stats_kernel(const float* __restrict__ g, const float* __restrict__ x,
+    bwd_stats_kernel(const T* __restrict__ g, const T* __restrict__ x,
                      const float* __restrict__ w, double* __restrict__ stats, int64_t B,
                      int64_t C) {
   // Moments are accumulated in fp64: products of fp32 inputs are exact in
@@ -816,8 +829,8 @@ __global__ void __launch_bounds__(128, 4)
     double acc[NS1];
 #pragma unroll
     for (int v = 0; v < NS1; ++v) acc[v] = 0.0;
-    const float* gb = g + b * N * C;
-    const float* xb = x + b * N * C;
+    const T* gb = g + b * N * C;
+    const T* xb = x + b * N * C;
     auto accum = [&](const float (&gf)[N], const float (&xf)[N], float wf) {
       double gv[N], xv[N];
 #pragma unroll
@@ -848,8 +861,8 @@ __global__ void __launch_bounds__(128, 4)
         float4 g4[N], x4[N];
 #pragma unroll
         for (int i = 0; i < N; ++i) {
-          g4[i] = __ldcs(reinterpret_cast<const float4*>(gb + i * C) + q);
-          x4[i] = __ldcs(reinterpret_cast<const float4*>(xb + i * C) + q);
+          g4[i] = IO<T>::load4(gb + i * C, q);
+          x4[i] = IO<T>::load4(xb + i * C, q);
         }
         const float4 w4 = __ldg(reinterpret_cast<const float4*>(w) + q);
         float gv[N], xv[N];
@@ -866,7 +879,8 @@ __global__ void __launch_bounds__(128, 4)
         for (int i = 0; i < N; ++i) { gv[i] = g4[i].w; xv[i] = x4[i].w; }
         accum(gv, xv, w4.w);
       }
-    } else if (VEC) {
+    } else if constexpr (sizeof(T) == 4) {
+      if (VEC) {
       // float2 per stream: keeps the live load registers low enough for
       // 4 CTAs (16 warps) per SM next to the 42 fp64 accumulators.
 #pragma unroll 2
@@ -893,6 +907,7 @@ __global__ void __launch_bounds__(128, 4)
         for (int i = 0; i < N; ++i) { gv[i] = gb[i * C + c]; xv[i] = xb[i * C + c]; }
         accum(gv, xv, w[c]);
       }
+    }
     }
     block_reduce_to_global<NS1>(acc, red, stats + b * NS1);
   }
@@ -1832,18 +1847,21 @@ __device__ __forceinline__ void umma_tf32_at(uint32_t d_tmem, uint32_t a_tmem, u
 //   full (TMA bytes), empty (operand warps done with x + MMA done with phi),
 //   aready / afree per tensor-memory A buffer.
 // ---------------------------------------------------------------------------
-template <int N>
+template <int N, typename T = float>
 struct PumCfg {
   static constexpr int NH = L<N>::NH, NHP = L<N>::NHP, NG = L<N>::NG;
   static constexpr int NB = (NH + 15) / 16 * 16;           // MMA N (padded phi rows)
-  static constexpr int TOK = 128, CH = 32, THREADS = 320;
-  static constexpr uint32_t XB = TOK * CH * 4;             // x tile of one stage
-  static constexpr uint32_t PB = NB * CH * 4;              // phi tile of one stage
+  // a stage is one 128-byte row of x per token: 32 fp32 or 64 bf16 channels
+  static constexpr int TOK = 128, CH = 128 / (int)sizeof(T), THREADS = 320;
+  static constexpr int PSUB = CH / 32;                     // 32-channel phi sub-tiles per stage
+  static constexpr bool BF16 = sizeof(T) == 2;             // bf16 x is exact in tf32: no lo part
+  static constexpr uint32_t XB = TOK * 128;                // x tile of one stage
+  static constexpr uint32_t PB = NB * CH * 4;              // phi tile (fp32) of one stage
   static constexpr uint32_t SLOT = XB + 2 * PB;            // x, phi_hi, phi_lo
   static constexpr uint32_t OFF_PH = XB, OFF_PL = XB + PB;
   static constexpr uint32_t TX = SLOT;                     // bytes TMA brings per stage
-  static constexpr int STAGES = 4, NA = 2;                 // smem stages, tensor-memory A buffers
-  static constexpr uint32_t TCOLS = 256;                   // D [0, 32); A[a] = [64 + 64 a, +64) hi|lo
+  static constexpr int STAGES = BF16 ? 3 : 4, NA = 2;      // smem stages, tensor-memory A buffers
+  static constexpr uint32_t TCOLS = 256;                   // D [0, 32); A[a] = [64 + 64 a, +64): fp32 hi|lo, bf16 hi
   static constexpr uint32_t ACOL = 64;
   static constexpr uint32_t OFF_GX = STAGES * SLOT;        // Gram exchange [128][NG]
   static constexpr uint32_t OFF_BAR = OFF_GX + TOK * NG * 4;
@@ -1914,12 +1932,12 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
   return false;
 }
 
-template <int N>
+template <int N, typename T = float>
 __global__ void __launch_bounds__(320, 2)
     proj_umma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap hmap,
                      const __grid_constant__ CUtensorMap lmap, float* __restrict__ ppart,
                      float* __restrict__ gpart, int64_t B, int64_t C, int cps) {
-  using P = PumCfg<N>;
+  using P = PumCfg<N, T>;
   constexpr int NG = P::NG, NHP = P::NHP, S = P::STAGES, NA = P::NA;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1982,8 +2000,11 @@ __global__ void __launch_bounds__(320, 2)
         const int i = k % N;
         mbar_expect_tx(&full[slot], P::TX);
         tma_load_3d(base, &xmap, c, i, (int)t0, &full[slot]);
-        tma_load_3d(base + P::OFF_PH, &hmap, c, i, 0, &full[slot]);
-        tma_load_3d(base + P::OFF_PL, &lmap, c, i, 0, &full[slot]);
+#pragma unroll
+        for (int ps = 0; ps < P::PSUB; ++ps) {
+          tma_load_3d(base + P::OFF_PH + ps * P::NB * 128, &hmap, c + 32 * ps, i, 0, &full[slot]);
+          tma_load_3d(base + P::OFF_PL + ps * P::NB * 128, &lmap, c + 32 * ps, i, 0, &full[slot]);
+        }
       }
       // no copy may still be landing when the CTA exits (bounded)
       for (int q = issued > S ? issued - S : 0; q < issued; ++q)
@@ -2005,11 +2026,17 @@ __global__ void __launch_bounds__(320, 2)
         const uint32_t at = tmem + P::ACOL + 64 * a;
 #pragma unroll
         for (int st = 0; st < P::CH / 8; ++st) {
-          const uint64_t bh = umma_desc_sw128(sb + P::OFF_PH + 32 * st);
-          const uint64_t bl = umma_desc_sw128(sb + P::OFF_PL + 32 * st);
-          umma_tf32_at(tmem, at + 32 + 8 * st, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
-          umma_tf32_at(tmem, at + 8 * st, bl, ID, 1u);
-          umma_tf32_at(tmem, at + 8 * st, bh, ID, 1u);
+          const uint32_t boff = (st / 4) * P::NB * 128 + 32 * (st % 4);
+          const uint64_t bh = umma_desc_sw128(sb + P::OFF_PH + boff);
+          const uint64_t bl = umma_desc_sw128(sb + P::OFF_PL + boff);
+          if constexpr (P::BF16) {
+            umma_tf32_at(tmem, at + 8 * st, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
+            umma_tf32_at(tmem, at + 8 * st, bl, ID, 1u);
+          } else {
+            umma_tf32_at(tmem, at + 32 + 8 * st, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
+            umma_tf32_at(tmem, at + 8 * st, bl, ID, 1u);
+            umma_tf32_at(tmem, at + 8 * st, bh, ID, 1u);
+          }
         }
         umma_commit(&empty[slot]);
         umma_commit(&afree[a]);
@@ -2031,7 +2058,8 @@ __global__ void __launch_bounds__(320, 2)
     for (int g = 0; g < NG; ++g) gacc[g] = 0.f;
     bool ok = true;
     for (int b = 0; b < nblocks && ok; ++b) {
-      float v[N][16];
+      // this thread's 16 (fp32) or 32 (bf16) channels of each stream, as stored
+      uint4 v[N][4];
 #pragma unroll
       for (int i = 0; i < N; ++i) {
         const int k = b * N + i;
@@ -2039,22 +2067,35 @@ __global__ void __launch_bounds__(320, 2)
         const unsigned char* base = sm + slot * P::SLOT;
         if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word)) { ok = false; break; }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float4 q4 = *reinterpret_cast<const float4*>(base + choff[j]);
-          v[i][4 * j + 0] = q4.x; v[i][4 * j + 1] = q4.y; v[i][4 * j + 2] = q4.z; v[i][4 * j + 3] = q4.w;
-        }
+        for (int j = 0; j < 4; ++j) v[i][j] = *reinterpret_cast<const uint4*>(base + choff[j]);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);  // x of this stage now lives in registers
         if (k >= NA && !mbar_wait_or_abort(&afree[a], (uint32_t)(((k / NA) - 1) & 1), abort_word)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + P::ACOL + 64 * a + 16 * h;
+        if constexpr (P::BF16) {
+          // bf16 -> fp32 is exact and already a tf32 value: hi only
+          const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + P::ACOL + 64 * a + 32 * h;
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t hi[8], lo[8];
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t hi[16];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) split_tf32(v[i][8 * hf + e], hi[e], lo[e]);
-          tmem_st8(ta + 8 * hf, hi);
-          tmem_st8(ta + 32 + 8 * hf, lo);
+            for (int e = 0; e < 8; ++e) {
+              const uint32_t w2 = (&v[i][2 * hf].x)[e];   // channels 2e, 2e+1 of chunks 2hf, 2hf+1
+              hi[2 * e] = w2 << 16;
+              hi[2 * e + 1] = w2 & 0xFFFF0000u;
+            }
+            tmem_st16(ta + 16 * hf, hi);
+          }
+        } else {
+          const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + P::ACOL + 64 * a + 16 * h;
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t hi[8], lo[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) split_tf32(__uint_as_float((&v[i][2 * hf].x)[e]), hi[e], lo[e]);
+            tmem_st8(ta + 8 * hf, hi);
+            tmem_st8(ta + 32 + 8 * hf, lo);
+          }
         }
         tmem_st_wait();
         tc_fence_before();
@@ -2069,9 +2110,17 @@ __global__ void __launch_bounds__(320, 2)
       for (int i = 0; i < N; ++i)
 #pragma unroll
         for (int j = i; j < N; ++j) {
-          float blk = v[i][0] * v[j][0];
+          float blk = 0.f;
 #pragma unroll
-          for (int q = 1; q < 16; ++q) blk = fmaf(v[i][q], v[j][q], blk);
+          for (int q = 0; q < 16; ++q) {
+            const uint32_t ui = (&v[i][0].x)[q], uj = (&v[j][0].x)[q];
+            if constexpr (P::BF16) {
+              blk = fmaf(__uint_as_float(ui << 16), __uint_as_float(uj << 16), blk);
+              blk = fmaf(__uint_as_float(ui & 0xFFFF0000u), __uint_as_float(uj & 0xFFFF0000u), blk);
+            } else {
+              blk = fmaf(__uint_as_float(ui), __uint_as_float(uj), blk);
+            }
+          }
           gacc[g] += blk;
           ++g;
         }
@@ -2144,18 +2193,20 @@ __global__ void __launch_bounds__(320, 2)
 // ---------------------------------------------------------------------------
 
 
+template <typename T>
 __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     grad_x6_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
                    const __grid_constant__ CUtensorMap omap, const float* __restrict__ img, const float* __restrict__ w,
                    const float* __restrict__ phi_pre, const float* __restrict__ phi_post,
-                   const float* __restrict__ phi_res, float* __restrict__ gx,
+                   const float* __restrict__ phi_res, T* __restrict__ gx,
                    float* __restrict__ dphi_part, float* __restrict__ gw_part, int64_t B,
                    int64_t C, int ntiles, int nsplit, int64_t nblk) {
   using F = Gx6Cfg;
+  using SM = Gx6S<T>;
   constexpr int SG = F::SG, SI = F::SI, ND = F::ND, CW = F::CW, COLS = F::COLS, TOK = F::TOK;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  uint64_t* gfull = reinterpret_cast<uint64_t*>(sm + F::OFF_BAR);
+  uint64_t* gfull = reinterpret_cast<uint64_t*>(sm + SM::OFF_BAR);
   uint64_t* gfree = gfull + SG;
   uint64_t* ifull = gfree + SG;
   uint64_t* ifree = ifull + SI;
@@ -2219,17 +2270,17 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         }
         const int64_t blk = blk0 + j;
         const int row = (int)(blk * TOK * 4);
-        unsigned char* gb = sm + sg * 2 * F::GB;
-        mbar_expect_tx(&gfull[sg], 2 * F::GB);
+        unsigned char* gb = sm + sg * 2 * SM::GB;
+        mbar_expect_tx(&gfull[sg], 2 * SM::GB);
         tma_load_2d(gb, &gmap, (int)c0, row, &gfull[sg]);
-        tma_load_2d(gb + F::GB, &xmap, (int)c0, row, &gfull[sg]);
+        tma_load_2d(gb + SM::GB, &xmap, (int)c0, row, &gfull[sg]);
         gi = j + 1;
         if (j >= SI && !mbar_wait_or_abort(&ifree[si], (uint32_t)(((j / SI) - 1) & 1), abort_word)) {
           *abort_word = 1;
           break;
         }
         mbar_expect_tx(&ifull[si], F::IMG);
-        bulk_load(sm + F::OFF_IMG + si * F::IMG, img + blk * F::IMG_FLOATS, F::IMG, &ifull[si]);
+        bulk_load(sm + SM::OFF_IMG + si * F::IMG, img + blk * F::IMG_FLOATS, F::IMG, &ifull[si]);
         ii = j + 1;
       }
       // no copy may still be landing when the CTA exits (bounded)
@@ -2249,7 +2300,7 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t im = sbase + F::OFF_IMG + si * F::IMG;
+        const uint32_t im = sbase + SM::OFF_IMG + si * F::IMG;
 #pragma unroll
         for (int ks = 0; ks < 3; ++ks) {
           const uint32_t ah = tmem + F::A1_COL + 8 * ks, al = tmem + F::A1L_COL + 8 * ks;
@@ -2272,16 +2323,21 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { *abort_word = 1; break; }
         if (!mbar_wait_or_abort(&a2_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { *abort_word = 1; break; }
         tc_fence_after();
-        const uint32_t im = sbase + F::OFF_IMG + si * F::IMG;
+        const uint32_t im = sbase + SM::OFF_IMG + si * F::IMG;
         const uint32_t a2 = tmem + F::XT_COL + 2 * TOK * b;
 #pragma unroll
         for (int ks = 0; ks < TOK / 8; ++ks) {
           const uint32_t ah = a2 + 8 * ks, al = a2 + TOK + 8 * ks;
           const uint64_t bh = umma_desc_k(im + F::IMG_B2H * 4, F::KP, ks, 0);
           const uint64_t bl = umma_desc_k(im + F::IMG_B2L * 4, F::KP, ks, 0);
-          umma_tf32_at(tmem + F::D2_COL, al, bh, ID2, (j > 0 || ks > 0) ? 1u : 0u);
-          umma_tf32_at(tmem + F::D2_COL, ah, bl, ID2, 1u);
-          umma_tf32_at(tmem + F::D2_COL, ah, bh, ID2, 1u);
+          if constexpr (SM::BF16) {
+            umma_tf32_at(tmem + F::D2_COL, ah, bl, ID2, (j > 0 || ks > 0) ? 1u : 0u);
+            umma_tf32_at(tmem + F::D2_COL, ah, bh, ID2, 1u);
+          } else {
+            umma_tf32_at(tmem + F::D2_COL, al, bh, ID2, (j > 0 || ks > 0) ? 1u : 0u);
+            umma_tf32_at(tmem + F::D2_COL, ah, bl, ID2, 1u);
+            umma_tf32_at(tmem + F::D2_COL, ah, bh, ID2, 1u);
+          }
         }
         umma_commit(&a2_free[b]);
         umma_commit(&ifree[si]);
@@ -2314,10 +2370,10 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     for (int j = 0; j < nb; ++j) {
       const int sg = j % SG, b = j % ND;
       if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { *abort_word = 1; break; }
-      const float* xs = reinterpret_cast<const float*>(sm + sg * 2 * F::GB) + F::GB / 4;
+      const T* xs = reinterpret_cast<const T*>(sm + sg * 2 * SM::GB) + SM::GB / sizeof(T);
       float xv[TOK];
 #pragma unroll
-      for (int t = 0; t < TOK; ++t) xv[t] = xs[(t * 4 + q) * CW + lane];
+      for (int t = 0; t < TOK; ++t) xv[t] = to_f32(xs[(t * 4 + q) * CW + lane]);
       __syncwarp();
       if (lane == 0) mbar_arrive(&gfree[sg]);
       if (j >= ND && !mbar_wait_or_abort(&a2_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) { *abort_word = 1; break; }
@@ -2327,9 +2383,12 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       for (int hf = 0; hf < TOK / 16; ++hf) {
         uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) split_tf32(xv[16 * hf + t], hi[t], lo[t]);
+        for (int t = 0; t < 16; ++t) {
+          if constexpr (SM::BF16) hi[t] = __float_as_uint(xv[16 * hf + t]);   // exact in tf32
+          else split_tf32(xv[16 * hf + t], hi[t], lo[t]);
+        }
         tmem_st16(ta + 16 * hf, hi);
-        tmem_st16(ta + TOK + 16 * hf, lo);
+        if constexpr (!SM::BF16) tmem_st16(ta + TOK + 16 * hf, lo);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -2338,8 +2397,8 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     }
   } else {
     const int64_t c = c0 + lane;
-    float* locs = reinterpret_cast<float*>(sm + F::OFF_LOC);
-    float* gws = reinterpret_cast<float*>(sm + F::OFF_GW);
+    float* locs = reinterpret_cast<float*>(sm + SM::OFF_LOC);
+    float* gws = reinterpret_cast<float*>(sm + SM::OFF_GW);
     bool ok = true;
     constexpr int TPE = F::TPE;
     if (warp < 2 + F::E_WARPS) {
@@ -2350,20 +2409,20 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       for (int j = 0; j < nb; ++j) {
         const int sg = j % SG, si = j % SI, b = j % ND;
         if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { ok = false; break; }
-        const float* gs = reinterpret_cast<const float*>(sm + sg * 2 * F::GB);
-        const float* xs = gs + F::GB / 4;
+        const T* gs = reinterpret_cast<const T*>(sm + sg * 2 * SM::GB);
+        const T* xs = gs + SM::GB / sizeof(T);
         float gv[TPE][4], xv[TPE][4];        // [token][stream]
 #pragma unroll
         for (int u = 0; u < TPE; ++u)
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
-            gv[u][jj] = gs[((TPE * e + u) * 4 + jj) * CW + lane];
-            xv[u][jj] = xs[((TPE * e + u) * 4 + jj) * CW + lane];
+            gv[u][jj] = to_f32(gs[((TPE * e + u) * 4 + jj) * CW + lane]);
+            xv[u][jj] = to_f32(xs[((TPE * e + u) * 4 + jj) * CW + lane]);
           }
         __syncwarp();
         if (lane == 0) mbar_arrive(&gfree[sg]);   // g, x now live in registers
         if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { ok = false; break; }
-        const float* sc = reinterpret_cast<const float*>(sm + F::OFF_IMG + si * F::IMG) + F::IMG_SC;
+        const float* sc = reinterpret_cast<const float*>(sm + SM::OFF_IMG + si * F::IMG) + F::IMG_SC;
         // local terms of the four streams
         if (j >= ND && !mbar_wait_or_abort(&loc_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) { ok = false; break; }
         float* lb = locs + b * (F::LOCB / 4);
@@ -2403,12 +2462,16 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         if (!mbar_wait_or_abort(&loc_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
         tc_fence_after();
         float* lb = locs + b * (F::LOCB / 4) + i * CW + lane;
+        __nv_bfloat16* sb16 = reinterpret_cast<__nv_bfloat16*>(sm + SM::OFF_STG + b * SM::STGB) + i * CW + lane;
 #pragma unroll
         for (int hf = 0; hf < TOK / 16; ++hf) {
           float d[16];
           tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + TOK * b + 16 * hf, d);
 #pragma unroll
-          for (int t = 0; t < 16; ++t) lb[(16 * hf + t) * COLS] += d[t];
+          for (int t = 0; t < 16; ++t) {
+            if constexpr (SM::BF16) sb16[(16 * hf + t) * COLS] = __float2bfloat16_rn(lb[(16 * hf + t) * COLS] + d[t]);
+            else lb[(16 * hf + t) * COLS] += d[t];
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -2416,7 +2479,9 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         fence_proxy_async_smem();
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (leader) {
-          tma_store_2d(&omap, locs + b * (F::LOCB / 4), (int)c0, (int)((blk0 + j) * TOK * 4));
+          tma_store_2d(&omap, SM::BF16 ? static_cast<const void*>(sm + SM::OFF_STG + b * SM::STGB)
+                                       : static_cast<const void*>(locs + b * (F::LOCB / 4)),
+                       (int)c0, (int)((blk0 + j) * TOK * 4));
           bulk_commit();
           // the previous block's buffer may be refilled once its store has read it
           if (j > 0) {
@@ -2799,10 +2864,16 @@ bool launch_grad_x_tma(const float* g, const float* x, const float* w, const flo
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
-template <int N>
-int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float* pq,
+template <typename T> constexpr CUtensorMapDataType tmap_dtype() {
+  return sizeof(T) == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+}
+
+// T = float, or __nv_bfloat16 for bf16 streams (x, out; fp32 arithmetic), which
+// needs the tensor-core projection (n <= 4, C % 64 == 0, 16-byte aligned).
+template <int N, typename T = float>
+int run_fwd_dynamic(const T* x, const float* w, const float* pp, const float* pq,
                     const float* pr, const float* ap, const float* aq, const float* ar,
-                    const float* bp, const float* bq, const float* br, float* out,
+                    const float* bp, const float* bq, const float* br, T* out,
                     float* token_state, int64_t B, int64_t C, int iters, float s_eps,
                     float r_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
   const bool need_rec = token_state == nullptr;
@@ -2821,29 +2892,37 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
   int ks = p.ks;
   if constexpr (N <= 4) {
     // tcgen05 projection: phi split once into tf32 hi/lo rows, x streamed by TMA.
-    using PU = PumCfg<N>;
+    using PU = PumCfg<N, T>;
     const int64_t nC = (int64_t)N * C;
     float* ph = phiT;
     float* pl = phiT + (size_t)PU::NB * nC;
     CUtensorMap xmap, hmap, lmap;
     const uint64_t cs = (uint64_t)C * 4, rs = (uint64_t)nC * 4;
-    if (p.uks > 0 && B > 0 && aligned16(x) && aligned16(ph) && aligned16(pl) &&
-        make_tmap_3d_f32(&xmap, x, C, N, B, cs, rs, PU::CH, 1, PU::TOK, CU_TENSOR_MAP_SWIZZLE_128B) &&
-        make_tmap_3d_f32(&hmap, ph, C, N, PU::NB, cs, rs, PU::CH, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B) &&
-        make_tmap_3d_f32(&lmap, pl, C, N, PU::NB, cs, rs, PU::CH, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B)) {
+    const uint64_t xcs = (uint64_t)C * sizeof(T), xrs = (uint64_t)nC * sizeof(T);
+    // channels per split: a multiple of the stage width
+    const int ucps = (p.ucps + PU::CH - 1) / PU::CH * PU::CH;
+    const int uks = p.ucps > 0 ? (int)((C + ucps - 1) / ucps) : 0;
+    if (p.uks > 0 && B > 0 && C % PU::CH == 0 && aligned16(x) && aligned16(ph) && aligned16(pl) &&
+        make_tmap_3d(&xmap, tmap_dtype<T>(), x, C, N, B, xcs, xrs, PU::CH, 1, PU::TOK, CU_TENSOR_MAP_SWIZZLE_128B) &&
+        make_tmap_3d_f32(&hmap, ph, C, N, PU::NB, cs, rs, 32, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B) &&
+        make_tmap_3d_f32(&lmap, pl, C, N, PU::NB, cs, rs, 32, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B)) {
       {
         const bool pvec = nC % 4 == 0 && aligned16(pp) && aligned16(pq) && aligned16(pr);
         ProfScope _ps("phi_split", s);
         phi_split_kernel<N><<<dim3(grid_1d(pvec ? nC / 4 : nC, 256, 64), PU::NB), 256, 0, s>>>(pp, pq, pr, ph, pl, C, pvec);
       }
-      cudaFuncSetAttribute(proj_umma_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PU::SMEM);
-      { ProfScope _ps("proj_stats", s); proj_umma_kernel<N><<<dim3((unsigned)p.utiles, (unsigned)p.uks), PU::THREADS, PU::SMEM, s>>>(
-          xmap, hmap, lmap, ppart, gpart, B, C, p.ucps); }
-      ks = p.uks;
+      cudaFuncSetAttribute(proj_umma_kernel<N, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PU::SMEM);
+      { ProfScope _ps("proj_stats", s); proj_umma_kernel<N, T><<<dim3((unsigned)p.utiles, (unsigned)uks), PU::THREADS, PU::SMEM, s>>>(
+          xmap, hmap, lmap, ppart, gpart, B, C, ucps); }
+      ks = uks;
       done = true;
     }
   }
-  if constexpr (N <= 4) if (!done) {
+  if constexpr (sizeof(T) == 2) {
+    MHC_REQUIRE(done, MHC_ERR_UNSUPPORTED,
+                "mhc_layer_fwd_dynamic_bf16: needs n <= 4, hidden %% 64 == 0 and 16-byte aligned x");
+  }
+  if constexpr (N <= 4 && sizeof(T) == 4) if (!done) {
     // TMA-pipelined projection when the layout allows it.
     using PT = PjtCfg<N>;
     CUtensorMap xmap, pmap;
@@ -2858,7 +2937,7 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
       done = true;
     }
   }
-  if (!done) {
+  if constexpr (sizeof(T) == 4) if (!done) {
     using P = ProjCfg<N>;
     const size_t smem = (size_t)P::SMEM_FLOATS * sizeof(float);
     // Opt in to > 48 KB of dynamic shared memory (cheap, idempotent, per device).
@@ -2877,9 +2956,11 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
   // the fp64 Gram matrix is only needed when the record is kept for a backward
   if (vec && !need_rec)
-    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, true, true><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
+    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, true, true, T><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
   else if (vec)
-    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, true, false><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
+    { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, true, false, T><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
+  else if constexpr (sizeof(T) == 2)
+    return fail(MHC_ERR_ALIGNMENT, "mhc_layer_fwd_dynamic_bf16: out and weight must be 16-byte aligned");
   else if (!need_rec)
     { ProfScope _ps("stream_fwd", s); stream_fwd_kernel<N, false, true><<<grid, 256, 0, s>>>(x, w, rec, L<N>::REC, nullptr, out, B, C, rec); }
   else
@@ -2887,11 +2968,13 @@ int run_fwd_dynamic(const float* x, const float* w, const float* pp, const float
   return check_launch("mhc_layer_fwd_dynamic/stream_fwd");
 }
 
-template <int N>
-int run_bwd_dynamic(const float* g, const float* x, const float* w, const float* pp,
+// T = float, or __nv_bfloat16 for bf16 streams (grad_out, x, grad_x; fp32
+// arithmetic), which needs the tensor-core grad_x (n = 4, C % 32 == 0, aligned).
+template <int N, typename T = float>
+int run_bwd_dynamic(const T* g, const T* x, const float* w, const float* pp,
                     const float* pq, const float* pr, const float* ap, const float* aq,
                     const float* ar, const float* bp, const float* bq, const float* br,
-                    const float* rec, float* gx, float* gw, float* gpp, float* gpq, float* gpr,
+                    const float* rec, T* gx, float* gw, float* gpp, float* gpq, float* gpr,
                     float* gap, float* gaq, float* gar, float* gbp, float* gbq, float* gbr,
                     int64_t B, int64_t C, int iters, float s_eps, float r_eps, void* ws,
                     size_t ws_bytes, cudaStream_t s) {
@@ -2910,8 +2993,13 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   float* img = cv.take(p.img);
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(w);
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
-  if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
-  else { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  if constexpr (sizeof(T) == 2) {
+    MHC_REQUIRE(N == 4 && vec && C % Gx6Cfg::CW == 0 && p.nsplit6 > 0 && aligned16(gx),
+                MHC_ERR_UNSUPPORTED,
+                "mhc_layer_bwd_dynamic_bf16: needs n == 4, hidden %% 32 == 0 and 16-byte aligned tensors");
+  }
+  if (vec) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, true, false, T><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
+  else if constexpr (sizeof(T) == 4) { ProfScope _ps("bwd_stats", s); bwd_stats_kernel<N, false, false><<<grid, 128, 0, s>>>(g, x, w, stats, B, C); }
   int rc = check_launch("mhc_layer_bwd_dynamic/bwd_stats");
   if (rc) return rc;
   constexpr int TG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);
@@ -2931,22 +3019,28 @@ int run_bwd_dynamic(const float* g, const float* x, const float* w, const float*
   if constexpr (N == 4) {
     // warp-specialised tensor-core grad_x
     using F6 = Gx6Cfg;
+    using S6 = Gx6S<T>;
+    constexpr CUtensorMapDataType dt = tmap_dtype<T>();
     CUtensorMap gm, xm, om;
     if (use6 &&
-        make_tmap_2d_f32(&gm, g, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW) &&
-        make_tmap_2d_f32(&xm, x, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW) &&
-        make_tmap_2d_f32(&om, gx, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW)) {
-      cudaFuncSetAttribute(grad_x6_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F6::SMEM);
+        make_tmap_2d(&gm, dt, sizeof(T), g, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW) &&
+        make_tmap_2d(&xm, dt, sizeof(T), x, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW) &&
+        make_tmap_2d(&om, dt, sizeof(T), gx, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW)) {
+      cudaFuncSetAttribute(grad_x6_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S6::SMEM);
       const int nt6 = (int)(C / F6::CW);
-      { ProfScope _ps("grad_x", s); grad_x6_kernel<<<(unsigned)(nt6 * p.nsplit6), F6::THREADS, F6::SMEM, s>>>(
+      { ProfScope _ps("grad_x", s); grad_x6_kernel<T><<<(unsigned)(nt6 * p.nsplit6), F6::THREADS, S6::SMEM, s>>>(
           gm, xm, om, img, w, pp, pq, pr, gx, dphi, gwp, B, C, nt6, p.nsplit6, p.nblk6); }
       nsplit = p.nsplit6;
       gx_done = true;
     }
   }
-  if (!gx_done && !launch_grad_x_tma<N, true>(g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p, &nsplit, s))
-    { ProfScope _ps("grad_x", s); grad_x_kernel<N, true><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
-        g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
+  if constexpr (sizeof(T) == 2) {
+    MHC_REQUIRE(gx_done, MHC_ERR_UNSUPPORTED, "mhc_layer_bwd_dynamic_bf16: tensor map creation failed");
+  } else {
+    if (!gx_done && !launch_grad_x_tma<N, true>(g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p, &nsplit, s))
+      { ProfScope _ps("grad_x", s); grad_x_kernel<N, true><<<(unsigned)(p.ntiles * p.nsplit), GX_CW * N, 0, s>>>(
+          g, x, w, pp, pq, pr, tokb, gx, dphi, gwp, B, C, p.ntiles, p.nsplit); }
+  }
   rc = check_launch("mhc_layer_bwd_dynamic/grad_x");
   if (rc) return rc;
   const int64_t nC = (int64_t)N * C;
@@ -3069,6 +3163,29 @@ extern "C" size_t mhc_layer_fwd_dynamic_workspace_bytes(int64_t batch, int32_t n
   }
 }
 
+template <typename T>
+static int fwd_dynamic_entry(const char* what, const T* x, const float* rmsnorm_weight,
+                             const float* phi_pre, const float* phi_post, const float* phi_res,
+                             const float* alpha_pre, const float* alpha_post,
+                             const float* alpha_res, const float* b_pre, const float* b_post,
+                             const float* b_res, T* out, float* token_state, int64_t batch,
+                             int32_t n, int64_t hidden, int32_t sinkhorn_iters,
+                             float sinkhorn_eps, float rmsnorm_eps, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  int rc = check_layer_args(what, batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(rmsnorm_weight); MHC_REQUIRE_PTR(phi_pre);
+  MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res); MHC_REQUIRE_PTR(alpha_pre);
+  MHC_REQUIRE_PTR(alpha_post); MHC_REQUIRE_PTR(alpha_res); MHC_REQUIRE_PTR(b_pre);
+  MHC_REQUIRE_PTR(b_post); MHC_REQUIRE_PTR(b_res); MHC_REQUIRE_PTR(out);
+  if (batch == 0) return MHC_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  MHC_DISPATCH_N(n, (run_fwd_dynamic<NN, T>(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
+                                            alpha_post, alpha_res, b_pre, b_post, b_res, out,
+                                            token_state, batch, hidden, sinkhorn_iters,
+                                            sinkhorn_eps, rmsnorm_eps, workspace, workspace_bytes, s)));
+}
+
 extern "C" int mhc_layer_fwd_dynamic(const float* x, const float* rmsnorm_weight,
                                      const float* phi_pre, const float* phi_post,
                                      const float* phi_res, const float* alpha_pre,
@@ -3078,19 +3195,27 @@ extern "C" int mhc_layer_fwd_dynamic(const float* x, const float* rmsnorm_weight
                                      int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
                                      float rmsnorm_eps, void* workspace, size_t workspace_bytes,
                                      void* stream) {
-  int rc = check_layer_args("mhc_layer_fwd_dynamic", batch, n, hidden, sinkhorn_iters,
-                            sinkhorn_eps, rmsnorm_eps);
-  if (rc) return rc;
-  MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(rmsnorm_weight); MHC_REQUIRE_PTR(phi_pre);
-  MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res); MHC_REQUIRE_PTR(alpha_pre);
-  MHC_REQUIRE_PTR(alpha_post); MHC_REQUIRE_PTR(alpha_res); MHC_REQUIRE_PTR(b_pre);
-  MHC_REQUIRE_PTR(b_post); MHC_REQUIRE_PTR(b_res); MHC_REQUIRE_PTR(out);
-  if (batch == 0) return MHC_OK;
-  cudaStream_t s = (cudaStream_t)stream;
-  MHC_DISPATCH_N(n, (run_fwd_dynamic<NN>(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
-                                         alpha_post, alpha_res, b_pre, b_post, b_res, out,
-                                         token_state, batch, hidden, sinkhorn_iters,
-                                         sinkhorn_eps, rmsnorm_eps, workspace, workspace_bytes, s)));
+  return fwd_dynamic_entry<float>("mhc_layer_fwd_dynamic", x, rmsnorm_weight, phi_pre, phi_post,
+                                  phi_res, alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
+                                  out, token_state, batch, n, hidden, sinkhorn_iters, sinkhorn_eps,
+                                  rmsnorm_eps, workspace, workspace_bytes, stream);
+}
+
+extern "C" int mhc_layer_fwd_dynamic_bf16(const void* x, const float* rmsnorm_weight,
+                                          const float* phi_pre, const float* phi_post,
+                                          const float* phi_res, const float* alpha_pre,
+                                          const float* alpha_post, const float* alpha_res,
+                                          const float* b_pre, const float* b_post,
+                                          const float* b_res, void* out, float* token_state,
+                                          int64_t batch, int32_t n, int64_t hidden,
+                                          int32_t sinkhorn_iters, float sinkhorn_eps,
+                                          float rmsnorm_eps, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  return fwd_dynamic_entry<__nv_bfloat16>(
+      "mhc_layer_fwd_dynamic_bf16", (const __nv_bfloat16*)x, rmsnorm_weight, phi_pre, phi_post,
+      phi_res, alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res, (__nv_bfloat16*)out,
+      token_state, batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace,
+      workspace_bytes, stream);
 }
 
 extern "C" size_t mhc_layer_bwd_dynamic_workspace_bytes(int64_t batch, int32_t n,
@@ -3108,17 +3233,17 @@ extern "C" size_t mhc_layer_bwd_dynamic_workspace_bytes(int64_t batch, int32_t n
   }
 }
 
-extern "C" int mhc_layer_bwd_dynamic(
-    const float* grad_out, const float* x, const float* rmsnorm_weight, const float* phi_pre,
-    const float* phi_post, const float* phi_res, const float* alpha_pre, const float* alpha_post,
-    const float* alpha_res, const float* b_pre, const float* b_post, const float* b_res,
-    const float* token_state, float* grad_x, float* grad_rmsnorm_weight, float* grad_phi_pre,
-    float* grad_phi_post, float* grad_phi_res, float* grad_alpha_pre, float* grad_alpha_post,
-    float* grad_alpha_res, float* grad_b_pre, float* grad_b_post, float* grad_b_res,
-    int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
-    float rmsnorm_eps, void* workspace, size_t workspace_bytes, void* stream) {
-  int rc = check_layer_args("mhc_layer_bwd_dynamic", batch, n, hidden, sinkhorn_iters,
-                            sinkhorn_eps, rmsnorm_eps);
+template <typename T>
+static int bwd_dynamic_entry(
+    const char* what, const T* grad_out, const T* x, const float* rmsnorm_weight,
+    const float* phi_pre, const float* phi_post, const float* phi_res, const float* alpha_pre,
+    const float* alpha_post, const float* alpha_res, const float* b_pre, const float* b_post,
+    const float* b_res, const float* token_state, T* grad_x, float* grad_rmsnorm_weight,
+    float* grad_phi_pre, float* grad_phi_post, float* grad_phi_res, float* grad_alpha_pre,
+    float* grad_alpha_post, float* grad_alpha_res, float* grad_b_pre, float* grad_b_post,
+    float* grad_b_res, int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters,
+    float sinkhorn_eps, float rmsnorm_eps, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_layer_args(what, batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps);
   if (rc) return rc;
   MHC_REQUIRE_PTR(grad_out); MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(rmsnorm_weight);
   MHC_REQUIRE_PTR(phi_pre); MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res);
@@ -3129,15 +3254,50 @@ extern "C" int mhc_layer_bwd_dynamic(
   MHC_REQUIRE_PTR(grad_phi_post); MHC_REQUIRE_PTR(grad_phi_res); MHC_REQUIRE_PTR(grad_alpha_pre);
   MHC_REQUIRE_PTR(grad_alpha_post); MHC_REQUIRE_PTR(grad_alpha_res);
   MHC_REQUIRE_PTR(grad_b_pre); MHC_REQUIRE_PTR(grad_b_post); MHC_REQUIRE_PTR(grad_b_res);
-  MHC_REQUIRE(batch > 0, MHC_ERR_INVALID_ARG, "mhc_layer_bwd_dynamic: batch must be > 0");
+  MHC_REQUIRE(batch > 0, MHC_ERR_INVALID_ARG, "%s: batch must be > 0", what);
   cudaStream_t s = (cudaStream_t)stream;
-  MHC_DISPATCH_N(n, (run_bwd_dynamic<NN>(grad_out, x, rmsnorm_weight, phi_pre, phi_post, phi_res,
-                                         alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
-                                         token_state, grad_x, grad_rmsnorm_weight, grad_phi_pre,
-                                         grad_phi_post, grad_phi_res, grad_alpha_pre,
-                                         grad_alpha_post, grad_alpha_res, grad_b_pre, grad_b_post,
-                                         grad_b_res, batch, hidden, sinkhorn_iters, sinkhorn_eps,
-                                         rmsnorm_eps, workspace, workspace_bytes, s)));
+  MHC_DISPATCH_N(n, (run_bwd_dynamic<NN, T>(grad_out, x, rmsnorm_weight, phi_pre, phi_post, phi_res,
+                                            alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
+                                            token_state, grad_x, grad_rmsnorm_weight, grad_phi_pre,
+                                            grad_phi_post, grad_phi_res, grad_alpha_pre,
+                                            grad_alpha_post, grad_alpha_res, grad_b_pre, grad_b_post,
+                                            grad_b_res, batch, hidden, sinkhorn_iters, sinkhorn_eps,
+                                            rmsnorm_eps, workspace, workspace_bytes, s)));
+}
+
+extern "C" int mhc_layer_bwd_dynamic(
+    const float* grad_out, const float* x, const float* rmsnorm_weight, const float* phi_pre,
+    const float* phi_post, const float* phi_res, const float* alpha_pre, const float* alpha_post,
+    const float* alpha_res, const float* b_pre, const float* b_post, const float* b_res,
+    const float* token_state, float* grad_x, float* grad_rmsnorm_weight, float* grad_phi_pre,
+    float* grad_phi_post, float* grad_phi_res, float* grad_alpha_pre, float* grad_alpha_post,
+    float* grad_alpha_res, float* grad_b_pre, float* grad_b_post, float* grad_b_res,
+    int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
+    float rmsnorm_eps, void* workspace, size_t workspace_bytes, void* stream) {
+  return bwd_dynamic_entry<float>(
+      "mhc_layer_bwd_dynamic", grad_out, x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
+      alpha_post, alpha_res, b_pre, b_post, b_res, token_state, grad_x, grad_rmsnorm_weight,
+      grad_phi_pre, grad_phi_post, grad_phi_res, grad_alpha_pre, grad_alpha_post, grad_alpha_res,
+      grad_b_pre, grad_b_post, grad_b_res, batch, n, hidden, sinkhorn_iters, sinkhorn_eps,
+      rmsnorm_eps, workspace, workspace_bytes, stream);
+}
+
+extern "C" int mhc_layer_bwd_dynamic_bf16(
+    const void* grad_out, const void* x, const float* rmsnorm_weight, const float* phi_pre,
+    const float* phi_post, const float* phi_res, const float* alpha_pre, const float* alpha_post,
+    const float* alpha_res, const float* b_pre, const float* b_post, const float* b_res,
+    const float* token_state, void* grad_x, float* grad_rmsnorm_weight, float* grad_phi_pre,
+    float* grad_phi_post, float* grad_phi_res, float* grad_alpha_pre, float* grad_alpha_post,
+    float* grad_alpha_res, float* grad_b_pre, float* grad_b_post, float* grad_b_res,
+    int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
+    float rmsnorm_eps, void* workspace, size_t workspace_bytes, void* stream) {
+  return bwd_dynamic_entry<__nv_bfloat16>(
+      "mhc_layer_bwd_dynamic_bf16", (const __nv_bfloat16*)grad_out, (const __nv_bfloat16*)x,
+      rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre, alpha_post, alpha_res, b_pre, b_post,
+      b_res, token_state, (__nv_bfloat16*)grad_x, grad_rmsnorm_weight, grad_phi_pre, grad_phi_post,
+      grad_phi_res, grad_alpha_pre, grad_alpha_post, grad_alpha_res, grad_b_pre, grad_b_post,
+      grad_b_res, batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace,
+      workspace_bytes, stream);
 }
 
 extern "C" size_t mhc_layer_static_workspace_bytes(int64_t batch, int32_t n, int64_t hidden) {

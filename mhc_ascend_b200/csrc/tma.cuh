@@ -41,41 +41,55 @@ inline EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-// 2D fp32 tensor map over a row-major matrix rows x cols (row stride in
-// elements, a multiple of 4), box box_rows x box_cols, optional shared-memory
-// swizzle; elements outside the matrix read as zero.  Returns false on failure.
-inline bool make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                             uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols,
-                             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
+// 2D tensor map (element type dt of esize bytes) over a row-major matrix rows x
+// cols (row stride in elements; stride x esize a multiple of 16), box
+// box_rows x box_cols, optional shared-memory swizzle; elements outside the
+// matrix read as zero.  Returns false on failure.
+inline bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base,
+                         uint64_t rows, uint64_t cols, uint64_t row_stride_elems, uint32_t box_rows,
+                         uint32_t box_cols, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {row_stride_elems * sizeof(float)};
+  const cuuint64_t strides[1] = {row_stride_elems * esize};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
+inline bool make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                             uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols,
+                             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
+  return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, row_stride_elems,
+                      box_rows, box_cols, swizzle);
+}
 
-// 3D fp32 tensor map: dims (d0 innermost, d1, d2), byte strides of d1 and d2
+// 3D tensor map: dims (d0 innermost, d1, d2), byte strides of d1 and d2
 // (multiples of 16), box (b0, b1, b2), optional swizzle; out-of-range
 // elements read as zero.  Returns false on failure.
-inline bool make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
-                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
-                             uint32_t b0, uint32_t b1, uint32_t b2,
-                             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
+inline bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0,
+                         uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                         uint32_t b0, uint32_t b1, uint32_t b2,
+                         CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {d0, d1, d2};
   const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
   const cuuint32_t box[3] = {b0, b1, b2};
   const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+inline bool make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                             uint32_t b0, uint32_t b1, uint32_t b2,
+                             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
+  return make_tmap_3d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, d0, d1, d2, stride1_bytes,
+                      stride2_bytes, b0, b1, b2, swizzle);
 }
 
 // ---------------------------------------------------------------------------

@@ -39,9 +39,10 @@ class MHCLayer(nn.Module):
         use_dynamic_h: per-token H (True) or shared learnable H (False)
         alpha_init: initial value of the alpha scales (dynamic H) / scale of the
             H_res initialisation (static H)
-        bf16_io: static-H inference only -- when the input is bf16, read bf16
-            and write bf16 (fp32 arithmetic).  Off by default: like the
-            reference, the layer then returns fp32.
+        bf16_io: when the input is bf16, read bf16 and write bf16 (fp32
+            arithmetic): static-H inference, and dynamic-H training and
+            inference at n <= 4 (n == 4 for training), hidden % 64 == 0.  Off
+            by default: like the reference, the layer then returns fp32.
     """
 
     def __init__(self, hidden_dim: int, expansion_rate: int = 4, num_sinkhorn_iters: int = 20,
@@ -81,9 +82,11 @@ class MHCLayer(nn.Module):
             args = (self.rmsnorm_weight, self.phi_pre, self.phi_post, self.phi_res,
                     self.alpha_pre, self.alpha_post, self.alpha_res, self.b_pre, self.b_post,
                     self.b_res, self.num_sinkhorn_iters, self.sinkhorn_eps, self.rmsnorm_eps)
+            bf16 = self.bf16_io and x.dtype == torch.bfloat16
+            xin = x if bf16 else x.float()
             if (not self.training) and (not torch.is_grad_enabled()):
-                return mhc_layer_fused_dynamic_inference(x.float(), *args)
-            return mhc_layer_fused_dynamic_training(x.float(), *args)
+                return mhc_layer_fused_dynamic_inference(xin, *args, bf16_io=bf16)
+            return mhc_layer_fused_dynamic_training(xin, *args, bf16_io=bf16)
         hp = (self.num_sinkhorn_iters, self.sinkhorn_eps, self.rmsnorm_eps)
         if not torch.is_grad_enabled() or not (x.requires_grad or any(
                 p.requires_grad for p in (self.rmsnorm_weight, self.H_pre, self.H_post,

@@ -398,14 +398,18 @@ def _as_scalar_tensor(a, like):
 
 def mhc_layer_fwd_dynamic(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre, alpha_post,
                           alpha_res, b_pre, b_post, b_res, sinkhorn_iters=20, sinkhorn_eps=1e-8,
-                          rmsnorm_eps=1e-5, save_state=True):
+                          rmsnorm_eps=1e-5, save_state=True, bf16_io=False):
     """One fused dynamic-H forward (reference mhc_ascend.mhc_layer_fwd_dynamic,
-    bindings.cpp:880-952).  Returns (out, token_state or None)."""
+    bindings.cpp:880-952).  Returns (out, token_state or None).  With bf16_io
+    x must be bf16 and out is bf16 (fp32 arithmetic inside; n <= 4 and
+    hidden % 64 == 0)."""
     _require_cuda("mhc_layer_fwd_dynamic", x, rmsnorm_weight, phi_pre, phi_post, phi_res)
     if x.dim() != 3:
         raise RuntimeError("x_expanded must be [B, n, C]")
     B, n, C = x.shape
-    xf = _f32(x)
+    if bf16_io and x.dtype != torch.bfloat16:
+        raise RuntimeError("bf16_io needs a bf16 input")
+    xf = x.contiguous() if bf16_io else _f32(x)
     w = _f32(rmsnorm_weight)
     pp, pq, pr = _f32(phi_pre), _f32(phi_post), _f32(phi_res).reshape(n * n, n * C)
     if pp.shape != (n, n * C) or pq.shape != (n, n * C) or w.shape != (C,):
@@ -416,25 +420,32 @@ def mhc_layer_fwd_dynamic(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_p
     state = torch.empty(B, token_state_stride(n), dtype=torch.float32, device=xf.device) \
         if save_state else None
     ws = _workspace(_lib.mhc_layer_fwd_dynamic_workspace_bytes(B, n, C), xf.device)
+    fn = _lib.mhc_layer_fwd_dynamic_bf16 if bf16_io else _lib.mhc_layer_fwd_dynamic
     with _DevGuard(xf):
-        rc = _lib.mhc_layer_fwd_dynamic(
+        rc = fn(
             xf.data_ptr(), w.data_ptr(), pp.data_ptr(), pq.data_ptr(), pr.data_ptr(),
             ap.data_ptr(), aq.data_ptr(), ar.data_ptr(), bp.data_ptr(), bq.data_ptr(),
             br.data_ptr(), out.data_ptr(), _ptr(state), B, n, C, int(sinkhorn_iters),
             float(sinkhorn_eps), float(rmsnorm_eps), ws.data_ptr(), ws.numel(),
             _stream(xf.device))
-    _C.check(rc, "mhc_layer_fwd_dynamic")
+    _C.check(rc, "mhc_layer_fwd_dynamic_bf16" if bf16_io else "mhc_layer_fwd_dynamic")
     return out, state
 
 
 def mhc_layer_bwd_dynamic(grad_output, x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
                           alpha_post, alpha_res, b_pre, b_post, b_res, token_state,
-                          sinkhorn_iters=20, sinkhorn_eps=1e-8, rmsnorm_eps=1e-5):
+                          sinkhorn_iters=20, sinkhorn_eps=1e-8, rmsnorm_eps=1e-5, bf16_io=False):
     """Fused dynamic-H backward (reference mhc_ascend.mhc_layer_bwd_dynamic,
-    bindings.cpp:600-874).  Returns the 11 gradients in the reference's order."""
+    bindings.cpp:600-874).  Returns the 11 gradients in the reference's order.
+    With bf16_io, grad_output / x are read and grad_x written in bf16 (n == 4,
+    hidden % 32 == 0); the parameter gradients stay fp32."""
     B, n, C = x.shape
-    g = _f32(grad_output)
-    xf = _f32(x)
+    if bf16_io:
+        g = grad_output.to(torch.bfloat16).contiguous()
+        xf = x.contiguous()
+    else:
+        g = _f32(grad_output)
+        xf = _f32(x)
     w = _f32(rmsnorm_weight)
     pp, pq, pr = _f32(phi_pre), _f32(phi_post), _f32(phi_res).reshape(n * n, n * C)
     ap, aq, ar = (_as_scalar_tensor(a, xf) for a in (alpha_pre, alpha_post, alpha_res))
@@ -451,26 +462,29 @@ def mhc_layer_bwd_dynamic(grad_output, x, rmsnorm_weight, phi_pre, phi_post, phi
     gbr = torch.empty(n, n, dtype=torch.float32, device=dev)
     ws = _workspace(_lib.mhc_layer_bwd_dynamic_workspace_bytes(B, n, C), dev)
     a0 = galpha.data_ptr()
+    fn = _lib.mhc_layer_bwd_dynamic_bf16 if bf16_io else _lib.mhc_layer_bwd_dynamic
     with _DevGuard(xf):
-        rc = _lib.mhc_layer_bwd_dynamic(
+        rc = fn(
             g.data_ptr(), xf.data_ptr(), w.data_ptr(), pp.data_ptr(), pq.data_ptr(),
             pr.data_ptr(), ap.data_ptr(), aq.data_ptr(), ar.data_ptr(), bp.data_ptr(),
             bq.data_ptr(), br.data_ptr(), token_state.data_ptr(), gx.data_ptr(), gw.data_ptr(),
             gpp.data_ptr(), gpq.data_ptr(), gpr.data_ptr(), a0, a0 + 4, a0 + 8, gbp.data_ptr(),
             gbq.data_ptr(), gbr.data_ptr(), B, n, C, int(sinkhorn_iters), float(sinkhorn_eps),
             float(rmsnorm_eps), ws.data_ptr(), ws.numel(), _stream(dev))
-    _C.check(rc, "mhc_layer_bwd_dynamic")
+    _C.check(rc, "mhc_layer_bwd_dynamic_bf16" if bf16_io else "mhc_layer_bwd_dynamic")
     return (gx, gw, gpp, gpq, gpr.reshape(phi_res.shape), galpha[0], galpha[1], galpha[2],
             gbp, gbq, gbr)
 
 
 def mhc_layer_fused_dynamic_inference(x_expanded, rmsnorm_weight, phi_pre, phi_post, phi_res,
                                       alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
-                                      sinkhorn_iters=20, sinkhorn_eps=1e-8, rmsnorm_eps=1e-5):
+                                      sinkhorn_iters=20, sinkhorn_eps=1e-8, rmsnorm_eps=1e-5,
+                                      bf16_io=False):
     """Fused dynamic-H forward without autograd (reference ops.py:337-380)."""
     out, _ = mhc_layer_fwd_dynamic(x_expanded, rmsnorm_weight, phi_pre, phi_post, phi_res,
                                    alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
-                                   sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, save_state=False)
+                                   sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, save_state=False,
+                                   bf16_io=bf16_io)
     return out
 
 
@@ -485,21 +499,22 @@ class MHCLayerDynamicFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_expanded, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
                 alpha_post, alpha_res, b_pre, b_post, b_res, sinkhorn_iters, sinkhorn_eps,
-                rmsnorm_eps):
+                rmsnorm_eps, bf16_io=False):
         out, state = mhc_layer_fwd_dynamic(x_expanded, rmsnorm_weight, phi_pre, phi_post,
                                            phi_res, alpha_pre, alpha_post, alpha_res, b_pre,
                                            b_post, b_res, sinkhorn_iters, sinkhorn_eps,
-                                           rmsnorm_eps, save_state=True)
+                                           rmsnorm_eps, save_state=True, bf16_io=bf16_io)
         ctx.save_for_backward(x_expanded, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
                               alpha_post, alpha_res, b_pre, b_post, b_res, state)
         ctx.hp = (sinkhorn_iters, sinkhorn_eps, rmsnorm_eps)
+        ctx.bf16_io = bf16_io
         return out
 
     @staticmethod
     def backward(ctx, grad_output):
         (x, w, pp, pq, pr, ap, aq, ar, bp, bq, br, state) = ctx.saved_tensors
         grads = mhc_layer_bwd_dynamic(grad_output, x, w, pp, pq, pr, ap, aq, ar, bp, bq, br,
-                                      state, *ctx.hp)
+                                      state, *ctx.hp, bf16_io=ctx.bf16_io)
         (gx, gw, gpp, gpq, gpr, gap, gaq, gar, gbp, gbq, gbr) = grads
         gx = gx.to(x.dtype)
         gw = gw.to(w.dtype)
@@ -507,12 +522,13 @@ class MHCLayerDynamicFunction(torch.autograd.Function):
         gaq = gaq.to(aq.dtype).view_as(aq)
         gar = gar.to(ar.dtype).view_as(ar)
         return (gx, gw, gpp.to(pp.dtype), gpq.to(pq.dtype), gpr.to(pr.dtype), gap, gaq, gar,
-                gbp.to(bp.dtype), gbq.to(bq.dtype), gbr.to(br.dtype), None, None, None)
+                gbp.to(bp.dtype), gbq.to(bq.dtype), gbr.to(br.dtype), None, None, None, None)
 
 
 def mhc_layer_fused_dynamic_training(x_expanded, rmsnorm_weight, phi_pre, phi_post, phi_res,
                                      alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
-                                     sinkhorn_iters=20, sinkhorn_eps=1e-8, rmsnorm_eps=1e-5):
+                                     sinkhorn_iters=20, sinkhorn_eps=1e-8, rmsnorm_eps=1e-5,
+                                     bf16_io=False):
     """Dynamic-H layer forward with autograd support (reference ops.py:567-628)."""
     dev = phi_pre.device
     if not torch.is_tensor(alpha_pre):
@@ -523,7 +539,7 @@ def mhc_layer_fused_dynamic_training(x_expanded, rmsnorm_weight, phi_pre, phi_po
         alpha_res = torch.tensor(alpha_res, device=dev, dtype=torch.float32)
     return MHCLayerDynamicFunction.apply(x_expanded, rmsnorm_weight, phi_pre, phi_post, phi_res,
                                          alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
-                                         sinkhorn_iters, sinkhorn_eps, rmsnorm_eps)
+                                         sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, bf16_io)
 
 
 # =============================================================================

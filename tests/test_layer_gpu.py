@@ -191,6 +191,34 @@ def test_static_bf16_io(cuda):
     close(out.float(), ro, rtol=8e-3, atol=1e-2, what="bf16 out")
 
 
+@pytest.mark.parametrize("B,C", [(256, 4096), (37, 1024)])
+def test_dynamic_bf16_io(cuda, B, C):
+    """bf16 streams (x, out, grad_out, grad_x) with fp32 arithmetic, against the
+    oracle in fp64 on the same bf16-rounded x and grad_out.  out and grad_x
+    carry one bf16 rounding of the result (relative 2^-9): rtol 8e-3 / atol
+    1e-2 at the tensor's scale.  The parameter gradients are fp32 and keep the
+    fp32 tolerances."""
+    n = 4
+    x, params, grad = oracle_case(B, n, C, seed=B + C, alpha=0.5, bias_std=0.5, weight="rand")
+    xb, gb = x.bfloat16(), grad.bfloat16()
+    ro, rg = O.dynamic_fwd_bwd(xb.double(), {k: v.double() for k, v in params.items()},
+                               gb.double())
+    layer = make_layer(params, n, C, cuda)
+    layer.bf16_io = True
+    xd = xb.to(cuda).requires_grad_(True)
+    out = layer(xd)
+    assert out.dtype == torch.bfloat16
+    out.backward(gb.to(cuda))
+    assert xd.grad.dtype == torch.bfloat16
+    close(out.float(), ro, rtol=8e-3, atol=1e-2, what="bf16 out")
+    close(xd.grad.float(), rg["x"], rtol=8e-3, atol=1e-2, what="bf16 grad_x")
+    for k in KEYS:
+        close(getattr(layer, k).grad, rg[k], what="grad_" + k)
+    layer.eval()
+    with torch.no_grad():
+        assert torch.equal(layer(xb.to(cuda)), out.detach())
+
+
 def test_residual_wrapper(cuda):
     B, T, C, n = 2, 5, 64, 4
     gen = torch.Generator().manual_seed(3)
