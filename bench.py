@@ -37,6 +37,7 @@ sys.path.insert(0, ROOT)
 CONFIGS = {
     # name: (tokens per GPU, n, C, mode)
     "cfg3": (8192, 4, 4096, "dynamic"),
+    "cfg3_bf16": (8192, 4, 4096, "dynamic_bf16"),
     "cfg5": (32768, 4, 7168, "dynamic"),
     "cfg4": (65536, 4, 4096, "static_fwd"),
     "cfg4_bf16": (65536, 4, 4096, "static_fwd_bf16"),
@@ -61,6 +62,8 @@ def algorithmic_bytes(mode, B, n, C):
     P = nC * (n * n + 2 * n)
     if mode == "dynamic":
         return B * 5 * nC * s + 12 * P + 8 * C
+    if mode == "dynamic_bf16":
+        return B * 5 * nC * 2 + 12 * P + 8 * C
     if mode == "static_fwd":
         return B * 2 * nC * 4
     if mode == "static_fwd_bf16":
@@ -183,7 +186,7 @@ def time_cpu_oracle(n, C, mode, sample_tokens, seconds, min_reps=2):
     grad = torch.randn(sample_tokens, n, C, generator=gen)
 
     def step():
-        if mode == "dynamic":
+        if mode.startswith("dynamic"):
             O.dynamic_fwd_bwd(x, params, grad)
         else:
             with torch.no_grad():
@@ -226,7 +229,7 @@ def run_reference(args, world, rank):
     x, grad = make(sample)
 
     def calib():
-        if mode == "dynamic":
+        if mode.startswith("dynamic"):
             O.dynamic_fwd_bwd(x, params, grad)
         else:
             with torch.no_grad():
@@ -241,7 +244,7 @@ def run_reference(args, world, rank):
     x, grad = make(sample)
 
     def step():
-        if mode == "dynamic":
+        if mode.startswith("dynamic"):
             O.dynamic_fwd_bwd(x, params, grad)
         else:
             with torch.no_grad():
@@ -255,7 +258,7 @@ def run_reference(args, world, rank):
     dt = (time.perf_counter() - t0) / args.steps
     value = sample / dt
     line = {
-        "metric": "mHC layer fwd+bwd tokens/s (n=4, C=4096)" if mode == "dynamic"
+        "metric": "mHC layer fwd+bwd tokens/s (n=4, C=4096)" if mode.startswith("dynamic")
         else "mHC static-H layer forward tokens/s",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
@@ -288,10 +291,12 @@ def run_mine(args, world, rank, local):
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     x = torch.randn(tokens, n, C, device=dev, generator=gen)
     g = torch.randn(tokens, n, C, device=dev, generator=gen)
-    dynamic = mode == "dynamic"
+    dynamic = mode.startswith("dynamic")
     layer = mhc.MHCLayer(hidden_dim=C, expansion_rate=n, use_dynamic_h=dynamic,
-                         bf16_io=(mode == "static_fwd_bf16")).to(dev)
+                         bf16_io=mode.endswith("bf16")).to(dev)
     bucket = GradBucket(layer.parameters())
+    if mode == "dynamic_bf16":
+        x, g = x.bfloat16(), g.bfloat16()
     if mode == "static_fwd_bf16":
         x = x.bfloat16()
         layer.eval()
@@ -443,7 +448,7 @@ def run_mine(args, world, rank, local):
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16" if mode == "static_fwd_bf16" else "f32", "data": "synthetic",
+            "dtype": "bf16" if mode.endswith("bf16") else "f32", "data": "synthetic",
             "impl": "mine",
             "config": {"workload": f"{args.config}: {mode}, n={n}, C={C}, {tokens} tokens per GPU "
                                    f"per step" + (", NCCL grad all-reduce" if world > 1 else ""),
