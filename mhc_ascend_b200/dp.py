@@ -58,10 +58,27 @@ class GradBucket:
                 p.grad.copy_(src)
             off += k
 
+    def _shared_flat(self) -> Optional[torch.Tensor]:
+        """The gradients as one contiguous range of a single buffer, in
+        parameter order (the fused backward writes them that way), or None."""
+        grads = [p.grad for p in self.params]
+        if any(g is None or not g.is_contiguous() or g.dtype != self.dtype for g in grads):
+            return None
+        base = grads[0]
+        ptr = base.data_ptr()
+        esize = base.element_size()
+        for g in grads:
+            if g.untyped_storage().data_ptr() != base.untyped_storage().data_ptr() or \
+                    g.data_ptr() != ptr:
+                return None
+            ptr += g.numel() * esize
+        return torch.as_strided(base, (self.numel,), (1,), base.storage_offset())
+
     def allreduce(self, group=None, async_op: bool = False):
         """Sum (or average) the gradients of all ranks in place."""
-        flat = self.pack()
         world = dist.get_world_size(group)
+        shared = self._shared_flat() if world > 1 else None
+        flat = shared if shared is not None else self.pack()
         if world == 1:
             return None
         work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
@@ -71,7 +88,8 @@ class GradBucket:
                 work.wait()
             if self.average:
                 flat.div_(world)
-            self.unpack(flat)
+            if shared is None:
+                self.unpack(flat)
 
         if async_op:
             return finish

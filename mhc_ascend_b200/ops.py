@@ -452,14 +452,17 @@ def mhc_layer_bwd_dynamic(grad_output, x, rmsnorm_weight, phi_pre, phi_post, phi
     bp, bq, br = _f32(b_pre), _f32(b_post), _f32(b_res)
     dev = xf.device
     gx = torch.empty_like(xf)
-    gw = torch.empty(C, dtype=torch.float32, device=dev)
-    gpp = torch.empty(n, n * C, dtype=torch.float32, device=dev)
-    gpq = torch.empty(n, n * C, dtype=torch.float32, device=dev)
-    gpr = torch.empty(n * n, n * C, dtype=torch.float32, device=dev)
-    galpha = torch.empty(3, dtype=torch.float32, device=dev)
-    gbp = torch.empty(n, dtype=torch.float32, device=dev)
-    gbq = torch.empty(n, dtype=torch.float32, device=dev)
-    gbr = torch.empty(n, n, dtype=torch.float32, device=dev)
+    # all parameter gradients live in one flat fp32 buffer, in the order of
+    # MHCLayer.parameters() (weight, phi_pre/post/res, b_pre/post/res,
+    # alpha_pre/post/res): data-parallel training all-reduces it as it is
+    nC = n * C
+    sizes = [C, n * nC, n * nC, n * n * nC, n, n, n * n, 3]
+    flat = torch.empty(sum(sizes), dtype=torch.float32, device=dev)
+    parts = list(torch.split(flat, sizes))
+    gw = parts[0]
+    gpp, gpq, gpr = parts[1].view(n, nC), parts[2].view(n, nC), parts[3].view(n * n, nC)
+    gbp, gbq, gbr = parts[4], parts[5], parts[6].view(n, n)
+    galpha = parts[7]
     ws = _workspace(_lib.mhc_layer_bwd_dynamic_workspace_bytes(B, n, C), dev)
     a0 = galpha.data_ptr()
     fn = _lib.mhc_layer_bwd_dynamic_bf16 if bf16_io else _lib.mhc_layer_bwd_dynamic

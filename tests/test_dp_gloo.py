@@ -74,6 +74,43 @@ def test_bucket_allreduce_equals_full_batch(average):
             torch.testing.assert_close(results[r][k], expect, rtol=1e-10, atol=1e-12)
 
 
+def _shared_worker(rank, world, port, q):
+    """Gradients already laid out as consecutive views of one buffer (what the
+    fused backward produces) are all-reduced in place, without pack/unpack."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        params = [torch.nn.Parameter(torch.zeros(s)) for s in ((5,), (2, 3), (4,))]
+        flat = torch.arange(15, dtype=torch.float32) + 100 * rank
+        for p, g in zip(params, torch.split(flat, [5, 6, 4])):
+            p.grad = g.view_as(p)
+        bucket = GradBucket(params, average=True)
+        shared = bucket._shared_flat()
+        assert shared is not None and shared.data_ptr() == flat.data_ptr()
+        bucket.allreduce()
+        q.put((rank, flat.clone(), all(p.grad.data_ptr() >= flat.data_ptr() for p in params)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bucket_allreduces_shared_gradient_buffer_in_place():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shared_worker, args=(r, world, port, q)) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for pr in procs:
+        pr.join(timeout=60)
+    expect = torch.arange(15, dtype=torch.float32) + 50.0   # mean of rank 0 and rank 1 values
+    for _, flat, views in res:
+        assert torch.equal(flat, expect)
+        assert views
+
+
 def _dying_worker(rank, world, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
