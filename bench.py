@@ -376,32 +376,54 @@ def run_mine(args, world, rank, local):
     step_gbs = step_bytes / (ms * 1e-3) / 1e9
 
     # End to end through the public API with host buffers: pinned x -> device,
-    # fwd + loss + bwd, loss -> host, every step.
+    # fwd + loss + bwd, loss -> host, every step.  The next step's input is
+    # copied on a side stream while the current step computes (two device
+    # buffers), as a training loop would; every step's copy lies inside the
+    # timed region.
     e2e = None
     if dynamic and not args.no_e2e:
         xh = x.cpu().pin_memory()
         e2e_steps = max(3, min(args.steps // 20, 30))
+        xds = [torch.empty_like(x), torch.empty_like(x)]
+        cs = torch.cuda.Stream(dev)
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        used = [torch.cuda.Event(), torch.cuda.Event()]
+        for ev in used:
+            ev.record(stream)
 
-        def e2e_step():
-            xd = xh.to(dev, non_blocking=True)
-            out = layer(xd)
+        def issue_copy(k):
+            b = k % 2
+            with torch.cuda.stream(cs):
+                cs.wait_event(used[b])           # the buffer's previous step is done with it
+                xds[b].copy_(xh, non_blocking=True)
+                copied[b].record(cs)
+
+        def e2e_step(k):
+            b = k % 2
+            issue_copy(k + 1)
+            stream.wait_event(copied[b])
+            out = layer(xds[b])
             loss = (out * out).sum()
             loss.backward()
             if world > 1:
                 bucket.allreduce()
             for p in layer.parameters():
                 p.grad = None
+            used[b].record(stream)
             return loss.item()
 
-        for _ in range(2):
-            e2e_step()
+        issue_copy(0)
+        for k in range(2):
+            e2e_step(k)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
+        cs.wait_event(e0)
+        issue_copy(0)
+        for k in range(e2e_steps):
+            e2e_step(k)
         e1.record(stream)
         torch.cuda.synchronize()
         ems = e0.elapsed_time(e1) / e2e_steps
@@ -412,7 +434,8 @@ def run_mine(args, world, rank, local):
         e2e = {"value": tokens * world / (ems * 1e-3), "unit": "tokens/s",
                "h2d_bytes_per_step": xh.numel() * xh.element_size(), "d2h_bytes_per_step": 4,
                "ms_per_step": ems,
-               "note": "MHCLayer(x) with x copied from pinned host memory each step, "
+               "note": "MHCLayer(x) with x copied from pinned host memory each step "
+                       "(next step's copy overlapping this step's compute), "
                        "loss=sum(out^2), backward, loss.item()"}
     elif not dynamic and not args.no_e2e:
         xh = x.cpu().pin_memory()

@@ -179,8 +179,8 @@ MHC_API int mhc_layer_fwd_dynamic_bf16(const void* x, const float* rmsnorm_weigh
  * cudaFree because they can synchronise the device): the scratch comes from
  * a 16 MiB array in the library's device image, which every GPU that loads
  * the library holds until the process exits.  Requests needing more than
- * 16 MiB (mhc_layer_fwd_dynamic_workspace_bytes > 16 MiB, e.g. more than
- * ~30k tokens at n=4, C=4096) return MHC_ERR_UNSUPPORTED.  The first call on a
+ * 16 MiB (e.g. more than ~18k tokens at n=4, C=4096 with a token_state, ~10k
+ * without) return MHC_ERR_UNSUPPORTED.  The first call on a
  * device looks up the array's device address (make it before any stream
  * capture).  All calls on a device share the array: calls whose kernels may
  * overlap on the GPU race and must be serialised by the caller. */

@@ -2745,7 +2745,11 @@ FwdPlan plan_fwd(int64_t B, int64_t C) {
     const int ks = choose_proj_splits(p.utiles, C, 2 * num_sms());
     p.ucps = (int)(((C + ks - 1) / ks + 31) / 32 * 32);
     p.uks = (int)((C + p.ucps - 1) / p.ucps);
-    if (p.uks > mks) mks = p.uks;
+    // the fallback projections (misaligned x) reuse this split plan, so the
+    // partial buffers are sized for the plan that actually runs
+    p.ks = p.uks;
+    p.cps = p.ucps;
+    mks = p.uks;
     uphi = (size_t)2 * PumCfg<(N <= 4 ? N : 4)>::NB * N * C;
   }
   p.ppart = (size_t)mks * B * L<N>::NHP;

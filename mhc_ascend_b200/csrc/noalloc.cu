@@ -26,8 +26,9 @@
 namespace {
 
 // Fixed scratch capacity: 16 MiB per device that loads the library, held
-// until the process exits.  Covers the dynamic forward up to ~30k tokens at
-// n = 4, C = 4096 (8192 tokens need ~6.2 MiB).
+// until the process exits.  Covers the dynamic forward up to ~18k tokens at
+// n = 4, C = 4096 when the caller keeps the token state (~10k when the
+// record is scratch too; 8192 tokens need ~6 MiB).
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
