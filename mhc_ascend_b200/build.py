@@ -43,8 +43,8 @@ def sources():
 
 
 def _deps():
-    return sources() + [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh")] + [
-        os.path.join(ROOT, "include", "mhc_b200.h")]
+    headers = [os.path.join(d, f) for d, _, fs in os.walk(CSRC) for f in fs if f.endswith(".cuh")]
+    return sources() + headers + [os.path.join(ROOT, "include", "mhc_b200.h")]
 
 
 def up_to_date():

@@ -1,0 +1,787 @@
+// tcgen05 kernels: helpers (shared-memory descriptors, tensor-memory loads and
+// stores, MMA issue), the warp-specialised projection and grad_x.
+// Part of the fused layer translation unit (included by layer.cu, in order).
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "../common.cuh"
+#include "../sinkhorn.cuh"
+#include "../sinkhorn_lanes.cuh"
+#include "../tma.cuh"
+
+namespace mhc {
+namespace {
+
+// ---------------------------------------------------------------------------
+// tcgen05 (UMMA) helpers: kind::tf32, operands in shared memory in the
+// K-major "interleaved" (no swizzle) layout -- 8 rows x 16 bytes core
+// matrices -- accumulators in tensor memory.
+// ---------------------------------------------------------------------------
+// byte offset of element (row r, k) in an R-row K-major operand
+__host__ __device__ __forceinline__ uint32_t umma_kmaj_off(int r, int k, int R) {
+  return (uint32_t)((k >> 2) * (R >> 3) * 128 + (r >> 3) * 128 + (r & 7) * 16 + (k & 3) * 4);
+}
+// smem matrix descriptor: start address, leading (K-chunk) and stride (8-row
+// group) byte offsets, sm100 descriptor version, no swizzle
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
+}
+// descriptor of K-step s (k in [8s, 8s+8)) of an R-row operand, rows from rb
+__device__ __forceinline__ uint64_t umma_desc_k(uint32_t base, int R, int s, int rb) {
+  return umma_desc(base + (uint32_t)(2 * s * (R >> 3) * 128 + (rb >> 3) * 128), (uint32_t)((R >> 3) * 128), 128);
+}
+// instruction descriptor: D f32, A/B tf32, both K-major, M x N
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// 32 lanes x 16 columns of fp32 from tensor memory (this warp's lane quadrant)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// 32 lanes x 16 columns of 32-bit values into tensor memory (this warp's lane quadrant)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// D (tmem) (+)= A (tmem, M lanes x 8 columns) . B (smem descriptor)^T, kind::tf32
+__device__ __forceinline__ void umma_tf32_at(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Forward 1 on tcgen05: projection p = x_flat . phi^T and the per-token Gram
+// matrix of the n streams, for n <= 4 (C % 4 == 0, x 16-byte aligned).
+//   CTA = 128 tokens (one M=128 MMA tile) x one split of the channels, two
+//   CTAs per SM, warp-specialised: warp 0 issues TMA, warp 1 issues MMAs,
+//   warps 2..9 (two threads per token, one per half of a 128-byte row)
+//   prepare the A operand.  A stage is one stream x 32 channels: x[128 tokens
+//   x 32] and phi_hi / phi_lo[NB rows x 32] (phi split once per call), both
+//   128-byte-swizzled as TMA writes them.  The operand threads read their
+//   token's row, keep the values of the n streams of a channel block in
+//   registers for the Gram entries, and store the row split into tf32 hi/lo
+//   into tensor memory with tcgen05.st (lane = token, column = channel: the
+//   A operand, no proxy fence); the MMA warp adds x_lo.phi_hi + x_hi.phi_lo +
+//   x_hi.phi_hi (3xTF32) into the accumulator in tensor memory.  Barriers:
+//   full (TMA bytes), empty (operand warps done with x + MMA done with phi),
+//   aready / afree per tensor-memory A buffer.
+// ---------------------------------------------------------------------------
+template <int N, typename T = float>
+struct PumCfg {
+  static constexpr int NH = L<N>::NH, NHP = L<N>::NHP, NG = L<N>::NG;
+  static constexpr int NB = (NH + 15) / 16 * 16;           // MMA N (padded phi rows)
+  // a stage is one 128-byte row of x per token: 32 fp32 or 64 bf16 channels
+  static constexpr int TOK = 128, CH = 128 / (int)sizeof(T), THREADS = 320;
+  static constexpr int PSUB = CH / 32;                     // 32-channel phi sub-tiles per stage
+  static constexpr bool BF16 = sizeof(T) == 2;             // bf16 x is exact in tf32: no lo part
+  static constexpr uint32_t XB = TOK * 128;                // x tile of one stage
+  static constexpr uint32_t PB = NB * CH * 4;              // phi tile (fp32) of one stage
+  static constexpr uint32_t SLOT = XB + 2 * PB;            // x, phi_hi, phi_lo
+  static constexpr uint32_t OFF_PH = XB, OFF_PL = XB + PB;
+  static constexpr uint32_t TX = SLOT;                     // bytes TMA brings per stage
+  static constexpr int STAGES = BF16 ? 3 : 4, NA = 2;      // smem stages, tensor-memory A buffers
+  static constexpr uint32_t TCOLS = 256;                   // D [0, 32); A[a] = [64 + 64 a, +64): fp32 hi|lo, bf16 hi
+  static constexpr uint32_t ACOL = 64;
+  static constexpr uint32_t OFF_GX = STAGES * SLOT;        // Gram exchange [128][NG]
+  static constexpr uint32_t OFF_BAR = OFF_GX + TOK * NG * 4;
+  static constexpr size_t SMEM = OFF_BAR + (2 * STAGES + 2 * NA + 1) * 8 + 16 + 1024;
+  static_assert(NB <= 32, "one 32-column accumulator");
+  static_assert(XB % 1024 == 0 && PB % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+};
+
+// phi_hi / phi_lo [NB rows x nC]: rows k < NH hold phi_k split into tf32 hi +
+// tf32 lo, the padding rows are zero.
+template <int N>
+__global__ void __launch_bounds__(256)
+    phi_split_kernel(const float* __restrict__ pp, const float* __restrict__ pq,
+                     const float* __restrict__ pr, float* __restrict__ ph,
+                     float* __restrict__ pl, int64_t C, bool vec) {
+  // blockIdx.y = row k; float4 columns when every row start is 16-byte aligned
+  using P = PumCfg<N>;
+  const int64_t nC = (int64_t)N * C;
+  const int k = blockIdx.y;
+  const float* src = k < P::NH ? phi_row(pp, pq, pr, k, N, nC) : nullptr;
+  float* dh = ph + (int64_t)k * nC;
+  float* dl = pl + (int64_t)k * nC;
+  if (vec) {
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nC / 4;
+         q += (int64_t)gridDim.x * blockDim.x) {
+      const float4 v = src ? __ldg(reinterpret_cast<const float4*>(src) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      uint4 hi, lo;
+      split_tf32(v.x, hi.x, lo.x); split_tf32(v.y, hi.y, lo.y);
+      split_tf32(v.z, hi.z, lo.z); split_tf32(v.w, hi.w, lo.w);
+      reinterpret_cast<uint4*>(dh)[q] = hi;
+      reinterpret_cast<uint4*>(dl)[q] = lo;
+    }
+  } else {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nC;
+         e += (int64_t)gridDim.x * blockDim.x) {
+      uint32_t hi, lo;
+      split_tf32(src ? src[e] : 0.f, hi, lo);
+      dh[e] = __uint_as_float(hi);
+      dl[e] = __uint_as_float(lo);
+    }
+  }
+}
+
+// smem descriptor of a K-major, 128-byte-swizzled operand (8-row groups
+// 1024 B apart); the start may advance by 32 B per K-step inside the atom
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Bounded mbarrier wait that also gives up once another role of the CTA has
+// raised the abort word.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity,
+                                                   const volatile int* abort_word) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 255) == 255 && *abort_word) return false;
+  }
+  atomicExch(&g_mhc_device_error, 1);
+  return false;
+}
+
+template <int N, typename T = float>
+__global__ void __launch_bounds__(320, 2)
+    proj_umma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap hmap,
+                     const __grid_constant__ CUtensorMap lmap, float* __restrict__ ppart,
+                     float* __restrict__ gpart, int64_t B, int64_t C, int cps) {
+  using P = PumCfg<N, T>;
+  constexpr int NG = P::NG, NHP = P::NHP, S = P::STAGES, NA = P::NA;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* gx_s = reinterpret_cast<float*>(sm + P::OFF_GX);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + P::OFF_BAR);
+  uint64_t* empty = full + S;
+  uint64_t* aready = empty + S;
+  uint64_t* afree = aready + NA;
+  uint64_t* done = afree + NA;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t sbase = smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t t0 = (int64_t)blockIdx.x * P::TOK;
+  const int split = blockIdx.y;
+  const int64_t c_begin = (int64_t)split * cps;
+  const int64_t c_end = c_begin + cps < C ? c_begin + cps : C;
+  const int nblocks = c_begin < c_end ? (int)((c_end - c_begin + P::CH - 1) / P::CH) : 0;
+  const int nchunks = nblocks * N;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(P::TCOLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 32) {
+    prefetch_tmap(&xmap);
+    prefetch_tmap(&hmap);
+    prefetch_tmap(&lmap);
+    for (int st = 0; st < S; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1 + 8);
+    }
+    for (int a = 0; a < NA; ++a) {
+      mbar_init(&aready[a], 8);
+      mbar_init(&afree[a], 1);
+    }
+    mbar_init(done, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int k = 0; k < nchunks; ++k) {
+        const int slot = k % S;
+        if (k >= S && !mbar_wait_or_abort(&empty[slot], (uint32_t)(((k / S) - 1) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        issued = k + 1;
+        unsigned char* base = sm + slot * P::SLOT;
+        const int c = (int)(c_begin + (int64_t)(k / N) * P::CH);
+        const int i = k % N;
+        mbar_expect_tx(&full[slot], P::TX);
+        tma_load_3d(base, &xmap, c, i, (int)t0, &full[slot]);
+#pragma unroll
+        for (int ps = 0; ps < P::PSUB; ++ps) {
+          tma_load_3d(base + P::OFF_PH + ps * P::NB * 128, &hmap, c + 32 * ps, i, 0, &full[slot]);
+          tma_load_3d(base + P::OFF_PL + ps * P::NB * 128, &lmap, c + 32 * ps, i, 0, &full[slot]);
+        }
+      }
+      // no copy may still be landing when the CTA exits (bounded)
+      for (int q = issued > S ? issued - S : 0; q < issued; ++q)
+        mbar_wait(&full[q % S], (uint32_t)((q / S) & 1));
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t ID = umma_idesc_tf32(128, P::NB);
+      for (int k = 0; k < nchunks; ++k) {
+        const int slot = k % S, a = k % NA;
+        if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word) ||
+            !mbar_wait_or_abort(&aready[a], (uint32_t)((k / NA) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sb = sbase + slot * P::SLOT;
+        const uint32_t at = tmem + P::ACOL + 64 * a;
+#pragma unroll
+        for (int st = 0; st < P::CH / 8; ++st) {
+          const uint32_t boff = (st / 4) * P::NB * 128 + 32 * (st % 4);
+          const uint64_t bh = umma_desc_sw128(sb + P::OFF_PH + boff);
+          const uint64_t bl = umma_desc_sw128(sb + P::OFF_PL + boff);
+          if constexpr (P::BF16) {
+            umma_tf32_at(tmem, at + 8 * st, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
+            umma_tf32_at(tmem, at + 8 * st, bl, ID, 1u);
+          } else {
+            umma_tf32_at(tmem, at + 32 + 8 * st, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
+            umma_tf32_at(tmem, at + 8 * st, bl, ID, 1u);
+            umma_tf32_at(tmem, at + 8 * st, bh, ID, 1u);
+          }
+        }
+        umma_commit(&empty[slot]);
+        umma_commit(&afree[a]);
+      }
+      umma_commit(done);
+    }
+  } else {
+    // ---------------- A operand (tensor memory) + Gram ----------------
+    const int cw = warp - 2;               // 0..7
+    const int h = cw >> 2;                 // half of the 128-byte row
+    const int qd = warp & 3;               // tensor-memory lane quadrant
+    const int r = 32 * qd + lane;          // token row = tensor-memory lane
+    const uint32_t rowoff = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    uint32_t choff[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) choff[j] = rowoff + (uint32_t)((((4 * h + j) ^ (r & 7))) * 16);
+    float gacc[NG];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) gacc[g] = 0.f;
+    bool ok = true;
+    for (int b = 0; b < nblocks && ok; ++b) {
+      // this thread's 16 (fp32) or 32 (bf16) channels of each stream, as stored
+      uint4 v[N][4];
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int k = b * N + i;
+        const int slot = k % S, a = k % NA;
+        const unsigned char* base = sm + slot * P::SLOT;
+        if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word)) { ok = false; break; }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] = *reinterpret_cast<const uint4*>(base + choff[j]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);  // x of this stage now lives in registers
+        if (k >= NA && !mbar_wait_or_abort(&afree[a], (uint32_t)(((k / NA) - 1) & 1), abort_word)) { ok = false; break; }
+        tc_fence_after();
+        if constexpr (P::BF16) {
+          // bf16 -> fp32 is exact and already a tf32 value: hi only
+          const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + P::ACOL + 64 * a + 32 * h;
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t hi[16];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const uint32_t w2 = (&v[i][2 * hf].x)[e];   // channels 2e, 2e+1 of chunks 2hf, 2hf+1
+              hi[2 * e] = w2 << 16;
+              hi[2 * e + 1] = w2 & 0xFFFF0000u;
+            }
+            tmem_st16(ta + 16 * hf, hi);
+          }
+        } else {
+          const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + P::ACOL + 64 * a + 16 * h;
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t hi[8], lo[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) split_tf32(__uint_as_float((&v[i][2 * hf].x)[e]), hi[e], lo[e]);
+            tmem_st8(ta + 8 * hf, hi);
+            tmem_st8(ta + 32 + 8 * hf, lo);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aready[a]);
+      }
+      if (!ok) break;
+      // Gram of this block first, then the running sum: the rounding error
+      // grows with the number of blocks, not of channels
+      int g = 0;
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int j = i; j < N; ++j) {
+          float blk = 0.f;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const uint32_t ui = (&v[i][0].x)[q], uj = (&v[j][0].x)[q];
+            if constexpr (P::BF16) {
+              blk = fmaf(__uint_as_float(ui << 16), __uint_as_float(uj << 16), blk);
+              blk = fmaf(__uint_as_float(ui & 0xFFFF0000u), __uint_as_float(uj & 0xFFFF0000u), blk);
+            } else {
+              blk = fmaf(__uint_as_float(ui), __uint_as_float(uj), blk);
+            }
+          }
+          gacc[g] += blk;
+          ++g;
+        }
+    }
+    if (!ok) *abort_word = 1;
+    // results: D columns [16h, 16h + 16) of this token, Gram halves summed
+    bool have = ok && nchunks > 0 && mbar_wait_or_abort(done, 0u, abort_word);
+    have = __all_sync(0xffffffffu, have);
+    tc_fence_after();
+    const int64_t tok = t0 + r;
+    if (16 * h < NHP) {
+      float d[16];
+      if (have) {
+        tmem_ld16(tmem + ((uint32_t)(32 * qd) << 16) + 16 * h, d);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) d[e] = 0.f;
+      }
+      if (tok < B && (have || nchunks == 0)) {
+        float* pd = ppart + ((int64_t)split * B + tok) * NHP + 16 * h;
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (16 * h + e < NHP) pd[e] = d[e];
+      }
+    }
+    if (h == 1) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g) gx_s[r * NG + g] = gacc[g];
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (h == 0 && tok < B && (have || nchunks == 0)) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g)
+        gpart[((int64_t)split * B + tok) * NG + g] = gacc[g] + gx_s[r * NG + g];
+    }
+  }
+  // the MMA issuer drains its last batch before tensor memory is released
+  if (warp == 1 && lane == 0 && nchunks > 0) mbar_wait_or_abort(done, 0u, abort_word);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P::TCOLS));
+}
+
+// ---------------------------------------------------------------------------
+// Backward 3 for n = 4, dynamic H, on tcgen05 with warp specialisation.
+//   CTA = 32 channels x 4 streams = 128 columns (col = 32 i + c) = one M=128
+//   MMA tile, a contiguous range of 32-token blocks; 27 warps: warp 0 TMA,
+//   warp 1 issues D1, warps 2..17 "E" (two tokens each, lane = channel, all
+//   four streams), warps 18..21 epilogue and warps 23..26 X^T (stream = the
+//   tensor-memory lane quadrant of the warp, lane = channel), warp 22 issues
+//   D2.  Per block j:
+//     TMA:  g, x [32 tokens x 4 streams x 32 channels] and the block's
+//           operand image (d_p split into tf32 hi/lo in both the B layout of
+//           D1 and of D2, plus the per-token scalars), written by
+//           token_bwd (gx_image_row) in the exact K-major shared-memory layout;
+//     MMA:  D1[b] = Phi^T[col x 24] . D_p^T      (M=128, N=32, 3xTF32)
+//           D2   += X^T[col x 32 tok] . D_p      (M=128, N=32, 3xTF32)
+//           with Phi^T resident in shared memory, X^T (A of D2) and D1 in
+//           tensor memory, ND-deep;
+//     X^T:  x of the warp's stream split into tf32 hi/lo and stored into
+//           tensor memory (tcgen05.st: lane = column, column = token), which
+//           transposes for free and needs no proxy fence;
+//     E:    the local terms of all four streams into a shared buffer
+//           (overlapping the MMAs);
+//     epilogue: grad_x = D1 + local term, added in place in the local-term
+//           buffer (its [token][stream][channel] layout is the grad_x tile)
+//           and written with one TMA store.
+//   After the range: D2 -> this split's dphi partial, sum of gy.xa.inv_r ->
+//   this split's grad-w partial.
+// ---------------------------------------------------------------------------
+
+
+template <typename T>
+__global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
+    grad_x6_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
+                   const __grid_constant__ CUtensorMap omap, const float* __restrict__ img, const float* __restrict__ w,
+                   const float* __restrict__ phi_pre, const float* __restrict__ phi_post,
+                   const float* __restrict__ phi_res, T* __restrict__ gx,
+                   float* __restrict__ dphi_part, float* __restrict__ gw_part, int64_t B,
+                   int64_t C, int ntiles, int nsplit, int64_t nblk) {
+  using F = Gx6Cfg;
+  using SM = Gx6S<T>;
+  constexpr int SG = F::SG, SI = F::SI, ND = F::ND, CW = F::CW, COLS = F::COLS, TOK = F::TOK;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* gfull = reinterpret_cast<uint64_t*>(sm + SM::OFF_BAR);
+  uint64_t* gfree = gfull + SG;
+  uint64_t* ifull = gfree + SG;
+  uint64_t* ifree = ifull + SI;
+  uint64_t* a2_ready = ifree + SI;
+  uint64_t* a2_free = a2_ready + ND;
+  uint64_t* d1_full = a2_free + ND;
+  uint64_t* d1_free = d1_full + ND;
+  uint64_t* loc_ready = d1_free + ND;
+  uint64_t* loc_free = loc_ready + ND;
+  uint64_t* d2_done = loc_free + ND;
+  uint64_t* phi_ready = d2_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(phi_ready + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t sbase = smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x % ntiles;
+  const int split = blockIdx.x / ntiles;
+  const int64_t c0 = (int64_t)tile * CW;
+  const int64_t nC = 4 * C;
+  const int64_t blk0 = nblk * split / nsplit, blk1 = nblk * (split + 1) / nsplit;
+  const int nb = (int)(blk1 - blk0);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(F::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 32) {
+    prefetch_tmap(&gmap);
+    prefetch_tmap(&xmap);
+    prefetch_tmap(&omap);
+    for (int st = 0; st < SG; ++st) { mbar_init(&gfull[st], 1); mbar_init(&gfree[st], F::E_WARPS + 4); }
+    for (int st = 0; st < SI; ++st) { mbar_init(&ifull[st], 1); mbar_init(&ifree[st], 2 + F::E_WARPS); }
+    for (int b = 0; b < ND; ++b) {
+      mbar_init(&a2_ready[b], 4);
+      mbar_init(&a2_free[b], 1);
+      mbar_init(&d1_full[b], 1);
+      mbar_init(&d1_free[b], 4);
+      mbar_init(&loc_ready[b], F::E_WARPS);
+      mbar_init(&loc_free[b], 1);
+    }
+    mbar_init(d2_done, 1);
+    mbar_init(phi_ready, 4);
+    *abort_word = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int gi = 0, ii = 0;
+      for (int j = 0; j < nb; ++j) {
+        const int sg = j % SG, si = j % SI;
+        if (j >= SG && !mbar_wait_or_abort(&gfree[sg], (uint32_t)(((j / SG) - 1) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        const int64_t blk = blk0 + j;
+        const int row = (int)(blk * TOK * 4);
+        unsigned char* gb = sm + sg * 2 * SM::GB;
+        mbar_expect_tx(&gfull[sg], 2 * SM::GB);
+        tma_load_2d(gb, &gmap, (int)c0, row, &gfull[sg]);
+        tma_load_2d(gb + SM::GB, &xmap, (int)c0, row, &gfull[sg]);
+        gi = j + 1;
+        if (j >= SI && !mbar_wait_or_abort(&ifree[si], (uint32_t)(((j / SI) - 1) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        mbar_expect_tx(&ifull[si], F::IMG);
+        bulk_load(sm + SM::OFF_IMG + si * F::IMG, img + blk * F::IMG_FLOATS, F::IMG, &ifull[si]);
+        ii = j + 1;
+      }
+      // no copy may still be landing when the CTA exits (bounded)
+      for (int q = gi > SG ? gi - SG : 0; q < gi; ++q) mbar_wait(&gfull[q % SG], (uint32_t)((q / SG) & 1));
+      for (int q = ii > SI ? ii - SI : 0; q < ii; ++q) mbar_wait(&ifull[q % SI], (uint32_t)((q / SI) & 1));
+    }
+  } else if (warp == 1) {
+    // ---------------- D1 issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t ID1 = umma_idesc_tf32(128, TOK);
+      if (nb > 0 && !mbar_wait_or_abort(phi_ready, 0u, abort_word)) *abort_word = 1;
+      for (int j = 0; j < nb && !*abort_word; ++j) {
+        const int si = j % SI, b = j % ND;
+        if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { *abort_word = 1; break; }
+        if (j >= ND && !mbar_wait_or_abort(&d1_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t im = sbase + SM::OFF_IMG + si * F::IMG;
+#pragma unroll
+        for (int ks = 0; ks < 3; ++ks) {
+          const uint32_t ah = tmem + F::A1_COL + 8 * ks, al = tmem + F::A1L_COL + 8 * ks;
+          const uint64_t bh = umma_desc_k(im + F::IMG_B1H * 4, TOK, ks, 0);
+          const uint64_t bl = umma_desc_k(im + F::IMG_B1L * 4, TOK, ks, 0);
+          umma_tf32_at(tmem + TOK * b, al, bh, ID1, ks > 0 ? 1u : 0u);
+          umma_tf32_at(tmem + TOK * b, ah, bl, ID1, 1u);
+          umma_tf32_at(tmem + TOK * b, ah, bh, ID1, 1u);
+        }
+        umma_commit(&d1_full[b]);
+        umma_commit(&ifree[si]);
+      }
+    }
+  } else if (warp == F::D2_WARP) {
+    // ---------------- D2 issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t ID2 = umma_idesc_tf32(128, F::KP);
+      for (int j = 0; j < nb; ++j) {
+        const int si = j % SI, b = j % ND;
+        if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { *abort_word = 1; break; }
+        if (!mbar_wait_or_abort(&a2_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { *abort_word = 1; break; }
+        tc_fence_after();
+        const uint32_t im = sbase + SM::OFF_IMG + si * F::IMG;
+        const uint32_t a2 = tmem + F::XT_COL + 2 * TOK * b;
+#pragma unroll
+        for (int ks = 0; ks < TOK / 8; ++ks) {
+          const uint32_t ah = a2 + 8 * ks, al = a2 + TOK + 8 * ks;
+          const uint64_t bh = umma_desc_k(im + F::IMG_B2H * 4, F::KP, ks, 0);
+          const uint64_t bl = umma_desc_k(im + F::IMG_B2L * 4, F::KP, ks, 0);
+          if constexpr (SM::BF16) {
+            umma_tf32_at(tmem + F::D2_COL, ah, bl, ID2, (j > 0 || ks > 0) ? 1u : 0u);
+            umma_tf32_at(tmem + F::D2_COL, ah, bh, ID2, 1u);
+          } else {
+            umma_tf32_at(tmem + F::D2_COL, al, bh, ID2, (j > 0 || ks > 0) ? 1u : 0u);
+            umma_tf32_at(tmem + F::D2_COL, ah, bl, ID2, 1u);
+            umma_tf32_at(tmem + F::D2_COL, ah, bh, ID2, 1u);
+          }
+        }
+        umma_commit(&a2_free[b]);
+        umma_commit(&ifree[si]);
+      }
+      umma_commit(d2_done);
+    }
+  } else if (warp >= F::XT_WARP0) {
+    // ---------------- X^T operand into tensor memory ----------------
+    const int q = warp & 3;                  // stream = tensor-memory lane quadrant
+    {
+      // resident Phi^T (A of D1): lane = column (stream q, channel lane), column = k
+      const float* ph = nullptr;
+      uint32_t hi[24], lo[24];
+#pragma unroll
+      for (int k = 0; k < F::NH; ++k) {
+        ph = phi_row(phi_pre, phi_post, phi_res, k, 4, nC);
+        split_tf32(__ldg(ph + (int64_t)q * C + c0 + lane), hi[k], lo[k]);
+      }
+      const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16);
+#pragma unroll
+      for (int k8 = 0; k8 < 3; ++k8) {
+        tmem_st8(ta + F::A1_COL + 8 * k8, *reinterpret_cast<const uint32_t(*)[8]>(hi + 8 * k8));
+        tmem_st8(ta + F::A1L_COL + 8 * k8, *reinterpret_cast<const uint32_t(*)[8]>(lo + 8 * k8));
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(phi_ready);
+    }
+    for (int j = 0; j < nb; ++j) {
+      const int sg = j % SG, b = j % ND;
+      if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { *abort_word = 1; break; }
+      const T* xs = reinterpret_cast<const T*>(sm + sg * 2 * SM::GB) + SM::GB / sizeof(T);
+      float xv[TOK];
+#pragma unroll
+      for (int t = 0; t < TOK; ++t) xv[t] = to_f32(xs[(t * 4 + q) * CW + lane]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&gfree[sg]);
+      if (j >= ND && !mbar_wait_or_abort(&a2_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) { *abort_word = 1; break; }
+      tc_fence_after();
+      const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + F::XT_COL + 2 * TOK * b;
+#pragma unroll
+      for (int hf = 0; hf < TOK / 16; ++hf) {
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          if constexpr (SM::BF16) hi[t] = __float_as_uint(xv[16 * hf + t]);   // exact in tf32
+          else split_tf32(xv[16 * hf + t], hi[t], lo[t]);
+        }
+        tmem_st16(ta + 16 * hf, hi);
+        if constexpr (!SM::BF16) tmem_st16(ta + TOK + 16 * hf, lo);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a2_ready[b]);
+    }
+  } else {
+    const int64_t c = c0 + lane;
+    float* locs = reinterpret_cast<float*>(sm + SM::OFF_LOC);
+    float* gws = reinterpret_cast<float*>(sm + SM::OFF_GW);
+    bool ok = true;
+    constexpr int TPE = F::TPE;
+    if (warp < 2 + F::E_WARPS) {
+      // ---------------- E: X^T operand and local terms ----------------
+      const int e = warp - 2;                // tokens TPE e .. TPE e + TPE - 1
+      const float wc = __ldg(w + c);
+      float gwacc = 0.f;
+      for (int j = 0; j < nb; ++j) {
+        const int sg = j % SG, si = j % SI, b = j % ND;
+        if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { ok = false; break; }
+        const T* gs = reinterpret_cast<const T*>(sm + sg * 2 * SM::GB);
+        const T* xs = gs + SM::GB / sizeof(T);
+        float gv[TPE][4], xv[TPE][4];        // [token][stream]
+#pragma unroll
+        for (int u = 0; u < TPE; ++u)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            gv[u][jj] = to_f32(gs[((TPE * e + u) * 4 + jj) * CW + lane]);
+            xv[u][jj] = to_f32(xs[((TPE * e + u) * 4 + jj) * CW + lane]);
+          }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&gfree[sg]);   // g, x now live in registers
+        if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { ok = false; break; }
+        const float* sc = reinterpret_cast<const float*>(sm + SM::OFF_IMG + si * F::IMG) + F::IMG_SC;
+        // local terms of the four streams
+        if (j >= ND && !mbar_wait_or_abort(&loc_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) { ok = false; break; }
+        float* lb = locs + b * (F::LOCB / 4);
+#pragma unroll
+        for (int u = 0; u < TPE; ++u) {
+          const int t = TPE * e + u;
+          const float* st = sc + t * 32;
+          const float4 s0 = *reinterpret_cast<const float4*>(st);
+          const float4 h4 = *reinterpret_cast<const float4*>(st + 4);
+          const float4 q4 = *reinterpret_cast<const float4*>(st + 8);
+          const float gy = q4.x * gv[u][0] + q4.y * gv[u][1] + q4.z * gv[u][2] + q4.w * gv[u][3];
+          const float xa = h4.x * xv[u][0] + h4.y * xv[u][1] + h4.z * xv[u][2] + h4.w * xv[u][3];
+          const float agg = gy * wc * s0.y - xa * s0.x;
+          const float hh[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 m4 = *reinterpret_cast<const float4*>(st + 12 + 4 * i);
+            const float mix = m4.x * gv[u][0] + m4.y * gv[u][1] + m4.z * gv[u][2] + m4.w * gv[u][3];
+            lb[t * COLS + i * CW + lane] = mix + hh[i] * agg + s0.z * xv[u][i];
+          }
+          gwacc = fmaf(gy * xa, s0.y, gwacc);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&loc_ready[b]);
+          mbar_arrive(&ifree[si]);
+        }
+      }
+      gws[e * CW + lane] = gwacc;
+    } else {
+      // ---------------- epilogue: grad_x = D1 + local term ----------------
+      const int i = warp & 3;                // stream = tensor-memory lane quadrant
+      const bool leader = warp == 2 + F::E_WARPS && lane == 0;
+      for (int j = 0; j < nb; ++j) {
+        const int b = j % ND;
+        if (!mbar_wait_or_abort(&d1_full[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
+        if (!mbar_wait_or_abort(&loc_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
+        tc_fence_after();
+        float* lb = locs + b * (F::LOCB / 4) + i * CW + lane;
+        __nv_bfloat16* sb16 = reinterpret_cast<__nv_bfloat16*>(sm + SM::OFF_STG + b * SM::STGB) + i * CW + lane;
+#pragma unroll
+        for (int hf = 0; hf < TOK / 16; ++hf) {
+          float d[16];
+          tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + TOK * b + 16 * hf, d);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            if constexpr (SM::BF16) sb16[(16 * hf + t) * COLS] = __float2bfloat16_rn(lb[(16 * hf + t) * COLS] + d[t]);
+            else lb[(16 * hf + t) * COLS] += d[t];
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&d1_free[b]);
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (leader) {
+          tma_store_2d(&omap, SM::BF16 ? static_cast<const void*>(sm + SM::OFF_STG + b * SM::STGB)
+                                       : static_cast<const void*>(locs + b * (F::LOCB / 4)),
+                       (int)c0, (int)((blk0 + j) * TOK * 4));
+          bulk_commit();
+          // the previous block's buffer may be refilled once its store has read it
+          if (j > 0) {
+            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            mbar_arrive(&loc_free[(j - 1) % ND]);
+          }
+        }
+      }
+      if (leader) {
+        bulk_wait0();
+        if (ok && nb > 0) mbar_arrive(&loc_free[(nb - 1) % ND]);
+      }
+    }
+    if (!ok) *abort_word = 1;
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * (F::E_WARPS + 4)) : "memory");
+    ok = *abort_word == 0;
+    if (warp >= 2 + F::E_WARPS) {
+      const int i = warp & 3;
+      bool have = ok && nb > 0 && mbar_wait_or_abort(d2_done, 0u, abort_word);
+      have = __all_sync(0xffffffffu, have);
+      const bool write = have || (ok && nb == 0);
+      tc_fence_after();
+      float a[16], bb[16];
+      if (have) {
+        tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + F::D2_COL, a);
+        tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + F::D2_COL + 16, bb);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) { a[q] = 0.f; bb[q] = 0.f; }
+      }
+      if (write) {
+        float* dd = dphi_part + (int64_t)split * F::NH * nC + (int64_t)i * C + c;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) dd[(int64_t)k * nC] = a[k];
+#pragma unroll
+        for (int k = 16; k < F::NH; ++k) dd[(int64_t)k * nC] = bb[k - 16];
+        if (i == 0) {
+          float gsum = 0.f;
+#pragma unroll
+          for (int q = 0; q < F::E_WARPS; ++q) gsum += gws[q * CW + lane];
+          gw_part[(int64_t)split * C + c] = gsum;
+        }
+      }
+    }
+  }
+  if (warp == F::D2_WARP && lane == 0 && nb > 0) mbar_wait_or_abort(d2_done, 0u, abort_word);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(F::TMEM_COLS));
+}
+
+}  // namespace
+}  // namespace mhc
