@@ -219,6 +219,24 @@ def test_dynamic_bf16_io(cuda, B, C):
         assert torch.equal(layer(xb.to(cuda)), out.detach())
 
 
+def test_dynamic_bf16_io_rejects_unsupported_shapes(cuda):
+    """bf16 streams need the tensor-core kernels: other shapes fail loudly
+    (no silent fp32 or CPU fallback)."""
+    for n, C, train in ((4, 96, False), (2, 128, True)):
+        x, params, grad = oracle_case(8, n, C, seed=3, alpha=0.5, bias_std=0.5)
+        layer = make_layer(params, n, C, cuda)
+        layer.bf16_io = True
+        xd = x.bfloat16().to(cuda).requires_grad_(train)
+        with pytest.raises(RuntimeError, match="bf16"):
+            if train:
+                layer(xd).backward(grad.bfloat16().to(cuda))
+            else:
+                with torch.no_grad():
+                    layer.eval()
+                    layer(xd)
+        torch.cuda.synchronize()
+
+
 def test_residual_wrapper(cuda):
     B, T, C, n = 2, 5, 64, 4
     gen = torch.Generator().manual_seed(3)
