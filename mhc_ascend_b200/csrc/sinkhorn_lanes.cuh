@@ -34,13 +34,22 @@ __device__ __forceinline__ void skl_step(T (&a)[N], T eps, int r, T* dr, T* dc_o
 #pragma unroll
     for (int j = 0; j < N; ++j) a[j] = a[j] / d;
   }
+  T cs[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) cs[j] = group_sum<G>(a[j]) + eps;
   T mine = 0;
 #pragma unroll
-  for (int j = 0; j < N; ++j) {
-    const T dcj = group_sum<G>(a[j]) + eps;
-    if (j == r) mine = dcj;
-    if (sizeof(T) == 8) a[j] *= T(1) / dcj;
-    else a[j] = a[j] / dcj;
+  for (int j = 0; j < N; ++j)
+    if (j == r) mine = cs[j];
+  if (sizeof(T) == 8) {
+    // one reciprocal per lane (its own column), shared over the group
+    const T inv_mine = T(1) / mine;
+    const int base = (int)(threadIdx.x & 31) & ~(G - 1);
+#pragma unroll
+    for (int j = 0; j < N; ++j) a[j] *= __shfl_sync(0xffffffffu, inv_mine, base + j);
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) a[j] = a[j] / cs[j];
   }
   if (dc_own) *dc_own = mine;
 }
@@ -69,12 +78,14 @@ __device__ __forceinline__ void skl_backward(const T (&x0)[N], T (&g)[N], int it
       skl_step<N, G, T>(z, eps, r, dr + (t - seg_start), dco + (t - seg_start));
     for (int t = seg_end - 1; t >= seg_start; --t) {
       const T dmine = dco[t - seg_start];
+      const T imine = T(1) / dmine;   // this lane's column; shared over the group
       // column step: Z = Y / dc
 #pragma unroll
       for (int j = 0; j < N; ++j) {
         const T d = __shfl_sync(0xffffffffu, dmine, base + j);
+        const T inv = __shfl_sync(0xffffffffu, imine, base + j);
         const T s = group_sum<G>(g[j] * z[j]);
-        g[j] = (g[j] - s) * (T(1) / d);
+        g[j] = (g[j] - s) * inv;
         z[j] = z[j] * d;  // now Y_t
       }
       // row step: Y = X / dr
