@@ -2,7 +2,7 @@
 """Benchmark of the mHC layer hot path (dynamic-H forward + backward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
-                    [--config cfg3|cfg5|cfg4|cfg4_bf16]
+                    [--config cfg3|cfg5|cfg4|cfg4_bf16|paper_n8|paper_n32]
 
 Metric: mHC layer fwd+bwd tokens/s at n=4, C=4096; weak
 scaling (8192 tokens per GPU, the cfg3 workload) on 1/2/4/8 GPUs of one node.
@@ -41,6 +41,9 @@ CONFIGS = {
     "cfg5": (32768, 4, 7168, "dynamic"),
     "cfg4": (65536, 4, 4096, "static_fwd"),
     "cfg4_bf16": (65536, 4, 4096, "static_fwd_bf16"),
+    # the reference's paper shapes with wider expansion rates (benchmark.py:302-312)
+    "paper_n8": (256, 8, 1280, "dynamic"),
+    "paper_n32": (128, 32, 1280, "dynamic"),
 }
 
 
@@ -84,7 +87,20 @@ def kernel_bytes(name, B, n, C, elem=4):
         "bwd_stats": 2 * x + C * 4,
         "grad_x": 3 * x + 2 * NH * nC * 4 + C * 4,
         "static_fwd": 2 * x,
+        # wide rates (n > 8): the GEMMs read phi once, the stream kernels x (and g) twice
+        "wide_gemm_proj": x + NH * nC * 4,
+        "wide_gemm_gx": 2 * x + NH * nC * 4,
+        "wide_gemm_dphi": x + 2 * NH * nC * 4,
+        "wide_stream_fwd": 2 * x,
+        "wide_bwd_stream": 3 * x,
     }.get(name)
+
+
+def kernel_flops(name, B, n, C):
+    """FLOPs per launch of the wide-rate GEMMs (2 per multiply-add)."""
+    if name in ("wide_gemm_proj", "wide_gemm_gx", "wide_gemm_dphi"):
+        return 2 * B * (n * n + 2 * n) * n * C
+    return None
 
 
 class ClockSampler:
@@ -328,15 +344,31 @@ def run_mine(args, world, rank, local):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    start.record(stream)
-    for _ in range(args.steps):
-        step()
-    stop.record(stream)
+    # Steps whose streamed data fits in L2 flush it before each timed step
+    # (a 512 MiB write, outside the per-step events).
+    flush = (2 * x.numel() * x.element_size()) < (1 << 30)
+    if flush:
+        scratch = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for e0, e1 in evs:
+            scratch.fill_(1)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+    else:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
-    ms = start.elapsed_time(stop) / args.steps
+    if flush:
+        ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps
+    else:
+        ms = start.elapsed_time(stop) / args.steps
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -360,6 +392,9 @@ def run_mine(args, world, rank, local):
         kernels[name] = {"launches_per_step": cnt / prof_steps, "avg_ms": avg,
                          "share": tot / sum(t for _, t in rep.values()),
                          "gbs": (kb / (avg * 1e-3) / 1e9) if kb else None}
+        kf = kernel_flops(name, tokens, n, C)
+        if kf:
+            kernels[name]["tflops"] = kf / (avg * 1e-3) / 1e12
     dom = max(rep, key=lambda k: rep[k][1])
     peak, peak_kind = peaks()
     dom_avg = rep[dom][1] / rep[dom][0]
@@ -465,7 +500,7 @@ def run_mine(args, world, rank, local):
         cpu = time_cpu_oracle(n, C, mode, 512 if C <= 4096 else 256, args.cpu_seconds)
 
     if rank == 0:
-        metric = ("mHC layer fwd+bwd tokens/s (n=4, C=4096)" if dynamic
+        metric = (f"mHC layer fwd+bwd tokens/s (n={n}, C={C})" if dynamic
                   else "mHC static-H layer forward tokens/s")
         line = {
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -477,7 +512,9 @@ def run_mine(args, world, rank, local):
                                    f"per step" + (", NCCL grad all-reduce" if world > 1 else ""),
                        "tokens_per_gpu": tokens, "global_batch": tokens * world,
                        "parallelism": f"dp{world}",
-                       "l2": "no flush: each step streams >= 1 GiB (x, grad_out), > 126 MB L2"},
+                       "l2": ("flushed: 512 MiB write before each timed step, outside its "
+                              "events" if flush else
+                              "no flush: each step streams >= 1 GiB (x, grad_out), > 126 MB L2")},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
                          "traffic": traffic, "peak_kind": peak_kind,

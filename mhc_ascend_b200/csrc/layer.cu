@@ -46,6 +46,7 @@
 #include "layer/grad_x_legacy.cuh"
 #include "layer/tcgen05.cuh"
 #include "layer/reduce.cuh"
+#include "layer/wide.cuh"
 
 namespace mhc {
 namespace {
@@ -512,12 +513,195 @@ int run_bwd_static(const float* g, const float* x, const float* w, const float* 
   return check_launch("mhc_layer_bwd_static/reduce");
 }
 
+// ---------------------------------------------------------------------------
+// Wide expansion rates (8 < n <= 32): kernels in layer/wide.cuh
+// ---------------------------------------------------------------------------
+constexpr size_t kWidePartCap = size_t(256) << 20;  // split-K partials, bytes per GEMM
+
+struct WideSplit {
+  int S;
+  int64_t kchunk;
+};
+
+// Split K until the GEMM has about two waves of CTAs, keeping >= 256 k per
+// split and the partials under kWidePartCap.
+WideSplit wide_split(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ((M + WG_BM - 1) / WG_BM) * ((N + WG_BN - 1) / WG_BN);
+  const int64_t sms = num_sms();
+  int S = 1;
+  while (tiles * S < 2 * sms && S < 64 && K / (2 * S) >= 256 &&
+         (size_t)(2 * S) * M * N * sizeof(float) <= kWidePartCap)
+    S *= 2;
+  int64_t kchunk = (K + S - 1) / S;
+  kchunk = (kchunk + WG_BK - 1) / WG_BK * WG_BK;
+  if (kchunk < WG_BK) kchunk = WG_BK;
+  S = (int)((K + kchunk - 1) / kchunk);
+  if (S < 1) S = 1;
+  return WideSplit{S, kchunk};
+}
+
+size_t wide_fwd_ws_bytes(int64_t B, int n, int64_t C, bool need_rec) {
+  const int64_t NH = (int64_t)n * n + 2 * n;
+  const WideSplit sp = wide_split(B, NH, (int64_t)n * C);
+  Carve cv(nullptr);
+  if (need_rec) cv.take((size_t)B * rec_stride(n));
+  cv.take((size_t)sp.S * B * NH);
+  cv.take((size_t)B * n * n);
+  cv.take((size_t)B * n * n);
+  return cv.off;
+}
+
+size_t wide_bwd_ws_bytes(int64_t B, int n, int64_t C) {
+  const int64_t NH = (int64_t)n * n + 2 * n, nC = (int64_t)n * C;
+  const WideSplit s1 = wide_split(B, nC, NH), s2 = wide_split(NH, nC, B);
+  Carve cv(nullptr);
+  for (int q = 0; q < 3; ++q) cv.take((size_t)B * n * n);  // E, gE, gM
+  cv.take((size_t)B * 2 * n);                                // gh | ghp
+  cv.take((size_t)B * NH);                                   // d_p
+  cv.take((size_t)B * (NH + 3));                             // bias / alpha rows
+  cv.take((size_t)B);                                        // rms_h coefficient
+  cv.take((size_t)B * C);                                    // weight-gradient rows
+  cv.take((size_t)NH + 3);                                   // their sums
+  if (s1.S > 1) cv.take((size_t)s1.S * B * nC);
+  if (s2.S > 1) cv.take((size_t)s2.S * NH * nC);
+  return cv.off;
+}
+
+// dynamic shared memory of the per-token stream kernels
+inline size_t wide_fwd_smem(int NM, int64_t C) { return (size_t)(NM * NM + 2 * NM + C) * sizeof(float); }
+inline size_t wide_bwd_smem(int NM, int64_t C) {
+  return (size_t)(NM * NM + 2 * NM + 2 * NM * 33 + 2 * C) * sizeof(float);
+}
+constexpr size_t kWideSmemMax = 200 * 1024;
+
+int run_fwd_wide(const float* x, const float* w, const float* pp, const float* pq, const float* pr,
+                 const float* ap, const float* aq, const float* ar, const float* bp,
+                 const float* bq, const float* br, float* out, float* token_state, int64_t B,
+                 int n, int64_t C, int iters, float s_eps, float r_eps, void* ws, size_t ws_bytes,
+                 cudaStream_t s) {
+  const int NM = n <= 16 ? 16 : 32;
+  const int64_t NH = (int64_t)n * n + 2 * n, nC = (int64_t)n * C;
+  const int RS = rec_stride(n);
+  const size_t smem = wide_fwd_smem(NM, C);
+  MHC_REQUIRE(smem <= kWideSmemMax, MHC_ERR_UNSUPPORTED,
+              "mhc_layer_fwd_dynamic: hidden_dim %lld too large for n = %d", (long long)C, n);
+  const size_t need = wide_fwd_ws_bytes(B, n, C, token_state == nullptr);
+  MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
+              "mhc_layer_fwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
+  const WideSplit sp = wide_split(B, NH, nC);
+  Carve cv(ws);
+  float* rec = token_state ? token_state : cv.take((size_t)B * RS);
+  float* part = cv.take((size_t)sp.S * B * NH);
+  float* E = cv.take((size_t)B * n * n);
+  float* Mb = cv.take((size_t)B * n * n);
+  { ProfScope _ps("wide_rms", s); wide_rms_kernel<<<(unsigned)B, 256, 0, s>>>(x, nC, rec, RS, r_eps); }
+  {
+    ProfScope _ps("wide_gemm_proj", s);
+    const dim3 grid((unsigned)((NH + WG_BN - 1) / WG_BN), (unsigned)((B + WG_BM - 1) / WG_BM), (unsigned)sp.S);
+    wide_gemm_kernel<true, true, 0><<<grid, WG_THREADS, 0, s>>>(
+        rows1(x, nC), rows3(pp, pq, pr, n, 2 * n, nC), B, NH, nC, sp.kchunk, part, Rows3{}, nullptr, Rows3{});
+  }
+  { ProfScope _ps("wide_gates", s); wide_gates_kernel<<<(unsigned)B, 256, 0, s>>>(part, sp.S, B, n, ap, aq, ar, bp, bq, br, rec, RS, E); }
+  int rc = check_launch("mhc_layer_fwd_dynamic/wide_proj");
+  if (rc) return rc;
+  rc = mhc_sinkhorn_knopp_fwd(E, Mb, B, n, iters, s_eps, s);
+  if (rc) return rc;
+  {
+    ProfScope _ps("wide_stream_fwd", s);
+    if (NM == 16) {
+      cudaFuncSetAttribute(wide_stream_fwd_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      wide_stream_fwd_kernel<16><<<(unsigned)B, 256, smem, s>>>(x, w, Mb, rec, RS, out, n, C, r_eps);
+    } else {
+      cudaFuncSetAttribute(wide_stream_fwd_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      wide_stream_fwd_kernel<32><<<(unsigned)B, 256, smem, s>>>(x, w, Mb, rec, RS, out, n, C, r_eps);
+    }
+  }
+  return check_launch("mhc_layer_fwd_dynamic/wide_stream_fwd");
+}
+
+int run_bwd_wide(const float* g, const float* x, const float* w, const float* pp, const float* pq,
+                 const float* pr, const float* ap, const float* aq, const float* ar,
+                 const float* br, const float* rec, float* gx, float* gw, float* gpp, float* gpq,
+                 float* gpr, float* gap, float* gaq, float* gar, float* gbp, float* gbq,
+                 float* gbr, int64_t B, int n, int64_t C, int iters, float s_eps, void* ws,
+                 size_t ws_bytes, cudaStream_t s) {
+  const int NM = n <= 16 ? 16 : 32;
+  const int64_t NH = (int64_t)n * n + 2 * n, nC = (int64_t)n * C;
+  const int RS = rec_stride(n);
+  const size_t smem = wide_bwd_smem(NM, C);
+  MHC_REQUIRE(smem <= kWideSmemMax, MHC_ERR_UNSUPPORTED,
+              "mhc_layer_bwd_dynamic: hidden_dim %lld too large for n = %d", (long long)C, n);
+  const size_t need = wide_bwd_ws_bytes(B, n, C);
+  MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
+              "mhc_layer_bwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
+  const WideSplit s1 = wide_split(B, nC, NH), s2 = wide_split(NH, nC, B);
+  Carve cv(ws);
+  float* E = cv.take((size_t)B * n * n);
+  float* gE = cv.take((size_t)B * n * n);
+  float* gM = cv.take((size_t)B * n * n);
+  float* ghh = cv.take((size_t)B * 2 * n);
+  float* GP = cv.take((size_t)B * NH);
+  float* rows = cv.take((size_t)B * (NH + 3));
+  float* coef = cv.take((size_t)B);
+  float* gwt = cv.take((size_t)B * C);
+  float* tot = cv.take((size_t)NH + 3);
+  float* part1 = s1.S > 1 ? cv.take((size_t)s1.S * B * nC) : nullptr;
+  float* part2 = s2.S > 1 ? cv.take((size_t)s2.S * NH * nC) : nullptr;
+  {
+    ProfScope _ps("wide_bwd_stream", s);
+    if (NM == 16) {
+      cudaFuncSetAttribute(wide_bwd_stream_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      wide_bwd_stream_kernel<16><<<(unsigned)B, 256, smem, s>>>(g, x, w, rec, RS, ar, br, n, C, gx, gwt, ghh, gM, E);
+    } else {
+      cudaFuncSetAttribute(wide_bwd_stream_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      wide_bwd_stream_kernel<32><<<(unsigned)B, 256, smem, s>>>(g, x, w, rec, RS, ar, br, n, C, gx, gwt, ghh, gM, E);
+    }
+  }
+  int rc = check_launch("mhc_layer_bwd_dynamic/wide_bwd_stream");
+  if (rc) return rc;
+  rc = mhc_sinkhorn_knopp_bwd(gM, E, E, gE, B, n, iters, s_eps, s);
+  if (rc) return rc;
+  { ProfScope _ps("wide_bwd_token", s); wide_bwd_token_kernel<<<(unsigned)B, 128, 0, s>>>(rec, RS, ghh, gE, E, ap, aq, ar, n, nC, GP, rows, coef); }
+  const Rows3 phi = rows3(pp, pq, pr, n, 2 * n, nC);
+  const Rows3 xr = rows1(x, nC), gxr = rows1(gx, nC), gpr_ = rows1(GP, NH);
+  {
+    // grad_x += d_p phi + coef x   (M = tokens, N = nC, K = NH)
+    ProfScope _ps("wide_gemm_gx", s);
+    const dim3 grid((unsigned)((nC + WG_BN - 1) / WG_BN), (unsigned)((B + WG_BM - 1) / WG_BM), (unsigned)s1.S);
+    if (s1.S == 1) {
+      wide_gemm_kernel<true, false, 2><<<grid, WG_THREADS, 0, s>>>(gpr_, phi, B, nC, NH, s1.kchunk, nullptr, gxr, coef, xr);
+    } else {
+      wide_gemm_kernel<true, false, 0><<<grid, WG_THREADS, 0, s>>>(gpr_, phi, B, nC, NH, s1.kchunk, part1, Rows3{}, nullptr, Rows3{});
+      wide_split_reduce_kernel<2><<<grid_1d(B * nC, 256, 4096), 256, 0, s>>>(part1, s1.S, B, nC, gxr, coef, xr);
+    }
+  }
+  {
+    // d_phi = d_p^T X   (M = NH, N = nC, K = tokens)
+    ProfScope _ps("wide_gemm_dphi", s);
+    const Rows3 gphi = rows3(gpp, gpq, gpr, n, 2 * n, nC);
+    const dim3 grid((unsigned)((nC + WG_BN - 1) / WG_BN), (unsigned)((NH + WG_BM - 1) / WG_BM), (unsigned)s2.S);
+    if (s2.S == 1) {
+      wide_gemm_kernel<false, false, 1><<<grid, WG_THREADS, 0, s>>>(gpr_, xr, NH, nC, B, s2.kchunk, nullptr, gphi, nullptr, Rows3{});
+    } else {
+      wide_gemm_kernel<false, false, 0><<<grid, WG_THREADS, 0, s>>>(gpr_, xr, NH, nC, B, s2.kchunk, part2, Rows3{}, nullptr, Rows3{});
+      wide_split_reduce_kernel<1><<<grid_1d(NH * nC, 256, 4096), 256, 0, s>>>(part2, s2.S, NH, nC, gphi, nullptr, Rows3{});
+    }
+  }
+  {
+    ProfScope _ps("wide_colsum", s);
+    wide_colsum_kernel<<<(unsigned)((C + 31) / 32), 256, 0, s>>>(gwt, B, C, C, gw);
+    wide_colsum_kernel<<<(unsigned)((NH + 3 + 31) / 32), 256, 0, s>>>(rows, B, NH + 3, NH + 3, tot);
+    wide_param_finalize_kernel<<<1, 256, 0, s>>>(tot, n, gbp, gbq, gbr, gap, gaq, gar);
+  }
+  return check_launch("mhc_layer_bwd_dynamic/wide");
+}
+
 int check_layer_args(const char* what, int64_t B, int n, int64_t C, int iters, float s_eps,
-                     float r_eps) {
+                     float r_eps, int max_n = 8) {
   MHC_REQUIRE(B >= 0, MHC_ERR_INVALID_ARG, "%s: batch must be >= 0", what);
   MHC_REQUIRE(C >= 1, MHC_ERR_INVALID_ARG, "%s: hidden_dim must be >= 1", what);
-  MHC_REQUIRE(n >= 1 && n <= 8, MHC_ERR_UNSUPPORTED, "%s: expansion_rate n must be in [1, 8], got %d",
-              what, n);
+  MHC_REQUIRE(n >= 1 && n <= max_n, MHC_ERR_UNSUPPORTED,
+              "%s: expansion_rate n must be in [1, %d], got %d", what, max_n, n);
   MHC_REQUIRE(iters >= 0, MHC_ERR_INVALID_ARG, "%s: sinkhorn_iters must be >= 0", what);
   MHC_REQUIRE(s_eps >= 0.f && r_eps >= 0.f, MHC_ERR_INVALID_ARG, "%s: eps must be >= 0", what);
   MHC_REQUIRE((int64_t)n * C < (1LL << 31), MHC_ERR_UNSUPPORTED, "%s: n*C too large", what);
@@ -546,7 +730,8 @@ extern "C" int32_t mhc_token_state_stride(int32_t n) { return rec_stride(n); }
 
 extern "C" size_t mhc_layer_fwd_dynamic_workspace_bytes(int64_t batch, int32_t n,
                                                         int64_t hidden) {
-  if (batch <= 0 || hidden <= 0 || n < 1 || n > 8) return 0;
+  if (batch <= 0 || hidden <= 0 || n < 1 || n > WIDE_MAX_N) return 0;
+  if (n > 8) return wide_fwd_ws_bytes(batch, n, hidden, true);
   switch (n) {
     case 1: return fwd_ws_bytes<1>(batch, hidden, true);
     case 2: return fwd_ws_bytes<2>(batch, hidden, true);
@@ -568,7 +753,8 @@ static int fwd_dynamic_entry(const char* what, const T* x, const float* rmsnorm_
                              int32_t n, int64_t hidden, int32_t sinkhorn_iters,
                              float sinkhorn_eps, float rmsnorm_eps, void* workspace,
                              size_t workspace_bytes, void* stream) {
-  int rc = check_layer_args(what, batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps);
+  int rc = check_layer_args(what, batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps,
+                            sizeof(T) == 4 ? WIDE_MAX_N : 8);
   if (rc) return rc;
   MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(rmsnorm_weight); MHC_REQUIRE_PTR(phi_pre);
   MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res); MHC_REQUIRE_PTR(alpha_pre);
@@ -576,6 +762,12 @@ static int fwd_dynamic_entry(const char* what, const T* x, const float* rmsnorm_
   MHC_REQUIRE_PTR(b_post); MHC_REQUIRE_PTR(b_res); MHC_REQUIRE_PTR(out);
   if (batch == 0) return MHC_OK;
   cudaStream_t s = (cudaStream_t)stream;
+  if constexpr (sizeof(T) == 4) {
+    if (n > 8)
+      return run_fwd_wide(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre, alpha_post,
+                          alpha_res, b_pre, b_post, b_res, out, token_state, batch, n, hidden,
+                          sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace, workspace_bytes, s);
+  }
   MHC_DISPATCH_N(n, (run_fwd_dynamic<NN, T>(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
                                             alpha_post, alpha_res, b_pre, b_post, b_res, out,
                                             token_state, batch, hidden, sinkhorn_iters,
@@ -616,7 +808,8 @@ extern "C" int mhc_layer_fwd_dynamic_bf16(const void* x, const float* rmsnorm_we
 
 extern "C" size_t mhc_layer_bwd_dynamic_workspace_bytes(int64_t batch, int32_t n,
                                                         int64_t hidden) {
-  if (batch <= 0 || hidden <= 0 || n < 1 || n > 8) return 0;
+  if (batch <= 0 || hidden <= 0 || n < 1 || n > WIDE_MAX_N) return 0;
+  if (n > 8) return wide_bwd_ws_bytes(batch, n, hidden);
   switch (n) {
     case 1: return bwd_ws_bytes<1, true>(batch, hidden);
     case 2: return bwd_ws_bytes<2, true>(batch, hidden);
@@ -639,7 +832,8 @@ static int bwd_dynamic_entry(
     float* grad_alpha_post, float* grad_alpha_res, float* grad_b_pre, float* grad_b_post,
     float* grad_b_res, int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters,
     float sinkhorn_eps, float rmsnorm_eps, void* workspace, size_t workspace_bytes, void* stream) {
-  int rc = check_layer_args(what, batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps);
+  int rc = check_layer_args(what, batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps,
+                            sizeof(T) == 4 ? WIDE_MAX_N : 8);
   if (rc) return rc;
   MHC_REQUIRE_PTR(grad_out); MHC_REQUIRE_PTR(x); MHC_REQUIRE_PTR(rmsnorm_weight);
   MHC_REQUIRE_PTR(phi_pre); MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res);
@@ -652,6 +846,15 @@ static int bwd_dynamic_entry(
   MHC_REQUIRE_PTR(grad_b_pre); MHC_REQUIRE_PTR(grad_b_post); MHC_REQUIRE_PTR(grad_b_res);
   MHC_REQUIRE(batch > 0, MHC_ERR_INVALID_ARG, "%s: batch must be > 0", what);
   cudaStream_t s = (cudaStream_t)stream;
+  if constexpr (sizeof(T) == 4) {
+    if (n > 8)
+      return run_bwd_wide(grad_out, x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
+                          alpha_post, alpha_res, b_res, token_state, grad_x, grad_rmsnorm_weight,
+                          grad_phi_pre, grad_phi_post, grad_phi_res, grad_alpha_pre,
+                          grad_alpha_post, grad_alpha_res, grad_b_pre, grad_b_post, grad_b_res,
+                          batch, n, hidden, sinkhorn_iters, sinkhorn_eps, workspace,
+                          workspace_bytes, s);
+  }
   MHC_DISPATCH_N(n, (run_bwd_dynamic<NN, T>(grad_out, x, rmsnorm_weight, phi_pre, phi_post, phi_res,
                                             alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
                                             token_state, grad_x, grad_rmsnorm_weight, grad_phi_pre,

@@ -37,6 +37,7 @@ struct L {
 
 __host__ __device__ inline int rec_stride(int n) {
   const int raw = 2 + 2 * n + n * n + (n * n + 2 * n);
+  if (n > 8) return (raw + 3) / 4 * 4;  // wide rates keep no Gram block
   const int og = (raw + 1) / 2 * 2;
   return (og + n * (n + 1) + 3) / 4 * 4;
 }

@@ -1,0 +1,531 @@
+// Wide expansion rates (8 < n <= 32) of the dynamic-H layer.
+//
+// At these rates the projection has n^2 + 2n = 99..1088 outputs over nC
+// channels (a real GEMM, not a skinny dot-product pass) and the per-token
+// mixes are n x n mat-vecs over C, so the layer is built from different
+// pieces than the n <= 8 kernels:
+//   fwd : wide_rms (rms_h) -> wide_gemm (P = X phi^T, split-K partials)
+//         -> wide_gates (fixed-order split sum, gates, E = exp(t_res))
+//         -> Sinkhorn (sinkhorn.cu, warp per matrix) -> wide_stream_fwd
+//   bwd : wide_bwd_stream (gy, ghp, RMSNorm reverse, gh, gM, grad_x of the
+//         mix / aggregate, gw terms, E) -> Sinkhorn reverse (sinkhorn.cu)
+//         -> wide_bwd_token (gate derivatives, d_p, per-token rows of the
+//         bias / alpha sums, rms_h coefficient)
+//         -> wide_gemm (grad_x += d_p phi + coef x)
+//         -> wide_gemm (d_phi = d_p^T X) -> wide_colsum (gw, gb, galpha)
+// Every reduction over tokens or splits runs in a fixed order: results are
+// bitwise reproducible.  Token-state record: the n <= 8 layout without the
+// Gram block (rec_stride).
+#pragma once
+
+namespace mhc {
+
+constexpr int WIDE_MAX_N = 32;
+
+// Row-addressed fp32 matrix whose rows may live in up to three tensors (the
+// phi_pre | phi_post | phi_res stack): row r < r1 -> p0, r < r2 -> p1, else p2.
+struct Rows3 {
+  float* p0;
+  float* p1;
+  float* p2;
+  int64_t r1, r2, ld;
+  __device__ __forceinline__ float* row(int64_t r) const {
+    return r < r1 ? p0 + r * ld : (r < r2 ? p1 + (r - r1) * ld : p2 + (r - r2) * ld);
+  }
+};
+inline Rows3 rows1(const float* p, int64_t ld) {
+  return Rows3{const_cast<float*>(p), const_cast<float*>(p), const_cast<float*>(p), INT64_MAX,
+               INT64_MAX, ld};
+}
+inline Rows3 rows3(const float* a, const float* b, const float* c, int64_t r1, int64_t r2,
+                   int64_t ld) {
+  return Rows3{const_cast<float*>(a), const_cast<float*>(b), const_cast<float*>(c), r1, r2, ld};
+}
+
+// ---------------------------------------------------------------------------
+// fp32 GEMM: C(m, n) = sum_k A(m, k) B(n, k), FFMA in k order within a split.
+// 128 x 128 tile, BK = 8, 256 threads with 8 x 8 outputs each, shared-memory
+// double buffer with register staging (one barrier per k-step).
+//   A_KC: A(m, k) = A.row(m)[k] (k contiguous), else A.row(k)[m]
+//   B_KC: B(n, k) = B.row(n)[k],                 else B.row(k)[n]
+//   MODE 0: part[z][m][n] = acc              (split-K partials, row length N)
+//   MODE 1: Cw.row(m)[n] = acc
+//   MODE 2: Cw.row(m)[n] += acc + coef[m] * X.row(m)[n]
+// ---------------------------------------------------------------------------
+constexpr int WG_BM = 128, WG_BN = 128, WG_BK = 8, WG_THREADS = 256;
+
+template <bool A_KC, bool B_KC, int MODE>
+__global__ void __launch_bounds__(WG_THREADS)
+    wide_gemm_kernel(Rows3 A, Rows3 Bm, int64_t M, int64_t N, int64_t K, int64_t kchunk,
+                     float* __restrict__ part, Rows3 Cw, const float* __restrict__ coef, Rows3 X) {
+  __shared__ __align__(16) float As[2][WG_BK][WG_BM];
+  __shared__ __align__(16) float Bs[2][WG_BK][WG_BN];
+  const int tid = threadIdx.x;
+  const int64_t m0 = (int64_t)blockIdx.y * WG_BM, n0 = (int64_t)blockIdx.x * WG_BN;
+  const int64_t kb = (int64_t)blockIdx.z * kchunk;
+  const int64_t ke = kb + kchunk < K ? kb + kchunk : K;
+  float ra[4], rb[4];
+
+  auto load = [&](int64_t k0) {
+    if (A_KC) {
+      const int r = tid >> 1, kk = (tid & 1) * 4;
+      const float* src = (m0 + r < M) ? A.row(m0 + r) : nullptr;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t k = k0 + kk + i;
+        ra[i] = (src && k < ke) ? __ldg(src + k) : 0.f;
+      }
+    } else {
+      const int kk = tid >> 5, c = (tid & 31) * 4;
+      const float* src = (k0 + kk < ke) ? A.row(k0 + kk) : nullptr;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ra[i] = (src && m0 + c + i < M) ? __ldg(src + m0 + c + i) : 0.f;
+    }
+    if (B_KC) {
+      const int r = tid >> 1, kk = (tid & 1) * 4;
+      const float* src = (n0 + r < N) ? Bm.row(n0 + r) : nullptr;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t k = k0 + kk + i;
+        rb[i] = (src && k < ke) ? __ldg(src + k) : 0.f;
+      }
+    } else {
+      const int kk = tid >> 5, c = (tid & 31) * 4;
+      const float* src = (k0 + kk < ke) ? Bm.row(k0 + kk) : nullptr;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rb[i] = (src && n0 + c + i < N) ? __ldg(src + n0 + c + i) : 0.f;
+    }
+  };
+  auto store = [&](int buf) {
+    if (A_KC) {
+      const int r = tid >> 1, kk = (tid & 1) * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) As[buf][kk + i][r] = ra[i];
+    } else {
+      *reinterpret_cast<float4*>(&As[buf][tid >> 5][(tid & 31) * 4]) = make_float4(ra[0], ra[1], ra[2], ra[3]);
+    }
+    if (B_KC) {
+      const int r = tid >> 1, kk = (tid & 1) * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) Bs[buf][kk + i][r] = rb[i];
+    } else {
+      *reinterpret_cast<float4*>(&Bs[buf][tid >> 5][(tid & 31) * 4]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+    }
+  };
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  const int tx = tid & 15, ty = tid >> 4;
+  if (kb < ke) {
+    load(kb);
+    store(0);
+  }
+  __syncthreads();
+  int buf = 0;
+  for (int64_t k0 = kb; k0 < ke; k0 += WG_BK) {
+    const bool more = k0 + WG_BK < ke;
+    if (more) load(k0 + WG_BK);
+#pragma unroll
+    for (int kk = 0; kk < WG_BK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (more) store(buf ^ 1);
+    __syncthreads();
+    buf ^= 1;
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (m >= M) continue;
+    float* dst;
+    const float* xr = nullptr;
+    float cf = 0.f;
+    if (MODE == 0) {
+      dst = part + ((int64_t)blockIdx.z * M + m) * N;
+    } else {
+      dst = Cw.row(m);
+      if (MODE == 2) { xr = X.row(m); cf = coef[m]; }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t nn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+      if (nn >= N) continue;
+      if (MODE == 2) dst[nn] = dst[nn] + acc[i][j] + cf * xr[nn];
+      else dst[nn] = acc[i][j];
+    }
+  }
+}
+
+// Fixed-order sum of S split-K partials [S][M][N] into the MODE 1 / MODE 2
+// destination of wide_gemm_kernel.
+template <int MODE>
+__global__ void __launch_bounds__(256)
+    wide_split_reduce_kernel(const float* __restrict__ part, int S, int64_t M, int64_t N, Rows3 Cw,
+                             const float* __restrict__ coef, Rows3 X) {
+  const int64_t total = M * N;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int z = 0; z < S; ++z) acc += part[z * total + e];
+    const int64_t m = e / N, nn = e - m * N;
+    float* dst = Cw.row(m);
+    if (MODE == 2) dst[nn] = dst[nn] + acc + coef[m] * X.row(m)[nn];
+    else dst[nn] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// forward, per token
+// ---------------------------------------------------------------------------
+
+// rec[0] = rms_h = sqrt(mean(xf^2) + eps)  (compute_rms, ops_pytorch_backward.py:65-75)
+__global__ void __launch_bounds__(256)
+    wide_rms_kernel(const float* __restrict__ x, int64_t nC, float* __restrict__ rec, int RS,
+                    float eps) {
+  __shared__ float red[8];
+  __shared__ float out_s[1];
+  const int64_t b = blockIdx.x;
+  const float* xb = x + b * nC;
+  double s = 0.0;
+  for (int64_t e = threadIdx.x; e < nC; e += blockDim.x) {
+    const float v = xb[e];
+    s += (double)(v * v);
+  }
+  float acc[1] = {(float)s};
+  block_sum_array<1>(acc, red, out_s);
+  if (threadIdx.x == 0) rec[b * RS] = sqrtf(out_s[0] / (float)nC + eps);
+}
+
+// Sums the split-K partials of p in fixed order, stores p and the gates in
+// the record and E = exp(t_res) (the Sinkhorn input) in E[b][n*n].
+__global__ void __launch_bounds__(256)
+    wide_gates_kernel(const float* __restrict__ part, int S, int64_t B, int n,
+                      const float* __restrict__ ap, const float* __restrict__ aq,
+                      const float* __restrict__ ar, const float* __restrict__ bp,
+                      const float* __restrict__ bq, const float* __restrict__ br,
+                      float* __restrict__ rec, int RS, float* __restrict__ E) {
+  const int64_t b = blockIdx.x;
+  const int NH = n * n + 2 * n;
+  float* r = rec + b * RS;
+  const float inv_rh = 1.0f / r[0];
+  const float a0 = *ap, a1 = *aq, a2 = *ar;
+  for (int k = threadIdx.x; k < NH; k += blockDim.x) {
+    float p = 0.f;
+    for (int z = 0; z < S; ++z) p += part[((int64_t)z * B + b) * NH + k];
+    r[2 + 2 * n + n * n + k] = p;
+    if (k < n) {
+      r[2 + k] = sigmoidf_(a0 * p * inv_rh + bp[k]);
+    } else if (k < 2 * n) {
+      r[2 + k] = 2.0f * sigmoidf_(a1 * p * inv_rh + bq[k - n]);
+    } else {
+      E[b * n * n + (k - 2 * n)] = expf(a2 * p * inv_rh + br[k - 2 * n]);
+    }
+  }
+}
+
+// Aggregate, RMSNorm and distribute-mix-add of one token per block:
+//   a = sum_i h_i x_i ; r = sqrt(mean(a^2) + eps) ; y = a / r * w
+//   out_i = hp_i y + sum_j M_ij x_j
+// Copies M (from the Sinkhorn output) into the record and stores r.
+// Dynamic shared memory: NM*NM + 2*NM + C floats.
+template <int NM>
+__global__ void __launch_bounds__(256)
+    wide_stream_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                           const float* __restrict__ Mbuf, float* __restrict__ rec, int RS,
+                           float* __restrict__ out, int n, int64_t C, float eps) {
+  extern __shared__ __align__(16) float wsm[];
+  float* sM = wsm;                 // [NM][NM]
+  float* sh = sM + NM * NM;        // [NM]
+  float* shp = sh + NM;            // [NM]
+  float* sa = shp + NM;            // [C]
+  __shared__ float red[8];
+  __shared__ float tot_s[1];
+  const int64_t b = blockIdx.x;
+  float* r = rec + b * RS;
+  const float* xb = x + b * n * C;
+  for (int e = threadIdx.x; e < NM * NM; e += blockDim.x) {
+    const int i = e / NM, j = e % NM;
+    float v = 0.f;
+    if (i < n && j < n) {
+      v = Mbuf[b * n * n + i * n + j];
+      r[2 + 2 * n + i * n + j] = v;
+    }
+    sM[e] = v;
+  }
+  for (int i = threadIdx.x; i < NM; i += blockDim.x) {
+    sh[i] = i < n ? r[2 + i] : 0.f;
+    shp[i] = i < n ? r[2 + n + i] : 0.f;
+  }
+  __syncthreads();
+  float ss[1] = {0.f};
+  for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+    float a = 0.f;
+    for (int i = 0; i < n; ++i) a += sh[i] * xb[i * C + c];
+    sa[c] = a;
+    ss[0] += a * a;
+  }
+  block_sum_array<1>(ss, red, tot_s);
+  const float rr = sqrtf(tot_s[0] / (float)C + eps);
+  if (threadIdx.x == 0) r[1] = rr;
+  float* ob = out + b * n * C;
+  for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+    const float y = sa[c] / rr * w[c];
+    float xr[NM];
+#pragma unroll
+    for (int j = 0; j < NM; ++j) xr[j] = j < n ? xb[j * C + c] : 0.f;
+    for (int i = 0; i < n; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < NM; j += 4) {
+        const float4 m4 = *reinterpret_cast<const float4*>(&sM[i * NM + j]);
+        acc = fmaf(m4.x, xr[j], acc);
+        acc = fmaf(m4.y, xr[j + 1], acc);
+        acc = fmaf(m4.z, xr[j + 2], acc);
+        acc = fmaf(m4.w, xr[j + 3], acc);
+      }
+      ob[i * C + c] = shp[i] * y + acc;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// backward, per token
+// ---------------------------------------------------------------------------
+
+// One token per block.  Writes
+//   grad_x[i,c] = sum_k M_ki g_k[c] + h_i ga[c]    (mix and aggregate paths)
+//   gwt[b][c]   = gy[c] a[c] / r                    (rows of the weight gradient)
+//   ghh[b]      = [gh (n) | ghp (n)]
+//   gM[b]       = g x^T  (n x n)
+//   E[b]        = exp(t_res) (the Sinkhorn input, from the saved projections)
+// with a = sum h_i x_i, y = a w / r, gy = sum hp_i g_i, ghp_i = <g_i, y>,
+// ga = w gy / r - a S / (C r^3), S = sum gy w a, gh_i = <ga, x_i>.
+// Dynamic shared memory: NM*NM + 2*NM + 2*NM*33 + 2*C floats.
+template <int NM>
+__global__ void __launch_bounds__(256)
+    wide_bwd_stream_kernel(const float* __restrict__ g, const float* __restrict__ x,
+                           const float* __restrict__ w, const float* __restrict__ rec, int RS,
+                           const float* __restrict__ ar, const float* __restrict__ br, int n,
+                           int64_t C, float* __restrict__ gx, float* __restrict__ gwt,
+                           float* __restrict__ ghh, float* __restrict__ gM,
+                           float* __restrict__ E) {
+  extern __shared__ __align__(16) float wsm[];
+  float* sM = wsm;                 // [NM][NM]
+  float* sh = sM + NM * NM;
+  float* shp = sh + NM;
+  float* sg = shp + NM;            // [NM][33] chunk of g
+  float* sx = sg + NM * 33;        // [NM][33] chunk of x
+  float* sa = sx + NM * 33;        // [C]
+  float* sgy = sa + C;             // [C]
+  __shared__ float red[8 * (NM + 1)];
+  __shared__ float tot_s[NM + 1];
+  const int64_t b = blockIdx.x;
+  const float* r = rec + b * RS;
+  const float* xb = x + b * n * C;
+  const float* gb = g + b * n * C;
+  const int nn = n * n;
+  for (int e = threadIdx.x; e < NM * NM; e += blockDim.x) {
+    const int i = e / NM, j = e % NM;
+    sM[e] = (i < n && j < n) ? r[2 + 2 * n + i * n + j] : 0.f;
+  }
+  for (int i = threadIdx.x; i < NM; i += blockDim.x) {
+    sh[i] = i < n ? r[2 + i] : 0.f;
+    shp[i] = i < n ? r[2 + n + i] : 0.f;
+  }
+  {
+    const float inv_rh = 1.0f / r[0], a2 = *ar;
+    for (int e = threadIdx.x; e < nn; e += blockDim.x)
+      E[b * nn + e] = expf(a2 * r[2 + 2 * n + nn + 2 * n + e] * inv_rh + br[e]);
+  }
+  __syncthreads();
+  const float rr = r[1];
+  const float inv_r = 1.0f / rr;
+
+  // pass 1: a, gy, S, ghp, gw rows
+  float acc1[NM + 1];
+#pragma unroll
+  for (int i = 0; i <= NM; ++i) acc1[i] = 0.f;
+  for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+    float a = 0.f, gy = 0.f;
+    float gr[NM];
+#pragma unroll
+    for (int i = 0; i < NM; ++i) {
+      gr[i] = i < n ? gb[i * C + c] : 0.f;
+      if (i < n) {
+        a += sh[i] * xb[i * C + c];
+        gy += shp[i] * gr[i];
+      }
+    }
+    const float wc = w[c];
+    const float y = a * inv_r * wc;
+    sa[c] = a;
+    sgy[c] = gy;
+    gwt[b * C + c] = gy * a * inv_r;
+    acc1[NM] += gy * wc * a;
+#pragma unroll
+    for (int i = 0; i < NM; ++i) acc1[i] += gr[i] * y;
+  }
+  block_sum_array<NM + 1>(acc1, red, tot_s);
+  const float S = tot_s[NM];
+  if (threadIdx.x < n) ghh[b * 2 * n + n + threadIdx.x] = tot_s[threadIdx.x];
+  const float sc = S / ((float)C * rr * rr * rr);
+  __syncthreads();  // tot_s is reused below
+
+  // pass 2: ga, gh, grad_x
+  float acc2[NM];
+#pragma unroll
+  for (int i = 0; i < NM; ++i) acc2[i] = 0.f;
+  float* gxb = gx + b * n * C;
+  for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+    const float ga = w[c] * sgy[c] * inv_r - sa[c] * sc;
+    float gr[NM];
+#pragma unroll
+    for (int k = 0; k < NM; ++k) gr[k] = k < n ? gb[k * C + c] : 0.f;
+#pragma unroll
+    for (int i = 0; i < NM; ++i) {
+      if (i < n) {
+        acc2[i] = fmaf(ga, xb[i * C + c], acc2[i]);
+        float mix = 0.f;
+#pragma unroll
+        for (int k = 0; k < NM; ++k) mix = fmaf(sM[k * NM + i], gr[k], mix);
+        gxb[i * C + c] = mix + sh[i] * ga;
+      }
+    }
+  }
+  block_sum_array<NM>(acc2, red, tot_s);
+  if (threadIdx.x < n) ghh[b * 2 * n + threadIdx.x] = tot_s[threadIdx.x];
+
+  // pass 3: gM = g x^T over 32-channel chunks
+  constexpr int PAIRS = (NM * NM + 255) / 256;
+  float accm[PAIRS];
+#pragma unroll
+  for (int q = 0; q < PAIRS; ++q) accm[q] = 0.f;
+  for (int64_t c0 = 0; c0 < C; c0 += 32) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < NM * 32; e += blockDim.x) {
+      const int i = e >> 5, cc = e & 31;
+      const bool ok = i < n && c0 + cc < C;
+      sg[i * 33 + cc] = ok ? gb[i * C + c0 + cc] : 0.f;
+      sx[i * 33 + cc] = ok ? xb[i * C + c0 + cc] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < PAIRS; ++q) {
+      const int pr = threadIdx.x + 256 * q;
+      if (pr < NM * NM) {
+        const int i = pr / NM, j = pr % NM;
+        float s = accm[q];
+#pragma unroll 8
+        for (int cc = 0; cc < 32; ++cc) s = fmaf(sg[i * 33 + cc], sx[j * 33 + cc], s);
+        accm[q] = s;
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < PAIRS; ++q) {
+    const int pr = threadIdx.x + 256 * q;
+    if (pr < NM * NM) {
+      const int i = pr / NM, j = pr % NM;
+      if (i < n && j < n) gM[b * nn + i * n + j] = accm[q];
+    }
+  }
+}
+
+// Gate derivatives and projection gradient of one token per block:
+//   gt = gh h (1 - h) | ghp hp (1 - hp/2) | gE E ;  d_p = alpha gt / rms_h
+//   GP[b][k] = d_p ; rows[b] = [gt (NH) | sum gt p / rms_h per group (3)]
+//   coef[b] = d rms_h / (nC rms_h), d rms_h = -sum gt alpha p / rms_h^2
+__global__ void __launch_bounds__(128)
+    wide_bwd_token_kernel(const float* __restrict__ rec, int RS, const float* __restrict__ ghh,
+                          const float* __restrict__ gE, const float* __restrict__ E,
+                          const float* __restrict__ ap, const float* __restrict__ aq,
+                          const float* __restrict__ ar, int n, int64_t nC,
+                          float* __restrict__ GP, float* __restrict__ rows,
+                          float* __restrict__ coef) {
+  __shared__ float red[4 * 4];
+  __shared__ float tot_s[4];
+  const int64_t b = blockIdx.x;
+  const int NH = n * n + 2 * n, nn = n * n;
+  const float* r = rec + b * RS;
+  const float rh = r[0], inv_rh = 1.0f / rh;
+  const float al[3] = {*ap, *aq, *ar};
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k = threadIdx.x; k < NH; k += blockDim.x) {
+    const float p = r[2 + 2 * n + nn + k];
+    float gt;
+    int grp;
+    if (k < n) {
+      const float h = r[2 + k];
+      gt = ghh[b * 2 * n + k] * h * (1.0f - h);
+      grp = 0;
+    } else if (k < 2 * n) {
+      const float hp = r[2 + k];
+      gt = ghh[b * 2 * n + k] * hp * (1.0f - 0.5f * hp);
+      grp = 1;
+    } else {
+      gt = gE[b * nn + k - 2 * n] * E[b * nn + k - 2 * n];
+      grp = 2;
+    }
+    GP[b * NH + k] = al[grp] * gt * inv_rh;
+    rows[b * (NH + 3) + k] = gt;
+    const float tp = gt * p * inv_rh;
+    acc[grp] += tp;
+    acc[3] -= al[grp] * tp * inv_rh;
+  }
+  block_sum_array<4>(acc, red, tot_s);
+  if (threadIdx.x < 3) rows[b * (NH + 3) + NH + threadIdx.x] = tot_s[threadIdx.x];
+  if (threadIdx.x == 0) coef[b] = tot_s[3] / ((float)nC * rh);
+}
+
+// Fixed-order column sums of src [R][W] (row stride ld) into out[W]: each
+// block owns 32 columns, 8 row groups accumulate in fp64 and are combined in
+// group order.
+__global__ void __launch_bounds__(256)
+    wide_colsum_kernel(const float* __restrict__ src, int64_t R, int64_t W, int64_t ld,
+                       float* __restrict__ out) {
+  __shared__ double part[8][32];
+  const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int64_t col = (int64_t)blockIdx.x * 32 + lane;
+  double s = 0.0;
+  if (col < W)
+    for (int64_t rr = grp; rr < R; rr += 8) s += (double)src[rr * ld + col];
+  part[grp][lane] = s;
+  __syncthreads();
+  if (grp == 0 && col < W) {
+    double t = 0.0;
+    for (int q = 0; q < 8; ++q) t += part[q][lane];
+    out[col] = (float)t;
+  }
+}
+
+// tot = [gb_pre (n) | gb_post (n) | gb_res (n^2) | galpha (3)] -> parameter gradients
+__global__ void wide_param_finalize_kernel(const float* __restrict__ tot, int n,
+                                           float* __restrict__ gbp, float* __restrict__ gbq,
+                                           float* __restrict__ gbr, float* __restrict__ gap,
+                                           float* __restrict__ gaq, float* __restrict__ gar) {
+  const int NH = n * n + 2 * n;
+  for (int k = threadIdx.x; k < NH + 3; k += blockDim.x) {
+    const float v = tot[k];
+    if (k < n) gbp[k] = v;
+    else if (k < 2 * n) gbq[k - n] = v;
+    else if (k < NH) gbr[k - 2 * n] = v;
+    else if (k == NH) *gap = v;
+    else if (k == NH + 1) *gaq = v;
+    else *gar = v;
+  }
+}
+
+}  // namespace mhc

@@ -32,7 +32,8 @@ class MHCLayer(nn.Module):
 
     Args:
         hidden_dim: hidden size C
-        expansion_rate: number of residual streams n (1..8 on the fused path)
+        expansion_rate: number of residual streams n (1..32; the fused kernels
+            for n <= 8, the wide-rate kernels for 8 < n <= 32)
         num_sinkhorn_iters: Sinkhorn-Knopp iterations
         sinkhorn_eps: Sinkhorn epsilon
         rmsnorm_eps: epsilon of both RMS computations (dynamic-H rms and RMSNorm)
@@ -88,6 +89,16 @@ class MHCLayer(nn.Module):
                 return mhc_layer_fused_dynamic_inference(xin, *args, bf16_io=bf16)
             return mhc_layer_fused_dynamic_training(xin, *args, bf16_io=bf16)
         hp = (self.num_sinkhorn_iters, self.sinkhorn_eps, self.rmsnorm_eps)
+        if n > 8:
+            # the fused static kernels cover n <= 8; wider rates run the
+            # reference's own composition (layer.py:142-170) over this
+            # library's CUDA operators, with one Sinkhorn for the shared H_res
+            xf = x.float()
+            M = sinkhorn_knopp(torch.exp(self.H_res.float()).unsqueeze(0), hp[0], hp[1])
+            y = rmsnorm(stream_aggregate(xf, self.H_pre.unsqueeze(0).expand(B, -1)),
+                        self.rmsnorm_weight, hp[2])
+            return stream_distribute_mix_add(y, self.H_post.unsqueeze(0).expand(B, -1),
+                                             M.expand(B, -1, -1), xf)
         if not torch.is_grad_enabled() or not (x.requires_grad or any(
                 p.requires_grad for p in (self.rmsnorm_weight, self.H_pre, self.H_post,
                                           self.H_res))):

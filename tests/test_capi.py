@@ -49,9 +49,13 @@ def test_validation_errors_without_gpu():
     assert lib.mhc_sinkhorn_knopp_fwd(p, p, 4, 4, -1, 1e-8, None) == ERR_INVALID
     assert lib.mhc_sinkhorn_knopp_fwd(None, p, 4, 4, 20, 1e-8, None) == ERR_INVALID
     assert lib.mhc_rmsnorm_fwd(p, p, p, None, 4, 8, 1e-5, None) == ERR_INVALID
-    args = [p] * 13 + [8, 9, 64, 20, 1e-8, 1e-5, p, 1 << 30, None]
+    args = [p] * 13 + [8, 33, 64, 20, 1e-8, 1e-5, p, 1 << 30, None]
     assert lib.mhc_layer_fwd_dynamic(*args) == ERR_UNSUPPORTED
     assert "expansion_rate" in _C.last_error()
+    args = [p] * 13 + [8, 9, 64, 20, 1e-8, 1e-5, p, 1 << 30, None]
+    assert lib.mhc_layer_fwd_dynamic_bf16(*args) == ERR_UNSUPPORTED  # bf16 streams: n <= 8
+    args = [p] * 13 + [8, 16, 64, 20, 1e-8, 1e-5, p, 0, None]
+    assert lib.mhc_layer_fwd_dynamic(*args) == ERR_WORKSPACE  # wide rates plan a workspace too
     args = [p] * 13 + [8, 4, 64, 20, 1e-8, 1e-5, p, 0, None]
     assert lib.mhc_layer_fwd_dynamic(*args) == ERR_WORKSPACE
     assert "workspace" in _C.last_error()
@@ -74,5 +78,6 @@ def test_workspace_queries():
     assert 0 < fwd < 64 << 20
     assert 0 < bwd < 512 << 20
     assert lib.mhc_token_state_stride(4) == 72  # 50 record floats + padding + fp64 Gram (10 doubles)
+    assert lib.mhc_token_state_stride(32) == 2180  # 2 + 2n + n^2 + (n^2 + 2n) = 2178, 4-aligned; no Gram
     assert lib.mhc_layer_static_workspace_bytes(65536, 4, 4096) > 0
     assert lib.mhc_rmsnorm_bwd_workspace_bytes(1024, 4096) >= 4096 * 4

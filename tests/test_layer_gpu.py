@@ -70,6 +70,12 @@ def oracle_case(B, n, C, seed, alpha=0.01, bias_std=0.0, weight=None):
     (4, 1, 64, 1.0, 1.0),
     (2, 6, 72, 0.5, 0.5),
     (1, 4, 32, 1.0, 1.0),         # single token
+    # wide expansion rates (GEMM projection, warp Sinkhorn, n x n mixes)
+    (9, 16, 64, 0.5, 0.5),
+    (5, 32, 96, 1.0, 1.0),
+    (130, 12, 40, 0.5, 0.5),      # tokens span two GEMM row tiles
+    (3, 9, 33, 1.0, 1.0),         # odd n, odd C
+    (32, 32, 1280, 0.01, 0.0),    # the reference's paper shape (benchmark.py:302-312)
 ])
 def test_dynamic_vs_oracle(cuda, B, n, C, alpha, bias):
     x, params, grad = oracle_case(B, n, C, seed=B * 7 + n * 13 + C, alpha=alpha, bias_std=bias,
@@ -95,9 +101,10 @@ def test_dynamic_inference_matches_training_forward(cuda):
     assert torch.equal(out_train.detach(), out_inf)
 
 
-def test_dynamic_backward_is_deterministic(cuda):
-    x, params, grad = oracle_case(512, 4, 1024, seed=9)
-    layer = make_layer(params, 4, 1024, cuda)
+@pytest.mark.parametrize("B,n,C", [(512, 4, 1024), (64, 32, 256)])
+def test_dynamic_backward_is_deterministic(cuda, B, n, C):
+    x, params, grad = oracle_case(B, n, C, seed=9)
+    layer = make_layer(params, n, C, cuda)
     _, g1 = run_layer(layer, x.to(cuda), grad.to(cuda))
     layer.zero_grad()
     _, g2 = run_layer(layer, x.to(cuda), grad.to(cuda))
@@ -147,7 +154,7 @@ def test_static_golden(cuda):
 
 
 @pytest.mark.parametrize("B,n,C", [(64, 4, 4096), (7, 4, 7168), (3, 8, 100), (5, 2, 4097),
-                                   (2, 4, 20000)])
+                                   (2, 4, 20000), (6, 16, 96), (4, 32, 64), (3, 9, 33)])
 def test_static_vs_oracle(cuda, B, n, C):
     gen = torch.Generator().manual_seed(B + C)
     x = torch.randn(B, n, C, generator=gen)
