@@ -57,65 +57,90 @@ __global__ void __launch_bounds__(128) sk_bwd_thread_kernel(const float* __restr
 
 constexpr int WARPS_PER_BLOCK = 4;
 
-// One matrix per warp, lane j holds column j (rows 0..n-1), n <= 32.
-__device__ __forceinline__ void warp_sk_step(float (&a)[32], int n, int lane, float eps,
-                                             float* dr, float* dc) {
-  const bool active = lane < n;
-  for (int i = 0; i < n; ++i) {
-    const float s = warp_sum(active ? a[i] : 0.f);
-    const float d = s + eps;
-    if (dr && lane == 0) dr[i] = d;
-    if (active) a[i] = a[i] / d;
+// One matrix per warp, lane j holds column j (rows 0..n-1), n <= NM <= 32.
+// Loops run over the compile-time NM with `i < n` guards, so the rows stay
+// in registers.
+//
+// Row sums use a transpose-reduce: recursive halving over the lane bits
+// (16 + 8 + 4 + 2 + 1 = 31 shuffles for 32 rows) leaves lane l holding the
+// sum of row l over all lanes; that lane forms the row's denominator and
+// reciprocal once and the warp reads them back with one shuffle per row.
+// (A butterfly per row costs 5 shuffles per row and a division per element.)
+// Rows beyond NM are zero-padded to 32.
+template <int NM, typename T>
+__device__ __forceinline__ T warp_row_sums_to_lanes(const T (&v)[NM], int lane) {
+  T w[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) w[k] = k < NM ? v[k] : T(0);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int k = 0; k < o; ++k) {
+      const T send = up ? w[k] : w[k + o];
+      const T keep = up ? w[k + o] : w[k];
+      w[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
   }
-  float s = 0.f;
-  for (int i = 0; i < n; ++i) s += a[i];
-  const float d = s + eps;
-  if (dc && active) dc[lane] = d;
-  if (active)
-    for (int i = 0; i < n; ++i) a[i] = a[i] / d;
+  return w[0];  // sum of row `lane`
 }
 
+template <int NM, typename T>
+__device__ __forceinline__ void warp_sk_step(T (&a)[NM], int n, int lane, T eps, T* dr, T* dc) {
+  const bool active = lane < n;
+  {
+    T v[NM];
+#pragma unroll
+    for (int i = 0; i < NM; ++i) v[i] = (i < n && active) ? a[i] : T(0);
+    const T d_mine = warp_row_sums_to_lanes<NM, T>(v, lane) + eps;
+    const T inv_mine = T(1) / d_mine;
+    if (dr && lane < n) dr[lane] = d_mine;
+#pragma unroll
+    for (int i = 0; i < NM; ++i)
+      if (i < n) {
+        const T inv_i = __shfl_sync(0xffffffffu, inv_mine, i);  // every lane takes part
+        a[i] = active ? a[i] * inv_i : T(0);
+      }
+  }
+  T s = 0;
+#pragma unroll
+  for (int i = 0; i < NM; ++i)
+    if (i < n) s += a[i];
+  const T d = s + eps;
+  if (dc && active) dc[lane] = d;
+  if (active) {
+    const T inv = T(1) / d;
+#pragma unroll
+    for (int i = 0; i < NM; ++i)
+      if (i < n) a[i] = a[i] * inv;
+  }
+}
+
+template <int NM>
 __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32)
     sk_fwd_warp_kernel(const float* __restrict__ inp, float* __restrict__ out, int64_t batch,
                        int n, int iters, float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t b = (int64_t)blockIdx.x * WARPS_PER_BLOCK + (threadIdx.x >> 5);
   if (b >= batch) return;
-  float a[32];
+  float a[NM];
   const float* src = inp + b * n * n;
-  for (int i = 0; i < n; ++i) a[i] = lane < n ? src[i * n + lane] : 0.f;
-  for (int t = 0; t < iters; ++t) warp_sk_step(a, n, lane, eps, nullptr, nullptr);
+#pragma unroll
+  for (int i = 0; i < NM; ++i) a[i] = (i < n && lane < n) ? src[i * n + lane] : 0.f;
+  for (int t = 0; t < iters; ++t) warp_sk_step<NM, float>(a, n, lane, eps, nullptr, nullptr);
   float* dst = out + b * n * n;
-  if (lane < n)
-    for (int i = 0; i < n; ++i) dst[i * n + lane] = a[i];
+  if (lane < n) {
+#pragma unroll
+    for (int i = 0; i < NM; ++i)
+      if (i < n) dst[i * n + lane] = a[i];
+  }
 }
 
 // Reverse mode runs in fp64 (the doubly-stochastic projection cancels the
 // row/column-constant part of the incoming gradient).
 constexpr int BWD_WARPS = 2;
 
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-__device__ __forceinline__ void warp_sk_step_d(double (&a)[32], int n, int lane, double eps,
-                                               double* dr, double* dc) {
-  const bool active = lane < n;
-  for (int i = 0; i < n; ++i) {
-    const double d = warp_sum_d(active ? a[i] : 0.0) + eps;
-    if (dr && lane == 0) dr[i] = d;
-    if (active) a[i] = a[i] / d;
-  }
-  double s = 0.0;
-  for (int i = 0; i < n; ++i) s += a[i];
-  const double d = s + eps;
-  if (dc && active) dc[lane] = d;
-  if (active)
-    for (int i = 0; i < n; ++i) a[i] = a[i] / d;
-}
-
+template <int NM>
 __global__ void __launch_bounds__(BWD_WARPS * 32)
     sk_bwd_warp_kernel(const float* __restrict__ grad_out, const float* __restrict__ inp,
                        float* __restrict__ grad_inp, int64_t batch, int n, int iters,
@@ -127,41 +152,64 @@ __global__ void __launch_bounds__(BWD_WARPS * 32)
   const int64_t b = (int64_t)blockIdx.x * BWD_WARPS + w;
   if (b >= batch) return;
   const bool active = lane < n;
-  double g[32], z[32];
+  double g[NM], z[NM];
   const float* src = inp + b * n * n;
   const float* gsrc = grad_out + b * n * n;
-  for (int i = 0; i < n; ++i) g[i] = active ? gsrc[i * n + lane] : 0.f;
+#pragma unroll
+  for (int i = 0; i < NM; ++i) g[i] = (i < n && active) ? gsrc[i * n + lane] : 0.0;
   int seg_end = iters;
   while (seg_end > 0) {
     const int seg_start = seg_end > SK_SEG ? seg_end - SK_SEG : 0;
-    for (int i = 0; i < n; ++i) z[i] = active ? src[i * n + lane] : 0.f;
-    for (int t = 0; t < seg_start; ++t) warp_sk_step_d(z, n, lane, eps, nullptr, nullptr);
+#pragma unroll
+    for (int i = 0; i < NM; ++i) z[i] = (i < n && active) ? src[i * n + lane] : 0.0;
+    for (int t = 0; t < seg_start; ++t) warp_sk_step<NM, double>(z, n, lane, eps, nullptr, nullptr);
     for (int t = seg_start; t < seg_end; ++t)
-      warp_sk_step_d(z, n, lane, eps, s_dr[w][t - seg_start], s_dc[w][t - seg_start]);
+      warp_sk_step<NM, double>(z, n, lane, eps, s_dr[w][t - seg_start], s_dc[w][t - seg_start]);
     __syncwarp();
     for (int t = seg_end - 1; t >= seg_start; --t) {
       // column step
       const double dcj = active ? s_dc[w][t - seg_start][lane] : 1.0;
       double s = 0.0;
-      for (int i = 0; i < n; ++i) s += g[i] * z[i];
-      for (int i = 0; i < n; ++i) {
-        g[i] = active ? (g[i] - s) / dcj : 0.0;
-        z[i] = z[i] * dcj;
+#pragma unroll
+      for (int i = 0; i < NM; ++i)
+        if (i < n) s += g[i] * z[i];
+      const double inv = 1.0 / dcj;
+#pragma unroll
+      for (int i = 0; i < NM; ++i) {
+        if (i < n) {
+          g[i] = active ? (g[i] - s) * inv : 0.0;
+          z[i] = z[i] * dcj;
+        }
       }
-      // row step
-      for (int i = 0; i < n; ++i) {
-        const double d = s_dr[w][t - seg_start][i];
-        const double si = warp_sum_d(active ? g[i] * z[i] : 0.0);
-        g[i] = active ? (g[i] - si) / d : 0.0;
-        z[i] = z[i] * d;
+      // row step: lane l reduces row l, then broadcasts its sum and 1/d
+      {
+        double v[NM];
+#pragma unroll
+        for (int i = 0; i < NM; ++i) v[i] = (i < n && active) ? g[i] * z[i] : 0.0;
+        const double si_mine = warp_row_sums_to_lanes<NM, double>(v, lane);
+        const double d_mine = lane < n ? s_dr[w][t - seg_start][lane] : 1.0;
+        const double inv_mine = 1.0 / d_mine;
+#pragma unroll
+        for (int i = 0; i < NM; ++i) {
+          if (i < n) {
+            const double si = __shfl_sync(0xffffffffu, si_mine, i);
+            const double d = __shfl_sync(0xffffffffu, d_mine, i);
+            const double inv = __shfl_sync(0xffffffffu, inv_mine, i);
+            g[i] = active ? (g[i] - si) * inv : 0.0;
+            z[i] = z[i] * d;
+          }
+        }
       }
     }
     __syncwarp();
     seg_end = seg_start;
   }
   float* dst = grad_inp + b * n * n;
-  if (active)
-    for (int i = 0; i < n; ++i) dst[i * n + lane] = (float)g[i];
+  if (active) {
+#pragma unroll
+    for (int i = 0; i < NM; ++i)
+      if (i < n) dst[i * n + lane] = (float)g[i];
+  }
 }
 
 template <int N>
@@ -217,8 +265,11 @@ extern "C" int mhc_sinkhorn_knopp_fwd(const float* inp, float* out, int64_t batc
     case 8: return launch_thread_fwd<8>(inp, out, batch, num_iters, eps, s);
     default: {
       const int64_t blocks = (batch + WARPS_PER_BLOCK - 1) / WARPS_PER_BLOCK;
-      sk_fwd_warp_kernel<<<(unsigned)blocks, WARPS_PER_BLOCK * 32, 0, s>>>(inp, out, batch, n,
-                                                                           num_iters, eps);
+      ProfScope _ps("sinkhorn_fwd", s);
+      if (n <= 16)
+        sk_fwd_warp_kernel<16><<<(unsigned)blocks, WARPS_PER_BLOCK * 32, 0, s>>>(inp, out, batch, n, num_iters, eps);
+      else
+        sk_fwd_warp_kernel<32><<<(unsigned)blocks, WARPS_PER_BLOCK * 32, 0, s>>>(inp, out, batch, n, num_iters, eps);
       return check_launch("sinkhorn_knopp_fwd");
     }
   }
@@ -244,8 +295,11 @@ extern "C" int mhc_sinkhorn_knopp_bwd(const float* grad_out, const float* inp, c
     case 8: return launch_thread_bwd<8>(grad_out, inp, grad_inp, batch, num_iters, eps, s);
     default: {
       const int64_t blocks = (batch + BWD_WARPS - 1) / BWD_WARPS;
-      sk_bwd_warp_kernel<<<(unsigned)blocks, BWD_WARPS * 32, 0, s>>>(
-          grad_out, inp, grad_inp, batch, n, num_iters, eps);
+      ProfScope _ps("sinkhorn_bwd", s);
+      if (n <= 16)
+        sk_bwd_warp_kernel<16><<<(unsigned)blocks, BWD_WARPS * 32, 0, s>>>(grad_out, inp, grad_inp, batch, n, num_iters, eps);
+      else
+        sk_bwd_warp_kernel<32><<<(unsigned)blocks, BWD_WARPS * 32, 0, s>>>(grad_out, inp, grad_inp, batch, n, num_iters, eps);
       return check_launch("sinkhorn_knopp_bwd");
     }
   }

@@ -31,7 +31,11 @@ def test_sinkhorn_golden(cuda, case):
 
 
 @pytest.mark.parametrize("B,N,iters", [(65536, 4, 20), (1, 4, 20), (7, 3, 50), (5, 32, 20),
-                                       (9, 5, 0), (3, 8, 1)])
+                                       (9, 5, 0), (3, 8, 1),
+                                       # warp-per-matrix sizes with idle lanes, several blocks,
+                                       # and more iterations than one saved segment
+                                       (6, 12, 20), (4, 17, 33), (3, 31, 20), (2, 9, 5),
+                                       (41, 16, 20)])
 def test_sinkhorn_oracle(cuda, B, N, iters):
     gen = torch.Generator().manual_seed(B * 31 + N)
     inp = torch.rand(B, N, N, generator=gen)
