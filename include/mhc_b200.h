@@ -129,6 +129,28 @@ MHC_API int mhc_fused_rmsnorm_matmul_bwd(const float* grad_out, const float* inp
                                  void* stream);
 
 /* ---------------------------------------------------------------------------
+ * MHCResidualWrapper stream packing and stream mean (replace the framework ops
+ * of layer.py:287-316; the reference has no native counterpart).  Tokens are
+ * the flattened leading dims, x is [tokens, n, hidden] fp32, n <= 64.
+ * scales: host array of n floats; stream i (i != 1) is scales[i] * residual
+ * (scales[0] is taken as 1; "decay" mode passes 0.1^(i-1), "zero" mode 0, and
+ * a zero scale writes 0).  Stream 1 is the branch output.
+ * ------------------------------------------------------------------------- */
+MHC_API int mhc_wrapper_pack_fwd(const float* residual, const float* branch, float* out,
+                                 const float* scales, int64_t tokens, int32_t n, int64_t hidden,
+                                 void* stream);
+/* grad_residual = sum_{i != 1} scales[i] * grad[:, i]; grad_branch = grad[:, 1] (may be NULL) */
+MHC_API int mhc_wrapper_pack_bwd(const float* grad_out, float* grad_residual, float* grad_branch,
+                                 const float* scales, int64_t tokens, int32_t n, int64_t hidden,
+                                 void* stream);
+/* out[t, c] = mean_i inp[t, i, c]  (MHCResidualWrapper's output.mean(dim=1)) */
+MHC_API int mhc_stream_mean_fwd(const float* inp, float* out, int64_t tokens, int32_t n,
+                                int64_t hidden, void* stream);
+/* grad_inp[t, i, c] = grad_out[t, c] / n */
+MHC_API int mhc_stream_mean_bwd(const float* grad_out, float* grad_inp, int64_t tokens, int32_t n,
+                                int64_t hidden, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Fused mHC layer, dynamic H.
  *
  * Per-token record saved by the forward for the backward ("token_state",

@@ -41,6 +41,10 @@ SIGNATURES = {
     "mhc_fused_rmsnorm_matmul_bwd_workspace_bytes": (_SZ, [_I64, _I64, _I32]),
     "mhc_fused_rmsnorm_matmul_bwd": (ctypes.c_int,
                                      [_P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _SZ, _P]),
+    "mhc_wrapper_pack_fwd": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I64, _P]),
+    "mhc_wrapper_pack_bwd": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I64, _P]),
+    "mhc_stream_mean_fwd": (ctypes.c_int, [_P, _P, _I64, _I32, _I64, _P]),
+    "mhc_stream_mean_bwd": (ctypes.c_int, [_P, _P, _I64, _I32, _I64, _P]),
     "mhc_token_state_stride": (_I32, [_I32]),
     "mhc_layer_fwd_dynamic_workspace_bytes": (_SZ, [_I64, _I32, _I64]),
     "mhc_layer_fwd_dynamic": (ctypes.c_int,

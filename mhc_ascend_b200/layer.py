@@ -22,6 +22,8 @@ from .ops import (
     sinkhorn_knopp,
     stream_aggregate,
     stream_distribute_mix_add,
+    stream_mean,
+    wrapper_pack,
 )
 
 __all__ = ["MHCLayer", "create_mhc_layer", "MHCResidualWrapper", "replace_residual_with_mhc"]
@@ -154,15 +156,10 @@ class MHCResidualWrapper(nn.Module):
             B, C = original_shape
             T = 1
         n = self.expansion_rate
-        if self.residual_mode == "zero":
-            extra = [torch.zeros_like(residual)] * max(n - 2, 0)
-        elif self.residual_mode == "decay":
-            extra = [residual * (0.1 ** (i - 1)) for i in range(2, n)]
-        else:
-            raise ValueError(f"Unknown residual_mode: {self.residual_mode}")
-        streams = [residual, branch_output] + extra
-        mhc_input = torch.stack(streams[:n], dim=1) if n >= 2 else residual.unsqueeze(1)
-        output = self.mhc(mhc_input).mean(dim=1)
+        # one CUDA pass packs the streams, one averages them (the reference
+        # runs n - 1 scalings, a stack and a mean as framework ops)
+        mhc_input = wrapper_pack(residual, branch_output, n, self.residual_mode)
+        output = stream_mean(self.mhc(mhc_input))
         if T > 1:
             output = output.reshape(B, T, C)
         return output

@@ -22,6 +22,8 @@ from __future__ import annotations
 
 from typing import Tuple
 
+import ctypes
+
 import torch
 
 from . import _C
@@ -380,6 +382,94 @@ def compute_rms(x_flat: torch.Tensor, eps: float = 1e-8) -> torch.Tensor:
                                       float(eps), _stream(x.device))
     _C.check(rc, "compute_rms")
     return rms
+
+
+# =============================================================================
+# MHCResidualWrapper stream packing and stream mean (reference layer.py:287-316)
+# =============================================================================
+
+def wrapper_stream_scales(n: int, residual_mode: str = "decay"):
+    """Per-stream residual scales of MHCResidualWrapper: stream 0 is the
+    residual, stream 1 the branch output, streams i >= 2 are
+    residual * 0.1 ** (i - 1) ("decay", the reference's Python-float factor
+    applied in fp32) or zeros ("zero")."""
+    if residual_mode == "decay":
+        vals = [1.0, 0.0] + [0.1 ** (i - 1) for i in range(2, n)]
+    elif residual_mode == "zero":
+        vals = [1.0, 0.0] + [0.0] * max(n - 2, 0)
+    else:
+        raise ValueError(f"Unknown residual_mode: {residual_mode}")
+    return (ctypes.c_float * max(n, 1))(*vals[:max(n, 1)])
+
+
+class WrapperPackFunction(torch.autograd.Function):
+    """[T, C] residual and branch -> [T, n, C] mHC input in one pass."""
+
+    @staticmethod
+    def forward(ctx, residual, branch, n, residual_mode):
+        sc = wrapper_stream_scales(n, residual_mode)  # unknown modes: ValueError first
+        _require_cuda("wrapper_pack", residual, branch)
+        r, b = _f32(residual), _f32(branch)
+        T, C = r.shape
+        out = torch.empty(T, n, C, dtype=torch.float32, device=r.device)
+        with _DevGuard(r):
+            rc = _lib.mhc_wrapper_pack_fwd(r.data_ptr(), b.data_ptr(), out.data_ptr(), sc, T, n,
+                                           C, _stream(r.device))
+        _C.check(rc, "mhc_wrapper_pack_fwd")
+        ctx.n, ctx.sc, ctx.dtypes = n, sc, (residual.dtype, branch.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        g = _f32(grad_out)
+        T, n, C = g.shape
+        gr = torch.empty(T, C, dtype=torch.float32, device=g.device)
+        gb = torch.empty(T, C, dtype=torch.float32, device=g.device) if n >= 2 else None
+        with _DevGuard(g):
+            rc = _lib.mhc_wrapper_pack_bwd(g.data_ptr(), gr.data_ptr(),
+                                           gb.data_ptr() if n >= 2 else None, ctx.sc, T, n, C,
+                                           _stream(g.device))
+        _C.check(rc, "mhc_wrapper_pack_bwd")
+        # at n == 1 the branch output is not an input of the layer: no gradient
+        return gr.to(ctx.dtypes[0]), (gb.to(ctx.dtypes[1]) if gb is not None else None), None, None
+
+
+def wrapper_pack(residual: torch.Tensor, branch: torch.Tensor, n: int,
+                 residual_mode: str = "decay") -> torch.Tensor:
+    """Stream packing of MHCResidualWrapper.forward (reference layer.py:300-310)."""
+    return WrapperPackFunction.apply(residual, branch, n, residual_mode)
+
+
+class StreamMeanFunction(torch.autograd.Function):
+    """[T, n, C] -> [T, C] mean over the streams (reference layer.py:312)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        _require_cuda("stream_mean", x)
+        xf = _f32(x)
+        T, n, C = xf.shape
+        out = torch.empty(T, C, dtype=torch.float32, device=xf.device)
+        with _DevGuard(xf):
+            rc = _lib.mhc_stream_mean_fwd(xf.data_ptr(), out.data_ptr(), T, n, C,
+                                          _stream(xf.device))
+        _C.check(rc, "mhc_stream_mean_fwd")
+        ctx.shape, ctx.dtype = (T, n, C), x.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        g = _f32(grad_out)
+        T, n, C = ctx.shape
+        gx = torch.empty(T, n, C, dtype=torch.float32, device=g.device)
+        with _DevGuard(g):
+            rc = _lib.mhc_stream_mean_bwd(g.data_ptr(), gx.data_ptr(), T, n, C,
+                                          _stream(g.device))
+        _C.check(rc, "mhc_stream_mean_bwd")
+        return gx.to(ctx.dtype)
+
+
+def stream_mean(x: torch.Tensor) -> torch.Tensor:
+    return StreamMeanFunction.apply(x)
 
 
 # =============================================================================

@@ -130,7 +130,8 @@ def residual_wrapper_pack(residual, branch_output, n, residual_mode="decay"):
         T = 1
     streams = torch.zeros(B * T, n, C, dtype=residual.dtype)
     streams[:, 0] = residual
-    streams[:, 1] = branch_output
+    if n >= 2:  # n == 1 packs the residual alone (layer.py:310)
+        streams[:, 1] = branch_output
     if residual_mode == "decay":
         for i in range(2, n):
             streams[:, i] = residual * (0.1 ** (i - 1))

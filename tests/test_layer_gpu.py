@@ -244,18 +244,66 @@ def test_dynamic_bf16_io_rejects_unsupported_shapes(cuda):
         torch.cuda.synchronize()
 
 
-def test_residual_wrapper(cuda):
-    B, T, C, n = 2, 5, 64, 4
-    gen = torch.Generator().manual_seed(3)
-    r, b = torch.randn(B, T, C, generator=gen), torch.randn(B, T, C, generator=gen)
-    w = mhc.replace_residual_with_mhc(hidden_dim=C, expansion_rate=n).to(cuda)
-    out = w(r.to(cuda), b.to(cuda))
-    streams, _ = O.residual_wrapper_pack(r.double(), b.double(), n)
-    params = {k: p.detach().cpu().double() for k, p in w.mhc.named_parameters()}
+@pytest.mark.parametrize("n,mode,shape", [(4, "decay", (2, 5, 64)), (4, "zero", (3, 64)),
+                                          (8, "decay", (2, 3, 33)), (2, "decay", (7, 96)),
+                                          (1, "decay", (4, 64)), (32, "decay", (1, 3, 64))])
+def test_residual_wrapper(cuda, n, mode, shape):
+    """Wrapper forward and input / parameter gradients against the oracle's
+    packing + layer + mean, in fp64 autograd."""
+    gen = torch.Generator().manual_seed(3 + n)
+    r, b = torch.randn(*shape, generator=gen), torch.randn(*shape, generator=gen)
+    C = shape[-1]
+    w = mhc.replace_residual_with_mhc(hidden_dim=C, expansion_rate=n, residual_mode=mode).to(cuda)
+    rd, bd = r.to(cuda).requires_grad_(True), b.to(cuda).requires_grad_(True)
+    out = w(rd, bd)
+    gout = torch.randn(*shape, generator=gen)
+    out.backward(gout.to(cuda))
+    rr, br_ = r.double().requires_grad_(True), b.double().requires_grad_(True)
+    streams, _ = O.residual_wrapper_pack(rr, br_, n, mode)
+    params = {k: p.detach().cpu().double().requires_grad_(True) for k, p in w.mhc.named_parameters()}
     ref = O.mhc_layer_dynamic(streams, *[params[k] for k in O.DYNAMIC_PARAM_ORDER]).mean(dim=1)
-    close(out, ref.reshape(B, T, C), what="wrapper out")
-    out.sum().backward()
-    assert w.mhc.phi_res.grad is not None and torch.isfinite(w.mhc.phi_res.grad).all()
+    ref = ref.reshape(shape)
+    ref.backward(gout.double())
+    close(out, ref, what="wrapper out")
+    close(rd.grad, rr.grad, what="wrapper grad residual")
+    if n >= 2:
+        close(bd.grad, br_.grad, what="wrapper grad branch")
+    else:
+        assert bd.grad is None and br_.grad is None
+    for k, p in w.mhc.named_parameters():
+        close(p.grad, params[k].grad, what="wrapper grad " + k)
+
+
+@pytest.mark.parametrize("n,mode,C", [(4, "decay", 4096), (6, "decay", 33), (5, "zero", 64),
+                                      (1, "zero", 8), (32, "decay", 100)])
+def test_wrapper_pack_and_mean_ops(cuda, n, mode, C):
+    """Packing is bit-exact with the reference's fp32 ops (same fp32 scale
+    products); the mean and both reverses match torch's fp32 formulas."""
+    from mhc_ascend_b200 import ops
+    gen = torch.Generator().manual_seed(n * 100 + C)
+    T = 37
+    r, b = torch.randn(T, C, generator=gen), torch.randn(T, C, generator=gen)
+    packed = ops.wrapper_pack(r.to(cuda), b.to(cuda), n, mode)
+    ref, _ = O.residual_wrapper_pack(r, b, n, mode)
+    assert torch.equal(packed.cpu(), ref)
+    x = torch.randn(T, n, C, generator=gen)
+    m = ops.stream_mean(x.to(cuda))
+    close(m, x.mean(dim=1), rtol=1e-6, atol=1e-6, what="stream mean")
+    # reverses
+    g = torch.randn(T, n, C, generator=gen)
+    rd, bd = r.to(cuda).requires_grad_(True), b.to(cuda).requires_grad_(True)
+    ops.wrapper_pack(rd, bd, n, mode).backward(g.to(cuda))
+    rr, bb = r.clone().requires_grad_(True), b.clone().requires_grad_(True)
+    O.residual_wrapper_pack(rr, bb, n, mode)[0].backward(g)
+    close(rd.grad, rr.grad, rtol=1e-6, atol=1e-6, what="pack grad residual")
+    if n >= 2:
+        close(bd.grad, bb.grad, rtol=0, atol=0, what="pack grad branch")
+    else:
+        assert bd.grad is None and bb.grad is None
+    xd = x.to(cuda).requires_grad_(True)
+    gm = torch.randn(T, C, generator=gen)
+    ops.stream_mean(xd).backward(gm.to(cuda))
+    assert torch.equal(xd.grad.cpu(), (gm / n).unsqueeze(1).expand(T, n, C))
 
 
 def test_no_device_wait_timed_out(cuda):
