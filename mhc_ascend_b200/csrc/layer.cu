@@ -549,9 +549,32 @@ WideSplit wide_split(int64_t M, int64_t N, int64_t K) {
   return WideSplit{S, kchunk};
 }
 
+// Split K for the tcgen05 GEMM (one CTA per SM): waves times the k each CTA
+// runs (~16 ns per k: 12 MMAs per 32-k stage, issue-bound), plus the split
+// partials at HBM speed; K ranges are whole 32-k stages.
+WideSplit wide_split_umma(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ((M + WuCfg::BM - 1) / WuCfg::BM) * ((N + WuCfg::BN - 1) / WuCfg::BN);
+  const int64_t slots = num_sms();
+  int best = 1;
+  double best_ns = -1.0;
+  for (int S = 1; S <= 64; ++S) {
+    if (S > 1 && (K / S < 2 * WuCfg::BK || (size_t)S * M * N * sizeof(float) > kWidePartCap)) break;
+    const int64_t kc = ((K + S - 1) / S + WuCfg::BK - 1) / WuCfg::BK * WuCfg::BK;
+    const int64_t waves = (tiles * S + slots - 1) / slots;
+    const double ns = (double)waves * ((double)kc * 16.0 + 2000.0) +
+                      (S > 1 ? 2.0 * S * (double)M * N * sizeof(float) / 6500.0 : 0.0);
+    if (best_ns < 0 || ns < best_ns * 0.98) { best_ns = ns; best = S; }
+  }
+  int64_t kchunk = ((K + best - 1) / best + WuCfg::BK - 1) / WuCfg::BK * WuCfg::BK;
+  if (kchunk < WuCfg::BK) kchunk = WuCfg::BK;
+  int S = (int)((K + kchunk - 1) / kchunk);
+  if (S < 1) S = 1;
+  return WideSplit{S, kchunk};
+}
+
 size_t wide_fwd_ws_bytes(int64_t B, int n, int64_t C, bool need_rec) {
   const int64_t NH = (int64_t)n * n + 2 * n;
-  const WideSplit sp = wide_split(B, NH, (int64_t)n * C);
+  const WideSplit sp = wide_split_umma(B, NH, (int64_t)n * C);
   Carve cv(nullptr);
   if (need_rec) cv.take((size_t)B * rec_stride(n));
   cv.take((size_t)sp.S * B * NH);
@@ -597,7 +620,7 @@ int run_fwd_wide(const float* x, const float* w, const float* pp, const float* p
   const size_t need = wide_fwd_ws_bytes(B, n, C, token_state == nullptr);
   MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
               "mhc_layer_fwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
-  const WideSplit sp = wide_split(B, NH, nC);
+  const WideSplit sp = wide_split_umma(B, NH, nC);
   Carve cv(ws);
   float* rec = token_state ? token_state : cv.take((size_t)B * RS);
   float* part = cv.take((size_t)sp.S * B * NH);
@@ -606,9 +629,12 @@ int run_fwd_wide(const float* x, const float* w, const float* pp, const float* p
   { ProfScope _ps("wide_rms", s); wide_rms_kernel<<<(unsigned)B, 256, 0, s>>>(x, nC, rec, RS, r_eps); }
   {
     ProfScope _ps("wide_gemm_proj", s);
-    const dim3 grid((unsigned)((NH + WG_BN - 1) / WG_BN), (unsigned)((B + WG_BM - 1) / WG_BM), (unsigned)sp.S);
-    wide_gemm_kernel<true, true, 0><<<grid, WG_THREADS, 0, s>>>(
-        rows1(x, nC), rows3(pp, pq, pr, n, 2 * n, nC), B, NH, nC, sp.kchunk, part, Rows3{}, nullptr, Rows3{});
+    const dim3 grid((unsigned)((NH + WuCfg::BN - 1) / WuCfg::BN), (unsigned)((B + WuCfg::BM - 1) / WuCfg::BM), (unsigned)sp.S);
+    const bool xv = nC % 4 == 0 && aligned16(x);
+    const bool pv = nC % 4 == 0 && aligned16(pp) && aligned16(pq) && aligned16(pr);
+    cudaFuncSetAttribute(wide_umma_gemm_kernel<true, true, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WuCfg::SMEM);
+    wide_umma_gemm_kernel<true, true, 0><<<grid, WuCfg::THREADS, WuCfg::SMEM, s>>>(
+        rows1(x, nC), rows3(pp, pq, pr, n, 2 * n, nC), B, NH, nC, sp.kchunk, xv, pv, part, Rows3{}, nullptr, Rows3{});
   }
   { ProfScope _ps("wide_gates", s); wide_gates_kernel<<<(unsigned)B, 256, 0, s>>>(part, sp.S, B, n, ap, aq, ar, bp, bq, br, rec, RS, E); }
   int rc = check_launch("mhc_layer_fwd_dynamic/wide_proj");
@@ -674,7 +700,9 @@ int run_bwd_wide(const float* g, const float* x, const float* w, const float* pp
   const Rows3 phi = rows3(pp, pq, pr, n, 2 * n, nC);
   const Rows3 xr = rows1(x, nC), gxr = rows1(gx, nC), gpr_ = rows1(GP, NH);
   {
-    // grad_x += d_p phi + coef x   (M = tokens, N = nC, K = NH)
+    // grad_x += d_p phi + coef x   (M = tokens, N = nC, K = NH).  The FFMA
+    // GEMM: phi is an N-contiguous operand here, and staging such operands
+    // for tcgen05 measured 2-3x slower than this kernel.
     ProfScope _ps("wide_gemm_gx", s);
     const dim3 grid((unsigned)((nC + WG_BN - 1) / WG_BN), (unsigned)((B + WG_BM - 1) / WG_BM), (unsigned)s1.S);
     if (s1.S == 1) {
@@ -685,7 +713,8 @@ int run_bwd_wide(const float* g, const float* x, const float* w, const float* pp
     }
   }
   {
-    // d_phi = d_p^T X   (M = NH, N = nC, K = tokens)
+    // d_phi = d_p^T X   (M = NH, N = nC, K = tokens), FFMA GEMM (both operands
+    // M/N-contiguous)
     ProfScope _ps("wide_gemm_dphi", s);
     const Rows3 gphi = rows3(gpp, gpq, gpr, n, 2 * n, nC);
     const dim3 grid((unsigned)((nC + WG_BN - 1) / WG_BN), (unsigned)((NH + WG_BM - 1) / WG_BM), (unsigned)s2.S);

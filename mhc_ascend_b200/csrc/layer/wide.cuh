@@ -188,6 +188,256 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------
+// The same contractions on tcgen05 (kind::tf32, 3xTF32: a_lo b_hi + a_hi b_lo
+// + a_hi b_hi, fp32-class accuracy), accumulator in tensor memory.
+//   CTA = one 128 x 128 output tile and one K range; 288 threads: warps 0..7
+//   stage the operands (coalesced global loads in either layout, split into
+//   tf32 hi/lo, stored in the no-swizzle K-major core-matrix layout; the next
+//   stage's loads are issued before this stage's stores) and run the
+//   epilogue; warp 8 allocates tensor memory and one lane issues 12 MMAs
+//   (M = N = 128, K = 8) per 32-k stage.  Barriers: full (256 staging
+//   threads), empty and done (MMA commits).  Every wait is
+//   bounded; a wait that runs out raises the CTA's abort word and the device
+//   error word, and the CTA drains its MMAs before releasing tensor memory.
+//   Output modes as wide_gemm_kernel.
+// ---------------------------------------------------------------------------
+struct WuCfg {
+  static constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+  static constexpr int LOADERS = 256, THREADS = LOADERS + 32;  // 8 staging warps + MMA warp
+  static constexpr uint32_t OPB = 128 * BK * 4;         // one operand part (16 KB)
+  static constexpr uint32_t SLOT = 4 * OPB;             // A hi | A lo | B hi | B lo
+  static constexpr uint32_t OFF_BAR = STAGES * SLOT;
+  static constexpr size_t SMEM = OFF_BAR + (2 * STAGES + 1) * 8 + 16 + 1024;
+  static constexpr uint32_t TCOLS = 128;
+};
+
+// One staging thread's share of a 128-row x 32-k operand tile (rows r0..,
+// k k0..), 16 values held in registers between the load and the store so
+// the next stage's loads are in flight while this stage is stored.
+//   KC (element (r, k) at R.row(r)[k]): 4 float4 along k; a quarter-warp
+//     covers 8 rows of one 4-k group (conflict-free 16-byte stores);
+//   otherwise (at R.row(k)[r]): 4 k-rows x 4 consecutive rows (float4 along
+//     the rows; a warp reads 512 contiguous bytes per k-row), transposed in
+//     registers to 4-k groups.
+template <bool KC>
+__device__ __forceinline__ void wu_load(const Rows3& R, int64_t r0, int64_t rows, int64_t k0,
+                                        int64_t ke, bool vec, int w, int lane, float (&v)[16]) {
+  if (KC) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int kq = (lane >> 3) + 4 * (j & 1);
+      const int r = (j >> 1) * 64 + w * 8 + (lane & 7);
+      const int64_t k = k0 + 4 * kq;
+      float* d = v + 4 * j;
+      d[0] = d[1] = d[2] = d[3] = 0.f;
+      if (r0 + r < rows) {
+        const float* src = R.row(r0 + r);
+        if (vec && k + 3 < ke) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(src + k));
+          d[0] = q.x; d[1] = q.y; d[2] = q.z; d[3] = q.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d[e] = (k + e < ke) ? __ldg(src + k + e) : 0.f;
+        }
+      }
+    }
+  } else {
+    // 4 k-rows x 4 consecutive rows (float4 along the rows when aligned)
+    const int64_t r = r0 + 4 * lane;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const int64_t k = k0 + 4 * w + kk;
+      float* d = v + 4 * kk;
+      d[0] = d[1] = d[2] = d[3] = 0.f;
+      if (k < ke) {
+        const float* src = R.row(k);
+        if (vec && r + 3 < rows) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(src + r));
+          d[0] = q.x; d[1] = q.y; d[2] = q.z; d[3] = q.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d[e] = (r + e < rows) ? __ldg(src + r + e) : 0.f;
+        }
+      }
+    }
+  }
+}
+
+template <bool KC>
+__device__ __forceinline__ void wu_store(const float (&v)[16], unsigned char* hi, unsigned char* lo,
+                                         int w, int lane) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t off;
+    float a, b, c, d;
+    if (KC) {
+      const int kq = (lane >> 3) + 4 * (j & 1);
+      const int r = (j >> 1) * 64 + w * 8 + (lane & 7);
+      off = umma_kmaj_off(r, 4 * kq, 128);
+      a = v[4 * j]; b = v[4 * j + 1]; c = v[4 * j + 2]; d = v[4 * j + 3];
+    } else {
+      off = umma_kmaj_off(4 * lane + j, 4 * w, 128);
+      a = v[j]; b = v[4 + j]; c = v[8 + j]; d = v[12 + j];
+    }
+    uint4 h, l;
+    split_tf32(a, h.x, l.x); split_tf32(b, h.y, l.y);
+    split_tf32(c, h.z, l.z); split_tf32(d, h.w, l.w);
+    *reinterpret_cast<uint4*>(hi + off) = h;
+    *reinterpret_cast<uint4*>(lo + off) = l;
+  }
+}
+
+__device__ __forceinline__ void umma_tf32_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <bool A_KC, bool B_KC, int MODE>
+__global__ void __launch_bounds__(WuCfg::THREADS, 1)
+    wide_umma_gemm_kernel(Rows3 A, Rows3 Bm, int64_t M, int64_t N, int64_t K, int64_t kchunk,
+                          bool a_vec, bool b_vec, float* __restrict__ part, Rows3 Cw,
+                          const float* __restrict__ coef, Rows3 X) {
+  using W = WuCfg;
+  extern __shared__ unsigned char wu_smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(wu_smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + W::OFF_BAR);
+  uint64_t* empty = full + W::STAGES;
+  uint64_t* done = empty + W::STAGES;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tslot + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t m0 = (int64_t)blockIdx.y * W::BM, n0 = (int64_t)blockIdx.x * W::BN;
+  const int64_t kb = (int64_t)blockIdx.z * kchunk;
+  const int64_t ke = kb + kchunk < K ? kb + kchunk : K;
+  const int nsteps = ke > kb ? (int)((ke - kb + W::BK - 1) / W::BK) : 0;
+
+  if (warp == 8) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(W::TCOLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < W::STAGES; ++s) {
+      mbar_init(&full[s], W::LOADERS);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp < 8) {
+    // ---- staging: loads of stage it + 1 in flight while stage it is stored ----
+    float va[16], vb[16];
+    if (nsteps > 0) {
+      wu_load<A_KC>(A, m0, M, kb, ke, a_vec, warp, lane, va);
+      wu_load<B_KC>(Bm, n0, N, kb, ke, b_vec, warp, lane, vb);
+    }
+    for (int it = 0; it < nsteps; ++it) {
+      const int s = it % W::STAGES;
+      float na[16], nb[16];
+      if (it + 1 < nsteps) {
+        const int64_t k1 = kb + (int64_t)(it + 1) * W::BK;
+        wu_load<A_KC>(A, m0, M, k1, ke, a_vec, warp, lane, na);
+        wu_load<B_KC>(Bm, n0, N, k1, ke, b_vec, warp, lane, nb);
+      }
+      if (it >= W::STAGES && !mbar_wait_or_abort(&empty[s], (uint32_t)((it / W::STAGES - 1) & 1), abort_word)) {
+        *abort_word = 1;
+        break;
+      }
+      unsigned char* slot = sm + s * W::SLOT;
+      wu_store<A_KC>(va, slot, slot + W::OPB, warp, lane);
+      wu_store<B_KC>(vb, slot + 2 * W::OPB, slot + 3 * W::OPB, warp, lane);
+      fence_proxy_async_smem();
+      mbar_arrive(&full[s]);
+      if (it + 1 < nsteps) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) { va[e] = na[e]; vb[e] = nb[e]; }
+      }
+    }
+  } else if (lane == 0) {
+    // ---- MMA issue ----
+    constexpr uint32_t idesc = umma_idesc_tf32(128, 128);
+    for (int it = 0; it < nsteps; ++it) {
+      const int s = it % W::STAGES;
+      if (!mbar_wait_or_abort(&full[s], (uint32_t)((it / W::STAGES) & 1), abort_word)) {
+        *abort_word = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t base = smem_u32(sm + s * W::SLOT);
+#pragma unroll
+      for (int ks = 0; ks < W::BK / 8; ++ks) {
+        const uint64_t ah = umma_desc_k(base, 128, ks, 0), al = umma_desc_k(base + W::OPB, 128, ks, 0);
+        const uint64_t bh = umma_desc_k(base + 2 * W::OPB, 128, ks, 0);
+        const uint64_t bl = umma_desc_k(base + 3 * W::OPB, 128, ks, 0);
+        umma_tf32_ss(tmem, al, bh, idesc, (it > 0 || ks > 0) ? 1u : 0u);
+        umma_tf32_ss(tmem, ah, bl, idesc, 1u);
+        umma_tf32_ss(tmem, ah, bh, idesc, 1u);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(done);  // arrives once every MMA issued above has completed
+  }
+
+  // ---- epilogue: tensor memory -> global (warp w: lane quadrant w % 4,
+  // columns 64 (w / 4) ..) ----
+  if (warp < 8) {
+    // plain bounded wait: every MMA issued must have finished before tensor
+    // memory is read or released, abort or not
+    const bool ok = mbar_wait(done, 0u) && !*abort_word;
+    tc_fence_after();
+    const int q = warp & 3, cbase = 64 * (warp >> 2);
+    const int64_t m = m0 + 32 * q + lane;
+    if (ok) {
+      float* dst = nullptr;
+      const float* xr = nullptr;
+      float cf = 0.f;
+      if (m < M) {
+        if (MODE == 0) {
+          dst = part + ((int64_t)blockIdx.z * M + m) * N;
+        } else {
+          dst = Cw.row(m);
+          if (MODE == 2) { xr = X.row(m); cf = coef[m]; }
+        }
+      }
+#pragma unroll 1
+      for (int c0 = cbase; c0 < cbase + 64; c0 += 16) {
+        float v[16];
+        if (nsteps > 0) {
+          tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = 0.f;
+        }
+        if (dst) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int64_t nn = n0 + c0 + e;
+            if (nn < N) {
+              if (MODE == 2) dst[nn] = dst[nn] + v[e] + cf * xr[nn];
+              else dst[nn] = v[e];
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(W::TCOLS));
+}
+
+// ---------------------------------------------------------------------------
 // forward, per token
 // ---------------------------------------------------------------------------
 
