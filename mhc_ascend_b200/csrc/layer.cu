@@ -734,6 +734,15 @@ int run_bwd_wide(const float* g, const float* x, const float* w, const float* pp
   return check_launch("mhc_layer_bwd_dynamic/wide");
 }
 
+// Which kernels run the dynamic layer: the wide-rate set (GEMM projection,
+// warp Sinkhorn, block-per-token mixes) for n >= 8, and for n = 6, 7 from
+// 1024 tokens; the fused n <= 8 kernels otherwise.  Measured on B200 (fwd +
+// bwd, C = 1280): n = 8, 8192 tokens 12.1 -> 3.7 ms; n = 7, 4096 tokens
+// 4.8 -> 1.8 ms; n = 5 and small batches favour the fused kernels.  The
+// token record keeps rec_stride(n) either way (the wide kernels take the
+// stride and ignore the Gram block).
+inline bool use_wide(int n, int64_t B) { return n >= 8 || (n >= 6 && B >= 1024); }
+
 int check_layer_args(const char* what, int64_t B, int n, int64_t C, int iters, float s_eps,
                      float r_eps, int max_n = 8) {
   MHC_REQUIRE(B >= 0, MHC_ERR_INVALID_ARG, "%s: batch must be >= 0", what);
@@ -769,7 +778,7 @@ extern "C" int32_t mhc_token_state_stride(int32_t n) { return rec_stride(n); }
 extern "C" size_t mhc_layer_fwd_dynamic_workspace_bytes(int64_t batch, int32_t n,
                                                         int64_t hidden) {
   if (batch <= 0 || hidden <= 0 || n < 1 || n > WIDE_MAX_N) return 0;
-  if (n > 8) return wide_fwd_ws_bytes(batch, n, hidden, true);
+  if (use_wide(n, batch)) return wide_fwd_ws_bytes(batch, n, hidden, true);
   switch (n) {
     case 1: return fwd_ws_bytes<1>(batch, hidden, true);
     case 2: return fwd_ws_bytes<2>(batch, hidden, true);
@@ -801,7 +810,7 @@ static int fwd_dynamic_entry(const char* what, const T* x, const float* rmsnorm_
   if (batch == 0) return MHC_OK;
   cudaStream_t s = (cudaStream_t)stream;
   if constexpr (sizeof(T) == 4) {
-    if (n > 8)
+    if (use_wide(n, batch))
       return run_fwd_wide(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre, alpha_post,
                           alpha_res, b_pre, b_post, b_res, out, token_state, batch, n, hidden,
                           sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace, workspace_bytes, s);
@@ -847,7 +856,7 @@ extern "C" int mhc_layer_fwd_dynamic_bf16(const void* x, const float* rmsnorm_we
 extern "C" size_t mhc_layer_bwd_dynamic_workspace_bytes(int64_t batch, int32_t n,
                                                         int64_t hidden) {
   if (batch <= 0 || hidden <= 0 || n < 1 || n > WIDE_MAX_N) return 0;
-  if (n > 8) return wide_bwd_ws_bytes(batch, n, hidden);
+  if (use_wide(n, batch)) return wide_bwd_ws_bytes(batch, n, hidden);
   switch (n) {
     case 1: return bwd_ws_bytes<1, true>(batch, hidden);
     case 2: return bwd_ws_bytes<2, true>(batch, hidden);
@@ -885,7 +894,7 @@ static int bwd_dynamic_entry(
   MHC_REQUIRE(batch > 0, MHC_ERR_INVALID_ARG, "%s: batch must be > 0", what);
   cudaStream_t s = (cudaStream_t)stream;
   if constexpr (sizeof(T) == 4) {
-    if (n > 8)
+    if (use_wide(n, batch))
       return run_bwd_wide(grad_out, x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
                           alpha_post, alpha_res, b_res, token_state, grad_x, grad_rmsnorm_weight,
                           grad_phi_pre, grad_phi_post, grad_phi_res, grad_alpha_pre,

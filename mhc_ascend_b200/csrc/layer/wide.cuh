@@ -1,4 +1,5 @@
-// Wide expansion rates (8 < n <= 32) of the dynamic-H layer.
+// Wide expansion rates of the dynamic-H layer (n <= 32; used for n >= 8 and,
+// from 1024 tokens, for n = 6, 7 -- use_wide() in layer.cu).
 //
 // At these rates the projection has n^2 + 2n = 99..1088 outputs over nC
 // channels (a real GEMM, not a skinny dot-product pass) and the per-token
@@ -14,8 +15,8 @@
 //         -> wide_gemm (grad_x += d_p phi + coef x)
 //         -> wide_gemm (d_phi = d_p^T X) -> wide_colsum (gw, gb, galpha)
 // Every reduction over tokens or splits runs in a fixed order: results are
-// bitwise reproducible.  Token-state record: the n <= 8 layout without the
-// Gram block (rec_stride).
+// bitwise reproducible.  Token-state record: the prefix of the n <= 8 layout
+// (rec_stride; no Gram block is written), addressed with the stride passed in.
 #pragma once
 
 namespace mhc {

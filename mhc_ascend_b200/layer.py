@@ -34,8 +34,9 @@ class MHCLayer(nn.Module):
 
     Args:
         hidden_dim: hidden size C
-        expansion_rate: number of residual streams n (1..32; the fused kernels
-            for n <= 8, the wide-rate kernels for 8 < n <= 32)
+        expansion_rate: number of residual streams n (1..32; dynamic H: the
+            fused kernels for small n, the wide-rate kernels for n >= 8 and
+            for n = 6, 7 from 1024 tokens)
         num_sinkhorn_iters: Sinkhorn-Knopp iterations
         sinkhorn_eps: Sinkhorn epsilon
         rmsnorm_eps: epsilon of both RMS computations (dynamic-H rms and RMSNorm)

@@ -76,6 +76,9 @@ def oracle_case(B, n, C, seed, alpha=0.01, bias_std=0.0, weight=None):
     (130, 12, 40, 0.5, 0.5),      # tokens span two GEMM row tiles
     (3, 9, 33, 1.0, 1.0),         # odd n, odd C
     (32, 32, 1280, 0.01, 0.0),    # the reference's paper shape (benchmark.py:302-312)
+    (1024, 6, 64, 0.5, 0.5),      # n = 6, 7 switch to the wide-rate kernels from 1024 tokens
+    (1100, 7, 40, 1.0, 1.0),
+    (1023, 7, 40, 1.0, 1.0),      # ... and stay on the fused kernels below
 ])
 def test_dynamic_vs_oracle(cuda, B, n, C, alpha, bias):
     x, params, grad = oracle_case(B, n, C, seed=B * 7 + n * 13 + C, alpha=alpha, bias_std=bias,
