@@ -517,6 +517,7 @@ int run_bwd_static(const float* g, const float* x, const float* w, const float* 
 // Wide expansion rates (8 < n <= 32): kernels in layer/wide.cuh
 // ---------------------------------------------------------------------------
 constexpr size_t kWidePartCap = size_t(256) << 20;  // split-K partials, bytes per GEMM
+constexpr int kColsumChunks = 64;                   // row chunks of the column sums
 
 struct WideSplit {
   int S;
@@ -594,6 +595,7 @@ size_t wide_bwd_ws_bytes(int64_t B, int n, int64_t C) {
   cv.take((size_t)B);                                        // rms_h coefficient
   cv.take((size_t)B * C);                                    // weight-gradient rows
   cv.take((size_t)NH + 3);                                   // their sums
+  cv.take((size_t)2 * kColsumChunks * (C + NH + 3));         // fp64 column-sum partials
   if (s1.S > 1) cv.take((size_t)s1.S * B * nC);
   if (s2.S > 1) cv.take((size_t)s2.S * NH * nC);
   return cv.off;
@@ -606,12 +608,23 @@ inline size_t wide_bwd_smem(int NM, int64_t C) {
 }
 constexpr size_t kWideSmemMax = 200 * 1024;
 
+// Column sums of a [R][W] matrix in fixed order (chunks of rows, then the
+// chunk partials in order); part holds kColsumChunks * W doubles.
+void wide_colsum(const float* src, int64_t R, int64_t W, int64_t ld, double* part, float* out,
+                 cudaStream_t s) {
+  int64_t chunk = (R + kColsumChunks - 1) / kColsumChunks;
+  if (chunk < 64) chunk = 64;
+  const int RB = (int)((R + chunk - 1) / chunk);
+  wide_colsum_part_kernel<<<dim3((unsigned)((W + 31) / 32), (unsigned)RB), 256, 0, s>>>(src, R, W, ld, chunk, part);
+  wide_colsum_final_kernel<<<grid_1d(W, 256, 1024), 256, 0, s>>>(part, RB, W, out);
+}
+
 int run_fwd_wide(const float* x, const float* w, const float* pp, const float* pq, const float* pr,
                  const float* ap, const float* aq, const float* ar, const float* bp,
                  const float* bq, const float* br, float* out, float* token_state, int64_t B,
                  int n, int64_t C, int iters, float s_eps, float r_eps, void* ws, size_t ws_bytes,
                  cudaStream_t s) {
-  const int NM = n <= 16 ? 16 : 32;
+  const int NM = n <= 8 ? 8 : (n <= 16 ? 16 : 32);
   const int64_t NH = (int64_t)n * n + 2 * n, nC = (int64_t)n * C;
   const int RS = rec_stride(n);
   const size_t smem = wide_fwd_smem(NM, C);
@@ -643,7 +656,10 @@ int run_fwd_wide(const float* x, const float* w, const float* pp, const float* p
   if (rc) return rc;
   {
     ProfScope _ps("wide_stream_fwd", s);
-    if (NM == 16) {
+    if (NM == 8) {
+      cudaFuncSetAttribute(wide_stream_fwd_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      wide_stream_fwd_kernel<8><<<(unsigned)B, 256, smem, s>>>(x, w, Mb, rec, RS, out, n, C, r_eps);
+    } else if (NM == 16) {
       cudaFuncSetAttribute(wide_stream_fwd_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       wide_stream_fwd_kernel<16><<<(unsigned)B, 256, smem, s>>>(x, w, Mb, rec, RS, out, n, C, r_eps);
     } else {
@@ -660,7 +676,7 @@ int run_bwd_wide(const float* g, const float* x, const float* w, const float* pp
                  float* gpr, float* gap, float* gaq, float* gar, float* gbp, float* gbq,
                  float* gbr, int64_t B, int n, int64_t C, int iters, float s_eps, void* ws,
                  size_t ws_bytes, cudaStream_t s) {
-  const int NM = n <= 16 ? 16 : 32;
+  const int NM = n <= 8 ? 8 : (n <= 16 ? 16 : 32);
   const int64_t NH = (int64_t)n * n + 2 * n, nC = (int64_t)n * C;
   const int RS = rec_stride(n);
   const size_t smem = wide_bwd_smem(NM, C);
@@ -680,11 +696,15 @@ int run_bwd_wide(const float* g, const float* x, const float* w, const float* pp
   float* coef = cv.take((size_t)B);
   float* gwt = cv.take((size_t)B * C);
   float* tot = cv.take((size_t)NH + 3);
+  double* csp = reinterpret_cast<double*>(cv.take((size_t)2 * kColsumChunks * (C + NH + 3)));
   float* part1 = s1.S > 1 ? cv.take((size_t)s1.S * B * nC) : nullptr;
   float* part2 = s2.S > 1 ? cv.take((size_t)s2.S * NH * nC) : nullptr;
   {
     ProfScope _ps("wide_bwd_stream", s);
-    if (NM == 16) {
+    if (NM == 8) {
+      cudaFuncSetAttribute(wide_bwd_stream_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      wide_bwd_stream_kernel<8><<<(unsigned)B, 256, smem, s>>>(g, x, w, rec, RS, ar, br, n, C, gx, gwt, ghh, gM, E);
+    } else if (NM == 16) {
       cudaFuncSetAttribute(wide_bwd_stream_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       wide_bwd_stream_kernel<16><<<(unsigned)B, 256, smem, s>>>(g, x, w, rec, RS, ar, br, n, C, gx, gwt, ghh, gM, E);
     } else {
@@ -727,8 +747,8 @@ int run_bwd_wide(const float* g, const float* x, const float* w, const float* pp
   }
   {
     ProfScope _ps("wide_colsum", s);
-    wide_colsum_kernel<<<(unsigned)((C + 31) / 32), 256, 0, s>>>(gwt, B, C, C, gw);
-    wide_colsum_kernel<<<(unsigned)((NH + 3 + 31) / 32), 256, 0, s>>>(rows, B, NH + 3, NH + 3, tot);
+    wide_colsum(gwt, B, C, C, csp, gw, s);
+    wide_colsum(rows, B, NH + 3, NH + 3, csp + kColsumChunks * C, tot, s);
     wide_param_finalize_kernel<<<1, 256, 0, s>>>(tot, n, gbp, gbq, gbr, gap, gaq, gar);
   }
   return check_launch("mhc_layer_bwd_dynamic/wide");

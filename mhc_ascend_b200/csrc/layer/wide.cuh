@@ -581,8 +581,11 @@ __global__ void __launch_bounds__(256)
   float* sx = sg + NM * 33;        // [NM][33] chunk of x
   float* sa = sx + NM * 33;        // [C]
   float* sgy = sa + C;             // [C]
-  __shared__ float red[8 * (NM + 1)];
-  __shared__ float tot_s[NM + 1];
+  // NM <= 8: gM = g x^T is accumulated in pass 1 (NM^2 registers) and pass 3 is skipped
+  constexpr bool FUSE_GM = NM <= 8;
+  constexpr int V1 = NM + 1 + (FUSE_GM ? NM * NM : 0);
+  __shared__ float red[8 * V1];
+  __shared__ float tot_s[V1];
   const int64_t b = blockIdx.x;
   const float* r = rec + b * RS;
   const float* xb = x + b * n * C;
@@ -605,20 +608,27 @@ __global__ void __launch_bounds__(256)
   const float rr = r[1];
   const float inv_r = 1.0f / rr;
 
-  // pass 1: a, gy, S, ghp, gw rows
-  float acc1[NM + 1];
+  // pass 1: a, gy, S, ghp, gw rows (and gM when FUSE_GM)
+  float acc1[V1];
 #pragma unroll
-  for (int i = 0; i <= NM; ++i) acc1[i] = 0.f;
+  for (int i = 0; i < V1; ++i) acc1[i] = 0.f;
   for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
     float a = 0.f, gy = 0.f;
-    float gr[NM];
+    float gr[NM], xr[NM];
 #pragma unroll
     for (int i = 0; i < NM; ++i) {
       gr[i] = i < n ? gb[i * C + c] : 0.f;
+      xr[i] = i < n ? xb[i * C + c] : 0.f;
       if (i < n) {
-        a += sh[i] * xb[i * C + c];
+        a += sh[i] * xr[i];
         gy += shp[i] * gr[i];
       }
+    }
+    if (FUSE_GM) {
+#pragma unroll
+      for (int i = 0; i < NM; ++i)
+#pragma unroll
+        for (int j = 0; j < NM; ++j) acc1[NM + 1 + i * NM + j] = fmaf(gr[i], xr[j], acc1[NM + 1 + i * NM + j]);
     }
     const float wc = w[c];
     const float y = a * inv_r * wc;
@@ -629,9 +639,13 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int i = 0; i < NM; ++i) acc1[i] += gr[i] * y;
   }
-  block_sum_array<NM + 1>(acc1, red, tot_s);
+  block_sum_array<V1>(acc1, red, tot_s);
   const float S = tot_s[NM];
   if (threadIdx.x < n) ghh[b * 2 * n + n + threadIdx.x] = tot_s[threadIdx.x];
+  if (FUSE_GM) {
+    for (int e = threadIdx.x; e < nn; e += blockDim.x)
+      gM[b * nn + e] = tot_s[NM + 1 + (e / n) * NM + (e % n)];
+  }
   const float sc = S / ((float)C * rr * rr * rr);
   __syncthreads();  // tot_s is reused below
 
@@ -658,6 +672,8 @@ __global__ void __launch_bounds__(256)
   }
   block_sum_array<NM>(acc2, red, tot_s);
   if (threadIdx.x < n) ghh[b * 2 * n + threadIdx.x] = tot_s[threadIdx.x];
+
+  if (FUSE_GM) return;
 
   // pass 3: gM = g x^T over 32-channel chunks
   constexpr int PAIRS = (NM * NM + 255) / 256;
@@ -741,23 +757,37 @@ __global__ void __launch_bounds__(128)
   if (threadIdx.x == 0) coef[b] = tot_s[3] / ((float)nC * rh);
 }
 
-// Fixed-order column sums of src [R][W] (row stride ld) into out[W]: each
-// block owns 32 columns, 8 row groups accumulate in fp64 and are combined in
-// group order.
+// Fixed-order column sums of src [R][W] (row stride ld) in two launches:
+// block (x, y) owns 32 columns of row chunk y (8 row groups accumulate in
+// fp64, combined in group order) and writes part[y][col]; the second kernel
+// sums the RB chunk partials in chunk order into out[W].
 __global__ void __launch_bounds__(256)
-    wide_colsum_kernel(const float* __restrict__ src, int64_t R, int64_t W, int64_t ld,
-                       float* __restrict__ out) {
-  __shared__ double part[8][32];
+    wide_colsum_part_kernel(const float* __restrict__ src, int64_t R, int64_t W, int64_t ld,
+                            int64_t rows_per_chunk, double* __restrict__ part) {
+  __shared__ double acc[8][32];
   const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
   const int64_t col = (int64_t)blockIdx.x * 32 + lane;
+  const int64_t r_begin = (int64_t)blockIdx.y * rows_per_chunk;
+  const int64_t r_end = r_begin + rows_per_chunk < R ? r_begin + rows_per_chunk : R;
   double s = 0.0;
   if (col < W)
-    for (int64_t rr = grp; rr < R; rr += 8) s += (double)src[rr * ld + col];
-  part[grp][lane] = s;
+    for (int64_t rr = r_begin + grp; rr < r_end; rr += 8) s += (double)src[rr * ld + col];
+  acc[grp][lane] = s;
   __syncthreads();
   if (grp == 0 && col < W) {
     double t = 0.0;
-    for (int q = 0; q < 8; ++q) t += part[q][lane];
+    for (int q = 0; q < 8; ++q) t += acc[q][lane];
+    part[(int64_t)blockIdx.y * W + col] = t;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    wide_colsum_final_kernel(const double* __restrict__ part, int RB, int64_t W,
+                             float* __restrict__ out) {
+  for (int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; col < W;
+       col += (int64_t)gridDim.x * blockDim.x) {
+    double t = 0.0;
+    for (int y = 0; y < RB; ++y) t += part[(int64_t)y * W + col];
     out[col] = (float)t;
   }
 }
