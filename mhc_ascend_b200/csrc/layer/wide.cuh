@@ -565,8 +565,11 @@ __global__ void __launch_bounds__(256)
 // with a = sum h_i x_i, y = a w / r, gy = sum hp_i g_i, ghp_i = <g_i, y>,
 // ga = w gy / r - a S / (C r^3), S = sum gy w a, gh_i = <ga, x_i>.
 // Dynamic shared memory: NM*NM + 2*NM + 2*NM*33 + 2*C floats.
+// (NM <= 8: capped at 128 registers for two blocks per SM, no spills; the
+// uncapped 178-register build ran one block per SM, 1.16 vs 0.67 ms at
+// n = 8 and 8192 tokens.)
 template <int NM>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, NM <= 8 ? 2 : 1)
     wide_bwd_stream_kernel(const float* __restrict__ g, const float* __restrict__ x,
                            const float* __restrict__ w, const float* __restrict__ rec, int RS,
                            const float* __restrict__ ar, const float* __restrict__ br, int n,
