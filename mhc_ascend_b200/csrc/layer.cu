@@ -524,32 +524,6 @@ struct WideSplit {
   int64_t kchunk;
 };
 
-// Split K by a small cost model: waves of CTAs (two resident per SM) times
-// the k each CTA runs (~0.26 us per k of a 128 x 128 tile at half the FFMA
-// peak), plus
-// writing and re-reading the split partials at HBM speed; partials stay under
-// kWidePartCap.
-WideSplit wide_split(int64_t M, int64_t N, int64_t K) {
-  const int64_t tiles = ((M + WG_BM - 1) / WG_BM) * ((N + WG_BN - 1) / WG_BN);
-  const int64_t slots = 2 * (int64_t)num_sms();
-  int best = 1;
-  double best_ns = -1.0;
-  for (int S = 1; S <= 64; ++S) {
-    if (S > 1 && (K / S < 64 || (size_t)S * M * N * sizeof(float) > kWidePartCap)) break;
-    const int64_t kc = ((K + S - 1) / S + WG_BK - 1) / WG_BK * WG_BK;
-    const int64_t waves = (tiles * S + slots - 1) / slots;
-    const double ns = (double)waves * (double)kc * 262.0 +
-                      (S > 1 ? 2.0 * S * (double)M * N * sizeof(float) / 6500.0 : 0.0);
-    if (best_ns < 0 || ns < best_ns * 0.98) { best_ns = ns; best = S; }
-  }
-  int64_t kchunk = (K + best - 1) / best;
-  kchunk = (kchunk + WG_BK - 1) / WG_BK * WG_BK;
-  if (kchunk < WG_BK) kchunk = WG_BK;
-  int S = (int)((K + kchunk - 1) / kchunk);
-  if (S < 1) S = 1;
-  return WideSplit{S, kchunk};
-}
-
 // Split K for the tcgen05 GEMM (one CTA per SM): waves times the k each CTA
 // runs (~16 ns per k: 12 MMAs per 32-k stage, issue-bound), plus the split
 // partials at HBM speed; K ranges are whole 32-k stages.
@@ -586,7 +560,7 @@ size_t wide_fwd_ws_bytes(int64_t B, int n, int64_t C, bool need_rec) {
 
 size_t wide_bwd_ws_bytes(int64_t B, int n, int64_t C) {
   const int64_t NH = (int64_t)n * n + 2 * n, nC = (int64_t)n * C;
-  const WideSplit s1 = wide_split(B, nC, NH), s2 = wide_split(NH, nC, B);
+  const WideSplit s1 = wide_split_umma(B, nC, NH), s2 = wide_split_umma(NH, nC, B);
   Carve cv(nullptr);
   for (int q = 0; q < 3; ++q) cv.take((size_t)B * n * n);  // E, gE, gM
   cv.take((size_t)B * 2 * n);                                // gh | ghp
@@ -685,7 +659,7 @@ int run_bwd_wide(const float* g, const float* x, const float* w, const float* pp
   const size_t need = wide_bwd_ws_bytes(B, n, C);
   MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
               "mhc_layer_bwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
-  const WideSplit s1 = wide_split(B, nC, NH), s2 = wide_split(NH, nC, B);
+  const WideSplit s1 = wide_split_umma(B, nC, NH), s2 = wide_split_umma(NH, nC, B);
   Carve cv(ws);
   float* E = cv.take((size_t)B * n * n);
   float* gE = cv.take((size_t)B * n * n);
@@ -720,28 +694,33 @@ int run_bwd_wide(const float* g, const float* x, const float* w, const float* pp
   const Rows3 phi = rows3(pp, pq, pr, n, 2 * n, nC);
   const Rows3 xr = rows1(x, nC), gxr = rows1(gx, nC), gpr_ = rows1(GP, NH);
   {
-    // grad_x += d_p phi + coef x   (M = tokens, N = nC, K = NH).  The FFMA
-    // GEMM: phi is an N-contiguous operand here, and staging such operands
-    // for tcgen05 measured 2-3x slower than this kernel.
+    // grad_x += d_p phi + coef x   (M = tokens, N = nC, K = NH) on tcgen05;
+    // phi is an N-contiguous operand here (staged as such, no transposed copy)
     ProfScope _ps("wide_gemm_gx", s);
-    const dim3 grid((unsigned)((nC + WG_BN - 1) / WG_BN), (unsigned)((B + WG_BM - 1) / WG_BM), (unsigned)s1.S);
+    const dim3 grid((unsigned)((nC + WuCfg::BN - 1) / WuCfg::BN), (unsigned)((B + WuCfg::BM - 1) / WuCfg::BM), (unsigned)s1.S);
+    const bool gv = NH % 4 == 0 && aligned16(GP), tv = nC % 4 == 0 && aligned16(pp) && aligned16(pq) && aligned16(pr);
     if (s1.S == 1) {
-      wide_gemm_kernel<true, false, 2><<<grid, WG_THREADS, 0, s>>>(gpr_, phi, B, nC, NH, s1.kchunk, nullptr, gxr, coef, xr);
+      cudaFuncSetAttribute(wide_umma_gemm_kernel<true, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WuCfg::SMEM);
+      wide_umma_gemm_kernel<true, false, 2><<<grid, WuCfg::THREADS, WuCfg::SMEM, s>>>(gpr_, phi, B, nC, NH, s1.kchunk, gv, tv, nullptr, gxr, coef, xr);
     } else {
-      wide_gemm_kernel<true, false, 0><<<grid, WG_THREADS, 0, s>>>(gpr_, phi, B, nC, NH, s1.kchunk, part1, Rows3{}, nullptr, Rows3{});
+      cudaFuncSetAttribute(wide_umma_gemm_kernel<true, false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WuCfg::SMEM);
+      wide_umma_gemm_kernel<true, false, 0><<<grid, WuCfg::THREADS, WuCfg::SMEM, s>>>(gpr_, phi, B, nC, NH, s1.kchunk, gv, tv, part1, Rows3{}, nullptr, Rows3{});
       wide_split_reduce_kernel<2><<<grid_1d(B * nC, 256, 4096), 256, 0, s>>>(part1, s1.S, B, nC, gxr, coef, xr);
     }
   }
   {
-    // d_phi = d_p^T X   (M = NH, N = nC, K = tokens), FFMA GEMM (both operands
-    // M/N-contiguous)
+    // d_phi = d_p^T X   (M = NH, N = nC, K = tokens) on tcgen05, both
+    // operands M/N-contiguous
     ProfScope _ps("wide_gemm_dphi", s);
     const Rows3 gphi = rows3(gpp, gpq, gpr, n, 2 * n, nC);
-    const dim3 grid((unsigned)((nC + WG_BN - 1) / WG_BN), (unsigned)((NH + WG_BM - 1) / WG_BM), (unsigned)s2.S);
+    const bool gv2 = NH % 4 == 0 && aligned16(GP), xv = nC % 4 == 0 && aligned16(x);
+    const dim3 grid((unsigned)((nC + WuCfg::BN - 1) / WuCfg::BN), (unsigned)((NH + WuCfg::BM - 1) / WuCfg::BM), (unsigned)s2.S);
     if (s2.S == 1) {
-      wide_gemm_kernel<false, false, 1><<<grid, WG_THREADS, 0, s>>>(gpr_, xr, NH, nC, B, s2.kchunk, nullptr, gphi, nullptr, Rows3{});
+      cudaFuncSetAttribute(wide_umma_gemm_kernel<false, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WuCfg::SMEM);
+      wide_umma_gemm_kernel<false, false, 1><<<grid, WuCfg::THREADS, WuCfg::SMEM, s>>>(gpr_, xr, NH, nC, B, s2.kchunk, gv2, xv, nullptr, gphi, nullptr, Rows3{});
     } else {
-      wide_gemm_kernel<false, false, 0><<<grid, WG_THREADS, 0, s>>>(gpr_, xr, NH, nC, B, s2.kchunk, part2, Rows3{}, nullptr, Rows3{});
+      cudaFuncSetAttribute(wide_umma_gemm_kernel<false, false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WuCfg::SMEM);
+      wide_umma_gemm_kernel<false, false, 0><<<grid, WuCfg::THREADS, WuCfg::SMEM, s>>>(gpr_, xr, NH, nC, B, s2.kchunk, gv2, xv, part2, Rows3{}, nullptr, Rows3{});
       wide_split_reduce_kernel<1><<<grid_1d(NH * nC, 256, 4096), 256, 0, s>>>(part2, s2.S, NH, nC, gphi, nullptr, Rows3{});
     }
   }

@@ -5,15 +5,15 @@
 // channels (a real GEMM, not a skinny dot-product pass) and the per-token
 // mixes are n x n mat-vecs over C, so the layer is built from different
 // pieces than the n <= 8 kernels:
-//   fwd : wide_rms (rms_h) -> wide_gemm (P = X phi^T, split-K partials)
+//   fwd : wide_rms (rms_h) -> wide_umma_gemm (P = X phi^T, split-K partials)
 //         -> wide_gates (fixed-order split sum, gates, E = exp(t_res))
 //         -> Sinkhorn (sinkhorn.cu, warp per matrix) -> wide_stream_fwd
 //   bwd : wide_bwd_stream (gy, ghp, RMSNorm reverse, gh, gM, grad_x of the
 //         mix / aggregate, gw terms, E) -> Sinkhorn reverse (sinkhorn.cu)
 //         -> wide_bwd_token (gate derivatives, d_p, per-token rows of the
 //         bias / alpha sums, rms_h coefficient)
-//         -> wide_gemm (grad_x += d_p phi + coef x)
-//         -> wide_gemm (d_phi = d_p^T X) -> wide_colsum (gw, gb, galpha)
+//         -> wide_umma_gemm (grad_x += d_p phi + coef x)
+//         -> wide_umma_gemm (d_phi = d_p^T X) -> wide_colsum (gw, gb, galpha)
 // Every reduction over tokens or splits runs in a fixed order: results are
 // bitwise reproducible.  Token-state record: the prefix of the n <= 8 layout
 // (rec_stride; no Gram block is written), addressed with the stride passed in.
@@ -43,135 +43,13 @@ inline Rows3 rows3(const float* a, const float* b, const float* c, int64_t r1, i
   return Rows3{const_cast<float*>(a), const_cast<float*>(b), const_cast<float*>(c), r1, r2, ld};
 }
 
-// ---------------------------------------------------------------------------
-// fp32 GEMM: C(m, n) = sum_k A(m, k) B(n, k), FFMA in k order within a split.
-// 128 x 128 tile, BK = 8, 256 threads with 8 x 8 outputs each, shared-memory
-// double buffer with register staging (one barrier per k-step).
-//   A_KC: A(m, k) = A.row(m)[k] (k contiguous), else A.row(k)[m]
-//   B_KC: B(n, k) = B.row(n)[k],                 else B.row(k)[n]
+// Output modes of the contractions (C(m, n) = sum_k A(m, k) B(n, k)):
 //   MODE 0: part[z][m][n] = acc              (split-K partials, row length N)
 //   MODE 1: Cw.row(m)[n] = acc
 //   MODE 2: Cw.row(m)[n] += acc + coef[m] * X.row(m)[n]
-// ---------------------------------------------------------------------------
-constexpr int WG_BM = 128, WG_BN = 128, WG_BK = 8, WG_THREADS = 256;
-
-template <bool A_KC, bool B_KC, int MODE>
-__global__ void __launch_bounds__(WG_THREADS)
-    wide_gemm_kernel(Rows3 A, Rows3 Bm, int64_t M, int64_t N, int64_t K, int64_t kchunk,
-                     float* __restrict__ part, Rows3 Cw, const float* __restrict__ coef, Rows3 X) {
-  __shared__ __align__(16) float As[2][WG_BK][WG_BM];
-  __shared__ __align__(16) float Bs[2][WG_BK][WG_BN];
-  const int tid = threadIdx.x;
-  const int64_t m0 = (int64_t)blockIdx.y * WG_BM, n0 = (int64_t)blockIdx.x * WG_BN;
-  const int64_t kb = (int64_t)blockIdx.z * kchunk;
-  const int64_t ke = kb + kchunk < K ? kb + kchunk : K;
-  float ra[4], rb[4];
-
-  auto load = [&](int64_t k0) {
-    if (A_KC) {
-      const int r = tid >> 1, kk = (tid & 1) * 4;
-      const float* src = (m0 + r < M) ? A.row(m0 + r) : nullptr;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int64_t k = k0 + kk + i;
-        ra[i] = (src && k < ke) ? __ldg(src + k) : 0.f;
-      }
-    } else {
-      const int kk = tid >> 5, c = (tid & 31) * 4;
-      const float* src = (k0 + kk < ke) ? A.row(k0 + kk) : nullptr;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) ra[i] = (src && m0 + c + i < M) ? __ldg(src + m0 + c + i) : 0.f;
-    }
-    if (B_KC) {
-      const int r = tid >> 1, kk = (tid & 1) * 4;
-      const float* src = (n0 + r < N) ? Bm.row(n0 + r) : nullptr;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int64_t k = k0 + kk + i;
-        rb[i] = (src && k < ke) ? __ldg(src + k) : 0.f;
-      }
-    } else {
-      const int kk = tid >> 5, c = (tid & 31) * 4;
-      const float* src = (k0 + kk < ke) ? Bm.row(k0 + kk) : nullptr;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) rb[i] = (src && n0 + c + i < N) ? __ldg(src + n0 + c + i) : 0.f;
-    }
-  };
-  auto store = [&](int buf) {
-    if (A_KC) {
-      const int r = tid >> 1, kk = (tid & 1) * 4;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) As[buf][kk + i][r] = ra[i];
-    } else {
-      *reinterpret_cast<float4*>(&As[buf][tid >> 5][(tid & 31) * 4]) = make_float4(ra[0], ra[1], ra[2], ra[3]);
-    }
-    if (B_KC) {
-      const int r = tid >> 1, kk = (tid & 1) * 4;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) Bs[buf][kk + i][r] = rb[i];
-    } else {
-      *reinterpret_cast<float4*>(&Bs[buf][tid >> 5][(tid & 31) * 4]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
-    }
-  };
-
-  float acc[8][8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
-  const int tx = tid & 15, ty = tid >> 4;
-  if (kb < ke) {
-    load(kb);
-    store(0);
-  }
-  __syncthreads();
-  int buf = 0;
-  for (int64_t k0 = kb; k0 < ke; k0 += WG_BK) {
-    const bool more = k0 + WG_BK < ke;
-    if (more) load(k0 + WG_BK);
-#pragma unroll
-    for (int kk = 0; kk < WG_BK; ++kk) {
-      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
-    }
-    if (more) store(buf ^ 1);
-    __syncthreads();
-    buf ^= 1;
-  }
-
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
-    if (m >= M) continue;
-    float* dst;
-    const float* xr = nullptr;
-    float cf = 0.f;
-    if (MODE == 0) {
-      dst = part + ((int64_t)blockIdx.z * M + m) * N;
-    } else {
-      dst = Cw.row(m);
-      if (MODE == 2) { xr = X.row(m); cf = coef[m]; }
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int64_t nn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
-      if (nn >= N) continue;
-      if (MODE == 2) dst[nn] = dst[nn] + acc[i][j] + cf * xr[nn];
-      else dst[nn] = acc[i][j];
-    }
-  }
-}
 
 // Fixed-order sum of S split-K partials [S][M][N] into the MODE 1 / MODE 2
-// destination of wide_gemm_kernel.
+// destination.
 template <int MODE>
 __global__ void __launch_bounds__(256)
     wide_split_reduce_kernel(const float* __restrict__ part, int S, int64_t M, int64_t N, Rows3 Cw,
@@ -200,7 +78,7 @@ __global__ void __launch_bounds__(256)
 //   threads), empty and done (MMA commits).  Every wait is
 //   bounded; a wait that runs out raises the CTA's abort word and the device
 //   error word, and the CTA drains its MMAs before releasing tensor memory.
-//   Output modes as wide_gemm_kernel.
+//   Output modes as above.
 // ---------------------------------------------------------------------------
 struct WuCfg {
   static constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
@@ -390,43 +268,67 @@ __global__ void __launch_bounds__(WuCfg::THREADS, 1)
     umma_commit(done);  // arrives once every MMA issued above has completed
   }
 
-  // ---- epilogue: tensor memory -> global (warp w: lane quadrant w % 4,
-  // columns 64 (w / 4) ..) ----
+  // ---- epilogue: tensor memory -> shared tile (warp w: lane quadrant w % 4,
+  // columns 64 (w / 4) ..) -> global rows, lanes along the columns (float4),
+  // so every store instruction writes whole 128-byte lines ----
   if (warp < 8) {
     // plain bounded wait: every MMA issued must have finished before tensor
-    // memory is read or released, abort or not
+    // memory is read or released (and before the stage buffers are reused)
     const bool ok = mbar_wait(done, 0u) && !*abort_word;
     tc_fence_after();
+    constexpr int TS = 132;  // tile row stride (floats): 16-byte rows, conflict-free
+    float* tile = reinterpret_cast<float*>(sm);
     const int q = warp & 3, cbase = 64 * (warp >> 2);
-    const int64_t m = m0 + 32 * q + lane;
+    const int row = 32 * q + lane;
+#pragma unroll 1
+    for (int c0 = cbase; c0 < cbase + 64; c0 += 16) {
+      float v[16];
+      if (ok && nsteps > 0) {
+        tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 16; e += 4)
+        *reinterpret_cast<float4*>(&tile[row * TS + c0 + e]) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(W::LOADERS) : "memory");
     if (ok) {
-      float* dst = nullptr;
-      const float* xr = nullptr;
-      float cf = 0.f;
-      if (m < M) {
+      const int64_t nc = n0 + 4 * lane;
+#pragma unroll 1
+      for (int rr = warp; rr < W::BM; rr += 8) {
+        const int64_t m = m0 + rr;
+        if (m >= M) break;
+        float* dst;
+        const float* xr = nullptr;
+        float cf = 0.f;
         if (MODE == 0) {
           dst = part + ((int64_t)blockIdx.z * M + m) * N;
         } else {
           dst = Cw.row(m);
           if (MODE == 2) { xr = X.row(m); cf = coef[m]; }
         }
-      }
-#pragma unroll 1
-      for (int c0 = cbase; c0 < cbase + 64; c0 += 16) {
-        float v[16];
-        if (nsteps > 0) {
-          tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        const float4 t = *reinterpret_cast<const float4*>(&tile[rr * TS + 4 * lane]);
+        const float tv[4] = {t.x, t.y, t.z, t.w};
+        const bool vec4 = (nc + 3 < N) && ((reinterpret_cast<uintptr_t>(dst + nc) & 15) == 0) &&
+                          (MODE != 2 || (reinterpret_cast<uintptr_t>(xr + nc) & 15) == 0);
+        if (vec4) {
+          float4 o = t;
+          if (MODE == 2) {
+            const float4 d0 = *reinterpret_cast<const float4*>(dst + nc);
+            const float4 x0 = __ldg(reinterpret_cast<const float4*>(xr + nc));
+            o = make_float4(d0.x + t.x + cf * x0.x, d0.y + t.y + cf * x0.y,
+                            d0.z + t.z + cf * x0.z, d0.w + t.w + cf * x0.w);
+          }
+          *reinterpret_cast<float4*>(dst + nc) = o;
         } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = 0.f;
-        }
-        if (dst) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int64_t nn = n0 + c0 + e;
+          for (int e = 0; e < 4; ++e) {
+            const int64_t nn = nc + e;
             if (nn < N) {
-              if (MODE == 2) dst[nn] = dst[nn] + v[e] + cf * xr[nn];
-              else dst[nn] = v[e];
+              if (MODE == 2) dst[nn] = dst[nn] + tv[e] + cf * xr[nn];
+              else dst[nn] = tv[e];
             }
           }
         }
