@@ -170,7 +170,9 @@ MHC_API int32_t mhc_token_state_stride(int32_t n);
 
 /* replaces mhc_layer_fwd_dynamic (bindings.cpp:880-952).  alpha_* point to
  * one device float each; b_res is [n,n].  token_state may be NULL for
- * inference (nothing saved). */
+ * inference (nothing saved).  1 <= n <= 32; which kernels run depends on n and
+ * batch (n >= 8, or n = 6, 7 from 1024 tokens: the wide-rate set), so the
+ * workspace size must come from the same (batch, n, hidden). */
 MHC_API size_t mhc_layer_fwd_dynamic_workspace_bytes(int64_t batch, int32_t n, int64_t hidden);
 MHC_API int mhc_layer_fwd_dynamic(const float* x, const float* rmsnorm_weight, const float* phi_pre,
                           const float* phi_post, const float* phi_res, const float* alpha_pre,
