@@ -42,7 +42,9 @@ def _worker(rank, world, port, x, params, q, average):
         shard = x.chunk(world)[rank]
         (layer(shard) ** 2).sum().backward()
         GradBucket(layer.parameters(), average=average).allreduce()
-        q.put((rank, {k: p.grad.clone() for k, p in layer.named_parameters()}))
+        # numpy copies pickle by value: a tensor would travel as a shared-memory
+        # handle that can vanish when this process exits before the parent reads it
+        q.put((rank, {k: p.grad.detach().numpy().copy() for k, p in layer.named_parameters()}))
     finally:
         dist.destroy_process_group()
 
@@ -71,7 +73,8 @@ def test_bucket_allreduce_equals_full_batch(average):
     for r in range(world):
         for k, p in ref.named_parameters():
             expect = p.grad / world if average else p.grad
-            torch.testing.assert_close(results[r][k], expect, rtol=1e-10, atol=1e-12)
+            torch.testing.assert_close(torch.from_numpy(results[r][k]), expect, rtol=1e-10,
+                                       atol=1e-12)
 
 
 def _shared_worker(rank, world, port, q):
@@ -89,7 +92,7 @@ def _shared_worker(rank, world, port, q):
         shared = bucket._shared_flat()
         assert shared is not None and shared.data_ptr() == flat.data_ptr()
         bucket.allreduce()
-        q.put((rank, flat.clone(), all(p.grad.data_ptr() >= flat.data_ptr() for p in params)))
+        q.put((rank, flat.numpy().copy(), all(p.grad.data_ptr() >= flat.data_ptr() for p in params)))
     finally:
         dist.destroy_process_group()
 
@@ -107,7 +110,7 @@ def test_bucket_allreduces_shared_gradient_buffer_in_place():
         pr.join(timeout=60)
     expect = torch.arange(15, dtype=torch.float32) + 50.0   # mean of rank 0 and rank 1 values
     for _, flat, views in res:
-        assert torch.equal(flat, expect)
+        assert torch.equal(torch.from_numpy(flat), expect)
         assert views
 
 
