@@ -63,6 +63,20 @@ def test_validation_errors_without_gpu():
     assert lib.mhc_layer_bwd_dynamic(*args) == ERR_WORKSPACE
 
 
+def test_wrapper_entry_points_validate_without_gpu():
+    lib = _C.load()
+    p = ctypes.c_void_p(16)
+    sc = (ctypes.c_float * 65)(*([1.0] * 65))
+    assert lib.mhc_wrapper_pack_fwd(p, p, p, sc, 4, 65, 8, None) == ERR_UNSUPPORTED
+    assert "n must be in [1, 64]" in _C.last_error()
+    assert lib.mhc_wrapper_pack_fwd(p, None, p, sc, 4, 2, 8, None) == ERR_INVALID
+    assert "branch" in _C.last_error()
+    assert lib.mhc_wrapper_pack_fwd(p, None, p, sc, 0, 1, 8, None) == 0  # n = 1 needs no branch
+    assert lib.mhc_stream_mean_fwd(None, p, 4, 4, 8, None) == ERR_INVALID
+    assert lib.mhc_stream_mean_bwd(p, p, -1, 4, 8, None) == ERR_INVALID
+    assert lib.mhc_wrapper_pack_bwd(p, p, None, None, 4, 4, 8, None) == ERR_INVALID
+
+
 def test_empty_batch_is_a_noop():
     lib = _C.load()
     p = ctypes.c_void_p(16)
