@@ -58,7 +58,7 @@ def peaks():
 
 
 def algorithmic_bytes(mode, B, n, C):
-    """SURVEY 8(d) accounting: fwd reads x, writes out; bwd reads x and g,
+    """Algorithmic bytes of one step: fwd reads x, writes out; bwd reads x and g,
     writes gx; phi read twice + dphi written (fp32); w read + gw written."""
     s = 4
     nC = n * C
