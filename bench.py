@@ -319,12 +319,18 @@ def run_mine(args, world, rank, local):
     elif mode == "static_fwd":
         layer.eval()
 
-    def step():
+    def step(ar_evs=None):
         if dynamic:
             out = layer(x)
             out.backward(g)
             if world > 1:
+                if ar_evs is not None:
+                    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a0.record(stream)
                 bucket.allreduce()
+                if ar_evs is not None:
+                    a1.record(stream)
+                    ar_evs.append((a0, a1))
             for p in layer.parameters():
                 p.grad = None
         else:
@@ -379,11 +385,20 @@ def run_mine(args, world, rank, local):
     prof_steps = max(3, min(args.steps, 50))
     torch.cuda.synchronize()
     _C.profile_enable(True)
+    ar_evs = []
     for _ in range(prof_steps):
-        step()
+        step(ar_evs)
     torch.cuda.synchronize()
     _C.profile_enable(False)
     rep = _C.profile_report()
+    allreduce = None
+    if ar_evs:
+        ar_ms = sum(a.elapsed_time(b) for a, b in ar_evs) / len(ar_evs)
+        t = torch.tensor([ar_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        allreduce = {"ms_max_over_ranks": t.item(), "bytes": bucket.numel * 4,
+                     "op": "NCCL all_reduce AVG of the flat parameter-gradient bucket",
+                     "share_of_step": t.item() / ms}
     launches_per_step = sum(c for c, _ in rep.values()) / prof_steps
     kernels = {}
     for name, (cnt, tot) in rep.items():
@@ -418,7 +433,7 @@ def run_mine(args, world, rank, local):
     e2e = None
     if dynamic and not args.no_e2e:
         xh = x.cpu().pin_memory()
-        e2e_steps = max(3, min(args.steps // 20, 30))
+        e2e_steps = max(20, min(args.steps // 10, 50))
         xds = [torch.empty_like(x), torch.empty_like(x)]
         cs = torch.cuda.Stream(dev)
         copied = [torch.cuda.Event(), torch.cuda.Event()]
@@ -426,16 +441,24 @@ def run_mine(args, world, rank, local):
         for ev in used:
             ev.record(stream)
 
-        def issue_copy(k):
+        copy_evs = []   # (start, end) of each timed H2D copy, on the copy stream
+
+        def issue_copy(k, timed=False):
             b = k % 2
             with torch.cuda.stream(cs):
                 cs.wait_event(used[b])           # the buffer's previous step is done with it
+                if timed:
+                    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    c0.record(cs)
                 xds[b].copy_(xh, non_blocking=True)
+                if timed:
+                    c1.record(cs)
+                    copy_evs.append((c0, c1))
                 copied[b].record(cs)
 
-        def e2e_step(k):
+        def e2e_step(k, timed=False):
             b = k % 2
-            issue_copy(k + 1)
+            issue_copy(k + 1, timed)
             stream.wait_event(copied[b])
             out = layer(xds[b])
             loss = (out * out).sum()
@@ -456,26 +479,33 @@ def run_mine(args, world, rank, local):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         cs.wait_event(e0)
-        issue_copy(0)
+        issue_copy(0, True)
         for k in range(e2e_steps):
-            e2e_step(k)
+            e2e_step(k, k + 1 < e2e_steps)
         e1.record(stream)
         torch.cuda.synchronize()
         ems = e0.elapsed_time(e1) / e2e_steps
+        h2d_bytes = xh.numel() * xh.element_size()
+        copy_ms = sum(c0.elapsed_time(c1) for c0, c1 in copy_evs) / len(copy_evs)
+        h2d_gbs = h2d_bytes / (copy_ms * 1e-3) / 1e9
         if world > 1:
-            t = torch.tensor([ems], device=dev)
+            t = torch.tensor([ems, -h2d_gbs], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = t.item()
+            ems, h2d_gbs_min = t[0].item(), -t[1].item()
+        else:
+            h2d_gbs_min = h2d_gbs
         e2e = {"value": tokens * world / (ems * 1e-3), "unit": "tokens/s",
-               "h2d_bytes_per_step": xh.numel() * xh.element_size(), "d2h_bytes_per_step": 4,
-               "ms_per_step": ems,
+               "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": 4,
+               "ms_per_step": ems, "steps": e2e_steps,
+               "h2d_gbs_rank0": h2d_gbs, "h2d_gbs_min_over_ranks": h2d_gbs_min,
+               "h2d_ms_per_step": copy_ms,
                "note": "MHCLayer(x) with x copied from pinned host memory each step "
                        "(next step's copy overlapping this step's compute), "
                        "loss=sum(out^2), backward, loss.item()"}
     elif not dynamic and not args.no_e2e:
         xh = x.cpu().pin_memory()
         oh = torch.empty(tokens, n, C, dtype=x.dtype).pin_memory()
-        e2e_steps = max(3, min(args.steps // 20, 30))
+        e2e_steps = max(20, min(args.steps // 10, 50))
 
         def e2e_step():
             with torch.no_grad():
@@ -493,7 +523,8 @@ def run_mine(args, world, rank, local):
         ems = e0.elapsed_time(e1) / e2e_steps
         e2e = {"value": tokens * world / (ems * 1e-3), "unit": "tokens/s",
                "h2d_bytes_per_step": xh.numel() * xh.element_size(),
-               "d2h_bytes_per_step": oh.numel() * oh.element_size(), "ms_per_step": ems}
+               "d2h_bytes_per_step": oh.numel() * oh.element_size(), "ms_per_step": ems,
+               "steps": e2e_steps}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -526,6 +557,7 @@ def run_mine(args, world, rank, local):
             "clocks": clk,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "allreduce": allreduce,
         }
         print(json.dumps(line), flush=True)
 

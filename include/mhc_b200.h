@@ -139,6 +139,13 @@ MHC_API int mhc_fused_rmsnorm_matmul_bwd(const float* grad_out, const float* inp
 MHC_API int mhc_wrapper_pack_fwd(const float* residual, const float* branch, float* out,
                                  const float* scales, int64_t tokens, int32_t n, int64_t hidden,
                                  void* stream);
+/* bf16 residual / branch_output (tokens x hidden bf16, 8-byte aligned for the
+ * vector path), fp32 streams out: the reference packs in residual.dtype
+ * (layer.py:299-308), so streams i >= 2 are scales[i] * residual rounded to
+ * bf16 before the layer widens them (layer.py:101). */
+MHC_API int mhc_wrapper_pack_fwd_bf16(const void* residual, const void* branch, float* out,
+                                      const float* scales, int64_t tokens, int32_t n,
+                                      int64_t hidden, void* stream);
 /* grad_residual = sum_{i != 1} scales[i] * grad[:, i]; grad_branch = grad[:, 1] (may be NULL) */
 MHC_API int mhc_wrapper_pack_bwd(const float* grad_out, float* grad_residual, float* grad_branch,
                                  const float* scales, int64_t tokens, int32_t n, int64_t hidden,

@@ -42,6 +42,7 @@ SIGNATURES = {
     "mhc_fused_rmsnorm_matmul_bwd": (ctypes.c_int,
                                      [_P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _SZ, _P]),
     "mhc_wrapper_pack_fwd": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I64, _P]),
+    "mhc_wrapper_pack_fwd_bf16": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I64, _P]),
     "mhc_wrapper_pack_bwd": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I64, _P]),
     "mhc_stream_mean_fwd": (ctypes.c_int, [_P, _P, _I64, _I32, _I64, _P]),
     "mhc_stream_mean_bwd": (ctypes.c_int, [_P, _P, _I64, _I32, _I64, _P]),

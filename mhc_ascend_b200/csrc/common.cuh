@@ -62,6 +62,12 @@ struct ProfScope {
   }
 };
 
+// Dynamic-forward helpers defined in layer.cu, used by the allocation-free
+// entry point in noalloc.cu.
+int fwd_dynamic_check_args(const char* what, int64_t B, int n, int64_t C, int iters,
+                           float s_eps, float r_eps);
+size_t fwd_dynamic_scratch_bytes(int64_t B, int n, int64_t C, bool need_rec);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 #define MHC_REQUIRE(cond, code, ...)          \

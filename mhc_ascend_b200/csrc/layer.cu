@@ -755,6 +755,30 @@ int check_layer_args(const char* what, int64_t B, int n, int64_t C, int iters, f
 }
 
 }  // namespace
+
+// Shared with the allocation-free entry point (noalloc.cu): argument checks of
+// the fp32 dynamic forward, and its exact scratch need, which leaves out the
+// token record when the caller keeps it (token_state != NULL).
+int fwd_dynamic_check_args(const char* what, int64_t B, int n, int64_t C, int iters,
+                           float s_eps, float r_eps) {
+  return check_layer_args(what, B, n, C, iters, s_eps, r_eps, WIDE_MAX_N);
+}
+
+size_t fwd_dynamic_scratch_bytes(int64_t B, int n, int64_t C, bool need_rec) {
+  if (B <= 0 || C <= 0 || n < 1 || n > WIDE_MAX_N) return 0;
+  if (use_wide(n, B)) return wide_fwd_ws_bytes(B, n, C, need_rec);
+  switch (n) {
+    case 1: return fwd_ws_bytes<1>(B, C, need_rec);
+    case 2: return fwd_ws_bytes<2>(B, C, need_rec);
+    case 3: return fwd_ws_bytes<3>(B, C, need_rec);
+    case 4: return fwd_ws_bytes<4>(B, C, need_rec);
+    case 5: return fwd_ws_bytes<5>(B, C, need_rec);
+    case 6: return fwd_ws_bytes<6>(B, C, need_rec);
+    case 7: return fwd_ws_bytes<7>(B, C, need_rec);
+    default: return fwd_ws_bytes<8>(B, C, need_rec);
+  }
+}
+
 }  // namespace mhc
 
 using namespace mhc;
@@ -776,18 +800,7 @@ extern "C" int32_t mhc_token_state_stride(int32_t n) { return rec_stride(n); }
 
 extern "C" size_t mhc_layer_fwd_dynamic_workspace_bytes(int64_t batch, int32_t n,
                                                         int64_t hidden) {
-  if (batch <= 0 || hidden <= 0 || n < 1 || n > WIDE_MAX_N) return 0;
-  if (use_wide(n, batch)) return wide_fwd_ws_bytes(batch, n, hidden, true);
-  switch (n) {
-    case 1: return fwd_ws_bytes<1>(batch, hidden, true);
-    case 2: return fwd_ws_bytes<2>(batch, hidden, true);
-    case 3: return fwd_ws_bytes<3>(batch, hidden, true);
-    case 4: return fwd_ws_bytes<4>(batch, hidden, true);
-    case 5: return fwd_ws_bytes<5>(batch, hidden, true);
-    case 6: return fwd_ws_bytes<6>(batch, hidden, true);
-    case 7: return fwd_ws_bytes<7>(batch, hidden, true);
-    default: return fwd_ws_bytes<8>(batch, hidden, true);
-  }
+  return fwd_dynamic_scratch_bytes(batch, n, hidden, true);
 }
 
 template <typename T>

@@ -53,11 +53,19 @@ struct Gx6Cfg {
   static constexpr int IMG_SC = IMG_B2L + KP * TOK, IMG_FLOATS = IMG_SC + TOK * 32;
   static constexpr uint32_t IMG = IMG_FLOATS * 4;
   static constexpr uint32_t LOCB = TOK * COLS * 4;         // local terms [tokens][128 columns]
-  static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 2;
-  // tensor memory: D1[b] [TOK b, +TOK); D2 [64, 96); Phi^T hi [96, 120), lo [128, 152);
-  // X^T[b] [256 + 2 TOK b, +2 TOK) hi|lo
+  // D2 (the dphi contraction over tokens) alternates between two accumulators
+  // every DR2 blocks; the epilogue warps add each finished one into fp32 sums
+  // in shared memory LAG2 blocks later, so no tensor-memory accumulation chain
+  // spans more than DR2 blocks (12 MMAs each).  Tensor-memory accumulation
+  // rounds toward zero -- a uniform relative shrink of ~2e-8 per MMA, which
+  // over the 1024 blocks of a 32768-token split reached 5e-3 on dphi
+  static constexpr int DR2 = 8, LAG2 = 4;
+  static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 2 + 4;
+  // tensor memory: D1[b] [TOK b, +TOK); D2 [64, 96) and [160, 192); Phi^T hi
+  // [96, 120), lo [128, 152); X^T[b] [256 + 2 TOK b, +2 TOK) hi|lo
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t D2_COL = 64, A1_COL = 96, A1L_COL = 128, XT_COL = 256;
+  static constexpr uint32_t D2_COL = 64, D2B_COL = 160, A1_COL = 96, A1L_COL = 128, XT_COL = 256;
+  static_assert(LAG2 >= 1 && LAG2 <= DR2, "drain schedule");
   static_assert(ND * TOK <= 64 && XT_COL + 2 * TOK * ND <= TMEM_COLS && TOK % 16 == 0, "tensor-memory plan");
 };
 
@@ -72,7 +80,8 @@ struct Gx6S {
   static constexpr uint32_t STGB = BF16 ? F::TOK * F::COLS * 2 : 0; // bf16 grad_x staging tile
   static constexpr uint32_t OFF_STG = OFF_LOC + F::ND * F::LOCB;   // [ND buffers]
   static constexpr uint32_t OFF_GW = OFF_STG + F::ND * STGB;       // grad-w partials [E warps][32]
-  static constexpr uint32_t OFF_BAR = OFF_GW + F::E_WARPS * F::CW * 4;
+  static constexpr uint32_t OFF_D2S = OFF_GW + F::E_WARPS * F::CW * 4;  // drained D2 sums [NH][128]
+  static constexpr uint32_t OFF_BAR = OFF_D2S + F::NH * F::COLS * 4;
   static constexpr size_t SMEM = OFF_BAR + F::NBAR * 8 + 16 + 128;
 };
 

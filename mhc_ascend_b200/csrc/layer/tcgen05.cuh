@@ -87,37 +87,51 @@ __device__ __forceinline__ void umma_tf32_at(uint32_t d_tmem, uint32_t a_tmem, u
 //   CTAs per SM, warp-specialised: warp 0 issues TMA, warp 1 issues MMAs,
 //   warps 2..9 (two threads per token, one per half of a 128-byte row)
 //   prepare the A operand.  A stage is one stream x 32 channels: x[128 tokens
-//   x 32] and phi_hi / phi_lo[NB rows x 32] (phi split once per call), both
-//   128-byte-swizzled as TMA writes them.  The operand threads read their
-//   token's row, keep the values of the n streams of a channel block in
-//   registers for the Gram entries, and store the row split into tf32 hi/lo
-//   into tensor memory with tcgen05.st (lane = token, column = channel: the
-//   A operand, no proxy fence); the MMA warp adds x_lo.phi_hi + x_hi.phi_lo +
-//   x_hi.phi_hi (3xTF32) into the accumulator in tensor memory.  Barriers:
-//   full (TMA bytes), empty (operand warps done with x + MMA done with phi),
-//   aready / afree per tensor-memory A buffer.
+//   x 32] and phi[hi rows | lo rows][32] (phi split once per call into tf32
+//   hi + lo, both 128-byte-swizzled as TMA writes them).  The operand threads
+//   read their token's row, keep the values of the n streams of a channel
+//   block in registers for the Gram entries, and store the row split into
+//   tf32 hi/lo into tensor memory with tcgen05.st (lane = token, column =
+//   channel: the A operand, no proxy fence).  3xTF32 in two MMAs per K-step:
+//   x_hi . [phi_hi | phi_lo] (N = 2 NB: the hi.hi and hi.lo products land in
+//   separate accumulator columns) and x_lo . phi_hi (added to the hi.hi
+//   columns).  Every DR chunks the MMA warp switches between two accumulator
+//   sets and the operand warps add the finished set into fp32 registers, so
+//   no accumulation chain in tensor memory is longer than DR chunks.
+//   Barriers: full (TMA bytes), empty (operand warps done with x + MMA done
+//   with phi), aready / afree per tensor-memory A buffer, dready / dfree per
+//   accumulator set.
 // ---------------------------------------------------------------------------
 template <int N, typename T = float>
 struct PumCfg {
   static constexpr int NH = L<N>::NH, NHP = L<N>::NHP, NG = L<N>::NG;
-  static constexpr int NB = (NH + 15) / 16 * 16;           // MMA N (padded phi rows)
+  static constexpr int NB = (NH + 7) / 8 * 8;              // phi rows per tile (8-row swizzle atoms)
+  static constexpr int NC = 2 * NB;                        // MMA N of x_hi . [phi_hi | phi_lo]
+  static constexpr int NLO = (NB + 15) / 16 * 16;          // MMA N of x_lo . phi_hi (<= NC)
   // a stage is one 128-byte row of x per token: 32 fp32 or 64 bf16 channels
   static constexpr int TOK = 128, CH = 128 / (int)sizeof(T), THREADS = 320;
   static constexpr int PSUB = CH / 32;                     // 32-channel phi sub-tiles per stage
   static constexpr bool BF16 = sizeof(T) == 2;             // bf16 x is exact in tf32: no lo part
   static constexpr uint32_t XB = TOK * 128;                // x tile of one stage
-  static constexpr uint32_t PB = NB * CH * 4;              // phi tile (fp32) of one stage
-  static constexpr uint32_t SLOT = XB + 2 * PB;            // x, phi_hi, phi_lo
-  static constexpr uint32_t OFF_PH = XB, OFF_PL = XB + PB;
+  static constexpr uint32_t PT = NB * 128;                 // one phi_hi (or phi_lo) sub-tile
+  static constexpr uint32_t PB = 2 * PT * PSUB;            // phi of one stage: [hi | lo] per sub-tile
+  static constexpr uint32_t SLOT = XB + PB;
+  static constexpr uint32_t OFF_P = XB;
   static constexpr uint32_t TX = SLOT;                     // bytes TMA brings per stage
-  static constexpr int STAGES = BF16 ? 3 : 4, NA = 2;      // smem stages, tensor-memory A buffers
-  static constexpr uint32_t TCOLS = 256;                   // D [0, 32); A[a] = [64 + 64 a, +64): fp32 hi|lo, bf16 hi
-  static constexpr uint32_t ACOL = 64;
+  static constexpr int STAGES = BF16 ? 2 : 3, NA = 2;      // smem stages, tensor-memory A buffers
+  // tensor memory: accumulator sets D[s] = [64 s, 64 s + NC); A[a] = [128 + 64 a, +64): fp32 hi|lo, bf16 hi
+  static constexpr uint32_t TCOLS = 256, ACOL = 128;
+  // chunks accumulated into one set before the operand warps add it into fp32
+  // sums in shared memory.  Accumulation in tensor memory rounds toward zero
+  // (measured: a relative shrink of ~2e-8 per accumulating MMA, uniform over
+  // all outputs), so chains stay at DR x 8 MMAs: 32 at DR = 4, ~6e-7.
+  static constexpr int DR = 4;
   static constexpr uint32_t OFF_GX = STAGES * SLOT;        // Gram exchange [128][NG]
-  static constexpr uint32_t OFF_BAR = OFF_GX + TOK * NG * 4;
-  static constexpr size_t SMEM = OFF_BAR + (2 * STAGES + 2 * NA + 1) * 8 + 16 + 1024;
-  static_assert(NB <= 32, "one 32-column accumulator");
-  static_assert(XB % 1024 == 0 && PB % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+  static constexpr uint32_t OFF_ACC = OFF_GX + TOK * NG * 4; // drained sums [2 NB][128 tokens]
+  static constexpr uint32_t OFF_BAR = OFF_ACC + 2 * NB * TOK * 4;
+  static constexpr size_t SMEM = OFF_BAR + (2 * STAGES + 2 * NA + 4 + 1) * 8 + 16 + 1024;
+  static_assert(NC <= 64 && NB % 8 == 0, "one 64-column accumulator set");
+  static_assert(XB % 1024 == 0 && PT % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 };
 
 // phi_hi / phi_lo [NB rows x nC]: rows k < NH hold phi_k split into tf32 hi +
@@ -188,7 +202,7 @@ __global__ void __launch_bounds__(320, 2)
                      const __grid_constant__ CUtensorMap lmap, float* __restrict__ ppart,
                      float* __restrict__ gpart, int64_t B, int64_t C, int cps) {
   using P = PumCfg<N, T>;
-  constexpr int NG = P::NG, NHP = P::NHP, S = P::STAGES, NA = P::NA;
+  constexpr int NG = P::NG, NHP = P::NHP, NB = P::NB, S = P::STAGES, NA = P::NA, DR = P::DR;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* gx_s = reinterpret_cast<float*>(sm + P::OFF_GX);
@@ -196,7 +210,9 @@ __global__ void __launch_bounds__(320, 2)
   uint64_t* empty = full + S;
   uint64_t* aready = empty + S;
   uint64_t* afree = aready + NA;
-  uint64_t* done = afree + NA;
+  uint64_t* dready = afree + NA;
+  uint64_t* dfree = dready + 2;
+  uint64_t* done = dfree + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t sbase = smem_u32(sm);
@@ -225,6 +241,10 @@ __global__ void __launch_bounds__(320, 2)
       mbar_init(&aready[a], 8);
       mbar_init(&afree[a], 1);
     }
+    for (int d = 0; d < 2; ++d) {
+      mbar_init(&dready[d], 1);
+      mbar_init(&dfree[d], 8);
+    }
     mbar_init(done, 1);
     *abort_word = 0;
     fence_mbar_init();
@@ -252,8 +272,8 @@ __global__ void __launch_bounds__(320, 2)
         tma_load_3d(base, &xmap, c, i, (int)t0, &full[slot]);
 #pragma unroll
         for (int ps = 0; ps < P::PSUB; ++ps) {
-          tma_load_3d(base + P::OFF_PH + ps * P::NB * 128, &hmap, c + 32 * ps, i, 0, &full[slot]);
-          tma_load_3d(base + P::OFF_PL + ps * P::NB * 128, &lmap, c + 32 * ps, i, 0, &full[slot]);
+          tma_load_3d(base + P::OFF_P + ps * 2 * P::PT, &hmap, c + 32 * ps, i, 0, &full[slot]);
+          tma_load_3d(base + P::OFF_P + ps * 2 * P::PT + P::PT, &lmap, c + 32 * ps, i, 0, &full[slot]);
         }
       }
       // no copy may still be landing when the CTA exits (bounded)
@@ -263,10 +283,15 @@ __global__ void __launch_bounds__(320, 2)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t ID = umma_idesc_tf32(128, P::NB);
+      constexpr uint32_t IDC = umma_idesc_tf32(128, P::NC);
+      constexpr uint32_t IDL = umma_idesc_tf32(128, P::NLO);
       for (int k = 0; k < nchunks; ++k) {
         const int slot = k % S, a = k % NA;
-        if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word) ||
+        const int run = k / DR, ds = run & 1;
+        const bool first = k % DR == 0;
+        if ((first && run >= 2 &&
+             !mbar_wait_or_abort(&dfree[ds], (uint32_t)(((run - 2) >> 1) & 1), abort_word)) ||
+            !mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word) ||
             !mbar_wait_or_abort(&aready[a], (uint32_t)((k / NA) & 1), abort_word)) {
           *abort_word = 1;
           break;
@@ -274,38 +299,53 @@ __global__ void __launch_bounds__(320, 2)
         tc_fence_after();
         const uint32_t sb = sbase + slot * P::SLOT;
         const uint32_t at = tmem + P::ACOL + 64 * a;
+        const uint32_t dt = tmem + 64 * ds;
 #pragma unroll
         for (int st = 0; st < P::CH / 8; ++st) {
-          const uint32_t boff = (st / 4) * P::NB * 128 + 32 * (st % 4);
-          const uint64_t bh = umma_desc_sw128(sb + P::OFF_PH + boff);
-          const uint64_t bl = umma_desc_sw128(sb + P::OFF_PL + boff);
-          if constexpr (P::BF16) {
-            umma_tf32_at(tmem, at + 8 * st, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
-            umma_tf32_at(tmem, at + 8 * st, bl, ID, 1u);
-          } else {
-            umma_tf32_at(tmem, at + 32 + 8 * st, bh, ID, (k > 0 || st > 0) ? 1u : 0u);
-            umma_tf32_at(tmem, at + 8 * st, bl, ID, 1u);
-            umma_tf32_at(tmem, at + 8 * st, bh, ID, 1u);
-          }
+          const uint32_t boff = (st / 4) * 2 * P::PT + 32 * (st % 4);
+          const uint64_t bd = umma_desc_sw128(sb + P::OFF_P + boff);
+          umma_tf32_at(dt, at + 8 * st, bd, IDC, (first && st == 0) ? 0u : 1u);
+          if constexpr (!P::BF16) umma_tf32_at(dt, at + 32 + 8 * st, bd, IDL, 1u);
         }
         umma_commit(&empty[slot]);
         umma_commit(&afree[a]);
+        if (k % DR == DR - 1 || k == nchunks - 1) umma_commit(&dready[ds]);
       }
       umma_commit(done);
     }
   } else {
     // ---------------- A operand (tensor memory) + Gram ----------------
     const int cw = warp - 2;               // 0..7
-    const int h = cw >> 2;                 // half of the 128-byte row
+    const int h = cw >> 2;                 // half of the 128-byte row; accumulator half
     const int qd = warp & 3;               // tensor-memory lane quadrant
     const int r = 32 * qd + lane;          // token row = tensor-memory lane
     const uint32_t rowoff = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    const uint32_t dlane = (uint32_t)(32 * qd) << 16;
     uint32_t choff[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) choff[j] = rowoff + (uint32_t)((((4 * h + j) ^ (r & 7))) * 16);
     float gacc[NG];
 #pragma unroll
     for (int g = 0; g < NG; ++g) gacc[g] = 0.f;
+    // this thread's accumulator columns -- phi_hi terms (h = 0) or phi_lo terms
+    // (h = 1) -- summed in shared memory, [column][token] (conflict-free)
+    float* acc_s = reinterpret_cast<float*>(sm + P::OFF_ACC) + h * NB * P::TOK + r;
+#pragma unroll
+    for (int j = 0; j < NB; ++j) acc_s[j * P::TOK] = 0.f;
+    auto drain = [&](int ds) {
+#pragma unroll
+      for (int j = 0; j < NB; j += 8) {
+        uint32_t d[8];
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]),
+                       "=r"(d[6]), "=r"(d[7])
+                     : "r"(tmem + dlane + 64 * ds + NB * h + j));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc_s[(j + e) * P::TOK] += __uint_as_float(d[e]);
+      }
+    };
+    int drained = 0;  // accumulator runs already added into pacc
     bool ok = true;
     for (int b = 0; b < nblocks && ok; ++b) {
       // this thread's 16 (fp32) or 32 (bf16) channels of each stream, as stored
@@ -314,6 +354,17 @@ __global__ void __launch_bounds__(320, 2)
       for (int i = 0; i < N; ++i) {
         const int k = b * N + i;
         const int slot = k % S, a = k % NA;
+        // run `drained` ended DR chunks ago plus one: its MMAs are done or nearly
+        if (k == (drained + 1) * DR + 1) {
+          const int ds = drained & 1;
+          if (!mbar_wait_or_abort(&dready[ds], (uint32_t)((drained >> 1) & 1), abort_word)) { ok = false; break; }
+          tc_fence_after();
+          drain(ds);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&dfree[ds]);
+          ++drained;
+        }
         const unsigned char* base = sm + slot * P::SLOT;
         if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word)) { ok = false; break; }
 #pragma unroll
@@ -324,7 +375,7 @@ __global__ void __launch_bounds__(320, 2)
         tc_fence_after();
         if constexpr (P::BF16) {
           // bf16 -> fp32 is exact and already a tf32 value: hi only
-          const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + P::ACOL + 64 * a + 32 * h;
+          const uint32_t ta = tmem + dlane + P::ACOL + 64 * a + 32 * h;
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
             uint32_t hi[16];
@@ -337,7 +388,7 @@ __global__ void __launch_bounds__(320, 2)
             tmem_st16(ta + 16 * hf, hi);
           }
         } else {
-          const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + P::ACOL + 64 * a + 16 * h;
+          const uint32_t ta = tmem + dlane + P::ACOL + 64 * a + 16 * h;
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
             uint32_t hi[8], lo[8];
@@ -376,32 +427,26 @@ __global__ void __launch_bounds__(320, 2)
         }
     }
     if (!ok) *abort_word = 1;
-    // results: D columns [16h, 16h + 16) of this token, Gram halves summed
+    // the runs not drained yet (at most two): every MMA is complete after `done`
     bool have = ok && nchunks > 0 && mbar_wait_or_abort(done, 0u, abort_word);
     have = __all_sync(0xffffffffu, have);
     tc_fence_after();
-    const int64_t tok = t0 + r;
-    if (16 * h < NHP) {
-      float d[16];
-      if (have) {
-        tmem_ld16(tmem + ((uint32_t)(32 * qd) << 16) + 16 * h, d);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) d[e] = 0.f;
-      }
-      if (tok < B && (have || nchunks == 0)) {
-        float* pd = ppart + ((int64_t)split * B + tok) * NHP + 16 * h;
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          if (16 * h + e < NHP) pd[e] = d[e];
-      }
+    if (have) {
+      const int runs = (nchunks + DR - 1) / DR;
+      for (; drained < runs; ++drained) drain(drained & 1);
     }
+    // exchange: h = 1 hands its Gram half to h = 0, which adds the phi_hi and
+    // phi_lo columns of its token
     if (h == 1) {
 #pragma unroll
       for (int g = 0; g < NG; ++g) gx_s[r * NG + g] = gacc[g];
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
+    const int64_t tok = t0 + r;
     if (h == 0 && tok < B && (have || nchunks == 0)) {
+      float* pd = ppart + ((int64_t)split * B + tok) * NHP;
+#pragma unroll
+      for (int j = 0; j < NHP; ++j) pd[j] = acc_s[j * P::TOK] + acc_s[(NB + j) * P::TOK];
 #pragma unroll
       for (int g = 0; g < NG; ++g)
         gpart[((int64_t)split * B + tok) * NG + g] = gacc[g] + gx_s[r * NG + g];
@@ -443,6 +488,18 @@ __global__ void __launch_bounds__(320, 2)
 // ---------------------------------------------------------------------------
 
 
+// Add one D2 accumulator (this warp's 32 lanes x NH columns) into the fp32
+// sums in shared memory ([column][128 lanes], `d2s` already offset to the lane).
+__device__ __forceinline__ void gx6_drain_d2(uint32_t taddr, float* d2s) {
+  float a[16], b[16];
+  tmem_ld16(taddr, a);
+  tmem_ld16(taddr + 16, b);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) d2s[k * Gx6Cfg::COLS] += a[k];
+#pragma unroll
+  for (int k = 16; k < Gx6Cfg::NH; ++k) d2s[k * Gx6Cfg::COLS] += b[k - 16];
+}
+
 template <typename T>
 __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     grad_x6_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
@@ -468,6 +525,8 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
   uint64_t* loc_free = loc_ready + ND;
   uint64_t* d2_done = loc_free + ND;
   uint64_t* phi_ready = d2_done + 1;
+  uint64_t* d2_ready = phi_ready + 1;
+  uint64_t* d2_free = d2_ready + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(phi_ready + 1);
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t sbase = smem_u32(sm);
@@ -500,6 +559,10 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     }
     mbar_init(d2_done, 1);
     mbar_init(phi_ready, 4);
+    for (int d = 0; d < 2; ++d) {
+      mbar_init(&d2_ready[d], 1);
+      mbar_init(&d2_free[d], 4);
+    }
     *abort_word = 0;
     fence_mbar_init();
   }
@@ -570,27 +633,33 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       constexpr uint32_t ID2 = umma_idesc_tf32(128, F::KP);
       for (int j = 0; j < nb; ++j) {
         const int si = j % SI, b = j % ND;
+        const int run = j / F::DR2, ds = run & 1;
+        const bool first = j % F::DR2 == 0;
+        if (first && run >= 2 &&
+            !mbar_wait_or_abort(&d2_free[ds], (uint32_t)(((run - 2) >> 1) & 1), abort_word)) { *abort_word = 1; break; }
         if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { *abort_word = 1; break; }
         if (!mbar_wait_or_abort(&a2_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { *abort_word = 1; break; }
         tc_fence_after();
         const uint32_t im = sbase + SM::OFF_IMG + si * F::IMG;
         const uint32_t a2 = tmem + F::XT_COL + 2 * TOK * b;
+        const uint32_t d2 = tmem + (ds ? F::D2B_COL : F::D2_COL);
 #pragma unroll
         for (int ks = 0; ks < TOK / 8; ++ks) {
           const uint32_t ah = a2 + 8 * ks, al = a2 + TOK + 8 * ks;
           const uint64_t bh = umma_desc_k(im + F::IMG_B2H * 4, F::KP, ks, 0);
           const uint64_t bl = umma_desc_k(im + F::IMG_B2L * 4, F::KP, ks, 0);
           if constexpr (SM::BF16) {
-            umma_tf32_at(tmem + F::D2_COL, ah, bl, ID2, (j > 0 || ks > 0) ? 1u : 0u);
-            umma_tf32_at(tmem + F::D2_COL, ah, bh, ID2, 1u);
+            umma_tf32_at(d2, ah, bl, ID2, (!first || ks > 0) ? 1u : 0u);
+            umma_tf32_at(d2, ah, bh, ID2, 1u);
           } else {
-            umma_tf32_at(tmem + F::D2_COL, al, bh, ID2, (j > 0 || ks > 0) ? 1u : 0u);
-            umma_tf32_at(tmem + F::D2_COL, ah, bl, ID2, 1u);
-            umma_tf32_at(tmem + F::D2_COL, ah, bh, ID2, 1u);
+            umma_tf32_at(d2, al, bh, ID2, (!first || ks > 0) ? 1u : 0u);
+            umma_tf32_at(d2, ah, bl, ID2, 1u);
+            umma_tf32_at(d2, ah, bh, ID2, 1u);
           }
         }
         umma_commit(&a2_free[b]);
         umma_commit(&ifree[si]);
+        if (j % F::DR2 == F::DR2 - 1 || j == nb - 1) umma_commit(&d2_ready[ds]);
       }
       umma_commit(d2_done);
     }
@@ -706,8 +775,22 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       // ---------------- epilogue: grad_x = D1 + local term ----------------
       const int i = warp & 3;                // stream = tensor-memory lane quadrant
       const bool leader = warp == 2 + F::E_WARPS && lane == 0;
+      float* d2s = reinterpret_cast<float*>(sm + SM::OFF_D2S) + 32 * i + lane;
+#pragma unroll
+      for (int k = 0; k < F::NH; ++k) d2s[k * COLS] = 0.f;
+      int drained = 0;                       // D2 runs already added into d2s
       for (int j = 0; j < nb; ++j) {
         const int b = j % ND;
+        if (j == (drained + 1) * F::DR2 - 1 + F::LAG2) {
+          const int ds = drained & 1;
+          if (!mbar_wait_or_abort(&d2_ready[ds], (uint32_t)((drained >> 1) & 1), abort_word)) { ok = false; break; }
+          tc_fence_after();
+          gx6_drain_d2(tmem + ((uint32_t)(32 * i) << 16) + (ds ? F::D2B_COL : F::D2_COL), d2s);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&d2_free[ds]);
+          ++drained;
+        }
         if (!mbar_wait_or_abort(&d1_full[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
         if (!mbar_wait_or_abort(&loc_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
         tc_fence_after();
@@ -754,20 +837,19 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       have = __all_sync(0xffffffffu, have);
       const bool write = have || (ok && nb == 0);
       tc_fence_after();
-      float a[16], bb[16];
+      float* d2s = reinterpret_cast<float*>(sm + SM::OFF_D2S) + 32 * i + lane;
       if (have) {
-        tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + F::D2_COL, a);
-        tmem_ld16(tmem + ((uint32_t)(32 * i) << 16) + F::D2_COL + 16, bb);
-      } else {
-#pragma unroll
-        for (int q = 0; q < 16; ++q) { a[q] = 0.f; bb[q] = 0.f; }
+        // the runs not drained yet (at most two): every MMA is done after d2_done
+        const int runs = (nb + F::DR2 - 1) / F::DR2;
+        // the block loop drained run d at block (d + 1) DR2 - 1 + LAG2
+        int drained = nb >= F::LAG2 ? (nb - F::LAG2) / F::DR2 : 0;
+        for (; drained < runs; ++drained)
+          gx6_drain_d2(tmem + ((uint32_t)(32 * i) << 16) + ((drained & 1) ? F::D2B_COL : F::D2_COL), d2s);
       }
       if (write) {
         float* dd = dphi_part + (int64_t)split * F::NH * nC + (int64_t)i * C + c;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) dd[(int64_t)k * nC] = a[k];
-#pragma unroll
-        for (int k = 16; k < F::NH; ++k) dd[(int64_t)k * nC] = bb[k - 16];
+        for (int k = 0; k < F::NH; ++k) dd[(int64_t)k * nC] = d2s[k * COLS];
         if (i == 0) {
           float gsum = 0.f;
 #pragma unroll

@@ -69,7 +69,18 @@ extern "C" int mhc_layer_fwd_dynamic_noalloc(
     const float* b_pre, const float* b_post, const float* b_res, float* out, float* token_state,
     int64_t batch, int32_t n, int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps,
     float rmsnorm_eps, void* stream) {
-  const size_t need = mhc_layer_fwd_dynamic_workspace_bytes(batch, n, hidden);
+  // Bad arguments are reported as such, before the size check or any device call.
+  int rc = mhc::fwd_dynamic_check_args("mhc_layer_fwd_dynamic_noalloc", batch, n, hidden,
+                                       sinkhorn_iters, sinkhorn_eps, rmsnorm_eps);
+  if (rc) return rc;
+  if (batch == 0)  // nothing to compute: pointer checks only, no device work
+    return mhc_layer_fwd_dynamic(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
+                                 alpha_post, alpha_res, b_pre, b_post, b_res, out, token_state,
+                                 batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps,
+                                 nullptr, 0, stream);
+  // Exact need of this call: the token record is scratch only without token_state.
+  const size_t need =
+      mhc::fwd_dynamic_scratch_bytes(batch, n, hidden, token_state == nullptr);
   if (need > kNoAllocScratchBytes)
     return mhc::fail(MHC_ERR_UNSUPPORTED,
                      "mhc_layer_fwd_dynamic_noalloc: batch=%lld n=%d hidden=%lld needs %zu bytes of "
@@ -77,7 +88,7 @@ extern "C" int mhc_layer_fwd_dynamic_noalloc(
                      "or split the batch",
                      (long long)batch, n, (long long)hidden, need, kNoAllocScratchBytes);
   void* scratch = nullptr;
-  int rc = noalloc_scratch(&scratch);
+  rc = noalloc_scratch(&scratch);
   if (rc) return rc;
   return mhc_layer_fwd_dynamic(x, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
                                alpha_post, alpha_res, b_pre, b_post, b_res, out, token_state,

@@ -13,6 +13,8 @@
 // accesses when C % 4 == 0 and the pointers are 16-byte aligned.
 #include "common.cuh"
 
+#include <cuda_bf16.h>
+
 namespace mhc {
 namespace {
 
@@ -29,6 +31,10 @@ inline unsigned grid_for(int64_t work) {
 struct Scales {
   float s[kMaxStreams];
 };
+
+__device__ __forceinline__ float bf16_round(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
 
 __device__ __forceinline__ float4 scale4(float s, float4 v) {
   return make_float4(s * v.x, s * v.y, s * v.z, s * v.w);
@@ -59,6 +65,54 @@ __global__ void __launch_bounds__(256)
       float* o = out + t * n * C + q;
       for (int i = 0; i < n; ++i)
         o[i * C] = i == 1 ? br[e] : (i == 0 ? r : (sc.s[i] == 0.f ? 0.f : sc.s[i] * r));
+    }
+  }
+}
+
+// bf16 residual / branch (the reference packs in residual.dtype, layer.py:299-308):
+// streams i >= 2 are s_i * residual rounded to bf16 -- a bf16 tensor times a
+// Python float is computed in fp32 and rounded to bf16 -- then widened to the
+// fp32 layer input, as the reference's x.float() (layer.py:101) does.
+template <bool VEC>
+__global__ void __launch_bounds__(256)
+    pack_fwd_bf16_kernel(const __nv_bfloat16* __restrict__ res,
+                         const __nv_bfloat16* __restrict__ br, float* __restrict__ out,
+                         int64_t T, int n, int64_t C, Scales sc) {
+  const int64_t Cq = VEC ? C / 4 : C;
+  const int64_t total = T * Cq;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = e / Cq, q = e - t * Cq;
+    if (VEC) {
+      const uint2 rr = __ldg(reinterpret_cast<const uint2*>(res) + e);
+      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+      const float2 ra = __bfloat1622float2(r2[0]), rb = __bfloat1622float2(r2[1]);
+      const float4 r = make_float4(ra.x, ra.y, rb.x, rb.y);
+      float4* o = reinterpret_cast<float4*>(out) + t * n * Cq + q;
+      for (int i = 0; i < n; ++i) {
+        float4 v;
+        if (i == 1) {
+          const uint2 bb = __ldg(reinterpret_cast<const uint2*>(br) + e);
+          const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
+          const float2 ba = __bfloat1622float2(b2[0]), bc = __bfloat1622float2(b2[1]);
+          v = make_float4(ba.x, ba.y, bc.x, bc.y);
+        } else if (i == 0) {
+          v = r;
+        } else if (sc.s[i] == 0.f) {
+          v = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+          const float s = sc.s[i];
+          v = make_float4(bf16_round(s * r.x), bf16_round(s * r.y), bf16_round(s * r.z),
+                          bf16_round(s * r.w));
+        }
+        o[i * Cq] = v;
+      }
+    } else {
+      const float r = __bfloat162float(res[e]);
+      float* o = out + t * n * C + q;
+      for (int i = 0; i < n; ++i)
+        o[i * C] = i == 1 ? __bfloat162float(br[e])
+                          : (i == 0 ? r : (sc.s[i] == 0.f ? 0.f : bf16_round(sc.s[i] * r)));
     }
   }
 }
@@ -189,6 +243,31 @@ extern "C" int mhc_wrapper_pack_fwd(const float* residual, const float* branch, 
     pack_fwd_kernel<false><<<grid_for(tokens * hidden), 256, 0, s>>>(
         residual, branch, out, tokens, n, hidden, sc);
   return check_launch("mhc_wrapper_pack_fwd");
+}
+
+extern "C" int mhc_wrapper_pack_fwd_bf16(const void* residual, const void* branch, float* out,
+                                         const float* scales, int64_t tokens, int32_t n,
+                                         int64_t hidden, void* stream) {
+  int rc = check_shape("mhc_wrapper_pack_fwd_bf16", tokens, n, hidden);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(residual); MHC_REQUIRE_PTR(out); MHC_REQUIRE_PTR(scales);
+  MHC_REQUIRE(n < 2 || branch != nullptr, MHC_ERR_INVALID_ARG,
+              "mhc_wrapper_pack_fwd_bf16: branch must not be NULL for n >= 2");
+  if (tokens == 0 || hidden == 0) return MHC_OK;
+  const Scales sc = host_scales(scales, n);
+  cudaStream_t s = (cudaStream_t)stream;
+  const __nv_bfloat16* r = (const __nv_bfloat16*)residual;
+  const __nv_bfloat16* b = (const __nv_bfloat16*)branch;
+  const bool vec = hidden % 4 == 0 && ((uintptr_t)residual & 7) == 0 &&
+                   (branch == nullptr || ((uintptr_t)branch & 7) == 0) && aligned16(out);
+  ProfScope _ps("wrapper_pack_bf16", s);
+  if (vec)
+    pack_fwd_bf16_kernel<true><<<grid_for(tokens * hidden / 4), 256, 0, s>>>(r, b, out, tokens, n,
+                                                                           hidden, sc);
+  else
+    pack_fwd_bf16_kernel<false><<<grid_for(tokens * hidden), 256, 0, s>>>(r, b, out, tokens, n,
+                                                                        hidden, sc);
+  return check_launch("mhc_wrapper_pack_fwd_bf16");
 }
 
 extern "C" int mhc_wrapper_pack_bwd(const float* grad_out, float* grad_residual,

@@ -81,12 +81,16 @@ class GradBucket:
         flat = shared if shared is not None else self.pack()
         if world == 1:
             return None
-        work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+        # NCCL averages inside the collective (no separate scaling kernel);
+        # gloo has no AVG, so it sums and scales afterwards
+        nccl_avg = self.average and dist.get_backend(group) == "nccl"
+        op = dist.ReduceOp.AVG if nccl_avg else dist.ReduceOp.SUM
+        work = dist.all_reduce(flat, op=op, group=group, async_op=async_op)
 
         def finish():
             if work is not None and async_op:
                 work.wait()
-            if self.average:
+            if self.average and not nccl_avg:
                 flat.div_(world)
             if shared is None:
                 self.unpack(flat)

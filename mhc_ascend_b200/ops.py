@@ -409,13 +409,23 @@ class WrapperPackFunction(torch.autograd.Function):
     def forward(ctx, residual, branch, n, residual_mode):
         sc = wrapper_stream_scales(n, residual_mode)  # unknown modes: ValueError first
         _require_cuda("wrapper_pack", residual, branch)
-        r, b = _f32(residual), _f32(branch)
-        T, C = r.shape
-        out = torch.empty(T, n, C, dtype=torch.float32, device=r.device)
-        with _DevGuard(r):
-            rc = _lib.mhc_wrapper_pack_fwd(r.data_ptr(), b.data_ptr(), out.data_ptr(), sc, T, n,
-                                           C, _stream(r.device))
-        _C.check(rc, "mhc_wrapper_pack_fwd")
+        if residual.dtype == torch.bfloat16 and branch.dtype == torch.bfloat16:
+            # packed in bf16 like the reference (decayed copies rounded to bf16)
+            r, b = residual.contiguous(), branch.contiguous()
+            T, C = r.shape
+            out = torch.empty(T, n, C, dtype=torch.float32, device=r.device)
+            with _DevGuard(r):
+                rc = _lib.mhc_wrapper_pack_fwd_bf16(r.data_ptr(), b.data_ptr(), out.data_ptr(),
+                                                    sc, T, n, C, _stream(r.device))
+            _C.check(rc, "mhc_wrapper_pack_fwd_bf16")
+        else:
+            r, b = _f32(residual), _f32(branch)
+            T, C = r.shape
+            out = torch.empty(T, n, C, dtype=torch.float32, device=r.device)
+            with _DevGuard(r):
+                rc = _lib.mhc_wrapper_pack_fwd(r.data_ptr(), b.data_ptr(), out.data_ptr(), sc,
+                                               T, n, C, _stream(r.device))
+            _C.check(rc, "mhc_wrapper_pack_fwd")
         ctx.n, ctx.sc, ctx.dtypes = n, sc, (residual.dtype, branch.dtype)
         return out
 

@@ -26,20 +26,33 @@ def scaled_atol(expected, atol=ATOL):
     return atol * max(1.0, expected.detach().abs().max().item() if expected.numel() else 1.0)
 
 
-def close(actual, expected, rtol=RTOL, atol=ATOL, what=""):
+def close(actual, expected, rtol=RTOL, atol=ATOL, what="", scaled=False):
+    """|actual - expected| <= atol + rtol |expected| elementwise.  `scaled`
+    widens atol to the tensor's scale (scaled_atol) and is meant only for the
+    batch-reduced parameter gradients; per-token outputs (out, grad_x, ...)
+    are held to the unscaled bound.  Returns the max abs error (also printed)."""
     a = actual.detach().double().cpu()
     e = expected.detach().double().cpu()
     assert a.shape == e.shape, f"{what}: shape {tuple(a.shape)} != {tuple(e.shape)}"
     err = (a - e).abs()
-    atol = scaled_atol(e, atol)
+    if scaled:
+        atol = scaled_atol(e, atol)
     bound = atol + rtol * e.abs()
     bad = err > bound
+    max_err = err.max().item() if err.numel() else 0.0
+    print(f"{what}: max_abs_err={max_err:.3g} (atol={atol:.3g}, rtol={rtol:g})")
     if bad.any():
         idx = int(torch.argmax((err - bound).reshape(-1)))
         raise AssertionError(
             f"{what}: {int(bad.sum())}/{a.numel()} elements outside rtol={rtol} atol={atol}; "
             f"worst at flat index {idx}: actual={a.reshape(-1)[idx].item():.8g} "
-            f"expected={e.reshape(-1)[idx].item():.8g} max_abs_err={err.max().item():.3g}")
+            f"expected={e.reshape(-1)[idx].item():.8g} max_abs_err={max_err:.3g}")
+    return max_err
+
+
+def close_param(actual, expected, rtol=RTOL, atol=ATOL, what=""):
+    """Parameter gradients (sums over the batch): atol at the tensor's scale."""
+    return close(actual, expected, rtol, atol, what, scaled=True)
 
 
 def rel_err(actual, expected):
@@ -48,7 +61,7 @@ def rel_err(actual, expected):
     return ((a - e).norm() / e.norm().clamp_min(1e-30)).item()
 
 
-def close_ref(actual, ref32, truth, rtol=RTOL, atol=ATOL, what=""):
+def close_ref(actual, ref32, truth, rtol=RTOL, atol=ATOL, what="", scaled=False):
     """Parity with the reference's fp32 result `ref32`, judged against exact
     arithmetic `truth` (the same formulation evaluated in fp64):
 
@@ -57,11 +70,13 @@ def close_ref(actual, ref32, truth, rtol=RTOL, atol=ATOL, what=""):
       tolerance widened by the reference's own fp32 rounding error -- the fp32
       reference itself misses exact arithmetic by up to 3.6x the tolerance on
       ill-conditioned gradients (b_res, b_pre at BASELINE cfg1).
+
+    `scaled` (parameter gradients only) applies atol at the tensor's scale.
     """
-    close(actual, truth, rtol, atol, what + " (vs fp64 truth)")
+    close(actual, truth, rtol, atol, what + " (vs fp64 truth)", scaled=scaled)
     a = actual.detach().double().cpu()
     r = ref32.detach().double().cpu()
     t = truth.detach().double().cpu()
-    bound = scaled_atol(t, atol) + rtol * r.abs() + (r - t).abs()
+    bound = (scaled_atol(t, atol) if scaled else atol) + rtol * r.abs() + (r - t).abs()
     bad = (a - r).abs() > bound
     assert not bad.any(), f"{what}: {int(bad.sum())} elements outside the widened bound vs fp32 reference"

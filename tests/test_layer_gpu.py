@@ -6,7 +6,7 @@ import torch
 
 import mhc_ascend_b200 as mhc
 from oracle import mhc_oracle as O
-from tests.helpers import close, close_ref, golden, rel_err
+from tests.helpers import close, close_param, close_ref, golden, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -49,7 +49,7 @@ def test_dynamic_golden(cuda, case):
     close_ref(out, z["out"], ro, what="out")
     close_ref(grads["x"], z["grad_x"], rg["x"], what="grad_x")
     for k, v in KEYS.items():
-        close_ref(grads[k], z["grad_" + v], rg[k], what="grad_" + k)
+        close_ref(grads[k], z["grad_" + v], rg[k], what="grad_" + k, scaled=True)
 
 
 def oracle_case(B, n, C, seed, alpha=0.01, bias_std=0.0, weight=None):
@@ -90,7 +90,7 @@ def test_dynamic_vs_oracle(cuda, B, n, C, alpha, bias):
     close(out, ro, what="out")
     close(grads["x"], rg["x"], what="grad_x")
     for k in KEYS:
-        close(grads[k], rg[k], what="grad_" + k)
+        close_param(grads[k], rg[k], what="grad_" + k)
 
 
 def test_dynamic_inference_matches_training_forward(cuda):
@@ -128,14 +128,14 @@ def test_dynamic_cfg3_full_size(cuda):
     close(out, ro, what="out")
     close(grads["x"], rg["x"], what="grad_x")
     for k in KEYS:
-        close(grads[k], rg[k], what="grad_" + k)
+        close_param(grads[k], rg[k], what="grad_" + k)
     halves = []
     for sl in (slice(0, B // 2), slice(B // 2, B)):
         layer.zero_grad()
         _, gh = run_layer(layer, xd[sl], gd[sl])
         halves.append(gh)
     for k in KEYS:
-        close(halves[0][k] + halves[1][k], grads[k], what="linearity " + k)
+        close_param(halves[0][k] + halves[1][k], grads[k], what="linearity " + k)
 
 
 def test_static_golden(cuda):
@@ -151,9 +151,9 @@ def test_static_golden(cuda):
                               z["H_post"].double(), z["H_res"].double())
     close_ref(out, z["out"], ro, what="out")
     close_ref(grads["x"], z["grad_x"], rg["x"], what="grad_x")
-    close_ref(grads["rmsnorm_weight"], z["grad_w"], rg["rmsnorm_weight"], what="grad_w")
+    close_ref(grads["rmsnorm_weight"], z["grad_w"], rg["rmsnorm_weight"], what="grad_w", scaled=True)
     for k in ("H_pre", "H_post", "H_res"):
-        close_ref(grads[k], z["grad_" + k], rg[k], what=k)
+        close_ref(grads[k], z["grad_" + k], rg[k], what=k, scaled=True)
 
 
 @pytest.mark.parametrize("B,n,C", [(64, 4, 4096), (7, 4, 7168), (3, 8, 100), (5, 2, 4097),
@@ -175,7 +175,7 @@ def test_static_vs_oracle(cuda, B, n, C):
     close(out, ro, what="out")
     close(grads["x"], rg["x"], what="grad_x")
     for k in ("rmsnorm_weight", "H_pre", "H_post", "H_res"):
-        close(grads[k], rg[k], what=k)
+        close_param(grads[k], rg[k], what=k)
     layer.eval()
     with torch.no_grad():
         close(layer(x.to(cuda)), ro, what="inference out")
@@ -223,7 +223,7 @@ def test_dynamic_bf16_io(cuda, B, C):
     close(out.float(), ro, rtol=8e-3, atol=1e-2, what="bf16 out")
     close(xd.grad.float(), rg["x"], rtol=8e-3, atol=1e-2, what="bf16 grad_x")
     for k in KEYS:
-        close(getattr(layer, k).grad, rg[k], what="grad_" + k)
+        close_param(getattr(layer, k).grad, rg[k], what="grad_" + k)
     layer.eval()
     with torch.no_grad():
         assert torch.equal(layer(xb.to(cuda)), out.detach())
@@ -274,7 +274,51 @@ def test_residual_wrapper(cuda, n, mode, shape):
     else:
         assert bd.grad is None and br_.grad is None
     for k, p in w.mhc.named_parameters():
-        close(p.grad, params[k].grad, what="wrapper grad " + k)
+        close_param(p.grad, params[k].grad, what="wrapper grad " + k)
+
+
+@pytest.mark.parametrize("n,mode,shape", [(4, "decay", (2, 9, 4096)), (6, "decay", (5, 33)),
+                                          (3, "zero", (4, 64))])
+def test_residual_wrapper_bf16_inputs(cuda, n, mode, shape):
+    """bf16 residual / branch: the reference packs the streams in bf16
+    (layer.py:299-308: zeros in residual.dtype, decayed copies rounded to bf16),
+    then runs the layer in fp32 and returns fp32.  Packing is bit-exact with the
+    oracle's bf16 packing; the output meets the fp32 tolerance against the fp64
+    layer on those packed streams; input gradients come back bf16 (one bf16
+    rounding: rtol 8e-3 / atol 1e-2)."""
+    from mhc_ascend_b200 import ops
+    gen = torch.Generator().manual_seed(11 + n)
+    r = torch.randn(*shape, generator=gen).bfloat16()
+    b = torch.randn(*shape, generator=gen).bfloat16()
+    C = shape[-1]
+    streams_bf16, _ = O.residual_wrapper_pack(r, b, n, mode)
+    assert streams_bf16.dtype == torch.bfloat16
+    packed = ops.wrapper_pack(r.reshape(-1, C).to(cuda), b.reshape(-1, C).to(cuda), n, mode)
+    assert packed.dtype == torch.float32
+    assert torch.equal(packed.cpu(), streams_bf16.float())
+    w = mhc.replace_residual_with_mhc(hidden_dim=C, expansion_rate=n, residual_mode=mode).to(cuda)
+    with torch.no_grad():
+        for k, p in w.mhc.named_parameters():
+            if k.startswith("alpha"):
+                p.fill_(0.5)
+            elif k.startswith("b_"):
+                p.copy_(torch.randn(p.shape, generator=gen) * 0.5)
+    rd, bd = r.to(cuda).requires_grad_(True), b.to(cuda).requires_grad_(True)
+    out = w(rd, bd)
+    assert out.dtype == torch.float32 and out.shape == shape
+    gout = torch.randn(*shape, generator=gen)
+    out.backward(gout.to(cuda))
+    assert rd.grad.dtype == torch.bfloat16 and bd.grad.dtype == torch.bfloat16
+    params = {k: p.detach().cpu().double() for k, p in w.mhc.named_parameters()}
+    x64 = streams_bf16.double().requires_grad_(True)
+    ref = O.mhc_layer_dynamic(x64, *[params[k] for k in O.DYNAMIC_PARAM_ORDER]).mean(dim=1)
+    close(out.reshape(-1, C), ref, what="bf16 wrapper out")
+    ref.backward(gout.reshape(-1, C).double())
+    gx = x64.grad  # [T, n, C]; the pack's reverse in fp64
+    sc = [1.0, 0.0] + [(0.1 ** (i - 1) if mode == "decay" else 0.0) for i in range(2, n)]
+    g_res = sum(sc[i] * gx[:, i] for i in range(n) if i != 1)
+    close(rd.grad.float().reshape(-1, C), g_res, rtol=8e-3, atol=1e-2, what="bf16 wrapper grad residual")
+    close(bd.grad.float().reshape(-1, C), gx[:, 1], rtol=8e-3, atol=1e-2, what="bf16 wrapper grad branch")
 
 
 @pytest.mark.parametrize("n,mode,C", [(4, "decay", 4096), (6, "decay", 33), (5, "zero", 64),
