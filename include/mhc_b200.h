@@ -210,8 +210,10 @@ MHC_API int mhc_layer_fwd_dynamic_bf16(const void* x, const float* rmsnorm_weigh
  * cudaFree because they can synchronise the device): the scratch comes from
  * a 16 MiB array in the library's device image, which every GPU that loads
  * the library holds until the process exits.  Requests needing more than
- * 16 MiB (e.g. more than ~18k tokens at n=4, C=4096 with a token_state, ~10k
- * without) return MHC_ERR_UNSUPPORTED.  The first call on a
+ * 16 MiB return MHC_ERR_UNSUPPORTED; the need depends on the shape, on
+ * whether token_state is given (without it the record is scratch too) and on
+ * the SM count -- on a 148-SM B200 at n=4, C=4096 about 20k tokens fit with a
+ * token_state and about 16k without.  The first call on a
  * device looks up the array's device address (make it before any stream
  * capture).  All calls on a device share the array: calls whose kernels may
  * overlap on the GPU race and must be serialised by the caller. */

@@ -26,9 +26,10 @@
 namespace {
 
 // Fixed scratch capacity: 16 MiB per device that loads the library, held
-// until the process exits.  Covers the dynamic forward up to ~18k tokens at
-// n = 4, C = 4096 when the caller keeps the token state (~10k when the
-// record is scratch too; 8192 tokens need ~6 MiB).
+// until the process exits.  What fits depends on the shape and on the SM
+// count (the projection's split plan follows it): on a 148-SM B200 at n = 4,
+// C = 4096 about 20k tokens when the caller keeps token_state and about 16k
+// when the record lives in the scratch too (C = 7168: ~10.7k / ~5.4k).
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
