@@ -39,6 +39,7 @@
 #include "sinkhorn_lanes.cuh"
 #include "tma.cuh"
 #include <cuda_bf16.h>
+#include <type_traits>
 
 #include "layer/common.cuh"
 #include "layer/fwd.cuh"
@@ -286,6 +287,7 @@ int run_fwd_dynamic(const T* x, const float* w, const float* pp, const float* pq
 
   int rc = MHC_OK;
   bool done = false;
+  bool sumsq = false;  // the tensor-core projection: sum of squares only, r in stream_fwd_r
   int ks = p.ks;
   if constexpr (N <= 4) {
     // tcgen05 projection: phi split once into tf32 hi/lo rows, x streamed by TMA.
@@ -296,10 +298,12 @@ int run_fwd_dynamic(const T* x, const float* w, const float* pp, const float* pq
     CUtensorMap xmap, hmap, lmap;
     const uint64_t cs = (uint64_t)C * 4, rs = (uint64_t)nC * 4;
     const uint64_t xcs = (uint64_t)C * sizeof(T), xrs = (uint64_t)nC * sizeof(T);
-    // channels per split: a multiple of the stage width
-    const int ucps = (p.ucps + PU::CH - 1) / PU::CH * PU::CH;
+    // channels per split: a multiple of the x stage width
+    constexpr int SW = PU::CH * PU::XW;
+    const int ucps = (p.ucps + SW - 1) / SW * SW;
     const int uks = p.ucps > 0 ? (int)((C + ucps - 1) / ucps) : 0;
     if (p.uks > 0 && B > 0 && C % PU::CH == 0 && aligned16(x) && aligned16(ph) && aligned16(pl) &&
+        aligned16(out) && aligned16(w) &&
         make_tmap_3d(&xmap, tmap_dtype<T>(), x, C, N, B, xcs, xrs, PU::CH, 1, PU::TOK, CU_TENSOR_MAP_SWIZZLE_128B) &&
         make_tmap_3d_f32(&hmap, ph, C, N, PU::NB, cs, rs, 32, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B) &&
         make_tmap_3d_f32(&lmap, pl, C, N, PU::NB, cs, rs, 32, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B)) {
@@ -313,6 +317,7 @@ int run_fwd_dynamic(const T* x, const float* w, const float* pp, const float* pq
           xmap, hmap, lmap, ppart, gpart, B, C, ucps); }
       ks = uks;
       done = true;
+      sumsq = true;
     }
   }
   if constexpr (sizeof(T) == 2) {
@@ -345,10 +350,44 @@ int run_fwd_dynamic(const T* x, const float* w, const float* pp, const float* pq
   }
   rc = check_launch("mhc_layer_fwd_dynamic/proj_stats");
   if (rc) return rc;
-  { constexpr int TG = N <= 2 ? 2 : (N <= 4 ? 4 : 8); ProfScope _ps("token_fwd", s); if (B > 0) token_fwd_lanes_kernel<N><<<grid_1d(B * TG, 128), 128, 0, s>>>(ppart, gpart, ks, ap, aq, ar, bp, bq, br,
-                                                     rec, B, C, iters, s_eps, r_eps); }
+  {
+    constexpr int TG = N <= 2 ? 2 : (N <= 4 ? 4 : 8);
+    ProfScope _ps("token_fwd", s);
+    if (B > 0 && sumsq && N <= 4)
+      token_fwd_lanes_kernel<N, N <= 4><<<grid_1d(B * TG, 128), 128, 0, s>>>(
+          ppart, gpart, ks, ap, aq, ar, bp, bq, br, rec, B, C, iters, s_eps, r_eps);
+    else if (B > 0)
+      token_fwd_lanes_kernel<N, false><<<grid_1d(B * TG, 128), 128, 0, s>>>(
+          ppart, gpart, ks, ap, aq, ar, bp, bq, br, rec, B, C, iters, s_eps, r_eps);
+  }
   rc = check_launch("mhc_layer_fwd_dynamic/token_fwd");
   if (rc) return rc;
+  if constexpr (N <= 4) if (sumsq) {
+    // r and out from the token, register-resident when it fits
+    const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
+    const int64_t quads = C / 4;
+    ProfScope _ps("stream_fwd", s);
+    auto go = [&](auto gram) {
+      constexpr bool G = decltype(gram)::value;
+#ifdef MHC_EXP_QPT0
+      if (true) stream_fwd_r_kernel<N, 0, G, T><<<grid, 256, 0, s>>>(x, w, rec, out, B, C, r_eps); else
+#endif
+      if (quads <= 256)
+        stream_fwd_r_kernel<N, 1, G, T><<<grid, 256, 0, s>>>(x, w, rec, out, B, C, r_eps);
+      else if (quads <= 512)
+        stream_fwd_r_kernel<N, 2, G, T><<<grid, 256, 0, s>>>(x, w, rec, out, B, C, r_eps);
+      else if (quads <= 1024)
+        stream_fwd_r_kernel<N, 4, G, T><<<grid, 256, 0, s>>>(x, w, rec, out, B, C, r_eps);
+      else if (quads <= 2048)
+        stream_fwd_r_kernel<N, 4, G, T, 512><<<grid, 512, 0, s>>>(x, w, rec, out, B, C, r_eps);
+      else
+        stream_fwd_r_kernel<N, 0, G, T><<<grid, 256, 0, s>>>(x, w, rec, out, B, C, r_eps);
+    };
+    // the fp64 Gram matrix is only needed when the record is kept for a backward
+    if (need_rec) go(std::false_type{});
+    else go(std::true_type{});
+    return check_launch("mhc_layer_fwd_dynamic/stream_fwd");
+  }
   const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(out) && aligned16(w);
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
   // the fp64 Gram matrix is only needed when the record is kept for a backward

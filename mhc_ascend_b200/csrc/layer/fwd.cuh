@@ -297,7 +297,9 @@ __global__ void __launch_bounds__(PJT_THREADS, 1)
 // Forward 2: per-token gates, Sinkhorn and RMS (a group of lanes per token:
 // the Sinkhorn runs one row of M per lane, the rest is written by the first).
 // ---------------------------------------------------------------------------
-template <int N>
+// SUMSQ: the projection supplied only the sum of squares per split
+// (gpart = [ks][B]); r is then computed by stream_fwd_r_kernel.
+template <int N, bool SUMSQ = false>
 __global__ void __launch_bounds__(128)
     token_fwd_lanes_kernel(const float* __restrict__ ppart, const float* __restrict__ gpart, int ks,
                      const float* __restrict__ a_pre, const float* __restrict__ a_post,
@@ -315,22 +317,30 @@ __global__ void __launch_bounds__(128)
   // every lane of the warp takes part in the shuffles: dead groups evaluate
   // the last token and write nothing
   const int64_t b = live ? bt : B - 1;
-  float p[NH], G[NG];
+  float p[NH], G[SUMSQ ? 1 : NG];
 #pragma unroll
   for (int k = 0; k < NH; ++k) p[k] = 0.f;
 #pragma unroll
-  for (int g = 0; g < NG; ++g) G[g] = 0.f;
+  for (int g = 0; g < (SUMSQ ? 1 : NG); ++g) G[g] = 0.f;
   for (int s = 0; s < ks; ++s) {
     const float* pp = ppart + ((int64_t)s * B + b) * NHP;
-    const float* gp = gpart + ((int64_t)s * B + b) * NG;
 #pragma unroll
     for (int k = 0; k < NH; ++k) p[k] += pp[k];
+    if constexpr (SUMSQ) {
+      G[0] += gpart[(int64_t)s * B + b];
+    } else {
+      const float* gp = gpart + ((int64_t)s * B + b) * NG;
 #pragma unroll
-    for (int g = 0; g < NG; ++g) G[g] += gp[g];
+      for (int g = 0; g < NG; ++g) G[g] += gp[g];
+    }
   }
   float ss = 0.f;
+  if constexpr (SUMSQ) {
+    ss = G[0];
+  } else {
 #pragma unroll
-  for (int i = 0; i < N; ++i) ss += G[gram_index(i, i, N)];
+    for (int i = 0; i < N; ++i) ss += G[gram_index(i, i, N)];
+  }
   const float rms_h = sqrtf(ss / (float)(N * C) + r_eps);
   const float inv_h = 1.f / rms_h;
   const float ap = *a_pre, aq = *a_post, ar = *a_res;
@@ -352,14 +362,15 @@ __global__ void __launch_bounds__(128)
     for (int j = 0; j < N; ++j) o[Lc::OFF_M + row * N + j] = m[j];
   }
   if (row != 0) return;
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < N; ++i)
-#pragma unroll
-    for (int j = 0; j < N; ++j) q += h[i] * h[j] * G[gram_index(i, j, N)];
-  const float r = sqrtf(fmaxf(q, 0.f) / (float)C + r_eps);
   o[0] = rms_h;
-  o[1] = r;
+  if constexpr (!SUMSQ) {
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j) q += h[i] * h[j] * G[gram_index(i, j, N)];
+    o[1] = sqrtf(fmaxf(q, 0.f) / (float)C + r_eps);
+  }
 #pragma unroll
   for (int i = 0; i < N; ++i) {
     o[Lc::OFF_H + i] = h[i];
@@ -524,6 +535,164 @@ __global__ void __launch_bounds__(256)
         double t = 0.0;
         for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) t += s_g[wi * NG + threadIdx.x];
         reinterpret_cast<double*>(rec_w + b * Lc::REC + Lc::OFF_G64)[threadIdx.x] = t;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward 3 for the tensor-core projection (which supplies only sum(x^2)):
+// one CTA per token computes r = sqrt(mean_c x_agg^2 + eps) itself, then
+// out[i,c] = sum_j M_ij x[j,c] + hp_i * (w_c / r) * x_agg[c].
+//   QPT > 0: the token stays in registers (QPT channel quads per thread and
+//            stream, loaded up front), so x is read from HBM once;
+//   QPT = 0: any C -- the second loop reads x again (from L2: the CTA read it
+//            microseconds earlier).
+// Also the token's Gram matrix in fp64 (exact products) for the backward when
+// the record is kept.  Writes r into the record.
+// ---------------------------------------------------------------------------
+template <int N, int QPT, bool GRAM, typename T = float, int THREADS = 256>
+__global__ void __launch_bounds__(THREADS, THREADS <= 256 ? 2 : 1)
+    stream_fwd_r_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                        float* __restrict__ rec, T* __restrict__ out, int64_t B, int64_t C,
+                        float r_eps) {
+  using Lc = L<N>;
+  constexpr int NG = Lc::NG;
+  __shared__ float s_rec[Lc::REC];
+  __shared__ float red[32];
+  __shared__ double s_g[GRAM ? 32 * NG : 1];
+  const int64_t C4 = C / 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const T* xb = x + b * N * C;
+    T* ob = out + b * N * C;
+    // issue this token's loads before anything waits
+    typename IO<T>::raw4 xv[QPT > 0 ? QPT : 1][N];
+#pragma unroll
+    for (int u = 0; u < QPT; ++u) {
+      const int64_t q = threadIdx.x + (int64_t)u * blockDim.x;
+      if (q < C4) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) xv[u][j] = IO<T>::load_raw4(xb + j * C, q);
+      }
+    }
+    __syncthreads();  // s_rec / red of the previous token are no longer read
+    for (int e = threadIdx.x; e < Lc::REC; e += blockDim.x) s_rec[e] = rec[b * Lc::REC + e];
+    __syncthreads();
+    const float* h = s_rec + Lc::OFF_H;
+    const float* hp = s_rec + Lc::OFF_HP;
+    const float* m = s_rec + Lc::OFF_M;
+    double gacc[GRAM ? NG : 1];
+#pragma unroll
+    for (int g = 0; g < (GRAM ? NG : 1); ++g) gacc[g] = 0.0;
+    float sq = 0.f;
+    auto moments = [&](const float4 (&xf)[N]) {
+      if constexpr (GRAM) {
+        int g = 0;
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+#pragma unroll
+          for (int j = i; j < N; ++j) {
+            gacc[g] = fma((double)xf[i].x, (double)xf[j].x, gacc[g]);
+            gacc[g] = fma((double)xf[i].y, (double)xf[j].y, gacc[g]);
+            gacc[g] = fma((double)xf[i].z, (double)xf[j].z, gacc[g]);
+            gacc[g] = fma((double)xf[i].w, (double)xf[j].w, gacc[g]);
+            ++g;
+          }
+      }
+      float4 xa = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        xa.x = fmaf(h[j], xf[j].x, xa.x); xa.y = fmaf(h[j], xf[j].y, xa.y);
+        xa.z = fmaf(h[j], xf[j].z, xa.z); xa.w = fmaf(h[j], xf[j].w, xa.w);
+      }
+      sq += xa.x * xa.x + xa.y * xa.y + xa.z * xa.z + xa.w * xa.w;
+      return xa;
+    };
+    float4 xa_keep[QPT > 0 ? QPT : 1];
+    if constexpr (QPT > 0) {
+#pragma unroll
+      for (int u = 0; u < QPT; ++u) {
+        const int64_t q = threadIdx.x + (int64_t)u * blockDim.x;
+        xa_keep[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q < C4) {
+          float4 xf[N];
+#pragma unroll
+          for (int j = 0; j < N; ++j) xf[j] = IO<T>::to_f4(xv[u][j]);
+          xa_keep[u] = moments(xf);
+        }
+      }
+    } else {
+      for (int64_t q = threadIdx.x; q < C4; q += blockDim.x) {
+        float4 xf[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) xf[j] = IO<T>::to_f4(IO<T>::load_raw4(xb + j * C, q));
+        moments(xf);
+      }
+    }
+    // block sums: x_agg^2 (fp32) and the fp64 Gram, fixed order
+    sq = warp_sum(sq);
+    if (lane == 0) red[warp] = sq;
+    if constexpr (GRAM) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const double v = warp_sum_d(gacc[g]);
+        if (lane == 0) s_g[warp * NG + g] = v;
+      }
+    }
+    __syncthreads();
+    float tot = 0.f;
+    for (int k = 0; k < nw; ++k) tot += red[k];
+    const float r = sqrtf(tot / (float)C + r_eps);
+    const float inv_r = 1.f / r;
+    if (threadIdx.x == 0) rec[b * Lc::REC + 1] = r;
+    if constexpr (GRAM) {
+      if (threadIdx.x < NG) {
+        double t = 0.0;
+        for (int k = 0; k < nw; ++k) t += s_g[k * NG + threadIdx.x];
+        reinterpret_cast<double*>(rec + b * Lc::REC + Lc::OFF_G64)[threadIdx.x] = t;
+      }
+    }
+    auto emit = [&](int64_t q, const float4 (&xf)[N], float4 xa) {
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + q);
+      float4 y;
+      y.x = (xa.x * inv_r) * wv.x; y.y = (xa.y * inv_r) * wv.y;
+      y.z = (xa.z * inv_r) * wv.z; y.w = (xa.w * inv_r) * wv.w;
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float4 o;
+        o.x = hp[i] * y.x; o.y = hp[i] * y.y; o.z = hp[i] * y.z; o.w = hp[i] * y.w;
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          const float mij = m[i * N + j];
+          o.x = fmaf(mij, xf[j].x, o.x); o.y = fmaf(mij, xf[j].y, o.y);
+          o.z = fmaf(mij, xf[j].z, o.z); o.w = fmaf(mij, xf[j].w, o.w);
+        }
+        IO<T>::store4(ob + i * C, q, o);
+      }
+    };
+    if constexpr (QPT > 0) {
+#pragma unroll
+      for (int u = 0; u < QPT; ++u) {
+        const int64_t q = threadIdx.x + (int64_t)u * blockDim.x;
+        if (q < C4) {
+          float4 xf[N];
+#pragma unroll
+          for (int j = 0; j < N; ++j) xf[j] = IO<T>::to_f4(xv[u][j]);
+          emit(q, xf, xa_keep[u]);
+        }
+      }
+    } else {
+      for (int64_t q = threadIdx.x; q < C4; q += blockDim.x) {
+        float4 xf[N];
+        float4 xa = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          xf[j] = IO<T>::to_f4(IO<T>::load_raw4(xb + j * C, q));
+          xa.x = fmaf(h[j], xf[j].x, xa.x); xa.y = fmaf(h[j], xf[j].y, xa.y);
+          xa.z = fmaf(h[j], xf[j].z, xa.z); xa.w = fmaf(h[j], xf[j].w, xa.w);
+        }
+        emit(q, xf, xa);
       }
     }
   }

@@ -81,57 +81,65 @@ __device__ __forceinline__ void umma_tf32_at(uint32_t d_tmem, uint32_t a_tmem, u
 }
 
 // ---------------------------------------------------------------------------
-// Forward 1 on tcgen05: projection p = x_flat . phi^T and the per-token Gram
-// matrix of the n streams, for n <= 4 (C % 4 == 0, x 16-byte aligned).
+// Forward 1 on tcgen05: projection p = x_flat . phi^T and the per-token sum of
+// squares, for n <= 4 (C % 32 == 0 fp32 / % 64 bf16, x 16-byte aligned).
 //   CTA = 128 tokens (one M=128 MMA tile) x one split of the channels, two
 //   CTAs per SM, warp-specialised: warp 0 issues TMA, warp 1 issues MMAs,
 //   warps 2..9 (two threads per token, one per half of a 128-byte row)
-//   prepare the A operand.  A stage is one stream x 32 channels: x[128 tokens
-//   x 32] and phi[hi rows | lo rows][32] (phi split once per call into tf32
+//   prepare the A operand.  x arrives stream by stream in stages of XW
+//   128-byte boxes per token row (256 contiguous bytes per row: 128-byte row
+//   pieces cap DRAM at ~73% of its bandwidth, 256-byte ones reach ~90%); each
+//   box is one sub-chunk: x[128 tokens x 32 fp32 / 64 bf16 channels] and
+//   phi[hi rows | lo rows][those channels] (phi split once per call into tf32
 //   hi + lo, both 128-byte-swizzled as TMA writes them).  The operand threads
-//   read their token's row, keep the values of the n streams of a channel
-//   block in registers for the Gram entries, and store the row split into
-//   tf32 hi/lo into tensor memory with tcgen05.st (lane = token, column =
-//   channel: the A operand, no proxy fence).  3xTF32 in two MMAs per K-step:
+//   read their token's row, add its squares, and store it split into tf32
+//   hi/lo into tensor memory with tcgen05.st (lane = token, column = channel:
+//   the A operand, no proxy fence).  3xTF32 in two MMAs per K-step:
 //   x_hi . [phi_hi | phi_lo] (N = 2 NB: the hi.hi and hi.lo products land in
 //   separate accumulator columns) and x_lo . phi_hi (added to the hi.hi
-//   columns).  Every DR chunks the MMA warp switches between two accumulator
-//   sets and the operand warps add the finished set into fp32 registers, so
-//   no accumulation chain in tensor memory is longer than DR chunks.
-//   Barriers: full (TMA bytes), empty (operand warps done with x + MMA done
-//   with phi), aready / afree per tensor-memory A buffer, dready / dfree per
+//   columns).  Every DR sub-chunks the MMA warp switches between two
+//   accumulator sets and the operand warps add the finished set into fp32
+//   registers, so no accumulation chain in tensor memory is longer than DR
+//   sub-chunks.
+//   Barriers: xfull / xempty per x stage, pfull / pempty per phi stage,
+//   aready / afree per tensor-memory A buffer, dready / dfree per
 //   accumulator set.
 // ---------------------------------------------------------------------------
 template <int N, typename T = float>
 struct PumCfg {
-  static constexpr int NH = L<N>::NH, NHP = L<N>::NHP, NG = L<N>::NG;
+  static constexpr int NH = L<N>::NH, NHP = L<N>::NHP;
   static constexpr int NB = (NH + 7) / 8 * 8;              // phi rows per tile (8-row swizzle atoms)
   static constexpr int NC = 2 * NB;                        // MMA N of x_hi . [phi_hi | phi_lo]
   static constexpr int NLO = (NB + 15) / 16 * 16;          // MMA N of x_lo . phi_hi (<= NC)
-  // a stage is one 128-byte row of x per token: 32 fp32 or 64 bf16 channels
+  // a sub-chunk is one 128-byte box per token row: 32 fp32 or 64 bf16 channels
   static constexpr int TOK = 128, CH = 128 / (int)sizeof(T), THREADS = 320;
-  static constexpr int PSUB = CH / 32;                     // 32-channel phi sub-tiles per stage
+  static constexpr int PSUB = CH / 32;                     // 32-channel phi sub-tiles per sub-chunk
   static constexpr bool BF16 = sizeof(T) == 2;             // bf16 x is exact in tf32: no lo part
-  static constexpr uint32_t XB = TOK * 128;                // x tile of one stage
+  static constexpr int XW = 2;                             // boxes per x stage
+  static constexpr uint32_t XB = TOK * 128;                // one box of x
+  static constexpr uint32_t XS = XW * XB;                  // one x stage
   static constexpr uint32_t PT = NB * 128;                 // one phi_hi (or phi_lo) sub-tile
-  static constexpr uint32_t PB = 2 * PT * PSUB;            // phi of one stage: [hi | lo] per sub-tile
-  static constexpr uint32_t SLOT = XB + PB;
-  static constexpr uint32_t OFF_P = XB;
-  static constexpr uint32_t TX = SLOT;                     // bytes TMA brings per stage
-  static constexpr int STAGES = BF16 ? 2 : 3, NA = 2;      // smem stages, tensor-memory A buffers
+  static constexpr uint32_t PB = 2 * PT * PSUB;            // phi of one sub-chunk: [hi | lo] per sub-tile
+  // two rings, each refilled by its own producer thread: x (released once the
+  // operand warps hold it in registers) and phi (released when the
+  // sub-chunk's MMAs are done; deep, to hide the L2 latency between a
+  // sub-chunk's MMAs and the load of the phi tile SP sub-chunks later)
+  static constexpr int SX = 2, SP = BF16 ? 3 : 6, NA = 2;  // x stages, phi stages, tensor-memory A buffers
+  static constexpr uint32_t OFF_PR = SX * XS;              // phi ring after the x ring
   // tensor memory: accumulator sets D[s] = [64 s, 64 s + NC); A[a] = [128 + 64 a, +64): fp32 hi|lo, bf16 hi
   static constexpr uint32_t TCOLS = 256, ACOL = 128;
-  // chunks accumulated into one set before the operand warps add it into fp32
-  // sums in shared memory.  Accumulation in tensor memory rounds toward zero
-  // (measured: a relative shrink of ~2e-8 per accumulating MMA, uniform over
-  // all outputs), so chains stay at DR x 8 MMAs: 32 at DR = 4, ~6e-7.
+  // sub-chunks accumulated into one set before the operand warps add it into
+  // fp32 registers.  Accumulation in tensor memory rounds toward
+  // zero (measured: a relative shrink of ~2e-8 per accumulating MMA, uniform
+  // over all outputs), so chains stay at DR x 8 MMAs: 32 at DR = 4, ~6e-7.
   static constexpr int DR = 4;
-  static constexpr uint32_t OFF_GX = STAGES * SLOT;        // Gram exchange [128][NG]
-  static constexpr uint32_t OFF_ACC = OFF_GX + TOK * NG * 4; // drained sums [2 NB][128 tokens]
-  static constexpr uint32_t OFF_BAR = OFF_ACC + 2 * NB * TOK * 4;
-  static constexpr size_t SMEM = OFF_BAR + (2 * STAGES + 2 * NA + 4 + 1) * 8 + 16 + 1024;
+  static constexpr uint32_t OFF_BAR = OFF_PR + SP * PB;
+  // after the last MMA the x ring holds the exchange: sum of squares [128],
+  // phi_lo sums [NB][128]
+  static_assert(TOK * 4 + NB * TOK * 4 <= SX * XS, "exchange fits the x ring");
+  static constexpr size_t SMEM = OFF_BAR + (2 * SX + 2 * SP + 2 * NA + 4 + 1) * 8 + 16 + 1024;
   static_assert(NC <= 64 && NB % 8 == 0, "one 64-column accumulator set");
-  static_assert(XB % 1024 == 0 && PT % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+  static_assert(XB % 1024 == 0 && PT % 1024 == 0 && OFF_PR % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 };
 
 // phi_hi / phi_lo [NB rows x nC]: rows k < NH hold phi_k split into tf32 hi +
@@ -200,15 +208,16 @@ template <int N, typename T = float>
 __global__ void __launch_bounds__(320, 2)
     proj_umma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap hmap,
                      const __grid_constant__ CUtensorMap lmap, float* __restrict__ ppart,
-                     float* __restrict__ gpart, int64_t B, int64_t C, int cps) {
+                     float* __restrict__ sqpart, int64_t B, int64_t C, int cps) {
   using P = PumCfg<N, T>;
-  constexpr int NG = P::NG, NHP = P::NHP, NB = P::NB, S = P::STAGES, NA = P::NA, DR = P::DR;
+  constexpr int NHP = P::NHP, NB = P::NB, SX = P::SX, SP = P::SP, NA = P::NA, DR = P::DR, XW = P::XW;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* gx_s = reinterpret_cast<float*>(sm + P::OFF_GX);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + P::OFF_BAR);
-  uint64_t* empty = full + S;
-  uint64_t* aready = empty + S;
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(sm + P::OFF_BAR);
+  uint64_t* xempty = xfull + SX;
+  uint64_t* pfull = xempty + SX;
+  uint64_t* pempty = pfull + SP;
+  uint64_t* aready = pempty + SP;
   uint64_t* afree = aready + NA;
   uint64_t* dready = afree + NA;
   uint64_t* dfree = dready + 2;
@@ -221,8 +230,11 @@ __global__ void __launch_bounds__(320, 2)
   const int split = blockIdx.y;
   const int64_t c_begin = (int64_t)split * cps;
   const int64_t c_end = c_begin + cps < C ? c_begin + cps : C;
-  const int nblocks = c_begin < c_end ? (int)((c_end - c_begin + P::CH - 1) / P::CH) : 0;
-  const int nchunks = nblocks * N;
+  // boxes per stream, x stages per stream (the last one may hold fewer boxes)
+  const int nbox = c_begin < c_end ? (int)((c_end - c_begin + P::CH - 1) / P::CH) : 0;
+  const int nst = (nbox + XW - 1) / XW;
+  const int nstages = nst * N;
+  const int nchunks = nbox * N;            // sub-chunks, stream-major
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -233,9 +245,13 @@ __global__ void __launch_bounds__(320, 2)
     prefetch_tmap(&xmap);
     prefetch_tmap(&hmap);
     prefetch_tmap(&lmap);
-    for (int st = 0; st < S; ++st) {
-      mbar_init(&full[st], 1);
-      mbar_init(&empty[st], 1 + 8);
+    for (int st = 0; st < SX; ++st) {
+      mbar_init(&xfull[st], 1);
+      mbar_init(&xempty[st], 8);
+    }
+    for (int st = 0; st < SP; ++st) {
+      mbar_init(&pfull[st], 1);
+      mbar_init(&pempty[st], 1);
     }
     for (int a = 0; a < NA; ++a) {
       mbar_init(&aready[a], 8);
@@ -255,30 +271,43 @@ __global__ void __launch_bounds__(320, 2)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producers: lane 0 x, lane 1 phi ----------------
+    // (separate threads, so neither ring's refill waits on the other's)
     if (lane == 0) {
-      int issued = 0;
-      for (int k = 0; k < nchunks; ++k) {
-        const int slot = k % S;
-        if (k >= S && !mbar_wait_or_abort(&empty[slot], (uint32_t)(((k / S) - 1) & 1), abort_word)) {
+      int kx = 0;
+      for (; kx < nstages; ++kx) {
+        if (kx >= SX && !mbar_wait_or_abort(&xempty[kx % SX], (uint32_t)(((kx / SX) - 1) & 1), abort_word)) {
           *abort_word = 1;
           break;
         }
-        issued = k + 1;
-        unsigned char* base = sm + slot * P::SLOT;
-        const int c = (int)(c_begin + (int64_t)(k / N) * P::CH);
-        const int i = k % N;
-        mbar_expect_tx(&full[slot], P::TX);
-        tma_load_3d(base, &xmap, c, i, (int)t0, &full[slot]);
-#pragma unroll
-        for (int ps = 0; ps < P::PSUB; ++ps) {
-          tma_load_3d(base + P::OFF_P + ps * 2 * P::PT, &hmap, c + 32 * ps, i, 0, &full[slot]);
-          tma_load_3d(base + P::OFF_P + ps * 2 * P::PT + P::PT, &lmap, c + 32 * ps, i, 0, &full[slot]);
-        }
+        const int i = kx / nst, sb = kx % nst;
+        const int boxes = nbox - sb * XW < XW ? nbox - sb * XW : XW;
+        const int c = (int)(c_begin + (int64_t)sb * XW * P::CH);
+        unsigned char* xb = sm + (kx % SX) * P::XS;
+        mbar_expect_tx(&xfull[kx % SX], (uint32_t)boxes * P::XB);
+        for (int bb = 0; bb < boxes; ++bb)
+          tma_load_3d(xb + bb * P::XB, &xmap, c + bb * P::CH, i, (int)t0, &xfull[kx % SX]);
       }
       // no copy may still be landing when the CTA exits (bounded)
-      for (int q = issued > S ? issued - S : 0; q < issued; ++q)
-        mbar_wait(&full[q % S], (uint32_t)((q / S) & 1));
+      for (int q = kx > SX ? kx - SX : 0; q < kx; ++q) mbar_wait(&xfull[q % SX], (uint32_t)((q / SX) & 1));
+    } else if (lane == 1) {
+      int kp = 0;
+      for (; kp < nchunks; ++kp) {
+        if (kp >= SP && !mbar_wait_or_abort(&pempty[kp % SP], (uint32_t)(((kp / SP) - 1) & 1), abort_word)) {
+          *abort_word = 1;
+          break;
+        }
+        const int i = kp / nbox, bx = kp % nbox;
+        const int c = (int)(c_begin + (int64_t)bx * P::CH);
+        unsigned char* pb = sm + P::OFF_PR + (kp % SP) * P::PB;
+        mbar_expect_tx(&pfull[kp % SP], P::PB);
+#pragma unroll
+        for (int ps = 0; ps < P::PSUB; ++ps) {
+          tma_load_3d(pb + ps * 2 * P::PT, &hmap, c + 32 * ps, i, 0, &pfull[kp % SP]);
+          tma_load_3d(pb + ps * 2 * P::PT + P::PT, &lmap, c + 32 * ps, i, 0, &pfull[kp % SP]);
+        }
+      }
+      for (int q = kp > SP ? kp - SP : 0; q < kp; ++q) mbar_wait(&pfull[q % SP], (uint32_t)((q / SP) & 1));
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -286,35 +315,37 @@ __global__ void __launch_bounds__(320, 2)
       constexpr uint32_t IDC = umma_idesc_tf32(128, P::NC);
       constexpr uint32_t IDL = umma_idesc_tf32(128, P::NLO);
       for (int k = 0; k < nchunks; ++k) {
-        const int slot = k % S, a = k % NA;
+        const int slot = k % SP, a = k % NA;
         const int run = k / DR, ds = run & 1;
         const bool first = k % DR == 0;
         if ((first && run >= 2 &&
              !mbar_wait_or_abort(&dfree[ds], (uint32_t)(((run - 2) >> 1) & 1), abort_word)) ||
-            !mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word) ||
+            !mbar_wait_or_abort(&pfull[slot], (uint32_t)((k / SP) & 1), abort_word) ||
             !mbar_wait_or_abort(&aready[a], (uint32_t)((k / NA) & 1), abort_word)) {
           *abort_word = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t sb = sbase + slot * P::SLOT;
+        const uint32_t sb = sbase + P::OFF_PR + slot * P::PB;
         const uint32_t at = tmem + P::ACOL + 64 * a;
         const uint32_t dt = tmem + 64 * ds;
 #pragma unroll
         for (int st = 0; st < P::CH / 8; ++st) {
           const uint32_t boff = (st / 4) * 2 * P::PT + 32 * (st % 4);
-          const uint64_t bd = umma_desc_sw128(sb + P::OFF_P + boff);
+          const uint64_t bd = umma_desc_sw128(sb + boff);
+#ifndef MHC_EXP_NO_MMA
           umma_tf32_at(dt, at + 8 * st, bd, IDC, (first && st == 0) ? 0u : 1u);
           if constexpr (!P::BF16) umma_tf32_at(dt, at + 32 + 8 * st, bd, IDL, 1u);
+#endif
         }
-        umma_commit(&empty[slot]);
+        umma_commit(&pempty[slot]);
         umma_commit(&afree[a]);
         if (k % DR == DR - 1 || k == nchunks - 1) umma_commit(&dready[ds]);
       }
       umma_commit(done);
     }
   } else {
-    // ---------------- A operand (tensor memory) + Gram ----------------
+    // ---------------- A operand (tensor memory) + sum of squares ----------------
     const int cw = warp - 2;               // 0..7
     const int h = cw >> 2;                 // half of the 128-byte row; accumulator half
     const int qd = warp & 3;               // tensor-memory lane quadrant
@@ -324,14 +355,12 @@ __global__ void __launch_bounds__(320, 2)
     uint32_t choff[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) choff[j] = rowoff + (uint32_t)((((4 * h + j) ^ (r & 7))) * 16);
-    float gacc[NG];
-#pragma unroll
-    for (int g = 0; g < NG; ++g) gacc[g] = 0.f;
+    float sq = 0.f;
     // this thread's accumulator columns -- phi_hi terms (h = 0) or phi_lo terms
-    // (h = 1) -- summed in shared memory, [column][token] (conflict-free)
-    float* acc_s = reinterpret_cast<float*>(sm + P::OFF_ACC) + h * NB * P::TOK + r;
+    // (h = 1) -- summed in fp32 registers
+    float pacc[NB];
 #pragma unroll
-    for (int j = 0; j < NB; ++j) acc_s[j * P::TOK] = 0.f;
+    for (int j = 0; j < NB; ++j) pacc[j] = 0.f;
     auto drain = [&](int ds) {
 #pragma unroll
       for (int j = 0; j < NB; j += 8) {
@@ -342,19 +371,20 @@ __global__ void __launch_bounds__(320, 2)
                      : "r"(tmem + dlane + 64 * ds + NB * h + j));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc_s[(j + e) * P::TOK] += __uint_as_float(d[e]);
+        for (int e = 0; e < 8; ++e) pacc[j + e] += __uint_as_float(d[e]);
       }
     };
-    int drained = 0;  // accumulator runs already added into pacc
+    int drained = 0;  // accumulator runs already added into acc_s
     bool ok = true;
-    for (int b = 0; b < nblocks && ok; ++b) {
-      // this thread's 16 (fp32) or 32 (bf16) channels of each stream, as stored
-      uint4 v[N][4];
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        const int k = b * N + i;
-        const int slot = k % S, a = k % NA;
-        // run `drained` ended DR chunks ago plus one: its MMAs are done or nearly
+    int k = 0;        // sub-chunk
+    for (int ks = 0; ks < nstages && ok; ++ks) {
+      const int sb = ks % nst;
+      const int boxes = nbox - sb * XW < XW ? nbox - sb * XW : XW;
+      const int xslot = ks % SX;
+      if (!mbar_wait_or_abort(&xfull[xslot], (uint32_t)((ks / SX) & 1), abort_word)) { ok = false; break; }
+      for (int bb = 0; bb < boxes; ++bb, ++k) {
+        const int a = k % NA;
+        // run `drained` ended one sub-chunk ago: its MMAs are done or nearly
         if (k == (drained + 1) * DR + 1) {
           const int ds = drained & 1;
           if (!mbar_wait_or_abort(&dready[ds], (uint32_t)((drained >> 1) & 1), abort_word)) { ok = false; break; }
@@ -365,12 +395,15 @@ __global__ void __launch_bounds__(320, 2)
           if (lane == 0) mbar_arrive(&dfree[ds]);
           ++drained;
         }
-        const unsigned char* base = sm + slot * P::SLOT;
-        if (!mbar_wait_or_abort(&full[slot], (uint32_t)((k / S) & 1), abort_word)) { ok = false; break; }
+        // this thread's 16 (fp32) or 32 (bf16) channels, as stored
+        const unsigned char* base = sm + xslot * P::XS + bb * P::XB;
+        uint4 v[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[i][j] = *reinterpret_cast<const uint4*>(base + choff[j]);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);  // x of this stage now lives in registers
+        for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const uint4*>(base + choff[j]);
+        if (bb == boxes - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&xempty[xslot]);  // the stage now lives in registers
+        }
         if (k >= NA && !mbar_wait_or_abort(&afree[a], (uint32_t)(((k / NA) - 1) & 1), abort_word)) { ok = false; break; }
         tc_fence_after();
         if constexpr (P::BF16) {
@@ -381,50 +414,40 @@ __global__ void __launch_bounds__(320, 2)
             uint32_t hi[16];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const uint32_t w2 = (&v[i][2 * hf].x)[e];   // channels 2e, 2e+1 of chunks 2hf, 2hf+1
+              const uint32_t w2 = (&v[2 * hf].x)[e];   // channels 2e, 2e+1 of chunks 2hf, 2hf+1
               hi[2 * e] = w2 << 16;
               hi[2 * e + 1] = w2 & 0xFFFF0000u;
+              sq = fmaf(__uint_as_float(hi[2 * e]), __uint_as_float(hi[2 * e]), sq);
+              sq = fmaf(__uint_as_float(hi[2 * e + 1]), __uint_as_float(hi[2 * e + 1]), sq);
             }
             tmem_st16(ta + 16 * hf, hi);
           }
         } else {
           const uint32_t ta = tmem + dlane + P::ACOL + 64 * a + 16 * h;
+          float blk = 0.f;
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
             uint32_t hi[8], lo[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) split_tf32(__uint_as_float((&v[i][2 * hf].x)[e]), hi[e], lo[e]);
+            for (int e = 0; e < 8; ++e) {
+              const float xe = __uint_as_float((&v[2 * hf].x)[e]);
+              blk = fmaf(xe, xe, blk);
+              split_tf32(xe, hi[e], lo[e]);
+            }
+#ifndef MHC_EXP_NO_ST
             tmem_st8(ta + 8 * hf, hi);
             tmem_st8(ta + 32 + 8 * hf, lo);
+#else
+            if (hi[0] == 0x7fffffffu && lo[0] == 1u) tmem_st8(ta + 8 * hf, hi);
+#endif
           }
+          sq += blk;  // per-box partial first: the rounding grows with boxes, not channels
         }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&aready[a]);
       }
-      if (!ok) break;
-      // Gram of this block first, then the running sum: the rounding error
-      // grows with the number of blocks, not of channels
-      int g = 0;
-#pragma unroll
-      for (int i = 0; i < N; ++i)
-#pragma unroll
-        for (int j = i; j < N; ++j) {
-          float blk = 0.f;
-#pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const uint32_t ui = (&v[i][0].x)[q], uj = (&v[j][0].x)[q];
-            if constexpr (P::BF16) {
-              blk = fmaf(__uint_as_float(ui << 16), __uint_as_float(uj << 16), blk);
-              blk = fmaf(__uint_as_float(ui & 0xFFFF0000u), __uint_as_float(uj & 0xFFFF0000u), blk);
-            } else {
-              blk = fmaf(__uint_as_float(ui), __uint_as_float(uj), blk);
-            }
-          }
-          gacc[g] += blk;
-          ++g;
-        }
     }
     if (!ok) *abort_word = 1;
     // the runs not drained yet (at most two): every MMA is complete after `done`
@@ -435,21 +458,22 @@ __global__ void __launch_bounds__(320, 2)
       const int runs = (nchunks + DR - 1) / DR;
       for (; drained < runs; ++drained) drain(drained & 1);
     }
-    // exchange: h = 1 hands its Gram half to h = 0, which adds the phi_hi and
-    // phi_lo columns of its token
+    // exchange: h = 1 hands its sum of squares and phi_lo columns to h = 0
+    // ([column][token]: conflict-free)
+    float* sq_s = reinterpret_cast<float*>(sm);  // the x ring is idle once every MMA is done
+    float* px_s = sq_s + P::TOK + r;
     if (h == 1) {
+      sq_s[r] = sq;
 #pragma unroll
-      for (int g = 0; g < NG; ++g) gx_s[r * NG + g] = gacc[g];
+      for (int j = 0; j < NB; ++j) px_s[j * P::TOK] = pacc[j];
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
     const int64_t tok = t0 + r;
     if (h == 0 && tok < B && (have || nchunks == 0)) {
       float* pd = ppart + ((int64_t)split * B + tok) * NHP;
 #pragma unroll
-      for (int j = 0; j < NHP; ++j) pd[j] = acc_s[j * P::TOK] + acc_s[(NB + j) * P::TOK];
-#pragma unroll
-      for (int g = 0; g < NG; ++g)
-        gpart[((int64_t)split * B + tok) * NG + g] = gacc[g] + gx_s[r * NG + g];
+      for (int j = 0; j < NHP; ++j) pd[j] = pacc[j] + px_s[j * P::TOK];
+      sqpart[(int64_t)split * B + tok] = sq + sq_s[r];
     }
   }
   // the MMA issuer drains its last batch before tensor memory is released
@@ -619,9 +643,11 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
           const uint32_t ah = tmem + F::A1_COL + 8 * ks, al = tmem + F::A1L_COL + 8 * ks;
           const uint64_t bh = umma_desc_k(im + F::IMG_B1H * 4, TOK, ks, 0);
           const uint64_t bl = umma_desc_k(im + F::IMG_B1L * 4, TOK, ks, 0);
+#ifndef MHC_EXP_G_NO_D1
           umma_tf32_at(tmem + TOK * b, al, bh, ID1, ks > 0 ? 1u : 0u);
           umma_tf32_at(tmem + TOK * b, ah, bl, ID1, 1u);
           umma_tf32_at(tmem + TOK * b, ah, bh, ID1, 1u);
+#endif
         }
         umma_commit(&d1_full[b]);
         umma_commit(&ifree[si]);
@@ -648,10 +674,19 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
           const uint32_t ah = a2 + 8 * ks, al = a2 + TOK + 8 * ks;
           const uint64_t bh = umma_desc_k(im + F::IMG_B2H * 4, F::KP, ks, 0);
           const uint64_t bl = umma_desc_k(im + F::IMG_B2L * 4, F::KP, ks, 0);
+#ifdef MHC_EXP_G_NO_D2
+          if (false) {
+#else
           if constexpr (SM::BF16) {
+#endif
             umma_tf32_at(d2, ah, bl, ID2, (!first || ks > 0) ? 1u : 0u);
             umma_tf32_at(d2, ah, bh, ID2, 1u);
-          } else {
+          } else
+#ifndef MHC_EXP_G_NO_D2
+          {
+#else
+          if (false) {
+#endif
             umma_tf32_at(d2, al, bh, ID2, (!first || ks > 0) ? 1u : 0u);
             umma_tf32_at(d2, ah, bl, ID2, 1u);
             umma_tf32_at(d2, ah, bh, ID2, 1u);
@@ -816,17 +851,13 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
                                        : static_cast<const void*>(locs + b * (F::LOCB / 4)),
                        (int)c0, (int)((blk0 + j) * TOK * 4));
           bulk_commit();
-          // the previous block's buffer may be refilled once its store has read it
-          if (j > 0) {
-            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-            mbar_arrive(&loc_free[(j - 1) % ND]);
-          }
+          // the buffer may be refilled as soon as its store has read it: the
+          // E warps then fill block j + 2 while this epilogue runs block j + 1
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          mbar_arrive(&loc_free[b]);
         }
       }
-      if (leader) {
-        bulk_wait0();
-        if (ok && nb > 0) mbar_arrive(&loc_free[(nb - 1) % ND]);
-      }
+      if (leader) bulk_wait0();
     }
     if (!ok) *abort_word = 1;
     asm volatile("bar.sync 1, %0;" ::"r"(32 * (F::E_WARPS + 4)) : "memory");
