@@ -597,28 +597,35 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
+    // g/x (SG-deep) and the operand image (SI-deep) are refilled
+    // independently: whichever ring has a free slot is served, so a late
+    // image slot does not hold back the g/x stream (bounded: a poll budget)
     if (lane == 0) {
       int gi = 0, ii = 0;
-      for (int j = 0; j < nb; ++j) {
-        const int sg = j % SG, si = j % SI;
-        if (j >= SG && !mbar_wait_or_abort(&gfree[sg], (uint32_t)(((j / SG) - 1) & 1), abort_word)) {
-          *abort_word = 1;
-          break;
+      uint32_t idle = 0;
+      while ((gi < nb || ii < nb) && !*abort_word) {
+        if (gi < nb && (gi < SG || mbar_try(&gfree[gi % SG], (uint32_t)(((gi / SG) - 1) & 1)))) {
+          const int sg = gi % SG;
+          const int row = (int)((blk0 + gi) * TOK * 4);
+          unsigned char* gb = sm + sg * 2 * SM::GB;
+          mbar_expect_tx(&gfull[sg], 2 * SM::GB);
+          tma_load_2d(gb, &gmap, (int)c0, row, &gfull[sg]);
+          tma_load_2d(gb + SM::GB, &xmap, (int)c0, row, &gfull[sg]);
+          ++gi;
+          idle = 0;
+        } else if (ii < nb && (ii < SI || mbar_try(&ifree[ii % SI], (uint32_t)(((ii / SI) - 1) & 1)))) {
+          const int si = ii % SI;
+          mbar_expect_tx(&ifull[si], F::IMG);
+          bulk_load(sm + SM::OFF_IMG + si * F::IMG, img + (blk0 + ii) * F::IMG_FLOATS, F::IMG, &ifull[si]);
+          ++ii;
+          idle = 0;
+        } else {
+          __nanosleep(64);
+          if (++idle >= kSpinLimit) {
+            atomicExch(&g_mhc_device_error, 1);
+            *abort_word = 1;
+          }
         }
-        const int64_t blk = blk0 + j;
-        const int row = (int)(blk * TOK * 4);
-        unsigned char* gb = sm + sg * 2 * SM::GB;
-        mbar_expect_tx(&gfull[sg], 2 * SM::GB);
-        tma_load_2d(gb, &gmap, (int)c0, row, &gfull[sg]);
-        tma_load_2d(gb + SM::GB, &xmap, (int)c0, row, &gfull[sg]);
-        gi = j + 1;
-        if (j >= SI && !mbar_wait_or_abort(&ifree[si], (uint32_t)(((j / SI) - 1) & 1), abort_word)) {
-          *abort_word = 1;
-          break;
-        }
-        mbar_expect_tx(&ifull[si], F::IMG);
-        bulk_load(sm + SM::OFF_IMG + si * F::IMG, img + blk * F::IMG_FLOATS, F::IMG, &ifull[si]);
-        ii = j + 1;
       }
       // no copy may still be landing when the CTA exits (bounded)
       for (int q = gi > SG ? gi - SG : 0; q < gi; ++q) mbar_wait(&gfull[q % SG], (uint32_t)((q / SG) & 1));
