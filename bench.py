@@ -536,7 +536,8 @@ def run_mine(args, world, rank, local):
         line = {
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if args.global_tokens else "weak",
+            "vs_baseline": None,
             "dtype": "bf16" if mode.endswith("bf16") else "f32", "data": "synthetic",
             "impl": "mine",
             "config": {"workload": f"{args.config}: {mode}, n={n}, C={C}, {tokens} tokens per GPU "
@@ -562,14 +563,78 @@ def run_mine(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_ops(args, world, rank, local):
+    """BASELINE cfg2: the standalone operators (reference ops.py:32-188) at
+    their stated shapes, each timed on its own through the C-ABI with CUDA
+    events (launch-scale work: GB/s is reported, not graded)."""
+    from mhc_ascend_b200 import ops
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+
+    def timed(name, fn, nbytes, reps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res[name] = {"ms": ms, "algorithmic_bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9}
+
+    reps = max(20, min(args.steps, 200))
+    # Sinkhorn fwd+bwd, [65536, 4, 4] ~ U[0,1), 20 iterations, upstream grad ~ N(0,1)
+    sk = torch.rand(65536, 4, 4, device=dev, generator=gen)
+    skg = torch.randn(65536, 4, 4, device=dev, generator=gen)
+
+    def sink():
+        out = ops.sinkhorn_knopp_fwd(sk, 20, 1e-8)
+        ops.sinkhorn_knopp_bwd(skg, sk, out, 20, 1e-8)
+    timed("sinkhorn_fwd_bwd_65536x4x4", sink, 5 * 65536 * 16 * 4, reps)
+    # RMSNorm fwd, x [1024, 4096] ~ N(0,1), weight ~ U[0.5, 1.5)
+    rx = torch.randn(1024, 4096, device=dev, generator=gen)
+    rw = torch.rand(4096, device=dev, generator=gen) + 0.5
+    timed("rmsnorm_fwd_1024x4096", lambda: ops.rmsnorm_fwd(rx, rw, 1e-5),
+          2 * 1024 * 4096 * 4 + 4096 * 4, reps)
+    # stream_aggregate fwd+bwd, [32, 4, 256], H_pre [32, 4]
+    ax = torch.randn(32, 4, 256, device=dev, generator=gen)
+    ah = torch.randn(32, 4, device=dev, generator=gen)
+    ag = torch.randn(32, 256, device=dev, generator=gen)
+
+    def agg():
+        out, hact = ops.stream_aggregate_fwd(ax, ah)
+        ops.stream_aggregate_bwd(ag, ax, hact)
+    timed("stream_aggregate_fwd_bwd_32x4x256", agg,
+          131072 + 512 + 32768 + 32768 + 131072 + 512 + 131072 + 512, reps)
+    peak, peak_kind = peaks()
+    line = {"metric": "cfg2 standalone operators (GB/s reported, not graded)",
+            "value": res["sinkhorn_fwd_bwd_65536x4x4"]["gbs"], "unit": "GB/s",
+            "n_gpus": 1, "steps": reps, "warmup": max(3, args.warmup), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "mine", "config": {"workload": "cfg2: sinkhorn 65536x4x4 fwd+bwd, rmsnorm "
+                                                   "[1024,4096] fwd, stream_aggregate [32,4,256] fwd+bwd",
+                                       "l2": "operands fit in L2 (launch-scale work)"},
+            "ops": res, "peak_gbs": peak, "peak_kind": peak_kind}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg3")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg2"], default="cfg3")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU")
+    ap.add_argument("--global-tokens", type=int, default=0,
+                    help="strong scaling: a fixed global batch split evenly over the GPUs")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -578,7 +643,16 @@ def main():
         args.warmup = 3
     world, rank, local = dist_setup(args)
     try:
-        if args.impl == "reference":
+        if args.global_tokens:
+            args.tokens = args.global_tokens // world
+        if args.config == "cfg2":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable":
+                                      "cfg2 is reported for this build's operators only"}))
+            else:
+                run_ops(args, world, rank, local)
+        elif args.impl == "reference":
             run_reference(args, world, rank)
         else:
             run_mine(args, world, rank, local)

@@ -266,6 +266,35 @@ template <typename T> constexpr CUtensorMapDataType tmap_dtype() {
   return sizeof(T) == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
 }
 
+// Shared-memory staged forward 3 (token_stream_fwd_kernel): launched when a
+// ring of at least two token buffers fits in shared memory and the rows are
+// 16-byte aligned; returns false otherwise (the caller uses another kernel).
+template <int N, typename T, bool DYN, bool GRAM>
+bool launch_token_stream(const T* x, const float* w, float* rec, float* rms, T* out, int64_t B,
+                         int64_t C, float r_eps, cudaStream_t s) {
+  if (B <= 0 || (C * (int64_t)sizeof(T)) % 16 != 0 || !aligned16(x) || !aligned16(out) ||
+      !aligned16(w))
+    return false;
+  const size_t tok = ((size_t)N * C * sizeof(T) + (DYN ? L<N>::REC * 4 : 0) + 127) & ~(size_t)127;
+  // dynamic shared memory left next to the kernel's static arrays (227 KB opt-in)
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, token_stream_fwd_kernel<N, T, DYN, GRAM>) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  const size_t avail = (size_t)227 * 1024 - fa.sharedSizeBytes;
+  int nbuf = (int)((avail - 4 * 8) / tok);
+  if (nbuf > 4) nbuf = 4;
+  if (nbuf < 2) return false;
+  const size_t smem = (size_t)nbuf * tok + (size_t)nbuf * 8;
+  cudaFuncSetAttribute(token_stream_fwd_kernel<N, T, DYN, GRAM>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int64_t g = B < num_sms() ? B : num_sms();
+  token_stream_fwd_kernel<N, T, DYN, GRAM><<<(unsigned)g, kTsThreads, smem, s>>>(
+      x, w, rec, rms, out, B, C, r_eps, nbuf);
+  return true;
+}
+
 // T = float, or __nv_bfloat16 for bf16 streams (x, out; fp32 arithmetic), which
 // needs the tensor-core projection (n <= 4, C % 64 == 0, 16-byte aligned).
 template <int N, typename T = float>
@@ -369,9 +398,10 @@ int run_fwd_dynamic(const T* x, const float* w, const float* pp, const float* pq
     ProfScope _ps("stream_fwd", s);
     auto go = [&](auto gram) {
       constexpr bool G = decltype(gram)::value;
-#ifdef MHC_EXP_QPT0
-      if (true) stream_fwd_r_kernel<N, 0, G, T><<<grid, 256, 0, s>>>(x, w, rec, out, B, C, r_eps); else
-#endif
+      // tokens that fit two CTAs' registers per SM stream best from registers;
+      // larger ones from the shared-memory ring
+      if (quads > 1024 && launch_token_stream<N, T, true, G>(x, w, rec, nullptr, out, B, C, r_eps, s))
+        return;
       if (quads <= 256)
         stream_fwd_r_kernel<N, 1, G, T><<<grid, 256, 0, s>>>(x, w, rec, out, B, C, r_eps);
       else if (quads <= 512)
@@ -506,6 +536,14 @@ int run_fwd_static(const T* x, const float* w, const float* Hp, const float* Hq,
   const int64_t q = (C / 4 + 255) / 256;  // quads per thread
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
   if (B == 0) return MHC_OK;
+  {
+    bool staged;
+    {
+      ProfScope _ps("static_fwd", s);
+      staged = launch_token_stream<N, T, false, false>(x, w, rec, rms, out, B, C, r_eps, s);
+    }
+    if (staged) return check_launch("mhc_layer_fwd_static");
+  }
   if (vec && q <= 1) { ProfScope _ps("static_fwd", s); static_fwd_kernel<N, 1, T><<<grid, 256, 0, s>>>(x, w, rec, rms, out, B, C, r_eps); }
   else if (vec && q <= 2) { ProfScope _ps("static_fwd", s); static_fwd_kernel<N, 2, T><<<grid, 256, 0, s>>>(x, w, rec, rms, out, B, C, r_eps); }
   else if (vec && q <= 4) { ProfScope _ps("static_fwd", s); static_fwd_kernel<N, 4, T><<<grid, 256, 0, s>>>(x, w, rec, rms, out, B, C, r_eps); }

@@ -552,7 +552,7 @@ __global__ void __launch_bounds__(256)
 // the record is kept.  Writes r into the record.
 // ---------------------------------------------------------------------------
 template <int N, int QPT, bool GRAM, typename T = float, int THREADS = 256>
-__global__ void __launch_bounds__(THREADS, THREADS <= 256 ? 2 : 1)
+__global__ void __launch_bounds__(THREADS, THREADS <= 256 ? (sizeof(T) == 2 ? 3 : 2) : 1)
     stream_fwd_r_kernel(const T* __restrict__ x, const float* __restrict__ w,
                         float* __restrict__ rec, T* __restrict__ out, int64_t B, int64_t C,
                         float r_eps) {
@@ -695,6 +695,156 @@ __global__ void __launch_bounds__(THREADS, THREADS <= 256 ? 2 : 1)
         emit(q, xf, xa);
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward 3, shared-memory staged (n <= 4 dynamic H after the tensor-core
+// projection, and static H): a persistent CTA per SM walks tokens b =
+// blockIdx.x + k gridDim.x.  One thread keeps NBUF-1 tokens in flight with
+// bulk copies (one per stream row) into a ring of token buffers, so HBM is
+// busy while the CTA reduces and writes the current token; per token
+//   r = sqrt(mean_c x_agg^2 + eps), x_agg = sum_j h_j x[j,c]
+//   out[i,c] = sum_j M_ij x[j,c] + hp_i (w_c / r) x_agg[c]
+// DYN: h, hp, M from the token's record, r and (GRAM) the fp64 Gram matrix
+// written back into it; static: one shared record, r into rms[] (optional).
+// Needs C * sizeof(T) % 16 == 0 and 16-byte aligned x / out / w.
+// ---------------------------------------------------------------------------
+constexpr int kTsThreads = 512;
+
+template <int N, typename T, bool DYN, bool GRAM>
+__global__ void __launch_bounds__(kTsThreads, 1)
+    token_stream_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                            float* __restrict__ rec, float* __restrict__ rms,
+                            T* __restrict__ out, int64_t B, int64_t C, float r_eps, int nbuf) {
+  using Lc = L<N>;
+  constexpr int NG = Lc::NG;
+  extern __shared__ __align__(16) unsigned char ts_smem[];
+  // a token buffer: the n stream rows, then (DYN) the token's record
+  const uint32_t tok_bytes = (uint32_t)(N * C * sizeof(T));
+  constexpr uint32_t REC_BYTES = DYN ? Lc::REC * 4 : 0;
+  const uint32_t tok_stride = (tok_bytes + REC_BYTES + 127) & ~127u;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ts_smem + (size_t)nbuf * tok_stride);
+  __shared__ float s_rec0[DYN ? 1 : Lc::REC];
+  __shared__ float red[32];
+  __shared__ double s_g[GRAM ? 16 * NG : 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t C4 = C / 4;
+  const int64_t first = blockIdx.x, step = gridDim.x;
+  auto fetch = [&](int64_t b, int slot) {
+    mbar_expect_tx(&full[slot], tok_bytes + REC_BYTES);
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      bulk_load(ts_smem + (size_t)slot * tok_stride + (size_t)i * C * sizeof(T),
+                x + (b * N + i) * C, (uint32_t)(C * sizeof(T)), &full[slot]);
+    if (DYN)  // the record travels with its token
+      bulk_load(ts_smem + (size_t)slot * tok_stride + tok_bytes, rec + b * Lc::REC, REC_BYTES,
+                &full[slot]);
+  };
+  if (tid == 0) {
+    for (int q = 0; q < nbuf; ++q) mbar_init(&full[q], 1);
+    fence_mbar_init();
+    for (int q = 0; q < nbuf; ++q)
+      if (first + q * step < B) fetch(first + q * step, q);
+  }
+  if (!DYN) {
+    for (int e = tid; e < Lc::REC; e += blockDim.x) s_rec0[e] = rec[e];
+  }
+  __syncthreads();
+  int k = 0;
+  for (int64_t b = first; b < B; b += step, ++k) {
+    const int slot = k % nbuf;
+    const T* xs = reinterpret_cast<const T*>(ts_smem + (size_t)slot * tok_stride);
+    const float* s_rec = DYN ? reinterpret_cast<const float*>(ts_smem + (size_t)slot * tok_stride + tok_bytes) : s_rec0;
+    const float* h = s_rec + Lc::OFF_H;
+    const float* hp = s_rec + Lc::OFF_HP;
+    const float* m = s_rec + Lc::OFF_M;
+    if (!mbar_wait(&full[slot], (uint32_t)((k / nbuf) & 1))) break;  // bounded; error word set
+    double gacc[GRAM ? NG : 1];
+#pragma unroll
+    for (int g = 0; g < (GRAM ? NG : 1); ++g) gacc[g] = 0.0;
+    float sq = 0.f;
+    for (int64_t q = tid; q < C4; q += blockDim.x) {
+      float4 xf[N];
+#pragma unroll
+      for (int j = 0; j < N; ++j) xf[j] = IO<T>::to_f4(*reinterpret_cast<const typename IO<T>::raw4*>(xs + j * C + 4 * q));
+      if constexpr (GRAM) {
+        int g = 0;
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+#pragma unroll
+          for (int j = i; j < N; ++j) {
+            gacc[g] = fma((double)xf[i].x, (double)xf[j].x, gacc[g]);
+            gacc[g] = fma((double)xf[i].y, (double)xf[j].y, gacc[g]);
+            gacc[g] = fma((double)xf[i].z, (double)xf[j].z, gacc[g]);
+            gacc[g] = fma((double)xf[i].w, (double)xf[j].w, gacc[g]);
+            ++g;
+          }
+      }
+      float4 xa = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        xa.x = fmaf(h[j], xf[j].x, xa.x); xa.y = fmaf(h[j], xf[j].y, xa.y);
+        xa.z = fmaf(h[j], xf[j].z, xa.z); xa.w = fmaf(h[j], xf[j].w, xa.w);
+      }
+      sq += xa.x * xa.x + xa.y * xa.y + xa.z * xa.z + xa.w * xa.w;
+    }
+    // block sums in a fixed order
+    sq = warp_sum(sq);
+    if (lane == 0) red[warp] = sq;
+    if constexpr (GRAM) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const double v = warp_sum_d(gacc[g]);
+        if (lane == 0) s_g[warp * NG + g] = v;
+      }
+    }
+    __syncthreads();
+    float tot = 0.f;
+    for (int q = 0; q < (int)(blockDim.x >> 5); ++q) tot += red[q];
+    const float r = sqrtf(tot / (float)C + r_eps);
+    const float inv_r = 1.f / r;
+    if (tid == 0) {
+      if (DYN) rec[b * Lc::REC + 1] = r;
+      else if (rms) rms[b] = r;
+    }
+    if constexpr (GRAM) {
+      if (tid < NG) {
+        double t = 0.0;
+        for (int q = 0; q < (int)(blockDim.x >> 5); ++q) t += s_g[q * NG + tid];
+        reinterpret_cast<double*>(rec + b * Lc::REC + Lc::OFF_G64)[tid] = t;
+      }
+    }
+    T* ob = out + b * N * C;
+    for (int64_t q = tid; q < C4; q += blockDim.x) {
+      float4 xf[N];
+#pragma unroll
+      for (int j = 0; j < N; ++j) xf[j] = IO<T>::to_f4(*reinterpret_cast<const typename IO<T>::raw4*>(xs + j * C + 4 * q));
+      float4 xa = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        xa.x = fmaf(h[j], xf[j].x, xa.x); xa.y = fmaf(h[j], xf[j].y, xa.y);
+        xa.z = fmaf(h[j], xf[j].z, xa.z); xa.w = fmaf(h[j], xf[j].w, xa.w);
+      }
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + q);
+      float4 y;
+      y.x = (xa.x * inv_r) * wv.x; y.y = (xa.y * inv_r) * wv.y;
+      y.z = (xa.z * inv_r) * wv.z; y.w = (xa.w * inv_r) * wv.w;
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float4 o;
+        o.x = hp[i] * y.x; o.y = hp[i] * y.y; o.z = hp[i] * y.z; o.w = hp[i] * y.w;
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          const float mij = m[i * N + j];
+          o.x = fmaf(mij, xf[j].x, o.x); o.y = fmaf(mij, xf[j].y, o.y);
+          o.z = fmaf(mij, xf[j].z, o.z); o.w = fmaf(mij, xf[j].w, o.w);
+        }
+        IO<T>::store4(ob + i * C, q, o);
+      }
+    }
+    __syncthreads();  // the buffer and red are free again
+    if (tid == 0 && b + (int64_t)nbuf * step < B) fetch(b + (int64_t)nbuf * step, slot);
   }
 }
 
