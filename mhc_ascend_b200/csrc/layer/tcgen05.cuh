@@ -189,16 +189,12 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity,
                                                    const volatile int* abort_word) {
   const uint32_t addr = smem_u32(bar);
+  if (mbar_poll(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
   for (uint32_t it = 0; it < kSpinLimit; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((it & 255) == 255 && *abort_word) return false;
+    if (mbar_poll(addr, parity)) return true;
+    if (*abort_word) return false;
+    if (global_ns() - t0 > kWaitLimitNs) break;
   }
   atomicExch(&g_mhc_device_error, 1);
   return false;

@@ -119,19 +119,37 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+// One suspending poll: the thread sleeps in hardware until the phase
+// completes or about kSuspendNs pass, so waiting warps take no issue slots.
+constexpr uint32_t kSuspendNs = 20000;
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // a wait that runs past ~4 s gives up
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool mbar_poll(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(addr), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait for completion of the phase with the given parity; returns
 // false (and records the error) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
+  if (mbar_poll(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
   for (uint32_t it = 0; it < kSpinLimit; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
+    if (mbar_poll(addr, parity)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) break;
   }
   atomicExch(&g_mhc_device_error, 1);
   return false;
