@@ -60,7 +60,10 @@ struct Gx6Cfg {
   // rounds toward zero -- a uniform relative shrink of ~2e-8 per MMA, which
   // over the 1024 blocks of a 32768-token split reached 5e-3 on dphi
   static constexpr int DR2 = 8, LAG2 = 4;
-  static constexpr int NBAR = 2 * SG + 2 * SI + 6 * ND + 2 + 4;
+  // local-term / grad_x tile buffers: three, so the E warps fill block j + 2
+  // while block j's store drains and block j + 1's epilogue runs
+  static constexpr int NL = 3;
+  static constexpr int NBAR = 2 * SG + 2 * SI + 4 * ND + 2 * NL + 2 + 4;
   // tensor memory: D1[b] [TOK b, +TOK); D2 [64, 96) and [160, 192); Phi^T hi
   // [96, 120), lo [128, 152); X^T[b] [256 + 2 TOK b, +2 TOK) hi|lo
   static constexpr uint32_t TMEM_COLS = 512;
@@ -76,10 +79,10 @@ struct Gx6S {
   static constexpr bool BF16 = sizeof(T) == 2;
   static constexpr uint32_t GB = F::TOK * 4 * F::CW * sizeof(T);   // g (or x) tile bytes
   static constexpr uint32_t OFF_IMG = F::SG * 2 * GB;              // g/x ring, then the image ring
-  static constexpr uint32_t OFF_LOC = OFF_IMG + F::SI * F::IMG;    // [ND buffers]
+  static constexpr uint32_t OFF_LOC = OFF_IMG + F::SI * F::IMG;    // [NL buffers]
   static constexpr uint32_t STGB = BF16 ? F::TOK * F::COLS * 2 : 0; // bf16 grad_x staging tile
-  static constexpr uint32_t OFF_STG = OFF_LOC + F::ND * F::LOCB;   // [ND buffers]
-  static constexpr uint32_t OFF_GW = OFF_STG + F::ND * STGB;       // grad-w partials [E warps][32]
+  static constexpr uint32_t OFF_STG = OFF_LOC + F::NL * F::LOCB;   // [NL buffers]
+  static constexpr uint32_t OFF_GW = OFF_STG + F::NL * STGB;       // grad-w partials [E warps][32]
   static constexpr uint32_t OFF_D2S = OFF_GW + F::E_WARPS * F::CW * 4;  // drained D2 sums [NH][128]
   static constexpr uint32_t OFF_BAR = OFF_D2S + F::NH * F::COLS * 4;
   static constexpr size_t SMEM = OFF_BAR + F::NBAR * 8 + 16 + 128;

@@ -329,10 +329,8 @@ __global__ void __launch_bounds__(320, 2)
         for (int st = 0; st < P::CH / 8; ++st) {
           const uint32_t boff = (st / 4) * 2 * P::PT + 32 * (st % 4);
           const uint64_t bd = umma_desc_sw128(sb + boff);
-#ifndef MHC_EXP_NO_MMA
           umma_tf32_at(dt, at + 8 * st, bd, IDC, (first && st == 0) ? 0u : 1u);
           if constexpr (!P::BF16) umma_tf32_at(dt, at + 32 + 8 * st, bd, IDL, 1u);
-#endif
         }
         umma_commit(&pempty[slot]);
         umma_commit(&afree[a]);
@@ -430,12 +428,8 @@ __global__ void __launch_bounds__(320, 2)
               blk = fmaf(xe, xe, blk);
               split_tf32(xe, hi[e], lo[e]);
             }
-#ifndef MHC_EXP_NO_ST
             tmem_st8(ta + 8 * hf, hi);
             tmem_st8(ta + 32 + 8 * hf, lo);
-#else
-            if (hi[0] == 0x7fffffffu && lo[0] == 1u) tmem_st8(ta + 8 * hf, hi);
-#endif
           }
           sq += blk;  // per-box partial first: the rounding grows with boxes, not channels
         }
@@ -542,8 +536,8 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
   uint64_t* d1_full = a2_free + ND;
   uint64_t* d1_free = d1_full + ND;
   uint64_t* loc_ready = d1_free + ND;
-  uint64_t* loc_free = loc_ready + ND;
-  uint64_t* d2_done = loc_free + ND;
+  uint64_t* loc_free = loc_ready + F::NL;
+  uint64_t* d2_done = loc_free + F::NL;
   uint64_t* phi_ready = d2_done + 1;
   uint64_t* d2_ready = phi_ready + 1;
   uint64_t* d2_free = d2_ready + 2;
@@ -574,6 +568,8 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       mbar_init(&a2_free[b], 1);
       mbar_init(&d1_full[b], 1);
       mbar_init(&d1_free[b], 4);
+    }
+    for (int b = 0; b < F::NL; ++b) {
       mbar_init(&loc_ready[b], F::E_WARPS);
       mbar_init(&loc_free[b], 1);
     }
@@ -646,11 +642,9 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
           const uint32_t ah = tmem + F::A1_COL + 8 * ks, al = tmem + F::A1L_COL + 8 * ks;
           const uint64_t bh = umma_desc_k(im + F::IMG_B1H * 4, TOK, ks, 0);
           const uint64_t bl = umma_desc_k(im + F::IMG_B1L * 4, TOK, ks, 0);
-#ifndef MHC_EXP_G_NO_D1
           umma_tf32_at(tmem + TOK * b, al, bh, ID1, ks > 0 ? 1u : 0u);
           umma_tf32_at(tmem + TOK * b, ah, bl, ID1, 1u);
           umma_tf32_at(tmem + TOK * b, ah, bh, ID1, 1u);
-#endif
         }
         umma_commit(&d1_full[b]);
         umma_commit(&ifree[si]);
@@ -677,19 +671,10 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
           const uint32_t ah = a2 + 8 * ks, al = a2 + TOK + 8 * ks;
           const uint64_t bh = umma_desc_k(im + F::IMG_B2H * 4, F::KP, ks, 0);
           const uint64_t bl = umma_desc_k(im + F::IMG_B2L * 4, F::KP, ks, 0);
-#ifdef MHC_EXP_G_NO_D2
-          if (false) {
-#else
           if constexpr (SM::BF16) {
-#endif
             umma_tf32_at(d2, ah, bl, ID2, (!first || ks > 0) ? 1u : 0u);
             umma_tf32_at(d2, ah, bh, ID2, 1u);
-          } else
-#ifndef MHC_EXP_G_NO_D2
-          {
-#else
-          if (false) {
-#endif
+          } else {
             umma_tf32_at(d2, al, bh, ID2, (!first || ks > 0) ? 1u : 0u);
             umma_tf32_at(d2, ah, bl, ID2, 1u);
             umma_tf32_at(d2, ah, bh, ID2, 1u);
@@ -781,8 +766,9 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { ok = false; break; }
         const float* sc = reinterpret_cast<const float*>(sm + SM::OFF_IMG + si * F::IMG) + F::IMG_SC;
         // local terms of the four streams
-        if (j >= ND && !mbar_wait_or_abort(&loc_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) { ok = false; break; }
-        float* lb = locs + b * (F::LOCB / 4);
+        const int lbuf = j % F::NL;
+        if (j >= F::NL && !mbar_wait_or_abort(&loc_free[lbuf], (uint32_t)(((j / F::NL) - 1) & 1), abort_word)) { ok = false; break; }
+        float* lb = locs + lbuf * (F::LOCB / 4);
 #pragma unroll
         for (int u = 0; u < TPE; ++u) {
           const int t = TPE * e + u;
@@ -804,7 +790,7 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         }
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&loc_ready[b]);
+          mbar_arrive(&loc_ready[lbuf]);
           mbar_arrive(&ifree[si]);
         }
       }
@@ -830,10 +816,11 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
           ++drained;
         }
         if (!mbar_wait_or_abort(&d1_full[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
-        if (!mbar_wait_or_abort(&loc_ready[b], (uint32_t)((j / ND) & 1), abort_word)) { ok = false; break; }
+        const int lbuf = j % F::NL;
+        if (!mbar_wait_or_abort(&loc_ready[lbuf], (uint32_t)((j / F::NL) & 1), abort_word)) { ok = false; break; }
         tc_fence_after();
-        float* lb = locs + b * (F::LOCB / 4) + i * CW + lane;
-        __nv_bfloat16* sb16 = reinterpret_cast<__nv_bfloat16*>(sm + SM::OFF_STG + b * SM::STGB) + i * CW + lane;
+        float* lb = locs + lbuf * (F::LOCB / 4) + i * CW + lane;
+        __nv_bfloat16* sb16 = reinterpret_cast<__nv_bfloat16*>(sm + SM::OFF_STG + lbuf * SM::STGB) + i * CW + lane;
 #pragma unroll
         for (int hf = 0; hf < TOK / 16; ++hf) {
           float d[16];
@@ -850,17 +837,22 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         fence_proxy_async_smem();
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (leader) {
-          tma_store_2d(&omap, SM::BF16 ? static_cast<const void*>(sm + SM::OFF_STG + b * SM::STGB)
-                                       : static_cast<const void*>(locs + b * (F::LOCB / 4)),
+          tma_store_2d(&omap, SM::BF16 ? static_cast<const void*>(sm + SM::OFF_STG + lbuf * SM::STGB)
+                                       : static_cast<const void*>(locs + lbuf * (F::LOCB / 4)),
                        (int)c0, (int)((blk0 + j) * TOK * 4));
           bulk_commit();
-          // the buffer may be refilled as soon as its store has read it: the
-          // E warps then fill block j + 2 while this epilogue runs block j + 1
-          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-          mbar_arrive(&loc_free[b]);
+          // the previous block's buffer is free once its store has read it
+          // (NL = 3 buffers: the E warps work two blocks ahead)
+          if (j > 0) {
+            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            mbar_arrive(&loc_free[(j - 1) % F::NL]);
+          }
         }
       }
-      if (leader) bulk_wait0();
+      if (leader) {
+        bulk_wait0();
+        if (ok && nb > 0) mbar_arrive(&loc_free[(nb - 1) % F::NL]);
+      }
     }
     if (!ok) *abort_word = 1;
     asm volatile("bar.sync 1, %0;" ::"r"(32 * (F::E_WARPS + 4)) : "memory");
