@@ -22,6 +22,33 @@ __device__ __forceinline__ void block_reduce_to_global(double (&acc)[V], double*
                                                        double* __restrict__ dst) {
   // smem: [nwarps][V]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if constexpr (V == 32) {
+    // transpose-reduce: each butterfly step hands half of the remaining values
+    // to the partner lane, so after five steps lane l holds the warp's sum of
+    // value l (31 shuffles instead of 32 x 5)
+    double v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = acc[i];
+#pragma unroll
+    for (int o = 16, K = 32; o > 0; o >>= 1, K >>= 1) {
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < K / 2; ++i) {
+        const double give = upper ? v[i] : v[i + K / 2];
+        const double keep = upper ? v[i + K / 2] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, give, o);
+      }
+    }
+    smem[warp * 32 + lane] = v[0];
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      double t = 0.0;
+      for (int w = 0; w < nw; ++w) t += smem[w * 32 + threadIdx.x];
+      dst[threadIdx.x] = t;
+    }
+    __syncthreads();
+    return;
+  }
 #pragma unroll
   for (int v = 0; v < V; ++v) {
     double s = acc[v];
