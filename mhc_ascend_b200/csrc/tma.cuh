@@ -5,9 +5,10 @@
 // are plain tiled 2D loads into this CTA's own shared memory: no cluster
 // multicast anywhere in this library.
 //
-// Every wait on an mbarrier is bounded: after kSpinLimit polls the waiting
-// thread records the failure in the translation unit's device error word and
-// the kernel abandons its work instead of hanging the GPU.
+// Every wait on an mbarrier is bounded: the waiting thread sleeps in hardware
+// between polls, and after ~4 s (globaltimer) it records the failure in the
+// translation unit's device error word and the kernel abandons its work
+// instead of hanging the GPU.
 #pragma once
 
 #include <cuda.h>
