@@ -625,13 +625,78 @@ def run_ops(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_wrapper(args, world, rank, local):
+    """MHCResidualWrapper (reference layer.py:225-329) around the cfg3 layer:
+    8192 tokens, n = 4, C = 4096, fp32, fwd + bwd.  The fused path (streams
+    built inside the layer kernels, mean written by the output pass) against
+    the unfused composition pack -> layer -> mean, and the bare layer step."""
+    import mhc_ascend_b200 as mhc
+    from mhc_ascend_b200 import ops
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    T, n, C = (args.tokens or 8192), 4, 4096
+    gen = torch.Generator(device=dev).manual_seed(0)
+    r = torch.randn(T, C, device=dev, generator=gen).requires_grad_(True)
+    b = torch.randn(T, C, device=dev, generator=gen).requires_grad_(True)
+    gm = torch.randn(T, C, device=dev, generator=gen)
+    x = torch.randn(T, n, C, device=dev, generator=gen)
+    gx = torch.randn(T, n, C, device=dev, generator=gen)
+    w = mhc.replace_residual_with_mhc(hidden_dim=C, expansion_rate=n).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def clear():
+        for p in w.parameters():
+            p.grad = None
+        r.grad = None
+        b.grad = None
+
+    def fused():
+        w(r, b).backward(gm)
+        clear()
+
+    def unfused():
+        ops.stream_mean(w.mhc(ops.wrapper_pack(r, b, n, "decay"))).backward(gm)
+        clear()
+
+    def bare():
+        w.mhc(x).backward(gx)
+        clear()
+
+    res = {}
+    for name, fn in (("fused", fused), ("unfused", unfused), ("bare_layer", bare)):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = max(20, min(args.steps, 200))
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / steps
+    nbytes = 8 * T * C * 4 + 12 * (n * C) * (n * n + 2 * n) + 8 * C
+    line = {"metric": "MHCResidualWrapper fwd+bwd tokens/s (n=4, C=4096)",
+            "value": T / (res["fused"] * 1e-3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": max(20, min(args.steps, 200)), "warmup": max(3, args.warmup),
+            "ms_per_step": res["fused"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "mine",
+            "config": {"workload": f"wrapper: {T} tokens, n=4, C=4096, decay mode",
+                       "l2": "no flush: each step streams >= 0.4 GiB"},
+            "ms": res, "algorithmic_bytes_fused": nbytes,
+            "fused_gbs": nbytes / (res["fused"] * 1e-3) / 1e9}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg2"], default="cfg3")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg2", "wrapper"], default="cfg3")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU")
     ap.add_argument("--global-tokens", type=int, default=0,
                     help="strong scaling: a fixed global batch split evenly over the GPUs")
@@ -645,7 +710,14 @@ def main():
     try:
         if args.global_tokens:
             args.tokens = args.global_tokens // world
-        if args.config == "cfg2":
+        if args.config == "wrapper":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable":
+                                      "the wrapper mode compares this build's own paths"}))
+            else:
+                run_wrapper(args, world, rank, local)
+        elif args.config == "cfg2":
             if args.impl == "reference":
                 if rank == 0:
                     print(json.dumps({"impl": "reference", "unavailable":

@@ -129,6 +129,44 @@ MHC_API int mhc_fused_rmsnorm_matmul_bwd(const float* grad_out, const float* inp
                                  void* stream);
 
 /* ---------------------------------------------------------------------------
+ * MHCResidualWrapper in one piece (replaces layer.py:287-316 around the fused
+ * layer, bindings.cpp:600-952): for n = 4, fp32, hidden % 32 == 0 and 16-byte
+ * aligned tensors, the streams are built inside the layer kernels from
+ * residual / branch ([tokens, hidden] each; stream i = scales[i] * residual,
+ * stream 1 = branch, exactly as mhc_wrapper_pack_fwd computes them) and the
+ * forward writes the stream mean out_mean [tokens, hidden] -- the packed input
+ * and the layer output never reach memory.  Workspaces and token_state as for
+ * mhc_layer_fwd_dynamic / mhc_layer_bwd_dynamic with batch = tokens.  The
+ * backward takes the mean's gradient and writes the residual and branch
+ * gradients plus the parameter gradients (written, not accumulated).  Other
+ * shapes return MHC_ERR_UNSUPPORTED (use the pack / layer / mean entry points).
+ * ------------------------------------------------------------------------- */
+MHC_API int mhc_wrapper_fwd_dynamic(const float* residual, const float* branch, const float* scales,
+                                    const float* rmsnorm_weight, const float* phi_pre,
+                                    const float* phi_post, const float* phi_res,
+                                    const float* alpha_pre, const float* alpha_post,
+                                    const float* alpha_res, const float* b_pre,
+                                    const float* b_post, const float* b_res, float* out_mean,
+                                    float* token_state, int64_t tokens, int32_t n, int64_t hidden,
+                                    int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+MHC_API int mhc_wrapper_bwd_dynamic(const float* grad_mean, const float* residual,
+                                    const float* branch, const float* scales,
+                                    const float* rmsnorm_weight, const float* phi_pre,
+                                    const float* phi_post, const float* phi_res,
+                                    const float* alpha_pre, const float* alpha_post,
+                                    const float* alpha_res, const float* b_pre,
+                                    const float* b_post, const float* b_res,
+                                    const float* token_state, float* grad_residual,
+                                    float* grad_branch, float* grad_rmsnorm_weight,
+                                    float* grad_phi_pre, float* grad_phi_post, float* grad_phi_res,
+                                    float* grad_alpha_pre, float* grad_alpha_post,
+                                    float* grad_alpha_res, float* grad_b_pre, float* grad_b_post,
+                                    float* grad_b_res, int64_t tokens, int32_t n, int64_t hidden,
+                                    int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * MHCResidualWrapper stream packing and stream mean (replace the framework ops
  * of layer.py:287-316; the reference has no native counterpart).  Tokens are
  * the flattened leading dims, x is [tokens, n, hidden] fp32, n <= 64.

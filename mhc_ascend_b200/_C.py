@@ -54,6 +54,10 @@ SIGNATURES = {
                                       [_P] * 13 + [_I64, _I32, _I64, _I32, _F, _F, _P]),
     "mhc_layer_fwd_dynamic_bf16": (ctypes.c_int,
                                    [_P] * 13 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
+    "mhc_wrapper_fwd_dynamic": (ctypes.c_int,
+                                [_P] * 15 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
+    "mhc_wrapper_bwd_dynamic": (ctypes.c_int,
+                                [_P] * 27 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
     "mhc_layer_bwd_dynamic_workspace_bytes": (_SZ, [_I64, _I32, _I64]),
     "mhc_layer_bwd_dynamic": (ctypes.c_int,
                               [_P] * 24 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),

@@ -343,7 +343,7 @@ int run_fwd_dynamic(const T* x, const float* w, const float* pp, const float* pq
       }
       cudaFuncSetAttribute(proj_umma_kernel<N, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PU::SMEM);
       { ProfScope _ps("proj_stats", s); proj_umma_kernel<N, T><<<dim3((unsigned)p.utiles, (unsigned)uks), PU::THREADS, PU::SMEM, s>>>(
-          xmap, hmap, lmap, ppart, gpart, B, C, ucps); }
+          xmap, hmap, lmap, xmap, WrapScales{}, ppart, gpart, B, C, ucps); }
       ks = uks;
       done = true;
       sumsq = true;
@@ -495,7 +495,7 @@ int run_bwd_dynamic(const T* g, const T* x, const float* w, const float* pp,
       cudaFuncSetAttribute(grad_x6_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S6::SMEM);
       const int nt6 = (int)(C / F6::CW);
       { ProfScope _ps("grad_x", s); grad_x6_kernel<T><<<(unsigned)(nt6 * p.nsplit6), F6::THREADS, S6::SMEM, s>>>(
-          gm, xm, om, img, w, pp, pq, pr, gx, dphi, gwp, B, C, nt6, p.nsplit6, p.nblk6); }
+          gm, xm, om, xm, om, WrapScales{}, img, w, pp, pq, pr, gx, dphi, gwp, B, C, nt6, p.nsplit6, p.nblk6); }
       nsplit = p.nsplit6;
       gx_done = true;
     }
@@ -520,6 +520,142 @@ int run_bwd_dynamic(const T* g, const T* x, const float* w, const float* pp,
         gbp, gbq, gbr, gap, gaq, gar);
   }
   return check_launch("mhc_layer_bwd_dynamic/reduce");
+}
+
+// ---------------------------------------------------------------------------
+// MHCResidualWrapper with the streams built inside the kernels (n = 4, fp32):
+// the [T, n, C] packed input, the layer output and their gradients never
+// reach HBM.  Same split plans and workspaces as the bare layer.
+// ---------------------------------------------------------------------------
+int run_fwd_wrap(const float* res, const float* br, WrapScales sc, const float* w, const float* pp,
+                 const float* pq, const float* pr, const float* ap, const float* aq,
+                 const float* ar, const float* bp, const float* bq, const float* brs,
+                 float* mean, float* token_state, int64_t B, int64_t C, int iters, float s_eps,
+                 float r_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
+  constexpr int N = 4;
+  using PU = PumCfg<N, float>;
+  const bool need_rec = token_state == nullptr;
+  const size_t need = fwd_ws_bytes<N>(B, C, need_rec);
+  MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
+              "mhc_wrapper_fwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
+  MHC_REQUIRE(C % Gx6Cfg::CW == 0 && aligned16(res) && aligned16(br) && aligned16(mean) &&
+                  aligned16(w),
+              MHC_ERR_UNSUPPORTED,
+              "mhc_wrapper_fwd_dynamic: needs hidden %% 32 == 0 and 16-byte aligned tensors");
+  FwdPlan p = plan_fwd<N>(B, C);
+  Carve cv(ws);
+  float* ppart = cv.take(p.ppart);
+  float* gpart = cv.take(p.gpart);
+  float* phiT = cv.take(p.phiT);
+  float* rec = need_rec ? cv.take(p.rec_tmp) : token_state;
+  const int64_t nC = (int64_t)N * C;
+  float* ph = phiT;
+  float* pl = phiT + (size_t)PU::NB * nC;
+  constexpr int SW = PU::CH * PU::XW;
+  const int ucps = (p.ucps + SW - 1) / SW * SW;
+  const int uks = (int)((C + ucps - 1) / ucps);
+  CUtensorMap rmap, bmap, hmap, lmap;
+  const uint64_t cs = (uint64_t)C * 4, rs = (uint64_t)nC * 4;
+  MHC_REQUIRE(p.uks > 0 && aligned16(ph) && aligned16(pl) &&
+                  make_tmap_2d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, res, B, C, C, PU::TOK,
+                               PU::CH, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                  make_tmap_2d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, br, B, C, C, PU::TOK,
+                               PU::CH, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                  make_tmap_3d_f32(&hmap, ph, C, N, PU::NB, cs, rs, 32, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                  make_tmap_3d_f32(&lmap, pl, C, N, PU::NB, cs, rs, 32, 1, PU::NB, CU_TENSOR_MAP_SWIZZLE_128B),
+              MHC_ERR_UNSUPPORTED, "mhc_wrapper_fwd_dynamic: tensor map creation failed");
+  {
+    const bool pvec = nC % 4 == 0 && aligned16(pp) && aligned16(pq) && aligned16(pr);
+    ProfScope _ps("phi_split", s);
+    phi_split_kernel<N><<<dim3(grid_1d(pvec ? nC / 4 : nC, 256, 64), PU::NB), 256, 0, s>>>(pp, pq, pr, ph, pl, C, pvec);
+  }
+  cudaFuncSetAttribute(proj_umma_kernel<N, float, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PU::SMEM);
+  { ProfScope _ps("proj_stats", s); proj_umma_kernel<N, float, true><<<dim3((unsigned)p.utiles, (unsigned)uks), PU::THREADS, PU::SMEM, s>>>(
+      rmap, hmap, lmap, bmap, sc, ppart, gpart, B, C, ucps); }
+  int rc = check_launch("mhc_wrapper_fwd_dynamic/proj_stats");
+  if (rc) return rc;
+  { ProfScope _ps("token_fwd", s); token_fwd_lanes_kernel<N, true><<<grid_1d(B * 4, 128), 128, 0, s>>>(
+      ppart, gpart, uks, ap, aq, ar, bp, bq, brs, rec, B, C, iters, s_eps, r_eps); }
+  rc = check_launch("mhc_wrapper_fwd_dynamic/token_fwd");
+  if (rc) return rc;
+  const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
+  const int64_t quads = C / 4;
+  ProfScope _ps("stream_fwd", s);
+  auto go = [&](auto gram) {
+    constexpr bool G = decltype(gram)::value;
+    if (quads <= 256) wrap_fwd_r_kernel<N, 1, G><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
+    else if (quads <= 512) wrap_fwd_r_kernel<N, 2, G><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
+    else if (quads <= 1024) wrap_fwd_r_kernel<N, 4, G><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
+    else if (quads <= 2048) wrap_fwd_r_kernel<N, 4, G, 512><<<grid, 512, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
+    else wrap_fwd_r_kernel<N, 0, G><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
+  };
+  if (need_rec) go(std::false_type{});
+  else go(std::true_type{});
+  return check_launch("mhc_wrapper_fwd_dynamic/stream_fwd");
+}
+
+int run_bwd_wrap(const float* gmean, const float* res, const float* br, WrapScales sc,
+                 const float* w, const float* pp, const float* pq, const float* pr,
+                 const float* ap, const float* aq, const float* ar, const float* bp,
+                 const float* bq, const float* brs, const float* rec, float* gres, float* gbr,
+                 float* gw, float* gpp, float* gpq, float* gpr, float* gap, float* gaq,
+                 float* gar, float* gbp, float* gbq, float* gbr_b, int64_t B, int64_t C,
+                 int iters, float s_eps, float r_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
+  constexpr int N = 4;
+  const size_t need = bwd_ws_bytes<N, true>(B, C);
+  MHC_REQUIRE(ws != nullptr && ws_bytes >= need, MHC_ERR_WORKSPACE,
+              "mhc_wrapper_bwd_dynamic: workspace of %zu bytes required, got %zu", need, ws_bytes);
+  BwdPlan p = plan_bwd<N, true>(B, C);
+  Carve cv(ws);
+  double* stats = (double*)cv.take(p.stats);
+  float* tokb = cv.take(p.tokb);
+  double* tokr = (double*)cv.take(p.tokr);
+  float* dphi = cv.take(p.dphi);
+  float* gwp = cv.take(p.gw);
+  double* tot = (double*)cv.take(p.tot);
+  unsigned int* counter = reinterpret_cast<unsigned int*>(tot + (size_t)kTokPartBlocks * L<N>::NR);
+  float* img = cv.take(p.img);
+  using F6 = Gx6Cfg;
+  using S6 = Gx6S<float, true>;
+  MHC_REQUIRE(p.nsplit6 > 0 && C % F6::CW == 0 && aligned16(gmean) && aligned16(res) &&
+                  aligned16(br) && aligned16(gres) && aligned16(gbr) && aligned16(w) &&
+                  aligned16(img),
+              MHC_ERR_UNSUPPORTED,
+              "mhc_wrapper_bwd_dynamic: needs hidden %% 32 == 0 and 16-byte aligned tensors");
+  CUtensorMap gm, rm, bm, om, om2;
+  constexpr CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  MHC_REQUIRE(make_tmap_2d(&gm, dt, 4, gmean, B, C, C, F6::TOK, F6::CW) &&
+                  make_tmap_2d(&rm, dt, 4, res, B, C, C, F6::TOK, F6::CW) &&
+                  make_tmap_2d(&bm, dt, 4, br, B, C, C, F6::TOK, F6::CW) &&
+                  make_tmap_2d(&om, dt, 4, gres, B, C, C, F6::TOK, F6::CW) &&
+                  make_tmap_2d(&om2, dt, 4, gbr, B, C, C, F6::TOK, F6::CW),
+              MHC_ERR_UNSUPPORTED, "mhc_wrapper_bwd_dynamic: tensor map creation failed");
+  const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
+  { ProfScope _ps("bwd_stats", s); wrap_bwd_stats_kernel<N><<<grid, 128, 0, s>>>(gmean, res, br, sc, w, stats, B, C); }
+  int rc = check_launch("mhc_wrapper_bwd_dynamic/bwd_stats");
+  if (rc) return rc;
+  const int64_t img_tokens = p.nblk6 * F6::TOK;
+  const int64_t tb_tokens = B > img_tokens ? B : img_tokens;
+  { ProfScope _ps("token_bwd", s); token_bwd_lanes_kernel<N><<<grid_1d(tb_tokens * 4, 128), 128, 0, s>>>(
+      stats, rec, ap, aq, ar, bp, bq, brs, tokb, tokr, B, C, iters, s_eps, r_eps, counter, img,
+      img_tokens); }
+  rc = check_launch("mhc_wrapper_bwd_dynamic/token_bwd");
+  if (rc) return rc;
+  cudaFuncSetAttribute(grad_x6_kernel<float, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S6::SMEM);
+  const int nt6 = (int)(C / F6::CW);
+  { ProfScope _ps("grad_x", s); grad_x6_kernel<float, true><<<(unsigned)(nt6 * p.nsplit6), F6::THREADS, S6::SMEM, s>>>(
+      gm, rm, om, bm, om2, sc, img, w, pp, pq, pr, gres, dphi, gwp, B, C, nt6, p.nsplit6, p.nblk6); }
+  rc = check_launch("mhc_wrapper_bwd_dynamic/grad_x");
+  if (rc) return rc;
+  const int64_t nC = (int64_t)N * C;
+  const int nb_dphi = (int)grid_1d((int64_t)L<N>::NH * nC, 256, 4 * (int64_t)num_sms());
+  const int nb_gw = (int)grid_1d(C, 256, 64);
+  const int nb_tok = (int)(B / 128 < 1 ? 1 : (B / 128 < kTokPartBlocks ? B / 128 : kTokPartBlocks));
+  { ProfScope _ps("finish", s);
+    finish_dyn_bwd_kernel<N><<<(unsigned)(nb_dphi + nb_gw + nb_tok), 256, 0, s>>>(
+        dphi, gwp, p.nsplit6, C, gpp, gpq, gpr, gw, tokr, B, tot, counter, nb_dphi, nb_gw, nb_tok,
+        gbp, gbq, gbr_b, gap, gaq, gar); }
+  return check_launch("mhc_wrapper_bwd_dynamic/reduce");
 }
 
 template <int N, typename T>
@@ -1033,6 +1169,76 @@ extern "C" int mhc_layer_bwd_dynamic_bf16(
       grad_phi_res, grad_alpha_pre, grad_alpha_post, grad_alpha_res, grad_b_pre, grad_b_post,
       grad_b_res, batch, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace,
       workspace_bytes, stream);
+}
+
+static int wrap_scales(const char* what, const float* scales, int32_t n, WrapScales* sc) {
+  MHC_REQUIRE_PTR(scales);
+  MHC_REQUIRE(n == 4, MHC_ERR_UNSUPPORTED, "%s: the fused wrapper path needs expansion_rate 4, got %d",
+              what, n);
+  for (int i = 0; i < 4; ++i) sc->s[i] = scales[i];
+  sc->s[0] = 1.0f;
+  sc->s[1] = 1.0f;  // the branch stream is taken as is (the projection scales every stream)
+  return MHC_OK;
+}
+
+extern "C" int mhc_wrapper_fwd_dynamic(
+    const float* residual, const float* branch, const float* scales, const float* rmsnorm_weight,
+    const float* phi_pre, const float* phi_post, const float* phi_res, const float* alpha_pre,
+    const float* alpha_post, const float* alpha_res, const float* b_pre, const float* b_post,
+    const float* b_res, float* out_mean, float* token_state, int64_t tokens, int32_t n,
+    int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  const char* what = "mhc_wrapper_fwd_dynamic";
+  int rc = check_layer_args(what, tokens, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps);
+  if (rc) return rc;
+  WrapScales sc;
+  rc = wrap_scales(what, scales, n, &sc);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(residual); MHC_REQUIRE_PTR(branch); MHC_REQUIRE_PTR(rmsnorm_weight);
+  MHC_REQUIRE_PTR(phi_pre); MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res);
+  MHC_REQUIRE_PTR(alpha_pre); MHC_REQUIRE_PTR(alpha_post); MHC_REQUIRE_PTR(alpha_res);
+  MHC_REQUIRE_PTR(b_pre); MHC_REQUIRE_PTR(b_post); MHC_REQUIRE_PTR(b_res); MHC_REQUIRE_PTR(out_mean);
+  if (tokens == 0) return MHC_OK;
+  return run_fwd_wrap(residual, branch, sc, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
+                      alpha_post, alpha_res, b_pre, b_post, b_res, out_mean, token_state, tokens,
+                      hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace,
+                      workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int mhc_wrapper_bwd_dynamic(
+    const float* grad_mean, const float* residual, const float* branch, const float* scales,
+    const float* rmsnorm_weight, const float* phi_pre, const float* phi_post, const float* phi_res,
+    const float* alpha_pre, const float* alpha_post, const float* alpha_res, const float* b_pre,
+    const float* b_post, const float* b_res, const float* token_state, float* grad_residual,
+    float* grad_branch, float* grad_rmsnorm_weight, float* grad_phi_pre, float* grad_phi_post,
+    float* grad_phi_res, float* grad_alpha_pre, float* grad_alpha_post, float* grad_alpha_res,
+    float* grad_b_pre, float* grad_b_post, float* grad_b_res, int64_t tokens, int32_t n,
+    int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  const char* what = "mhc_wrapper_bwd_dynamic";
+  int rc = check_layer_args(what, tokens, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps);
+  if (rc) return rc;
+  WrapScales sc;
+  rc = wrap_scales(what, scales, n, &sc);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(grad_mean); MHC_REQUIRE_PTR(residual); MHC_REQUIRE_PTR(branch);
+  MHC_REQUIRE_PTR(rmsnorm_weight); MHC_REQUIRE_PTR(phi_pre); MHC_REQUIRE_PTR(phi_post);
+  MHC_REQUIRE_PTR(phi_res); MHC_REQUIRE_PTR(alpha_pre); MHC_REQUIRE_PTR(alpha_post);
+  MHC_REQUIRE_PTR(alpha_res); MHC_REQUIRE_PTR(b_pre); MHC_REQUIRE_PTR(b_post);
+  MHC_REQUIRE_PTR(b_res); MHC_REQUIRE_PTR(token_state); MHC_REQUIRE_PTR(grad_residual);
+  MHC_REQUIRE_PTR(grad_branch); MHC_REQUIRE_PTR(grad_rmsnorm_weight);
+  MHC_REQUIRE_PTR(grad_phi_pre); MHC_REQUIRE_PTR(grad_phi_post); MHC_REQUIRE_PTR(grad_phi_res);
+  MHC_REQUIRE_PTR(grad_alpha_pre); MHC_REQUIRE_PTR(grad_alpha_post);
+  MHC_REQUIRE_PTR(grad_alpha_res); MHC_REQUIRE_PTR(grad_b_pre); MHC_REQUIRE_PTR(grad_b_post);
+  MHC_REQUIRE_PTR(grad_b_res);
+  MHC_REQUIRE(tokens > 0, MHC_ERR_INVALID_ARG, "%s: tokens must be > 0", what);
+  return run_bwd_wrap(grad_mean, residual, branch, sc, rmsnorm_weight, phi_pre, phi_post, phi_res,
+                      alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res, token_state,
+                      grad_residual, grad_branch, grad_rmsnorm_weight, grad_phi_pre,
+                      grad_phi_post, grad_phi_res, grad_alpha_pre, grad_alpha_post,
+                      grad_alpha_res, grad_b_pre, grad_b_post, grad_b_res, tokens, hidden,
+                      sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace, workspace_bytes,
+                      (cudaStream_t)stream);
 }
 
 extern "C" size_t mhc_layer_static_workspace_bytes(int64_t batch, int32_t n, int64_t hidden) {

@@ -166,6 +166,65 @@ __global__ void __launch_bounds__(128, 4)
   }
 }
 
+// Backward 1 of MHCResidualWrapper (dynamic H, fp32): the moments gM and W of
+// the layer's streams without the streams in memory.  The layer's upstream
+// gradient is the mean's reverse, g[i, c] = gmean[c] / n for every stream
+// (as the framework's mean backward divides), and stream j is sc.s[j] *
+// residual (j != 1) or the branch output, as the forward packed them.
+template <int N>
+__global__ void __launch_bounds__(128, 4)
+    wrap_bwd_stats_kernel(const float* __restrict__ gmean, const float* __restrict__ res,
+                          const float* __restrict__ br, WrapScales sc,
+                          const float* __restrict__ w, double* __restrict__ stats, int64_t B,
+                          int64_t C) {
+  using Lc = L<N>;
+  constexpr int NS = Lc::NSD;
+  __shared__ double red[4 * NS];
+  const float nf = (float)N;
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    double acc[NS];
+#pragma unroll
+    for (int v = 0; v < NS; ++v) acc[v] = 0.0;
+    const float4* gb = reinterpret_cast<const float4*>(gmean + b * C);
+    const float4* rb = reinterpret_cast<const float4*>(res + b * C);
+    const float4* bb = reinterpret_cast<const float4*>(br + b * C);
+    auto accum = [&](float gq, float rq, float bq, float wq) {
+      const float gv = gq / nf;
+      double xv[N];
+#pragma unroll
+      for (int j = 0; j < N; ++j) xv[j] = (double)(j == 1 ? bq : sc.s[j] * rq);
+      const double g = gv, gw = (double)gv * (double)wq;
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          acc[i * N + j] = fma(g, xv[j], acc[i * N + j]);
+          acc[N * N + i * N + j] = fma(gw, xv[j], acc[N * N + i * N + j]);
+        }
+    };
+    const int64_t C4 = C / 4, NT = blockDim.x;
+    float4 g0, r0, b0, g1, r1, b1;
+    int64_t q = threadIdx.x;
+    if (q < C4) { g0 = __ldcs(gb + q); r0 = __ldcs(rb + q); b0 = __ldcs(bb + q); }
+#pragma unroll 1
+    for (; q < C4; q += 2 * NT) {
+      if (q + NT < C4) { g1 = __ldcs(gb + q + NT); r1 = __ldcs(rb + q + NT); b1 = __ldcs(bb + q + NT); }
+      {
+        const float4 w4 = __ldg(reinterpret_cast<const float4*>(w) + q);
+        accum(g0.x, r0.x, b0.x, w4.x); accum(g0.y, r0.y, b0.y, w4.y);
+        accum(g0.z, r0.z, b0.z, w4.z); accum(g0.w, r0.w, b0.w, w4.w);
+      }
+      if (q + 2 * NT < C4) { g0 = __ldcs(gb + q + 2 * NT); r0 = __ldcs(rb + q + 2 * NT); b0 = __ldcs(bb + q + 2 * NT); }
+      if (q + NT < C4) {
+        const float4 w4 = __ldg(reinterpret_cast<const float4*>(w) + q + NT);
+        accum(g1.x, r1.x, b1.x, w4.x); accum(g1.y, r1.y, b1.y, w4.y);
+        accum(g1.z, r1.z, b1.z, w4.z); accum(g1.w, r1.w, b1.w, w4.w);
+      }
+    }
+    block_reduce_to_global<NS>(acc, red, stats + b * NS);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Backward 2 (dynamic): per-token closed-form scalars, one group of lanes per
 // token (the Sinkhorn reverse runs one matrix row per lane, the rest is

@@ -35,6 +35,14 @@ struct L {
   static constexpr int NRS = 2 * N + N * N;               // static per-token reduce: dt_pre, dt_post, gM
 };
 
+// Per-stream scales of MHCResidualWrapper's packing (reference layer.py:
+// 299-310): stream i is s[i] * residual, stream 1 the branch output (s[1] = 1:
+// kernels that scale every stream leave the branch as is); "decay" 1, 1, 0.1,
+// 0.01, "zero" 1, 1, 0, 0.
+struct WrapScales {
+  float s[4];
+};
+
 __host__ __device__ inline int rec_stride(int n) {
   const int raw = 2 + 2 * n + n * n + (n * n + 2 * n);
   if (n > 8) return (raw + 3) / 4 * 4;  // wide rates keep no Gram block
@@ -73,19 +81,26 @@ struct Gx6Cfg {
 };
 
 // Shared-memory plan of grad_x6 for stream element type T (fp32 or bf16 I/O).
-template <typename T>
+// WRAP (MHCResidualWrapper, fp32): a stage holds the block's mean gradient,
+// residual and branch rows ([TOK][CW] each) instead of g and x of the four
+// streams, and the epilogue stages the residual / branch gradient tiles.
+template <typename T, bool WRAP = false>
 struct Gx6S {
   using F = Gx6Cfg;
   static constexpr bool BF16 = sizeof(T) == 2;
-  static constexpr uint32_t GB = F::TOK * 4 * F::CW * sizeof(T);   // g (or x) tile bytes
-  static constexpr uint32_t OFF_IMG = F::SG * 2 * GB;              // g/x ring, then the image ring
+  static constexpr uint32_t GB = WRAP ? F::TOK * F::CW * 4                 // one [TOK][CW] row tile
+                                      : F::TOK * 4 * F::CW * sizeof(T);    // g (or x) tile bytes
+  static constexpr uint32_t STAGE = (WRAP ? 3 : 2) * GB;          // g, x  /  gmean, residual, branch
+  static constexpr uint32_t OFF_IMG = F::SG * STAGE;               // g/x ring, then the image ring
   static constexpr uint32_t OFF_LOC = OFF_IMG + F::SI * F::IMG;    // [NL buffers]
-  static constexpr uint32_t STGB = BF16 ? F::TOK * F::COLS * 2 : 0; // bf16 grad_x staging tile
+  static constexpr uint32_t STGB = BF16 ? F::TOK * F::COLS * 2     // bf16 grad_x staging tile
+                                        : (WRAP ? 2 * F::TOK * F::CW * 4 : 0);  // residual | branch gradient tiles
   static constexpr uint32_t OFF_STG = OFF_LOC + F::NL * F::LOCB;   // [NL buffers]
   static constexpr uint32_t OFF_GW = OFF_STG + F::NL * STGB;       // grad-w partials [E warps][32]
   static constexpr uint32_t OFF_D2S = OFF_GW + F::E_WARPS * F::CW * 4;  // drained D2 sums [NH][128]
   static constexpr uint32_t OFF_BAR = OFF_D2S + F::NH * F::COLS * 4;
   static constexpr size_t SMEM = OFF_BAR + F::NBAR * 8 + 16 + 128;
+  static_assert(SMEM <= 227 * 1024, "shared-memory plan");
 };
 
 __device__ __forceinline__ int gram_index(int i, int j, int N) {

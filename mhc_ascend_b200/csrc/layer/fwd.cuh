@@ -699,6 +699,153 @@ __global__ void __launch_bounds__(THREADS, THREADS <= 256 ? (sizeof(T) == 2 ? 3 
 }
 
 // ---------------------------------------------------------------------------
+// Forward 3 of MHCResidualWrapper (fp32): the layer's streams are never in
+// memory -- stream j is sc.s[j] * residual, stream 1 the branch output, built
+// in registers exactly as the reference's packing rounds them -- and the
+// output is the wrapper's stream mean, (sum_i out[i, c]) / n, not the
+// [T, n, C] layer output.  Otherwise as stream_fwd_r_kernel (r, fp64 Gram).
+// ---------------------------------------------------------------------------
+template <int N, int QPT, bool GRAM, int THREADS = 256>
+__global__ void __launch_bounds__(THREADS, THREADS <= 256 ? 2 : 1)
+    wrap_fwd_r_kernel(const float* __restrict__ res, const float* __restrict__ br, WrapScales sc,
+                      const float* __restrict__ w, float* __restrict__ rec,
+                      float* __restrict__ mean, int64_t B, int64_t C, float r_eps) {
+  using Lc = L<N>;
+  constexpr int NG = Lc::NG;
+  __shared__ float s_rec[Lc::REC];
+  __shared__ float red[32];
+  __shared__ double s_g[GRAM ? 32 * NG : 1];
+  const int64_t C4 = C / 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  auto streams = [&](float4 rv, float4 bv, float4 (&xf)[N]) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      if (j == 1) { xf[j] = bv; continue; }
+      const float sj = sc.s[j];
+      xf[j] = make_float4(sj * rv.x, sj * rv.y, sj * rv.z, sj * rv.w);
+    }
+  };
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const float4* rb = reinterpret_cast<const float4*>(res + b * C);
+    const float4* bb = reinterpret_cast<const float4*>(br + b * C);
+    float4 rv[QPT > 0 ? QPT : 1], bv[QPT > 0 ? QPT : 1];
+#pragma unroll
+    for (int u = 0; u < QPT; ++u) {
+      const int64_t q = threadIdx.x + (int64_t)u * blockDim.x;
+      if (q < C4) { rv[u] = __ldcs(rb + q); bv[u] = __ldcs(bb + q); }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < Lc::REC; e += blockDim.x) s_rec[e] = rec[b * Lc::REC + e];
+    __syncthreads();
+    const float* h = s_rec + Lc::OFF_H;
+    const float* hp = s_rec + Lc::OFF_HP;
+    const float* m = s_rec + Lc::OFF_M;
+    double gacc[GRAM ? NG : 1];
+#pragma unroll
+    for (int g = 0; g < (GRAM ? NG : 1); ++g) gacc[g] = 0.0;
+    float sq = 0.f;
+    auto moments = [&](const float4 (&xf)[N]) {
+      if constexpr (GRAM) {
+        int g = 0;
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+#pragma unroll
+          for (int j = i; j < N; ++j) {
+            gacc[g] = fma((double)xf[i].x, (double)xf[j].x, gacc[g]);
+            gacc[g] = fma((double)xf[i].y, (double)xf[j].y, gacc[g]);
+            gacc[g] = fma((double)xf[i].z, (double)xf[j].z, gacc[g]);
+            gacc[g] = fma((double)xf[i].w, (double)xf[j].w, gacc[g]);
+            ++g;
+          }
+      }
+      float4 xa = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        xa.x = fmaf(h[j], xf[j].x, xa.x); xa.y = fmaf(h[j], xf[j].y, xa.y);
+        xa.z = fmaf(h[j], xf[j].z, xa.z); xa.w = fmaf(h[j], xf[j].w, xa.w);
+      }
+      sq += xa.x * xa.x + xa.y * xa.y + xa.z * xa.z + xa.w * xa.w;
+      return xa;
+    };
+    if constexpr (QPT > 0) {
+#pragma unroll
+      for (int u = 0; u < QPT; ++u) {
+        const int64_t q = threadIdx.x + (int64_t)u * blockDim.x;
+        if (q < C4) { float4 xf[N]; streams(rv[u], bv[u], xf); moments(xf); }
+      }
+    } else {
+      for (int64_t q = threadIdx.x; q < C4; q += blockDim.x) {
+        float4 xf[N];
+        streams(__ldg(rb + q), __ldg(bb + q), xf);
+        moments(xf);
+      }
+    }
+    sq = warp_sum(sq);
+    if (lane == 0) red[warp] = sq;
+    if constexpr (GRAM) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const double v = warp_sum_d(gacc[g]);
+        if (lane == 0) s_g[warp * NG + g] = v;
+      }
+    }
+    __syncthreads();
+    float tot = 0.f;
+    for (int k = 0; k < nw; ++k) tot += red[k];
+    const float r = sqrtf(tot / (float)C + r_eps);
+    const float inv_r = 1.f / r;
+    if (threadIdx.x == 0) rec[b * Lc::REC + 1] = r;
+    if constexpr (GRAM) {
+      if (threadIdx.x < NG) {
+        double t = 0.0;
+        for (int k = 0; k < nw; ++k) t += s_g[k * NG + threadIdx.x];
+        reinterpret_cast<double*>(rec + b * Lc::REC + Lc::OFF_G64)[threadIdx.x] = t;
+      }
+    }
+    float4* mb = reinterpret_cast<float4*>(mean + b * C);
+    const float nf = (float)N;
+    auto emit = [&](int64_t q, float4 rq, float4 bq) {
+      float4 xf[N];
+      streams(rq, bq, xf);
+      float4 xa = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        xa.x = fmaf(h[j], xf[j].x, xa.x); xa.y = fmaf(h[j], xf[j].y, xa.y);
+        xa.z = fmaf(h[j], xf[j].z, xa.z); xa.w = fmaf(h[j], xf[j].w, xa.w);
+      }
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + q);
+      float4 y;
+      y.x = (xa.x * inv_r) * wv.x; y.y = (xa.y * inv_r) * wv.y;
+      y.z = (xa.z * inv_r) * wv.z; y.w = (xa.w * inv_r) * wv.w;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float4 o;
+        o.x = hp[i] * y.x; o.y = hp[i] * y.y; o.z = hp[i] * y.z; o.w = hp[i] * y.w;
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          const float mij = m[i * N + j];
+          o.x = fmaf(mij, xf[j].x, o.x); o.y = fmaf(mij, xf[j].y, o.y);
+          o.z = fmaf(mij, xf[j].z, o.z); o.w = fmaf(mij, xf[j].w, o.w);
+        }
+        if (i == 0) acc = o;
+        else { acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w; }
+      }
+      __stcs(mb + q, make_float4(acc.x / nf, acc.y / nf, acc.z / nf, acc.w / nf));
+    };
+    if constexpr (QPT > 0) {
+#pragma unroll
+      for (int u = 0; u < QPT; ++u) {
+        const int64_t q = threadIdx.x + (int64_t)u * blockDim.x;
+        if (q < C4) emit(q, rv[u], bv[u]);
+      }
+    } else {
+      for (int64_t q = threadIdx.x; q < C4; q += blockDim.x) emit(q, __ldg(rb + q), __ldg(bb + q));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Forward 3, shared-memory staged (n <= 4 dynamic H after the tensor-core
 // projection, and static H): a persistent CTA per SM walks tokens b =
 // blockIdx.x + k gridDim.x.  One thread keeps NBUF-1 tokens in flight with

@@ -200,11 +200,16 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
   return false;
 }
 
-template <int N, typename T = float>
+// WRAP (MHCResidualWrapper, fp32): the streams are not in memory; stream i
+// is sc.s[i] * residual (xmap, 2D [tokens, C]) or, for i = 1, the branch
+// output (bmap), built in registers as the reference's packing computes them.
+template <int N, typename T = float, bool WRAP = false>
 __global__ void __launch_bounds__(320, 2)
     proj_umma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap hmap,
-                     const __grid_constant__ CUtensorMap lmap, float* __restrict__ ppart,
-                     float* __restrict__ sqpart, int64_t B, int64_t C, int cps) {
+                     const __grid_constant__ CUtensorMap lmap, const __grid_constant__ CUtensorMap bmap,
+                     WrapScales sc, float* __restrict__ ppart, float* __restrict__ sqpart, int64_t B,
+                     int64_t C, int cps) {
+  static_assert(!WRAP || sizeof(T) == 4, "wrapper streams are fp32");
   using P = PumCfg<N, T>;
   constexpr int NHP = P::NHP, NB = P::NB, SX = P::SX, SP = P::SP, NA = P::NA, DR = P::DR, XW = P::XW;
   extern __shared__ unsigned char smem_raw[];
@@ -281,8 +286,12 @@ __global__ void __launch_bounds__(320, 2)
         const int c = (int)(c_begin + (int64_t)sb * XW * P::CH);
         unsigned char* xb = sm + (kx % SX) * P::XS;
         mbar_expect_tx(&xfull[kx % SX], (uint32_t)boxes * P::XB);
-        for (int bb = 0; bb < boxes; ++bb)
-          tma_load_3d(xb + bb * P::XB, &xmap, c + bb * P::CH, i, (int)t0, &xfull[kx % SX]);
+        for (int bb = 0; bb < boxes; ++bb) {
+          if constexpr (WRAP)
+            tma_load_2d(xb + bb * P::XB, i == 1 ? &bmap : &xmap, c + bb * P::CH, (int)t0, &xfull[kx % SX]);
+          else
+            tma_load_3d(xb + bb * P::XB, &xmap, c + bb * P::CH, i, (int)t0, &xfull[kx % SX]);
+        }
       }
       // no copy may still be landing when the CTA exits (bounded)
       for (int q = kx > SX ? kx - SX : 0; q < kx; ++q) mbar_wait(&xfull[q % SX], (uint32_t)((q / SX) & 1));
@@ -375,6 +384,7 @@ __global__ void __launch_bounds__(320, 2)
       const int sb = ks % nst;
       const int boxes = nbox - sb * XW < XW ? nbox - sb * XW : XW;
       const int xslot = ks % SX;
+      const float scl = WRAP ? sc.s[ks / nst] : 1.f;  // this stage's stream scale
       if (!mbar_wait_or_abort(&xfull[xslot], (uint32_t)((ks / SX) & 1), abort_word)) { ok = false; break; }
       for (int bb = 0; bb < boxes; ++bb, ++k) {
         const int a = k % NA;
@@ -424,7 +434,8 @@ __global__ void __launch_bounds__(320, 2)
             uint32_t hi[8], lo[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float xe = __uint_as_float((&v[2 * hf].x)[e]);
+              float xe = __uint_as_float((&v[2 * hf].x)[e]);
+              if constexpr (WRAP) xe = scl * xe;  // the packed stream value, as the reference rounds it
               blk = fmaf(xe, xe, blk);
               split_tf32(xe, hi[e], lo[e]);
             }
@@ -514,16 +525,25 @@ __device__ __forceinline__ void gx6_drain_d2(uint32_t taddr, float* d2s) {
   for (int k = 16; k < Gx6Cfg::NH; ++k) d2s[k * Gx6Cfg::COLS] += b[k - 16];
 }
 
-template <typename T>
+// WRAP (MHCResidualWrapper, fp32): gmap / xmap / bmap are 2D [tokens, C] maps
+// of the stream mean's gradient, the residual and the branch output; the
+// streams and their gradient are built in registers (g = gmean / 4 for every
+// stream, stream j = wsc.s[j] * residual, stream 1 = branch) and the epilogue
+// folds the four stream gradients into the residual gradient (omap) and the
+// branch gradient (omap2), as the packing's reverse does.
+template <typename T, bool WRAP = false>
 __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     grad_x6_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
-                   const __grid_constant__ CUtensorMap omap, const float* __restrict__ img, const float* __restrict__ w,
+                   const __grid_constant__ CUtensorMap omap, const __grid_constant__ CUtensorMap bmap,
+                   const __grid_constant__ CUtensorMap omap2, WrapScales wsc,
+                   const float* __restrict__ img, const float* __restrict__ w,
                    const float* __restrict__ phi_pre, const float* __restrict__ phi_post,
                    const float* __restrict__ phi_res, T* __restrict__ gx,
                    float* __restrict__ dphi_part, float* __restrict__ gw_part, int64_t B,
                    int64_t C, int ntiles, int nsplit, int64_t nblk) {
   using F = Gx6Cfg;
-  using SM = Gx6S<T>;
+  using SM = Gx6S<T, WRAP>;
+  static_assert(!WRAP || sizeof(T) == 4, "wrapper streams are fp32");
   constexpr int SG = F::SG, SI = F::SI, ND = F::ND, CW = F::CW, COLS = F::COLS, TOK = F::TOK;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -598,11 +618,19 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       while ((gi < nb || ii < nb) && !*abort_word) {
         if (gi < nb && (gi < SG || mbar_try(&gfree[gi % SG], (uint32_t)(((gi / SG) - 1) & 1)))) {
           const int sg = gi % SG;
-          const int row = (int)((blk0 + gi) * TOK * 4);
-          unsigned char* gb = sm + sg * 2 * SM::GB;
-          mbar_expect_tx(&gfull[sg], 2 * SM::GB);
-          tma_load_2d(gb, &gmap, (int)c0, row, &gfull[sg]);
-          tma_load_2d(gb + SM::GB, &xmap, (int)c0, row, &gfull[sg]);
+          unsigned char* gb = sm + sg * SM::STAGE;
+          if constexpr (WRAP) {
+            const int trow = (int)((blk0 + gi) * TOK);
+            mbar_expect_tx(&gfull[sg], 3 * SM::GB);
+            tma_load_2d(gb, &gmap, (int)c0, trow, &gfull[sg]);
+            tma_load_2d(gb + SM::GB, &xmap, (int)c0, trow, &gfull[sg]);
+            tma_load_2d(gb + 2 * SM::GB, &bmap, (int)c0, trow, &gfull[sg]);
+          } else {
+            const int row = (int)((blk0 + gi) * TOK * 4);
+            mbar_expect_tx(&gfull[sg], 2 * SM::GB);
+            tma_load_2d(gb, &gmap, (int)c0, row, &gfull[sg]);
+            tma_load_2d(gb + SM::GB, &xmap, (int)c0, row, &gfull[sg]);
+          }
           ++gi;
           idle = 0;
         } else if (ii < nb && (ii < SI || mbar_try(&ifree[ii % SI], (uint32_t)(((ii / SI) - 1) & 1)))) {
@@ -712,10 +740,18 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     for (int j = 0; j < nb; ++j) {
       const int sg = j % SG, b = j % ND;
       if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { *abort_word = 1; break; }
-      const T* xs = reinterpret_cast<const T*>(sm + sg * 2 * SM::GB) + SM::GB / sizeof(T);
       float xv[TOK];
+      if constexpr (WRAP) {
+        const float* rs = reinterpret_cast<const float*>(sm + sg * SM::STAGE + SM::GB);
+        const float* bs = rs + TOK * CW;
+        const float sq = wsc.s[q];
 #pragma unroll
-      for (int t = 0; t < TOK; ++t) xv[t] = to_f32(xs[(t * 4 + q) * CW + lane]);
+        for (int t = 0; t < TOK; ++t) xv[t] = q == 1 ? bs[t * CW + lane] : sq * rs[t * CW + lane];
+      } else {
+        const T* xs = reinterpret_cast<const T*>(sm + sg * SM::STAGE) + SM::GB / sizeof(T);
+#pragma unroll
+        for (int t = 0; t < TOK; ++t) xv[t] = to_f32(xs[(t * 4 + q) * CW + lane]);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&gfree[sg]);
       if (j >= ND && !mbar_wait_or_abort(&a2_free[b], (uint32_t)(((j / ND) - 1) & 1), abort_word)) { *abort_word = 1; break; }
@@ -751,16 +787,32 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
       for (int j = 0; j < nb; ++j) {
         const int sg = j % SG, si = j % SI, b = j % ND;
         if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { ok = false; break; }
-        const T* gs = reinterpret_cast<const T*>(sm + sg * 2 * SM::GB);
-        const T* xs = gs + SM::GB / sizeof(T);
         float gv[TPE][4], xv[TPE][4];        // [token][stream]
+        if constexpr (WRAP) {
+          const float* gs = reinterpret_cast<const float*>(sm + sg * SM::STAGE);
+          const float* rs = gs + TOK * CW;
+          const float* bs = rs + TOK * CW;
 #pragma unroll
-        for (int u = 0; u < TPE; ++u)
+          for (int u = 0; u < TPE; ++u) {
+            const int t = TPE * e + u;
+            const float gq = gs[t * CW + lane] / 4.f, rq = rs[t * CW + lane], bq = bs[t * CW + lane];
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            gv[u][jj] = to_f32(gs[((TPE * e + u) * 4 + jj) * CW + lane]);
-            xv[u][jj] = to_f32(xs[((TPE * e + u) * 4 + jj) * CW + lane]);
+            for (int jj = 0; jj < 4; ++jj) {
+              gv[u][jj] = gq;
+              xv[u][jj] = jj == 1 ? bq : wsc.s[jj] * rq;
+            }
           }
+        } else {
+          const T* gs = reinterpret_cast<const T*>(sm + sg * SM::STAGE);
+          const T* xs = gs + SM::GB / sizeof(T);
+#pragma unroll
+          for (int u = 0; u < TPE; ++u)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              gv[u][jj] = to_f32(gs[((TPE * e + u) * 4 + jj) * CW + lane]);
+              xv[u][jj] = to_f32(xs[((TPE * e + u) * 4 + jj) * CW + lane]);
+            }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&gfree[sg]);   // g, x now live in registers
         if (!mbar_wait_or_abort(&ifull[si], (uint32_t)((j / SI) & 1), abort_word)) { ok = false; break; }
@@ -834,12 +886,36 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&d1_free[b]);
+        if constexpr (WRAP) {
+          // fold the stream gradients: residual = sum_{j != 1, s_j != 0} s_j
+          // g_j (stream 0 first), branch = g_1; warp i takes tokens 8i .. 8i + 7
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          const float* lt = locs + lbuf * (F::LOCB / 4);
+          float* stg = reinterpret_cast<float*>(sm + SM::OFF_STG + lbuf * SM::STGB);
+#pragma unroll
+          for (int u = 0; u < TOK / 4; ++u) {
+            const int t = (TOK / 4) * i + u;
+            const float* row = lt + t * COLS + lane;
+            float acc = row[0];
+#pragma unroll
+            for (int jj = 2; jj < 4; ++jj)
+              if (wsc.s[jj] != 0.f) acc += wsc.s[jj] * row[jj * CW];
+            stg[t * CW + lane] = acc;
+            stg[TOK * CW + t * CW + lane] = row[CW];
+          }
+        }
         fence_proxy_async_smem();
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (leader) {
-          tma_store_2d(&omap, SM::BF16 ? static_cast<const void*>(sm + SM::OFF_STG + lbuf * SM::STGB)
-                                       : static_cast<const void*>(locs + lbuf * (F::LOCB / 4)),
-                       (int)c0, (int)((blk0 + j) * TOK * 4));
+          if constexpr (WRAP) {
+            const float* stg = reinterpret_cast<const float*>(sm + SM::OFF_STG + lbuf * SM::STGB);
+            tma_store_2d(&omap, stg, (int)c0, (int)((blk0 + j) * TOK));
+            tma_store_2d(&omap2, stg + TOK * CW, (int)c0, (int)((blk0 + j) * TOK));
+          } else {
+            tma_store_2d(&omap, SM::BF16 ? static_cast<const void*>(sm + SM::OFF_STG + lbuf * SM::STGB)
+                                         : static_cast<const void*>(locs + lbuf * (F::LOCB / 4)),
+                         (int)c0, (int)((blk0 + j) * TOK * 4));
+          }
           bulk_commit();
           // the previous block's buffer is free once its store has read it
           // (NL = 3 buffers: the E warps work two blocks ahead)

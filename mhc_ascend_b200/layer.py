@@ -23,6 +23,8 @@ from .ops import (
     stream_aggregate,
     stream_distribute_mix_add,
     stream_mean,
+    wrapper_fused_dynamic,
+    wrapper_fused_supported,
     wrapper_pack,
 )
 
@@ -157,6 +159,17 @@ class MHCResidualWrapper(nn.Module):
             B, C = original_shape
             T = 1
         n = self.expansion_rate
+        m = self.mhc
+        if wrapper_fused_supported(residual, branch_output, n, C, m.use_dynamic_h) and \
+                self.residual_mode in ("decay", "zero"):
+            # n = 4, dynamic H: the streams are built inside the layer's kernels
+            # and the mean is written by its output pass -- no [B*T, n, C]
+            # tensor in either direction
+            output = wrapper_fused_dynamic(
+                residual, branch_output, self.residual_mode, m.rmsnorm_weight, m.phi_pre,
+                m.phi_post, m.phi_res, m.alpha_pre, m.alpha_post, m.alpha_res, m.b_pre, m.b_post,
+                m.b_res, m.num_sinkhorn_iters, m.sinkhorn_eps, m.rmsnorm_eps)
+            return output.reshape(B, T, C) if T > 1 else output
         # one CUDA pass packs the streams, one averages them (the reference
         # runs n - 1 scalings, a stack and a mean as framework ops)
         mhc_input = wrapper_pack(residual, branch_output, n, self.residual_mode)

@@ -646,6 +646,107 @@ def mhc_layer_fused_dynamic_training(x_expanded, rmsnorm_weight, phi_pre, phi_po
 
 
 # =============================================================================
+# MHCResidualWrapper in one piece (n = 4, fp32): streams built in the kernels
+# =============================================================================
+
+def wrapper_fused_supported(residual, branch, n, hidden, dynamic=True):
+    """Whether the fused wrapper entry points take this call: n = 4, dynamic
+    H, fp32 CUDA [tokens, hidden] inputs, hidden % 32 == 0, 16-byte aligned."""
+    if not (dynamic and n == 4 and hidden % 32 == 0):
+        return False
+    for t in (residual, branch):
+        if (t is None or not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous()
+                or t.data_ptr() % 16):
+            return False
+    return True
+
+
+def _flat_param_grads(n, C, dev):
+    nC = n * C
+    sizes = [C, n * nC, n * nC, n * n * nC, n, n, n * n, 3]
+    flat = torch.empty(sum(sizes), dtype=torch.float32, device=dev)
+    parts = list(torch.split(flat, sizes))
+    return (parts[0], parts[1].view(n, nC), parts[2].view(n, nC), parts[3].view(n * n, nC),
+            parts[4], parts[5], parts[6].view(n, n), parts[7])
+
+
+class WrapperDynamicFunction(torch.autograd.Function):
+    """MHCResidualWrapper.forward for a dynamic-H layer at n = 4 (reference
+    layer.py:287-316 around ops.py:387-564): the packed streams, the layer
+    output and their gradients stay inside the kernels."""
+
+    @staticmethod
+    def forward(ctx, residual, branch, residual_mode, rmsnorm_weight, phi_pre, phi_post,
+                phi_res, alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res, sinkhorn_iters,
+                sinkhorn_eps, rmsnorm_eps):
+        n = 4
+        T, C = residual.shape
+        sc = wrapper_stream_scales(n, residual_mode)
+        w = _f32(rmsnorm_weight)
+        pp, pq, pr = _f32(phi_pre), _f32(phi_post), _f32(phi_res).reshape(n * n, n * C)
+        ap, aq, ar = (_as_scalar_tensor(a, residual) for a in (alpha_pre, alpha_post, alpha_res))
+        bp, bq, br = _f32(b_pre), _f32(b_post), _f32(b_res)
+        mean = torch.empty(T, C, dtype=torch.float32, device=residual.device)
+        state = torch.empty(T, token_state_stride(n), dtype=torch.float32, device=residual.device)
+        ws = _workspace(_lib.mhc_layer_fwd_dynamic_workspace_bytes(T, n, C), residual.device)
+        with _DevGuard(residual):
+            rc = _lib.mhc_wrapper_fwd_dynamic(
+                residual.data_ptr(), branch.data_ptr(), sc, w.data_ptr(), pp.data_ptr(),
+                pq.data_ptr(), pr.data_ptr(), ap.data_ptr(), aq.data_ptr(), ar.data_ptr(),
+                bp.data_ptr(), bq.data_ptr(), br.data_ptr(), mean.data_ptr(), state.data_ptr(),
+                T, n, C, int(sinkhorn_iters), float(sinkhorn_eps), float(rmsnorm_eps),
+                ws.data_ptr(), ws.numel(), _stream(residual.device))
+        _C.check(rc, "mhc_wrapper_fwd_dynamic")
+        ctx.save_for_backward(residual, branch, rmsnorm_weight, phi_pre, phi_post, phi_res,
+                              alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res, state)
+        ctx.sc = sc
+        ctx.hp = (sinkhorn_iters, sinkhorn_eps, rmsnorm_eps)
+        return mean
+
+    @staticmethod
+    def backward(ctx, grad_mean):
+        (res, brn, w0, pp0, pq0, pr0, ap0, aq0, ar0, bp0, bq0, br0, state) = ctx.saved_tensors
+        n = 4
+        T, C = res.shape
+        g = _f32(grad_mean)
+        w = _f32(w0)
+        pp, pq, pr = _f32(pp0), _f32(pq0), _f32(pr0).reshape(n * n, n * C)
+        ap, aq, ar = (_as_scalar_tensor(a, res) for a in (ap0, aq0, ar0))
+        bp, bq, br = _f32(bp0), _f32(bq0), _f32(br0)
+        gres = torch.empty_like(res)
+        gbrn = torch.empty_like(brn)
+        gw, gpp, gpq, gpr, gbp, gbq, gbr, galpha = _flat_param_grads(n, C, res.device)
+        ws = _workspace(_lib.mhc_layer_bwd_dynamic_workspace_bytes(T, n, C), res.device)
+        a0 = galpha.data_ptr()
+        with _DevGuard(res):
+            rc = _lib.mhc_wrapper_bwd_dynamic(
+                g.data_ptr(), res.data_ptr(), brn.data_ptr(), ctx.sc, w.data_ptr(),
+                pp.data_ptr(), pq.data_ptr(), pr.data_ptr(), ap.data_ptr(), aq.data_ptr(),
+                ar.data_ptr(), bp.data_ptr(), bq.data_ptr(), br.data_ptr(), state.data_ptr(),
+                gres.data_ptr(), gbrn.data_ptr(), gw.data_ptr(), gpp.data_ptr(), gpq.data_ptr(),
+                gpr.data_ptr(), a0, a0 + 4, a0 + 8, gbp.data_ptr(), gbq.data_ptr(),
+                gbr.data_ptr(), T, n, C, int(ctx.hp[0]), float(ctx.hp[1]), float(ctx.hp[2]),
+                ws.data_ptr(), ws.numel(), _stream(res.device))
+        _C.check(rc, "mhc_wrapper_bwd_dynamic")
+        return (gres, gbrn, None, gw.to(w0.dtype), gpp.to(pp0.dtype), gpq.to(pq0.dtype),
+                gpr.reshape(pr0.shape).to(pr0.dtype), galpha[0].to(ap0.dtype).view_as(ap0),
+                galpha[1].to(aq0.dtype).view_as(aq0), galpha[2].to(ar0.dtype).view_as(ar0),
+                gbp.to(bp0.dtype), gbq.to(bq0.dtype), gbr.to(br0.dtype), None, None, None)
+
+
+def wrapper_fused_dynamic(residual, branch, residual_mode, rmsnorm_weight, phi_pre, phi_post,
+                          phi_res, alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res,
+                          sinkhorn_iters=20, sinkhorn_eps=1e-8, rmsnorm_eps=1e-5):
+    """[tokens, C] residual and branch -> [tokens, C] stream mean of the n = 4
+    dynamic-H layer over the packed streams, with autograd."""
+    _require_cuda("wrapper_fused_dynamic", residual, branch)
+    return WrapperDynamicFunction.apply(residual, branch, residual_mode, rmsnorm_weight, phi_pre,
+                                        phi_post, phi_res, alpha_pre, alpha_post, alpha_res,
+                                        b_pre, b_post, b_res, sinkhorn_iters, sinkhorn_eps,
+                                        rmsnorm_eps)
+
+
+# =============================================================================
 # Fused static-H layer (the reference composes it from four ops: layer.py:142-170)
 # =============================================================================
 

@@ -277,6 +277,52 @@ def test_residual_wrapper(cuda, n, mode, shape):
         close_param(p.grad, params[k].grad, what="wrapper grad " + k)
 
 
+@pytest.mark.parametrize("mode,shape,alpha", [("decay", (3, 345, 4096), 0.01),
+                                              ("zero", (700, 1024), 0.5),
+                                              ("decay", (2, 64, 7168), 0.5)])
+def test_residual_wrapper_fused(cuda, mode, shape, alpha):
+    """n = 4, dynamic H: MHCResidualWrapper builds the streams inside the layer
+    kernels and writes the stream mean directly (mhc_wrapper_fwd/bwd_dynamic).
+    Checked against the unfused composition (pack -> layer -> mean, the
+    reference's layer.py:287-316 over this library's kernels) and against the
+    fp64 oracle on a token sample."""
+    from mhc_ascend_b200 import ops
+    n, C = 4, shape[-1]
+    gen = torch.Generator().manual_seed(17 + C)
+    r, b = torch.randn(*shape, generator=gen), torch.randn(*shape, generator=gen)
+    gout = torch.randn(*shape, generator=gen)
+    params = O.make_dynamic_params(n, C, gen, alpha=alpha, bias_std=0.5, weight="rand")
+    w = mhc.replace_residual_with_mhc(hidden_dim=C, expansion_rate=n, residual_mode=mode).to(cuda)
+    with torch.no_grad():
+        for k, v in params.items():
+            getattr(w.mhc, k).copy_(v.reshape(getattr(w.mhc, k).shape))
+    T = r.numel() // C
+    assert ops.wrapper_fused_supported(r.reshape(T, C).to(cuda), b.reshape(T, C).to(cuda), n, C)
+    rd, bd = r.to(cuda).requires_grad_(True), b.to(cuda).requires_grad_(True)
+    out = w(rd, bd)
+    out.backward(gout.to(cuda))
+    fused = {"out": out.detach(), "res": rd.grad, "br": bd.grad}
+    fused.update({k: p.grad.clone() for k, p in w.mhc.named_parameters()})
+    # unfused: pack -> layer -> mean
+    w.mhc.zero_grad(set_to_none=True)
+    ru, bu = r.to(cuda).requires_grad_(True), b.to(cuda).requires_grad_(True)
+    x = ops.wrapper_pack(ru.reshape(T, C), bu.reshape(T, C), n, mode)
+    ref = ops.stream_mean(w.mhc(x)).reshape(shape)
+    ref.backward(gout.to(cuda))
+    close(fused["out"], ref.detach(), rtol=1e-6, atol=1e-6, what="fused vs unfused out")
+    close(fused["res"], ru.grad, rtol=1e-6, atol=1e-6, what="fused vs unfused grad residual")
+    close(fused["br"], bu.grad, rtol=1e-6, atol=1e-6, what="fused vs unfused grad branch")
+    for k, p in w.mhc.named_parameters():
+        close_param(fused[k], p.grad, rtol=1e-5, atol=1e-6, what="fused vs unfused grad " + k)
+    # fp64 oracle on a token sample (per-token rows depend on their token only)
+    idx = torch.randperm(T, generator=gen)[:64]
+    rs, bs = r.reshape(T, C)[idx].double(), b.reshape(T, C)[idx].double()
+    streams, _ = O.residual_wrapper_pack(rs, bs, n, mode)
+    p64 = {k: v.double() for k, v in params.items()}
+    o64 = O.mhc_layer_dynamic(streams, *[p64[k] for k in O.DYNAMIC_PARAM_ORDER]).mean(dim=1)
+    close(fused["out"].reshape(T, C)[idx.to(cuda)], o64, what="fused wrapper out vs fp64")
+
+
 @pytest.mark.parametrize("n,mode,shape", [(4, "decay", (2, 9, 4096)), (6, "decay", (5, 33)),
                                           (3, "zero", (4, 64))])
 def test_residual_wrapper_bf16_inputs(cuda, n, mode, shape):
