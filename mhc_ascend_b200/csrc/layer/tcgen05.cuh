@@ -513,6 +513,12 @@ __global__ void __launch_bounds__(320, 2)
 // ---------------------------------------------------------------------------
 
 
+// Two consecutive stream elements as fp32 (bf16 pairs widen exactly).
+__device__ __forceinline__ float2 to_f32x2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float2 to_f32x2(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+
 // Add one D2 accumulator (this warp's 32 lanes x NH columns) into the fp32
 // sums in shared memory ([column][128 lanes], `d2s` already offset to the lane).
 __device__ __forceinline__ void gx6_drain_d2(uint32_t taddr, float* d2s) {
@@ -780,38 +786,40 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
     bool ok = true;
     constexpr int TPE = F::TPE;
     if (warp < 2 + F::E_WARPS) {
-      // ---------------- E: X^T operand and local terms ----------------
-      const int e = warp - 2;                // tokens TPE e .. TPE e + TPE - 1
-      const float wc = __ldg(w + c);
-      float gwacc = 0.f;
+      // ---------------- E: local terms ----------------
+      // warp e takes tokens 2e (lanes 0-15) and 2e + 1 (lanes 16-31); each
+      // lane a channel pair (2 cp, 2 cp + 1), computed with packed fp32
+      // (f32x2) FMAs: half the instructions of a channel per lane
+      static_assert(TPE == 2 && CW == 32, "E-warp lane map");
+      const int e = warp - 2;
+      const int half = lane >> 4, cp = lane & 15;
+      const int t = TPE * e + half;          // this lane's token in the block
+      const float2 wc2 = __ldg(reinterpret_cast<const float2*>(w + c0) + cp);
+      float2 gwacc = make_float2(0.f, 0.f);
+      auto bc = [](float v) { return make_float2(v, v); };
       for (int j = 0; j < nb; ++j) {
-        const int sg = j % SG, si = j % SI, b = j % ND;
+        const int sg = j % SG, si = j % SI;
         if (!mbar_wait_or_abort(&gfull[sg], (uint32_t)((j / SG) & 1), abort_word)) { ok = false; break; }
-        float gv[TPE][4], xv[TPE][4];        // [token][stream]
+        float2 gv[4], xv[4];                 // [stream], channel pair
         if constexpr (WRAP) {
-          const float* gs = reinterpret_cast<const float*>(sm + sg * SM::STAGE);
-          const float* rs = gs + TOK * CW;
-          const float* bs = rs + TOK * CW;
+          const float2* gs = reinterpret_cast<const float2*>(sm + sg * SM::STAGE);
+          const float2* rs = gs + TOK * CW / 2;
+          const float2* bs = rs + TOK * CW / 2;
+          const float2 gq = gs[t * (CW / 2) + cp], rq = rs[t * (CW / 2) + cp], bq = bs[t * (CW / 2) + cp];
+          const float2 gq4 = make_float2(gq.x / 4.f, gq.y / 4.f);
 #pragma unroll
-          for (int u = 0; u < TPE; ++u) {
-            const int t = TPE * e + u;
-            const float gq = gs[t * CW + lane] / 4.f, rq = rs[t * CW + lane], bq = bs[t * CW + lane];
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              gv[u][jj] = gq;
-              xv[u][jj] = jj == 1 ? bq : wsc.s[jj] * rq;
-            }
+          for (int jj = 0; jj < 4; ++jj) {
+            gv[jj] = gq4;
+            xv[jj] = jj == 1 ? bq : make_float2(wsc.s[jj] * rq.x, wsc.s[jj] * rq.y);
           }
         } else {
           const T* gs = reinterpret_cast<const T*>(sm + sg * SM::STAGE);
           const T* xs = gs + SM::GB / sizeof(T);
 #pragma unroll
-          for (int u = 0; u < TPE; ++u)
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              gv[u][jj] = to_f32(gs[((TPE * e + u) * 4 + jj) * CW + lane]);
-              xv[u][jj] = to_f32(xs[((TPE * e + u) * 4 + jj) * CW + lane]);
-            }
+          for (int jj = 0; jj < 4; ++jj) {
+            gv[jj] = to_f32x2(gs + (t * 4 + jj) * CW + 2 * cp);
+            xv[jj] = to_f32x2(xs + (t * 4 + jj) * CW + 2 * cp);
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&gfree[sg]);   // g, x now live in registers
@@ -821,24 +829,34 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         const int lbuf = j % F::NL;
         if (j >= F::NL && !mbar_wait_or_abort(&loc_free[lbuf], (uint32_t)(((j / F::NL) - 1) & 1), abort_word)) { ok = false; break; }
         float* lb = locs + lbuf * (F::LOCB / 4);
-#pragma unroll
-        for (int u = 0; u < TPE; ++u) {
-          const int t = TPE * e + u;
+        {
           const float* st = sc + t * 32;
           const float4 s0 = *reinterpret_cast<const float4*>(st);
           const float4 h4 = *reinterpret_cast<const float4*>(st + 4);
           const float4 q4 = *reinterpret_cast<const float4*>(st + 8);
-          const float gy = q4.x * gv[u][0] + q4.y * gv[u][1] + q4.z * gv[u][2] + q4.w * gv[u][3];
-          const float xa = h4.x * xv[u][0] + h4.y * xv[u][1] + h4.z * xv[u][2] + h4.w * xv[u][3];
-          const float agg = gy * wc * s0.y - xa * s0.x;
+          float2 gy = __fmul2_rn(bc(q4.x), gv[0]);
+          gy = __ffma2_rn(bc(q4.y), gv[1], gy);
+          gy = __ffma2_rn(bc(q4.z), gv[2], gy);
+          gy = __ffma2_rn(bc(q4.w), gv[3], gy);
+          float2 xa = __fmul2_rn(bc(h4.x), xv[0]);
+          xa = __ffma2_rn(bc(h4.y), xv[1], xa);
+          xa = __ffma2_rn(bc(h4.z), xv[2], xa);
+          xa = __ffma2_rn(bc(h4.w), xv[3], xa);
+          // agg = gy w s0.y - xa s0.x
+          const float2 agg = __ffma2_rn(__fmul2_rn(gy, wc2), bc(s0.y), __fmul2_rn(xa, bc(-s0.x)));
           const float hh[4] = {h4.x, h4.y, h4.z, h4.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const float4 m4 = *reinterpret_cast<const float4*>(st + 12 + 4 * i);
-            const float mix = m4.x * gv[u][0] + m4.y * gv[u][1] + m4.z * gv[u][2] + m4.w * gv[u][3];
-            lb[t * COLS + i * CW + lane] = mix + hh[i] * agg + s0.z * xv[u][i];
+            float2 o = __fmul2_rn(bc(m4.x), gv[0]);
+            o = __ffma2_rn(bc(m4.y), gv[1], o);
+            o = __ffma2_rn(bc(m4.z), gv[2], o);
+            o = __ffma2_rn(bc(m4.w), gv[3], o);
+            o = __ffma2_rn(bc(hh[i]), agg, o);
+            o = __ffma2_rn(bc(s0.z), xv[i], o);
+            *reinterpret_cast<float2*>(lb + t * COLS + i * CW + 2 * cp) = o;
           }
-          gwacc = fmaf(gy * xa, s0.y, gwacc);
+          gwacc = __ffma2_rn(__fmul2_rn(gy, xa), bc(s0.y), gwacc);
         }
         __syncwarp();
         if (lane == 0) {
@@ -846,7 +864,10 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
           mbar_arrive(&ifree[si]);
         }
       }
-      gws[e * CW + lane] = gwacc;
+      // this warp's two tokens per channel pair, summed: lanes 0-15 hold the result
+      gwacc.x += __shfl_xor_sync(0xffffffffu, gwacc.x, 16);
+      gwacc.y += __shfl_xor_sync(0xffffffffu, gwacc.y, 16);
+      if (half == 0) *reinterpret_cast<float2*>(gws + e * CW + 2 * cp) = gwacc;
     } else {
       // ---------------- epilogue: grad_x = D1 + local term ----------------
       const int i = warp & 3;                // stream = tensor-memory lane quadrant
@@ -873,6 +894,9 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         tc_fence_after();
         float* lb = locs + lbuf * (F::LOCB / 4) + i * CW + lane;
         __nv_bfloat16* sb16 = reinterpret_cast<__nv_bfloat16*>(sm + SM::OFF_STG + lbuf * SM::STGB) + i * CW + lane;
+#ifdef MHC_EXP_NO_EPI
+        if (j < 0)
+#endif
 #pragma unroll
         for (int hf = 0; hf < TOK / 16; ++hf) {
           float d[16];
