@@ -894,9 +894,6 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
         tc_fence_after();
         float* lb = locs + lbuf * (F::LOCB / 4) + i * CW + lane;
         __nv_bfloat16* sb16 = reinterpret_cast<__nv_bfloat16*>(sm + SM::OFF_STG + lbuf * SM::STGB) + i * CW + lane;
-#ifdef MHC_EXP_NO_EPI
-        if (j < 0)
-#endif
 #pragma unroll
         for (int hf = 0; hf < TOK / 16; ++hf) {
           float d[16];
