@@ -639,7 +639,9 @@ def run_wrapper(args, world, rank, local):
     """MHCResidualWrapper (reference layer.py:225-329) around the cfg3 layer:
     8192 tokens, n = 4, C = 4096, fp32, fwd + bwd.  The fused path (streams
     built inside the layer kernels, mean written by the output pass) against
-    the unfused composition pack -> layer -> mean, and the bare layer step."""
+    the unfused composition pack -> layer -> mean, and the bare layer step;
+    and the wrapper followed by the next branch's input RMSNorm, fused into its
+    output pass (forward_prenorm) or run as a separate rmsnorm."""
     import mhc_ascend_b200 as mhc
     from mhc_ascend_b200 import ops
     if rank != 0:
@@ -674,8 +676,25 @@ def run_wrapper(args, world, rank, local):
         w.mhc(x).backward(gx)
         clear()
 
+    # with the next branch's input RMSNorm (pre-norm block): fused into the
+    # wrapper's output pass, or the wrapper then this library's rmsnorm
+    w2 = (torch.rand(C, device=dev, generator=gen) + 0.5).requires_grad_(True)
+    gn = torch.randn(T, C, device=dev, generator=gen)
+
+    def prenorm_fused():
+        torch.autograd.backward(list(w.forward_prenorm(r, b, w2)), [gm, gn])
+        clear()
+        w2.grad = None
+
+    def prenorm_unfused():
+        h = w(r, b)
+        torch.autograd.backward([h, ops.rmsnorm(h, w2)], [gm, gn])
+        clear()
+        w2.grad = None
+
     res = {}
-    for name, fn in (("fused", fused), ("unfused", unfused), ("bare_layer", bare)):
+    for name, fn in (("fused", fused), ("unfused", unfused), ("bare_layer", bare),
+                     ("prenorm_fused", prenorm_fused), ("prenorm_unfused", prenorm_unfused)):
         for _ in range(max(3, args.warmup)):
             fn()
         torch.cuda.synchronize()

@@ -150,6 +150,25 @@ MHC_API int mhc_wrapper_fwd_dynamic(const float* residual, const float* branch, 
                                     float* token_state, int64_t tokens, int32_t n, int64_t hidden,
                                     int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
                                     void* workspace, size_t workspace_bytes, void* stream);
+/* The wrapper forward fused with the next branch's input RMSNorm (a pre-norm
+ * block normalises the returned hidden state before its attention / MLP; the
+ * reference composes MHCResidualWrapper.forward (layer.py:287-316) with the
+ * branch's rmsnorm (ops.py:87-136) as two passes).  Writes out_mean as
+ * mhc_wrapper_fwd_dynamic does, and out_normed[t, c] = out_mean[t, c] /
+ * out_norm_rms[t] * norm_weight[c], out_norm_rms[t] = sqrt(mean_c out_mean^2
+ * + norm_eps), from the same pass.  The backward of the norm is
+ * mhc_rmsnorm_bwd on (grad_normed, out_mean, norm_weight, out_norm_rms); its
+ * input gradient adds to grad_mean of mhc_wrapper_bwd_dynamic.  Same
+ * requirements and workspace as mhc_wrapper_fwd_dynamic; norm_weight and
+ * out_normed 16-byte aligned. */
+MHC_API int mhc_wrapper_fwd_dynamic_prenorm(
+    const float* residual, const float* branch, const float* scales, const float* rmsnorm_weight,
+    const float* phi_pre, const float* phi_post, const float* phi_res, const float* alpha_pre,
+    const float* alpha_post, const float* alpha_res, const float* b_pre, const float* b_post,
+    const float* b_res, const float* norm_weight, float norm_eps, float* out_mean,
+    float* out_normed, float* out_norm_rms, float* token_state, int64_t tokens, int32_t n,
+    int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
+    void* workspace, size_t workspace_bytes, void* stream);
 MHC_API int mhc_wrapper_bwd_dynamic(const float* grad_mean, const float* residual,
                                     const float* branch, const float* scales,
                                     const float* rmsnorm_weight, const float* phi_pre,

@@ -56,6 +56,9 @@ SIGNATURES = {
                                    [_P] * 13 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
     "mhc_wrapper_fwd_dynamic": (ctypes.c_int,
                                 [_P] * 15 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
+    "mhc_wrapper_fwd_dynamic_prenorm": (ctypes.c_int,
+                                        [_P] * 14 + [_F] + [_P] * 4 +
+                                        [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
     "mhc_wrapper_bwd_dynamic": (ctypes.c_int,
                                 [_P] * 27 + [_I64, _I32, _I64, _I32, _F, _F, _P, _SZ, _P]),
     "mhc_layer_bwd_dynamic_workspace_bytes": (_SZ, [_I64, _I32, _I64]),

@@ -531,7 +531,7 @@ int run_fwd_wrap(const float* res, const float* br, WrapScales sc, const float* 
                  const float* pq, const float* pr, const float* ap, const float* aq,
                  const float* ar, const float* bp, const float* bq, const float* brs,
                  float* mean, float* token_state, int64_t B, int64_t C, int iters, float s_eps,
-                 float r_eps, void* ws, size_t ws_bytes, cudaStream_t s) {
+                 float r_eps, void* ws, size_t ws_bytes, cudaStream_t s, PreNorm pn = PreNorm{}) {
   constexpr int N = 4;
   using PU = PumCfg<N, float>;
   const bool need_rec = token_state == nullptr;
@@ -581,16 +581,19 @@ int run_fwd_wrap(const float* res, const float* br, WrapScales sc, const float* 
   const unsigned grid = (unsigned)(B < (1 << 30) ? B : (1 << 30));
   const int64_t quads = C / 4;
   ProfScope _ps("stream_fwd", s);
-  auto go = [&](auto gram) {
-    constexpr bool G = decltype(gram)::value;
-    if (quads <= 256) wrap_fwd_r_kernel<N, 1, G><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
-    else if (quads <= 512) wrap_fwd_r_kernel<N, 2, G><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
-    else if (quads <= 1024) wrap_fwd_r_kernel<N, 4, G><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
-    else if (quads <= 2048) wrap_fwd_r_kernel<N, 4, G, 512><<<grid, 512, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
-    else wrap_fwd_r_kernel<N, 0, G><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps);
+  auto go = [&](auto gram, auto pre) {
+    constexpr bool G = decltype(gram)::value, P = decltype(pre)::value;
+    if (quads <= 256) wrap_fwd_r_kernel<N, 1, G, 256, P><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps, pn);
+    else if (quads <= 512) wrap_fwd_r_kernel<N, 2, G, 256, P><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps, pn);
+    else if (quads <= 1024) wrap_fwd_r_kernel<N, 4, G, 256, P><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps, pn);
+    else if (quads <= 2048) wrap_fwd_r_kernel<N, 4, G, 512, P><<<grid, 512, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps, pn);
+    else wrap_fwd_r_kernel<N, 0, G, 256, P><<<grid, 256, 0, s>>>(res, br, sc, w, rec, mean, B, C, r_eps, pn);
   };
-  if (need_rec) go(std::false_type{});
-  else go(std::true_type{});
+  const bool pre = pn.normed != nullptr;
+  if (need_rec && pre) go(std::false_type{}, std::true_type{});
+  else if (need_rec) go(std::false_type{}, std::false_type{});
+  else if (pre) go(std::true_type{}, std::true_type{});
+  else go(std::true_type{}, std::false_type{});
   return check_launch("mhc_wrapper_fwd_dynamic/stream_fwd");
 }
 
@@ -1203,6 +1206,40 @@ extern "C" int mhc_wrapper_fwd_dynamic(
                       alpha_post, alpha_res, b_pre, b_post, b_res, out_mean, token_state, tokens,
                       hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace,
                       workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int mhc_wrapper_fwd_dynamic_prenorm(
+    const float* residual, const float* branch, const float* scales, const float* rmsnorm_weight,
+    const float* phi_pre, const float* phi_post, const float* phi_res, const float* alpha_pre,
+    const float* alpha_post, const float* alpha_res, const float* b_pre, const float* b_post,
+    const float* b_res, const float* norm_weight, float norm_eps, float* out_mean,
+    float* out_normed, float* out_norm_rms, float* token_state, int64_t tokens, int32_t n,
+    int64_t hidden, int32_t sinkhorn_iters, float sinkhorn_eps, float rmsnorm_eps,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  const char* what = "mhc_wrapper_fwd_dynamic_prenorm";
+  int rc = check_layer_args(what, tokens, n, hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps);
+  if (rc) return rc;
+  MHC_REQUIRE(norm_eps >= 0.f, MHC_ERR_INVALID_ARG, "%s: norm_eps must be >= 0", what);
+  WrapScales sc;
+  rc = wrap_scales(what, scales, n, &sc);
+  if (rc) return rc;
+  MHC_REQUIRE_PTR(residual); MHC_REQUIRE_PTR(branch); MHC_REQUIRE_PTR(rmsnorm_weight);
+  MHC_REQUIRE_PTR(phi_pre); MHC_REQUIRE_PTR(phi_post); MHC_REQUIRE_PTR(phi_res);
+  MHC_REQUIRE_PTR(alpha_pre); MHC_REQUIRE_PTR(alpha_post); MHC_REQUIRE_PTR(alpha_res);
+  MHC_REQUIRE_PTR(b_pre); MHC_REQUIRE_PTR(b_post); MHC_REQUIRE_PTR(b_res); MHC_REQUIRE_PTR(out_mean);
+  MHC_REQUIRE_PTR(norm_weight); MHC_REQUIRE_PTR(out_normed); MHC_REQUIRE_PTR(out_norm_rms);
+  MHC_REQUIRE(aligned16(norm_weight) && aligned16(out_normed), MHC_ERR_ALIGNMENT,
+              "%s: norm_weight and out_normed must be 16-byte aligned", what);
+  if (tokens == 0) return MHC_OK;
+  PreNorm pn;
+  pn.w2 = norm_weight;
+  pn.eps2 = norm_eps;
+  pn.normed = out_normed;
+  pn.rms2 = out_norm_rms;
+  return run_fwd_wrap(residual, branch, sc, rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
+                      alpha_post, alpha_res, b_pre, b_post, b_res, out_mean, token_state, tokens,
+                      hidden, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps, workspace,
+                      workspace_bytes, (cudaStream_t)stream, pn);
 }
 
 extern "C" int mhc_wrapper_bwd_dynamic(

@@ -704,12 +704,25 @@ __global__ void __launch_bounds__(THREADS, THREADS <= 256 ? (sizeof(T) == 2 ? 3 
 // in registers exactly as the reference's packing rounds them -- and the
 // output is the wrapper's stream mean, (sum_i out[i, c]) / n, not the
 // [T, n, C] layer output.  Otherwise as stream_fwd_r_kernel (r, fp64 Gram).
+// PRE: the next branch's input RMSNorm is written by the same pass (a
+// pre-norm block normalises this hidden state before its attention / MLP):
+// normed[c] = mean[c] / rms2 * w2[c], rms2 = sqrt(mean_c mean^2 + eps2) over
+// the mean exactly as stored, rms2 kept per token for the backward; the mean
+// is recomputed from the token's registers rather than read back from HBM.
 // ---------------------------------------------------------------------------
-template <int N, int QPT, bool GRAM, int THREADS = 256>
+struct PreNorm {
+  const float* w2 = nullptr;  // [C] weight of the next branch's RMSNorm
+  float eps2 = 0.f;
+  float* normed = nullptr;    // [B, C]
+  float* rms2 = nullptr;      // [B]
+};
+
+template <int N, int QPT, bool GRAM, int THREADS = 256, bool PRE = false>
 __global__ void __launch_bounds__(THREADS, THREADS <= 256 ? 2 : 1)
     wrap_fwd_r_kernel(const float* __restrict__ res, const float* __restrict__ br, WrapScales sc,
                       const float* __restrict__ w, float* __restrict__ rec,
-                      float* __restrict__ mean, int64_t B, int64_t C, float r_eps) {
+                      float* __restrict__ mean, int64_t B, int64_t C, float r_eps,
+                      PreNorm pn = PreNorm{}) {
   using Lc = L<N>;
   constexpr int NG = Lc::NG;
   __shared__ float s_rec[Lc::REC];
@@ -804,7 +817,8 @@ __global__ void __launch_bounds__(THREADS, THREADS <= 256 ? 2 : 1)
     }
     float4* mb = reinterpret_cast<float4*>(mean + b * C);
     const float nf = (float)N;
-    auto emit = [&](int64_t q, float4 rq, float4 bq) {
+    float sq2 = 0.f;                         // PRE: sum of the mean's squares
+    auto mean_of = [&](int64_t q, float4 rq, float4 bq) {
       float4 xf[N];
       streams(rq, bq, xf);
       float4 xa = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -831,7 +845,12 @@ __global__ void __launch_bounds__(THREADS, THREADS <= 256 ? 2 : 1)
         if (i == 0) acc = o;
         else { acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w; }
       }
-      __stcs(mb + q, make_float4(acc.x / nf, acc.y / nf, acc.z / nf, acc.w / nf));
+      return make_float4(acc.x / nf, acc.y / nf, acc.z / nf, acc.w / nf);
+    };
+    auto emit = [&](int64_t q, float4 rq, float4 bq) {
+      const float4 mv = mean_of(q, rq, bq);
+      __stcs(mb + q, mv);
+      if constexpr (PRE) sq2 += mv.x * mv.x + mv.y * mv.y + mv.z * mv.z + mv.w * mv.w;
     };
     if constexpr (QPT > 0) {
 #pragma unroll
@@ -841,6 +860,34 @@ __global__ void __launch_bounds__(THREADS, THREADS <= 256 ? 2 : 1)
       }
     } else {
       for (int64_t q = threadIdx.x; q < C4; q += blockDim.x) emit(q, __ldg(rb + q), __ldg(bb + q));
+    }
+    if constexpr (PRE) {
+      // second block sum (red is free: every thread has read it for r)
+      __syncthreads();
+      sq2 = warp_sum(sq2);
+      if (lane == 0) red[warp] = sq2;
+      __syncthreads();
+      float tot2 = 0.f;
+      for (int k = 0; k < nw; ++k) tot2 += red[k];
+      const float r2 = sqrtf(tot2 / (float)C + pn.eps2);
+      const float inv2 = 1.f / r2;
+      if (threadIdx.x == 0) pn.rms2[b] = r2;
+      float4* nb = reinterpret_cast<float4*>(pn.normed + b * C);
+      auto emit2 = [&](int64_t q, float4 rq, float4 bq) {
+        const float4 mv = mean_of(q, rq, bq);
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(pn.w2) + q);
+        __stcs(nb + q, make_float4((mv.x * inv2) * wv.x, (mv.y * inv2) * wv.y,
+                                   (mv.z * inv2) * wv.z, (mv.w * inv2) * wv.w));
+      };
+      if constexpr (QPT > 0) {
+#pragma unroll
+        for (int u = 0; u < QPT; ++u) {
+          const int64_t q = threadIdx.x + (int64_t)u * blockDim.x;
+          if (q < C4) emit2(q, rv[u], bv[u]);
+        }
+      } else {
+        for (int64_t q = threadIdx.x; q < C4; q += blockDim.x) emit2(q, __ldg(rb + q), __ldg(bb + q));
+      }
     }
   }
 }

@@ -567,7 +567,8 @@ __global__ void __launch_bounds__(Gx6Cfg::THREADS, 1)
   uint64_t* phi_ready = d2_done + 1;
   uint64_t* d2_ready = phi_ready + 1;
   uint64_t* d2_free = d2_ready + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(phi_ready + 1);
+  // the allocation slot and the abort word follow the last barrier
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d2_free + 2);
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t sbase = smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

@@ -42,6 +42,24 @@ inline EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
+// Encoding needs the device's context current on the calling thread.  A
+// thread that has only set the device (an autograd worker running a backward,
+// say) may not have it yet: make it current and retry once.
+inline CUresult encode_retry(EncodeTiledFn fn, CUtensorMap* map, CUtensorMapDataType dt,
+                             cuuint32_t rank, void* base, const cuuint64_t* dims,
+                             const cuuint64_t* strides, const cuuint32_t* box,
+                             const cuuint32_t* estr, CUtensorMapSwizzle swizzle) {
+  CUresult r = fn(map, dt, rank, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_ERROR_INVALID_CONTEXT) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess)
+      r = fn(map, dt, rank, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  return r;
+}
+
 // 2D tensor map (element type dt of esize bytes) over a row-major matrix rows x
 // cols (row stride in elements; stride x esize a multiple of 16), box
 // box_rows x box_cols, optional shared-memory swizzle; elements outside the
@@ -55,9 +73,7 @@ inline bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esiz
   const cuuint64_t strides[1] = {row_stride_elems * esize};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_retry(fn, map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, swizzle);
   return r == CUDA_SUCCESS;
 }
 inline bool make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
@@ -80,9 +96,7 @@ inline bool make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* b
   const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
   const cuuint32_t box[3] = {b0, b1, b2};
   const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_retry(fn, map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, swizzle);
   return r == CUDA_SUCCESS;
 }
 inline bool make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,

@@ -24,6 +24,7 @@ from .ops import (
     stream_distribute_mix_add,
     stream_mean,
     wrapper_fused_dynamic,
+    wrapper_fused_dynamic_prenorm,
     wrapper_fused_supported,
     wrapper_pack,
 )
@@ -177,6 +178,30 @@ class MHCResidualWrapper(nn.Module):
         if T > 1:
             output = output.reshape(B, T, C)
         return output
+
+    def forward_prenorm(self, residual: torch.Tensor, branch_output: torch.Tensor,
+                        norm_weight: torch.Tensor, norm_eps: float = 1e-5):
+        """forward() followed by the next branch's input RMSNorm, as a pre-norm
+        block uses them: returns (hidden, rmsnorm(hidden, norm_weight,
+        norm_eps)).  For n = 4, dynamic H, fp32 the normalised copy is written
+        by the same output pass as the hidden state (no second read of it);
+        otherwise the two run back to back on this library's CUDA operators.
+        The reference has no such entry: its model code would call
+        MHCResidualWrapper.forward (layer.py:287-316) and then rmsnorm
+        (ops.py:87-136)."""
+        shape = residual.shape
+        C = shape[-1]
+        r2, b2 = residual.reshape(-1, C), branch_output.reshape(-1, C)
+        m = self.mhc
+        if wrapper_fused_supported(r2, b2, self.expansion_rate, C, m.use_dynamic_h) and \
+                self.residual_mode in ("decay", "zero"):
+            hidden, normed = wrapper_fused_dynamic_prenorm(
+                r2, b2, self.residual_mode, norm_weight, norm_eps, m.rmsnorm_weight, m.phi_pre,
+                m.phi_post, m.phi_res, m.alpha_pre, m.alpha_post, m.alpha_res, m.b_pre, m.b_post,
+                m.b_res, m.num_sinkhorn_iters, m.sinkhorn_eps, m.rmsnorm_eps)
+            return hidden.reshape(shape), normed.reshape(shape)
+        hidden = self.forward(residual, branch_output)
+        return hidden, rmsnorm(hidden.reshape(-1, C), norm_weight, norm_eps).reshape(shape)
 
     def extra_repr(self) -> str:
         return (f"hidden_dim={self.hidden_dim}, expansion_rate={self.expansion_rate}, "

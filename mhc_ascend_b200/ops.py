@@ -705,33 +705,114 @@ class WrapperDynamicFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_mean):
-        (res, brn, w0, pp0, pq0, pr0, ap0, aq0, ar0, bp0, bq0, br0, state) = ctx.saved_tensors
+        grads = _wrapper_dynamic_bwd(ctx.saved_tensors, ctx.sc, ctx.hp, _f32(grad_mean))
+        return (grads[0], grads[1], None, *grads[2:], None, None, None)
+
+
+def _wrapper_dynamic_bwd(saved, sc, hp, g):
+    """Backward of the fused n = 4 wrapper forward for the stream-mean gradient
+    g: (grad residual, grad branch, then the gradients of rmsnorm_weight,
+    phi_pre, phi_post, phi_res, alpha_pre, alpha_post, alpha_res, b_pre, b_post,
+    b_res in their parameters' dtypes)."""
+    (res, brn, w0, pp0, pq0, pr0, ap0, aq0, ar0, bp0, bq0, br0, state) = saved
+    n = 4
+    T, C = res.shape
+    w = _f32(w0)
+    pp, pq, pr = _f32(pp0), _f32(pq0), _f32(pr0).reshape(n * n, n * C)
+    ap, aq, ar = (_as_scalar_tensor(a, res) for a in (ap0, aq0, ar0))
+    bp, bq, br = _f32(bp0), _f32(bq0), _f32(br0)
+    gres = torch.empty_like(res)
+    gbrn = torch.empty_like(brn)
+    gw, gpp, gpq, gpr, gbp, gbq, gbr, galpha = _flat_param_grads(n, C, res.device)
+    ws = _workspace(_lib.mhc_layer_bwd_dynamic_workspace_bytes(T, n, C), res.device)
+    a0 = galpha.data_ptr()
+    with _DevGuard(res):
+        rc = _lib.mhc_wrapper_bwd_dynamic(
+            g.data_ptr(), res.data_ptr(), brn.data_ptr(), sc, w.data_ptr(),
+            pp.data_ptr(), pq.data_ptr(), pr.data_ptr(), ap.data_ptr(), aq.data_ptr(),
+            ar.data_ptr(), bp.data_ptr(), bq.data_ptr(), br.data_ptr(), state.data_ptr(),
+            gres.data_ptr(), gbrn.data_ptr(), gw.data_ptr(), gpp.data_ptr(), gpq.data_ptr(),
+            gpr.data_ptr(), a0, a0 + 4, a0 + 8, gbp.data_ptr(), gbq.data_ptr(),
+            gbr.data_ptr(), T, n, C, int(hp[0]), float(hp[1]), float(hp[2]),
+            ws.data_ptr(), ws.numel(), _stream(res.device))
+    _C.check(rc, "mhc_wrapper_bwd_dynamic")
+    return (gres, gbrn, gw.to(w0.dtype), gpp.to(pp0.dtype), gpq.to(pq0.dtype),
+            gpr.reshape(pr0.shape).to(pr0.dtype), galpha[0].to(ap0.dtype).view_as(ap0),
+            galpha[1].to(aq0.dtype).view_as(aq0), galpha[2].to(ar0.dtype).view_as(ar0),
+            gbp.to(bp0.dtype), gbq.to(bq0.dtype), gbr.to(br0.dtype))
+
+
+class WrapperDynamicPreNormFunction(torch.autograd.Function):
+    """The fused n = 4 wrapper forward together with the next branch's input
+    RMSNorm (a pre-norm transformer block normalises the hidden state the
+    wrapper returns before its attention / MLP).  The reference runs
+    MHCResidualWrapper.forward (layer.py:287-316) and then the branch's
+    rmsnorm (ops.py:87-136) as separate passes; here the wrapper's output pass
+    writes both the hidden state and its normalised copy, so the hidden state
+    is not read back to be normalised.  Backward: the norm's input gradient
+    (mhc_rmsnorm_bwd) joins the hidden state's own gradient before the
+    wrapper's fused backward."""
+
+    @staticmethod
+    def forward(ctx, residual, branch, residual_mode, norm_weight, norm_eps, rmsnorm_weight,
+                phi_pre, phi_post, phi_res, alpha_pre, alpha_post, alpha_res, b_pre, b_post,
+                b_res, sinkhorn_iters, sinkhorn_eps, rmsnorm_eps):
         n = 4
-        T, C = res.shape
-        g = _f32(grad_mean)
-        w = _f32(w0)
-        pp, pq, pr = _f32(pp0), _f32(pq0), _f32(pr0).reshape(n * n, n * C)
-        ap, aq, ar = (_as_scalar_tensor(a, res) for a in (ap0, aq0, ar0))
-        bp, bq, br = _f32(bp0), _f32(bq0), _f32(br0)
-        gres = torch.empty_like(res)
-        gbrn = torch.empty_like(brn)
-        gw, gpp, gpq, gpr, gbp, gbq, gbr, galpha = _flat_param_grads(n, C, res.device)
-        ws = _workspace(_lib.mhc_layer_bwd_dynamic_workspace_bytes(T, n, C), res.device)
-        a0 = galpha.data_ptr()
-        with _DevGuard(res):
-            rc = _lib.mhc_wrapper_bwd_dynamic(
-                g.data_ptr(), res.data_ptr(), brn.data_ptr(), ctx.sc, w.data_ptr(),
-                pp.data_ptr(), pq.data_ptr(), pr.data_ptr(), ap.data_ptr(), aq.data_ptr(),
-                ar.data_ptr(), bp.data_ptr(), bq.data_ptr(), br.data_ptr(), state.data_ptr(),
-                gres.data_ptr(), gbrn.data_ptr(), gw.data_ptr(), gpp.data_ptr(), gpq.data_ptr(),
-                gpr.data_ptr(), a0, a0 + 4, a0 + 8, gbp.data_ptr(), gbq.data_ptr(),
-                gbr.data_ptr(), T, n, C, int(ctx.hp[0]), float(ctx.hp[1]), float(ctx.hp[2]),
-                ws.data_ptr(), ws.numel(), _stream(res.device))
-        _C.check(rc, "mhc_wrapper_bwd_dynamic")
-        return (gres, gbrn, None, gw.to(w0.dtype), gpp.to(pp0.dtype), gpq.to(pq0.dtype),
-                gpr.reshape(pr0.shape).to(pr0.dtype), galpha[0].to(ap0.dtype).view_as(ap0),
-                galpha[1].to(aq0.dtype).view_as(aq0), galpha[2].to(ar0.dtype).view_as(ar0),
-                gbp.to(bp0.dtype), gbq.to(bq0.dtype), gbr.to(br0.dtype), None, None, None)
+        T, C = residual.shape
+        sc = wrapper_stream_scales(n, residual_mode)
+        w = _f32(rmsnorm_weight)
+        w2 = _f32(norm_weight)
+        pp, pq, pr = _f32(phi_pre), _f32(phi_post), _f32(phi_res).reshape(n * n, n * C)
+        ap, aq, ar = (_as_scalar_tensor(a, residual) for a in (alpha_pre, alpha_post, alpha_res))
+        bp, bq, br = _f32(b_pre), _f32(b_post), _f32(b_res)
+        dev = residual.device
+        mean = torch.empty(T, C, dtype=torch.float32, device=dev)
+        normed = torch.empty(T, C, dtype=torch.float32, device=dev)
+        rms2 = torch.empty(T, dtype=torch.float32, device=dev)
+        state = torch.empty(T, token_state_stride(n), dtype=torch.float32, device=dev)
+        ws = _workspace(_lib.mhc_layer_fwd_dynamic_workspace_bytes(T, n, C), dev)
+        with _DevGuard(residual):
+            rc = _lib.mhc_wrapper_fwd_dynamic_prenorm(
+                residual.data_ptr(), branch.data_ptr(), sc, w.data_ptr(), pp.data_ptr(),
+                pq.data_ptr(), pr.data_ptr(), ap.data_ptr(), aq.data_ptr(), ar.data_ptr(),
+                bp.data_ptr(), bq.data_ptr(), br.data_ptr(), w2.data_ptr(), float(norm_eps),
+                mean.data_ptr(), normed.data_ptr(), rms2.data_ptr(), state.data_ptr(),
+                T, n, C, int(sinkhorn_iters), float(sinkhorn_eps), float(rmsnorm_eps),
+                ws.data_ptr(), ws.numel(), _stream(dev))
+        _C.check(rc, "mhc_wrapper_fwd_dynamic_prenorm")
+        ctx.save_for_backward(residual, branch, rmsnorm_weight, phi_pre, phi_post, phi_res,
+                              alpha_pre, alpha_post, alpha_res, b_pre, b_post, b_res, state,
+                              mean, norm_weight, rms2)
+        ctx.sc = sc
+        ctx.hp = (sinkhorn_iters, sinkhorn_eps, rmsnorm_eps)
+        return mean, normed
+
+    @staticmethod
+    def backward(ctx, grad_mean, grad_normed):
+        saved = ctx.saved_tensors
+        mean, w2, rms2 = saved[13:]
+        g = _f32(grad_mean) if grad_mean is not None else torch.zeros_like(mean)
+        gw2 = None
+        if grad_normed is not None:
+            gi, gw2 = rmsnorm_bwd(grad_normed, mean, w2, rms2)
+            g = g + gi
+            gw2 = gw2.to(w2.dtype)
+        grads = _wrapper_dynamic_bwd(saved[:13], ctx.sc, ctx.hp, g)
+        return (grads[0], grads[1], None, gw2, None, *grads[2:], None, None, None)
+
+
+def wrapper_fused_dynamic_prenorm(residual, branch, residual_mode, norm_weight, norm_eps,
+                                  rmsnorm_weight, phi_pre, phi_post, phi_res, alpha_pre,
+                                  alpha_post, alpha_res, b_pre, b_post, b_res, sinkhorn_iters=20,
+                                  sinkhorn_eps=1e-8, rmsnorm_eps=1e-5):
+    """[tokens, C] residual and branch -> ([tokens, C] stream mean, its RMSNorm
+    with norm_weight / norm_eps), n = 4 dynamic H, with autograd."""
+    _require_cuda("wrapper_fused_dynamic_prenorm", residual, branch, norm_weight)
+    return WrapperDynamicPreNormFunction.apply(residual, branch, residual_mode, norm_weight,
+                                               norm_eps, rmsnorm_weight, phi_pre, phi_post,
+                                               phi_res, alpha_pre, alpha_post, alpha_res, b_pre,
+                                               b_post, b_res, sinkhorn_iters, sinkhorn_eps,
+                                               rmsnorm_eps)
 
 
 def wrapper_fused_dynamic(residual, branch, residual_mode, rmsnorm_weight, phi_pre, phi_post,

@@ -323,6 +323,61 @@ def test_residual_wrapper_fused(cuda, mode, shape, alpha):
     close(fused["out"].reshape(T, C)[idx.to(cuda)], o64, what="fused wrapper out vs fp64")
 
 
+@pytest.mark.parametrize("mode,shape,alpha", [("decay", (3, 345, 4096), 0.5),
+                                              ("zero", (700, 1024), 0.01),
+                                              ("decay", (2, 64, 7168), 0.5),
+                                              ("decay", (5, 96), 0.5)])
+def test_residual_wrapper_prenorm(cuda, mode, shape, alpha):
+    """MHCResidualWrapper.forward_prenorm: the hidden state and the next
+    branch's input RMSNorm of it from one output pass (n = 4 dynamic H; C = 96
+    takes the unfused path).  Forward and every gradient, with upstream
+    gradients on both outputs, against the unfused composition (wrapper ->
+    rmsnorm over this library's kernels) and, on a token sample, the fp64
+    oracle (reference layer.py:287-316 then ops_pytorch_backward rmsnorm)."""
+    from mhc_ascend_b200 import ops
+    n, C = 4, shape[-1]
+    gen = torch.Generator().manual_seed(23 + C)
+    r, b = torch.randn(*shape, generator=gen), torch.randn(*shape, generator=gen)
+    gh, gn = torch.randn(*shape, generator=gen), torch.randn(*shape, generator=gen)
+    w2 = torch.rand(C, generator=gen) + 0.5
+    params = O.make_dynamic_params(n, C, gen, alpha=alpha, bias_std=0.5, weight="rand")
+    w = mhc.replace_residual_with_mhc(hidden_dim=C, expansion_rate=n, residual_mode=mode).to(cuda)
+    with torch.no_grad():
+        for k, v in params.items():
+            getattr(w.mhc, k).copy_(v.reshape(getattr(w.mhc, k).shape))
+    rd, bd = r.to(cuda).requires_grad_(True), b.to(cuda).requires_grad_(True)
+    w2d = w2.to(cuda).requires_grad_(True)
+    hid, nrm = w.forward_prenorm(rd, bd, w2d, 1e-5)
+    torch.autograd.backward([hid, nrm], [gh.to(cuda), gn.to(cuda)])
+    fused = {"hid": hid.detach(), "nrm": nrm.detach(), "res": rd.grad, "br": bd.grad,
+             "w2": w2d.grad.clone()}
+    fused.update({k: p.grad.clone() for k, p in w.mhc.named_parameters()})
+    w.mhc.zero_grad(set_to_none=True)
+    ru, bu = r.to(cuda).requires_grad_(True), b.to(cuda).requires_grad_(True)
+    w2u = w2.to(cuda).requires_grad_(True)
+    hu = w(ru, bu)
+    nu = ops.rmsnorm(hu.reshape(-1, C), w2u, 1e-5).reshape(shape)
+    torch.autograd.backward([hu, nu], [gh.to(cuda), gn.to(cuda)])
+    close(fused["hid"], hu.detach(), rtol=1e-6, atol=1e-6, what="prenorm hidden vs unfused")
+    close(fused["nrm"], nu.detach(), rtol=1e-5, atol=1e-6, what="prenorm normed vs unfused")
+    close(fused["res"], ru.grad, rtol=1e-5, atol=1e-6, what="prenorm grad residual vs unfused")
+    close(fused["br"], bu.grad, rtol=1e-5, atol=1e-6, what="prenorm grad branch vs unfused")
+    close_param(fused["w2"], w2u.grad, rtol=1e-5, atol=1e-6, what="prenorm grad norm weight")
+    for k, p in w.mhc.named_parameters():
+        close_param(fused[k], p.grad, rtol=1e-5, atol=1e-6, what="prenorm grad " + k)
+    # fp64 oracle on a token sample
+    T = r.numel() // C
+    idx = torch.randperm(T, generator=gen)[:64]
+    rs, bs = r.reshape(T, C)[idx].double(), b.reshape(T, C)[idx].double()
+    streams, _ = O.residual_wrapper_pack(rs, bs, n, mode)
+    p64 = {k: v.double() for k, v in params.items()}
+    h64 = O.mhc_layer_dynamic(streams, *[p64[k] for k in O.DYNAMIC_PARAM_ORDER]).mean(dim=1)
+    n64 = O.rmsnorm(h64, w2.double(), 1e-5)
+    di = idx.to(cuda)
+    close(fused["hid"].reshape(T, C)[di], h64, what="prenorm hidden vs fp64")
+    close(fused["nrm"].reshape(T, C)[di], n64, what="prenorm normed vs fp64")
+
+
 @pytest.mark.parametrize("n,mode,shape", [(4, "decay", (2, 9, 4096)), (6, "decay", (5, 33)),
                                           (3, "zero", (4, 64))])
 def test_residual_wrapper_bf16_inputs(cuda, n, mode, shape):
