@@ -156,10 +156,29 @@ FwdPlan plan_fwd(int64_t B, int64_t C) {
 
 constexpr int kTokPartBlocks = 64;
 
+// Token splits of the tensor-core grad_x (grad_x6_kernel, one CTA per SM):
+// minimise waves x (blocks per CTA x t_block + t_ramp), with t_block the
+// steady time of a 32-token block and t_ramp a CTA's start-up and drain,
+// fitted from measured launches over split counts 1..8 on a B200 at
+// n = 4, C = 4096 (fp32 streams 1.24 / 8.7 us, bf16 1.54 / 4.9 us).  Pure
+// wave balance ignores the ramp: at 8192 fp32 tokens it picked 8 splits
+// (0.339 ms) where one split takes 0.327 ms.
+int choose_gx6_splits(int64_t tiles, int64_t nblk, int sms, double t_block, double t_ramp) {
+  int best = 1;
+  double best_cost = 1e300;
+  const int64_t max_s = nblk < 1024 ? nblk : 1024;
+  for (int64_t s = 1; s <= max_s; ++s) {
+    const int64_t waves = (tiles * s + sms - 1) / sms;
+    const double cost = (double)waves * ((double)((nblk + s - 1) / s) * t_block + t_ramp);
+    if (cost < best_cost - 1e-9) { best_cost = cost; best = (int)s; }
+  }
+  return best;
+}
+
 struct BwdPlan {
   int ntiles, nsplit;
   int64_t nblk6;  // token blocks of the warp-specialised grad_x (n = 4, dynamic H)
-  int nsplit6;
+  int nsplit6, nsplit6b;  // fp32 streams, bf16 streams
   size_t img;
   size_t stats, tokb, tokr, dphi, gw, tot;
 };
@@ -170,10 +189,13 @@ BwdPlan plan_bwd(int64_t B, int64_t C) {
   p.ntiles = (int)((C + GX_CW - 1) / GX_CW);
   p.nsplit = choose_gx_splits(p.ntiles, B, num_sms(), N <= 4 ? 2 : 1);
   p.nblk6 = (N == 4 && DYN) ? (B + Gx6Cfg::TOK - 1) / Gx6Cfg::TOK : 0;
-  p.nsplit6 = (N == 4 && DYN && p.nblk6 > 0) ? choose_gx_splits((C + 31) / 32, p.nblk6, num_sms(), 1) : 0;
+  const bool six = N == 4 && DYN && p.nblk6 > 0;
+  p.nsplit6 = six ? choose_gx6_splits((C + 31) / 32, p.nblk6, num_sms(), 1.24, 8.7) : 0;
+  p.nsplit6b = six ? choose_gx6_splits((C + 31) / 32, p.nblk6, num_sms(), 1.54, 4.9) : 0;
   p.img = (size_t)p.nblk6 * Gx6Cfg::IMG_FLOATS;
   int64_t msplit = p.nsplit;
   if (p.nsplit6 > msplit) msplit = p.nsplit6;
+  if (p.nsplit6b > msplit) msplit = p.nsplit6b;
   p.stats = (size_t)B * (DYN ? L<N>::NSD : L<N>::NS1) * 2;  // fp64
   p.tokb = (size_t)B * L<N>::TB;
   p.tokr = (size_t)B * (DYN ? L<N>::NR : L<N>::NRS) * 2;  // fp64
@@ -494,9 +516,10 @@ int run_bwd_dynamic(const T* g, const T* x, const float* w, const float* pp,
         make_tmap_2d(&om, dt, sizeof(T), gx, (uint64_t)B * N, C, C, F6::TOK * N, F6::CW)) {
       cudaFuncSetAttribute(grad_x6_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S6::SMEM);
       const int nt6 = (int)(C / F6::CW);
-      { ProfScope _ps("grad_x", s); grad_x6_kernel<T><<<(unsigned)(nt6 * p.nsplit6), F6::THREADS, S6::SMEM, s>>>(
-          gm, xm, om, xm, om, WrapScales{}, img, w, pp, pq, pr, gx, dphi, gwp, B, C, nt6, p.nsplit6, p.nblk6); }
-      nsplit = p.nsplit6;
+      const int ns6 = sizeof(T) == 2 ? p.nsplit6b : p.nsplit6;
+      { ProfScope _ps("grad_x", s); grad_x6_kernel<T><<<(unsigned)(nt6 * ns6), F6::THREADS, S6::SMEM, s>>>(
+          gm, xm, om, xm, om, WrapScales{}, img, w, pp, pq, pr, gx, dphi, gwp, B, C, nt6, ns6, p.nblk6); }
+      nsplit = ns6;
       gx_done = true;
     }
   }
