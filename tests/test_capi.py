@@ -77,6 +77,25 @@ def test_wrapper_entry_points_validate_without_gpu():
     assert lib.mhc_wrapper_pack_bwd(p, p, None, None, 4, 4, 8, None) == ERR_INVALID
 
 
+def test_wrapper_prenorm_validates_without_gpu():
+    """mhc_wrapper_fwd_dynamic_prenorm checks its extra arguments (the next
+    branch's norm weight, eps and outputs) before any device work."""
+    lib = _C.load()
+    p, odd = ctypes.c_void_p(16), ctypes.c_void_p(20)
+    sc = (ctypes.c_float * 4)(1.0, 0.0, 0.1, 0.01)
+
+    def call(norm_w=p, eps=1e-5, normed=p, rms=p, tokens=8):
+        return lib.mhc_wrapper_fwd_dynamic_prenorm(
+            p, p, sc, p, p, p, p, p, p, p, p, p, p, norm_w, eps, p, normed, rms, p,
+            tokens, 4, 64, 20, 1e-8, 1e-5, None, 0, None)
+
+    assert call(eps=-1.0) == ERR_INVALID and "norm_eps" in _C.last_error()
+    assert call(norm_w=None) == ERR_INVALID and "norm_weight" in _C.last_error()
+    assert call(rms=None) == ERR_INVALID and "out_norm_rms" in _C.last_error()
+    assert call(normed=odd) == -3 and "aligned" in _C.last_error()
+    assert call(tokens=0) == 0
+
+
 def test_empty_batch_is_a_noop():
     lib = _C.load()
     p = ctypes.c_void_p(16)
