@@ -47,9 +47,11 @@ CONFIGS = {
 }
 
 
-def _spin_cycles(ms=2.0):
+def _spin_cycles(ms=8.0):
     """GPU clock cycles of an untimed spin of about `ms` milliseconds at the
-    B200's 1965 MHz maximum SM clock (longer at lower clocks: harmless)."""
+    B200's 1965 MHz maximum SM clock (longer at lower clocks: harmless).  8 ms
+    outlasts a GIL hand-off to the clock-sampling thread (Python's switch
+    interval is 5 ms), so the host stays ahead of the GPU."""
     return int(ms * 1.965e6)
 
 
